@@ -1,0 +1,357 @@
+#!/usr/bin/env python3
+"""Benchmark of the block-FP8 MoE expert path on B200.
+
+Workload: a Qwen3-30B-A3B-shaped MoE layer — hidden
+2048, 128 experts, moe_intermediate 768, top-8 with normalised probabilities,
+E4M3 weights with 128x128 f32 block scales, f32 router — decoding a batch of
+`--tokens` bf16 tokens (default 1; the config also lists 4 and 16).  One step =
+one MoE-layer forward over one batch.  Data are seeded synthetic tensors with
+the configured distributions (no checkpoint is available).
+
+Steps cycle through `--layers` distinct registered layers (default 16, 9.7 GB of
+expert weights) with a fresh token batch each step, so a layer's weights come
+back only after ~16 x 39 MB of other traffic: inputs larger than L2, no L2 reuse
+between timed iterations.
+
+value = tokens/s over all ranks, device-timed (CUDA events on the launch
+stream, max over ranks), inputs resident in HBM.  e2e = the same metric through
+the C ABI with host buffers (pinned H2D of the tokens and D2H of the outputs
+inside the timed region).  --gpus N > 1 runs one process per GPU (torchrun), each
+rank an independent replica of the workload (weak scaling).
+
+--impl reference times the reference path's CPU implementation (the oracle's C
+restatement of the Zig AVX2 path, all host threads) on the same config.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+EXPERT_BYTES = {}  # per config: bytes of one expert (3 projections + scales)
+
+
+def expert_bytes(d) -> int:
+    nb = lambda x: (x + 127) // 128
+    return 3 * d.inter * d.hidden + 4 * (2 * nb(d.inter) * nb(d.hidden) + nb(d.hidden) * nb(d.inter))
+
+
+def shared_bytes(d) -> int:
+    if not d.shared_inter:
+        return 0
+    nb = lambda x: (x + 127) // 128
+    return 3 * d.shared_inter * d.hidden + 4 * 3 * nb(d.shared_inter) * nb(d.hidden) + 4 * d.hidden
+
+
+def algorithmic_bytes(d, T: int, U: float) -> float:
+    """Bytes one layer call must move (survey 8d): U distinct experts' weights +
+    scales, the f32 router, the shared expert, bf16 tokens in, f32 outputs out."""
+    return U * expert_bytes(d) + shared_bytes(d) + d.experts * d.hidden * 4 + T * d.hidden * (2 + 4)
+
+
+def algorithmic_flops(d, T: int) -> float:
+    return T * (d.topk * 6 * d.hidden * d.inter + 2 * d.experts * d.hidden +
+                (6 * d.hidden * d.shared_inter if d.shared_inter else 0))
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_sample(d, layers_np, T, seconds, threads):
+    """Time the CPU oracle (restatement of the reference AVX2 path) on a bounded
+    sample of the workload: as many steps as fit in ~`seconds`."""
+    import torch
+
+    import oracle
+    from colizig_b200 import synth
+
+    oracle_layer = oracle.layer_from_dict
+    oracle.set_threads(threads)
+    od = oracle.Dims(d.hidden, d.experts, d.topk, d.inter, d.shared_inter, d.norm_topk)
+    ols = [oracle_layer(w) for w in layers_np]
+    toks = [synth.tokens_f32(synth.make_tokens(T, d.hidden, 5000 + i, device="cpu")) for i in range(64)]
+    oracle.moe_forward(ols[0], od, toks[0])  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        oracle.moe_forward(ols[n % len(ols)], od, toks[n % len(toks)])
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds or n >= 100000:
+            break
+    oracle.set_threads(1)
+    return n * T / dt, n, dt
+
+
+def reference_arm(args):
+    import torch
+
+    from colizig_b200 import synth
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    d = synth.CONFIGS[args.config]
+    T = args.tokens
+    cores = os.cpu_count() or 1
+    layers = [synth.to_numpy_layer(synth.make_layer(d, seed=i, device="cpu")) for i in range(args.cpu_layers)]
+    import oracle
+
+    oracle_layer = oracle.layer_from_dict
+    oracle.set_threads(cores)
+    od = oracle.Dims(d.hidden, d.experts, d.topk, d.inter, d.shared_inter, d.norm_topk)
+    ols = [oracle_layer(w) for w in layers]
+    toks = [synth.tokens_f32(synth.make_tokens(T, d.hidden, 9000 + i, device="cpu"))
+            for i in range(args.steps + args.warmup)]
+    for i in range(args.warmup):
+        oracle.moe_forward(ols[i % len(ols)], od, toks[i])
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        oracle.moe_forward(ols[i % len(ols)], od, toks[args.warmup + i])
+    dt = time.perf_counter() - t0
+    value = args.steps * T / dt
+    line = {
+        "impl": "reference", "metric": f"MoE-layer decode tokens/s ({args.config}, T={T})", "value": value,
+        "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_block(args, d),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} steps of the {args.config} T={T} layer forward over "
+                                   f"{args.cpu_layers} layers (C restatement of the reference AVX2 path)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_block(args, d):
+    return {"workload": f"{args.config} MoE layer decode, {args.tokens} token(s)/step (BASELINE config 2)",
+            "hidden": d.hidden, "experts": d.experts, "topk": d.topk, "moe_intermediate": d.inter,
+            "shared_intermediate": d.shared_inter, "tokens_per_step": args.tokens,
+            "global_batch": args.tokens * args.gpus, "layers_cycled": args.layers,
+            "l2": "inputs larger than L2: steps cycle through distinct layers (no flush)",
+            "parallelism": f"replicas x{args.gpus}" if args.gpus > 1 else "single GPU"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c2")
+    ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--cpu-layers", type=int, default=4)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import colizig_b200 as cz
+    from colizig_b200 import _abi, moe, synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    cz.gpu.init(local)
+    d = synth.CONFIGS[args.config]
+    T = args.tokens
+    dev = torch.device("cuda", local)
+
+    layers, host_layers = [], []
+    for l in range(args.layers):
+        w = synth.make_layer(d, seed=1000 * rank + l, device=dev)
+        layers.append(moe.Layer.from_weights(l, d, w))
+        if rank == 0 and world == 1 and l < args.cpu_layers and not args.no_cpu:
+            host_layers.append(synth.to_numpy_layer(w))
+        del w
+    torch.cuda.empty_cache()
+
+    n = args.warmup + args.steps
+    xs = [synth.make_tokens(T, d.hidden, 20000 + i, device=dev) for i in range(n)]
+    outs = torch.empty((n, T, d.hidden), dtype=torch.float32, device=dev)
+    idx = torch.empty((n, T, d.topk), dtype=torch.int32, device=dev)
+    gates = torch.empty((n, T, d.topk), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+    L = _abi.load()
+    sh = stream.cuda_stream
+
+    def step(i):
+        lay = layers[i % len(layers)]
+        rc = L.colizig_cuda_moe_forward(lay.id, xs[i].data_ptr(), _abi.COLIZIG_X_BF16, T, outs[i].data_ptr(),
+                                        idx[i].data_ptr(), gates[i].data_ptr(), _abi.COLIZIG_PTR_DEVICE, sh)
+        if rc:
+            raise cz.ColizigError("colizig_cuda_moe_forward", rc)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    moe.check()
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for k in range(args.steps):
+        ev[k][0].record(stream)
+        step(args.warmup + k)
+        ev[k][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    if world > 1:
+        dist.barrier()
+    moe.check()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    kernel_ms = [a.elapsed_time(b) for a, b in ev]
+    if world > 1:
+        tt = torch.tensor([elapsed_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(tt.item())
+    value = world * args.steps * T / (elapsed_ms / 1e3)
+
+    # realised distinct experts per step -> algorithmic bytes
+    ids = idx[args.warmup:].cpu().numpy()
+    U = np.array([len(np.unique(ids[k])) for k in range(args.steps)], np.float64)
+    bytes_per = np.array([algorithmic_bytes(d, T, u) for u in U])
+    hbm_peak, tf_peak, peak_kind = load_peaks()
+    achieved_gbs = float(bytes_per.sum() / (np.sum(kernel_ms) / 1e3) / 1e9)
+
+    # end to end through the C ABI with host buffers (pinned), synchronous calls
+    xh = [x.cpu().pin_memory() for x in xs[:min(n, 64)]]
+    oh = torch.empty((T, d.hidden), dtype=torch.float32).pin_memory()
+    ih = torch.empty((T, d.topk), dtype=torch.int32).pin_memory()
+    gh = torch.empty((T, d.topk), dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        lay = layers[i % len(layers)]
+        rc = L.colizig_cuda_moe_forward(lay.id, xh[i % len(xh)].data_ptr(), _abi.COLIZIG_X_BF16, T, oh.data_ptr(),
+                                        ih.data_ptr(), gh.data_ptr(), 0, None)
+        if rc:
+            raise cz.ColizigError("colizig_cuda_moe_forward", rc)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        e2e_step(args.warmup + k)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        tt = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_s = float(tt.item())
+    e2e = {"value": world * args.steps * T / e2e_s, "unit": "tokens/s",
+           "h2d_bytes_per_step": T * d.hidden * 2, "d2h_bytes_per_step": T * d.hidden * 4 + T * d.topk * 8,
+           "ms_per_step": e2e_s / args.steps * 1e3}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cores = os.cpu_count() or 1
+        v, nsteps, dt = cpu_sample(d, host_layers, T, args.cpu_seconds, cores)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{nsteps} layer forwards of {args.config} T={T} in {dt:.1f} s over {len(host_layers)} "
+                         f"layers (C restatement of the reference AVX2 path, {cores} threads)"}
+
+    if rank == 0:
+        line = {
+            "metric": f"MoE-layer decode tokens/s ({args.config}, T={T})", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_block(args, d),
+            "hbm_gbs": achieved_gbs,
+            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved_gbs / hbm_peak, "traffic": None,
+                         "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6.65 TB/s",
+                         "kernel": "moe_decode_kernel", "kernel_ms_avg": float(np.mean(kernel_ms)),
+                         "bytes_per_launch_avg": float(bytes_per.mean()), "distinct_experts_avg": float(U.mean())},
+            "tflops": algorithmic_flops(d, T) * args.steps / (np.sum(kernel_ms) / 1e3) / 1e12,
+            "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    for lay in layers:
+        lay.unregister()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,619 @@
+// Host side of libcolizig_cuda.so: the device context, the keyed resident
+// weight store behind colizig_cuda_matmul_fp8, the MoE layer registry and every
+// exported entry point of include/colizig_cuda.h.
+//
+// The reference keeps one global device context guarded by the caller's
+// spinlock (gpu.zig:51-62) and an LRU of VRAM slots (colizig_cuda.cu:80-169).
+// Here the context is guarded by a mutex inside the library, MoE weights are
+// registered once into resident HBM (no per-call upload), and every entry
+// point saves/restores the host MXCSR like the reference's CsrGuard
+// (colizig_cuda.cu:22-29): the CUDA runtime may turn on flush-to-zero on the
+// calling thread, which would silently change the caller's CPU float math.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <list>
+#include <map>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#if defined(__x86_64__) || defined(_M_X64)
+#include <xmmintrin.h>
+#define CZ_HAVE_MXCSR 1
+#endif
+
+#include "../../include/colizig_cuda.h"
+#include "cz_common.cuh"
+#include "cz_internal.h"
+
+#define CZ_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+struct CsrGuard {
+#ifdef CZ_HAVE_MXCSR
+    unsigned saved;
+    CsrGuard() : saved(_mm_getcsr()) {}
+    ~CsrGuard() { _mm_setcsr(saved); }
+#endif
+};
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+    bool ensure(size_t need) {
+        if (cap >= need && p) return true;
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+        if (need == 0) need = 16;
+        if (cudaMalloc(&p, need) != cudaSuccess) {
+            p = nullptr;
+            return false;
+        }
+        cap = need;
+        return true;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+    }
+    template <class T>
+    T* as() const {
+        return reinterpret_cast<T*>(p);
+    }
+};
+
+struct Keyed {
+    void* w = nullptr;
+    void* s = nullptr;
+    size_t wb = 0, sb = 0;
+    std::list<uint64_t>::iterator lru;
+};
+
+struct MoeLayer {
+    colizig_moe_dims d{};
+    void* mem = nullptr;
+    size_t bytes = 0;
+    float* router = nullptr;
+    uint8_t *gate_w = nullptr, *up_w = nullptr, *down_w = nullptr;
+    float *gate_s = nullptr, *up_s = nullptr, *down_s = nullptr;
+    uint8_t *sh_gate_w = nullptr, *sh_up_w = nullptr, *sh_down_w = nullptr;
+    float *sh_gate_s = nullptr, *sh_up_s = nullptr, *sh_down_s = nullptr;
+    float* sh_gate = nullptr;
+};
+
+struct Ctx {
+    bool inited = false;
+    int dev = 0;
+    int num_sms = 0;
+    char name[192] = {0};
+    cudaStream_t stream = nullptr;
+    // legacy matmul scratch
+    DevBuf d_x, d_y, d_w, d_s;
+    // keyed resident store
+    std::unordered_map<uint64_t, Keyed> keyed;
+    std::list<uint64_t> lru;  // front = most recent
+    size_t budget = 0, used = 0;
+    uint64_t hits = 0, misses = 0, uploaded = 0;
+    // MoE
+    std::map<uint32_t, MoeLayer> layers;
+    DevBuf logits, xf, hbuf, io_x, io_out, io_idx, io_gates, ones;
+    uint32_t* sync = nullptr;
+};
+
+Ctx g;
+std::mutex g_mu;
+
+size_t nb(size_t x) { return (x + 127) / 128; }
+
+int ensure_sync() {
+    if (g.sync) return CZ_OK;
+    if (cudaMalloc(&g.sync, cz::kSyncWords * sizeof(uint32_t)) != cudaSuccess) {
+        g.sync = nullptr;
+        return CZ_EALLOC;
+    }
+    if (cudaMemset(g.sync, 0, cz::kSyncWords * sizeof(uint32_t)) != cudaSuccess) return CZ_EALLOC;
+    return CZ_OK;
+}
+
+void free_layer(MoeLayer& L) {
+    if (L.mem) cudaFree(L.mem);
+    L = MoeLayer{};
+}
+
+void evict_lru_one() {
+    if (g.lru.empty()) return;
+    const uint64_t k = g.lru.back();
+    g.lru.pop_back();
+    auto it = g.keyed.find(k);
+    if (it != g.keyed.end()) {
+        cudaFree(it->second.w);
+        cudaFree(it->second.s);
+        g.used -= it->second.wb + it->second.sb;
+        g.keyed.erase(it);
+    }
+}
+
+void shutdown_locked() {
+    if (!g.inited) return;
+    cudaSetDevice(g.dev);
+    cudaDeviceSynchronize();
+    for (auto& kv : g.keyed) {
+        cudaFree(kv.second.w);
+        cudaFree(kv.second.s);
+    }
+    g.keyed.clear();
+    g.lru.clear();
+    for (auto& kv : g.layers) free_layer(kv.second);
+    g.layers.clear();
+    for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.xf, &g.hbuf, &g.io_x, &g.io_out, &g.io_idx,
+                      &g.io_gates, &g.ones})
+        b->release();
+    if (g.sync) cudaFree(g.sync);
+    if (g.stream) cudaStreamDestroy(g.stream);
+    g = Ctx{};
+}
+
+int init_locked(int device) {
+    if (g.inited) return g.dev == device ? CZ_OK : -2;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n < 1) return -1;
+    if (device < 0 || device >= n) return -2;
+    if (cudaSetDevice(device) != cudaSuccess) return -2;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return -3;
+    snprintf(g.name, sizeof g.name, "%s (sm_%d%d, %zu MiB)", prop.name, prop.major, prop.minor,
+             (size_t)(prop.totalGlobalMem >> 20));
+    g.num_sms = prop.multiProcessorCount;
+    g.dev = device;
+    if (cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking) != cudaSuccess) return -4;
+    g.budget = 0;  // keyed store disabled until set (colizig_cuda.cu:184)
+    g.inited = true;
+    return CZ_OK;
+}
+
+// Copy `count` items of `bytes` each from per-expert source pointers into a
+// contiguous destination, merging runs that are contiguous in the source.
+template <class T>
+int gather_copy(uint8_t* dst, const colizig_moe_expert* ex, int count, size_t bytes, T colizig_moe_expert::*field,
+                cudaMemcpyKind kind) {
+    int e = 0;
+    while (e < count) {
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(ex[e].*field);
+        if (!src) return CZ_EARGS;
+        int run = 1;
+        while (e + run < count && reinterpret_cast<const uint8_t*>(ex[e + run].*field) == src + run * bytes) ++run;
+        if (cudaMemcpyAsync(dst + (size_t)e * bytes, src, (size_t)run * bytes, kind, g.stream) != cudaSuccess)
+            return CZ_EH2D;
+        e += run;
+    }
+    return CZ_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+int ensure_decode_scratch(const colizig_moe_dims& d) {
+    const size_t T = cz::kDecodeMaxTokens;
+    const size_t HS = d.inter > d.shared_inter ? d.inter : d.shared_inter;
+    if (!g.logits.ensure(T * (d.experts + 1) * sizeof(float))) return CZ_EALLOC;
+    if (!g.xf.ensure(T * d.hidden * sizeof(float))) return CZ_EALLOC;
+    if (!g.hbuf.ensure(T * (d.topk + 1) * HS * sizeof(float))) return CZ_EALLOC;
+    return ensure_sync();
+}
+
+cz::DecodeParams make_params(const MoeLayer& L) {
+    cz::DecodeParams p{};
+    p.router = L.router;
+    p.gate_w = L.gate_w;
+    p.up_w = L.up_w;
+    p.down_w = L.down_w;
+    p.gate_s = L.gate_s;
+    p.up_s = L.up_s;
+    p.down_s = L.down_s;
+    p.sh_gate_w = L.sh_gate_w;
+    p.sh_up_w = L.sh_up_w;
+    p.sh_down_w = L.sh_down_w;
+    p.sh_gate_s = L.sh_gate_s;
+    p.sh_up_s = L.sh_up_s;
+    p.sh_down_s = L.sh_down_s;
+    p.sh_gate = L.sh_gate;
+    p.H = (int)L.d.hidden;
+    p.E = (int)L.d.experts;
+    p.K = (int)L.d.topk;
+    p.I = (int)L.d.inter;
+    p.SI = (int)L.d.shared_inter;
+    p.norm_topk = (int)L.d.norm_topk;
+    p.logits = g.logits.as<float>();
+    p.hbuf = g.hbuf.as<float>();
+    p.sync = g.sync;
+    return p;
+}
+
+// Runs one layer over T tokens (device pointers, stream-ordered), in launches
+// of at most kDecodeMaxTokens tokens.
+int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uint32_t* idx, float* gates,
+            const float* rms_w, float eps, const float* residual, cudaStream_t st) {
+    int rc = ensure_decode_scratch(L.d);
+    if (rc) return rc;
+    const size_t xelt = x_bf16 ? 2 : 4;
+    for (int t0 = 0; t0 < T; t0 += cz::kDecodeMaxTokens) {
+        const int n = T - t0 < cz::kDecodeMaxTokens ? T - t0 : cz::kDecodeMaxTokens;
+        cz::DecodeParams p = make_params(L);
+        p.x = reinterpret_cast<const uint8_t*>(x) + (size_t)t0 * L.d.hidden * xelt;
+        p.x_bf16 = x_bf16;
+        p.T = n;
+        p.rms_w = rms_w;
+        p.eps = eps;
+        p.residual = residual ? residual + (size_t)t0 * L.d.hidden : nullptr;
+        p.out = out + (size_t)t0 * L.d.hidden;
+        p.topk_idx = idx ? idx + (size_t)t0 * L.d.topk : nullptr;
+        p.topk_gates = gates ? gates + (size_t)t0 * L.d.topk : nullptr;
+        // phase A reads f32 tokens: the caller's f32 x directly, else a converted copy
+        p.xf = (x_bf16 || rms_w) ? g.xf.as<float>() : nullptr;
+        rc = cz::decode_launch(p, g.num_sms, st);
+        if (rc) return rc;
+    }
+    return CZ_OK;
+}
+
+// Read and clear the device error word (synchronises `st`).
+int check_device_error(cudaStream_t st) {
+    if (!g.sync) return CZ_OK;
+    uint32_t err = 0;
+    if (cudaMemcpyAsync(&err, g.sync + 1, sizeof err, cudaMemcpyDeviceToHost, st) != cudaSuccess) return CZ_ED2H;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return CZ_ED2H;
+    if (err) {
+        cudaMemsetAsync(g.sync + 1, 0, sizeof(uint32_t), st);
+        cudaStreamSynchronize(st);
+        return CZ_ETIMEOUT;
+    }
+    return CZ_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+// ============================ Part 1 ============================
+
+CZ_EXPORT int colizig_cuda_init(void) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    return init_locked(0);
+}
+
+// Same as colizig_cuda_init on an explicit device ordinal (one process per GPU
+// for expert parallelism).  Not in the reference surface.
+CZ_EXPORT int colizig_cuda_init_device(int device) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    return init_locked(device);
+}
+
+CZ_EXPORT const char* colizig_cuda_device_name(void) { return g.inited ? g.name : ""; }
+
+CZ_EXPORT void colizig_cuda_set_vram_budget(uint64_t bytes) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return;
+    cudaSetDevice(g.dev);
+    size_t freeb = 0, totalb = 0;
+    if (cudaMemGetInfo(&freeb, &totalb) == cudaSuccess) {
+        const size_t cap = freeb - freeb / 8 + g.used;
+        if (bytes > cap) bytes = cap;
+    }
+    g.budget = bytes;
+    while (g.used > g.budget && !g.lru.empty()) evict_lru_one();
+}
+
+CZ_EXPORT void colizig_cuda_stats(uint64_t* hits, uint64_t* misses, uint64_t* uploaded_mib, uint64_t* resident) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (hits) *hits = g.hits;
+    if (misses) *misses = g.misses;
+    if (uploaded_mib) *uploaded_mib = g.uploaded >> 20;
+    if (resident) *resident = (uint64_t)g.keyed.size();
+}
+
+CZ_EXPORT void colizig_cuda_shutdown(void) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    shutdown_locked();
+}
+
+CZ_EXPORT int colizig_cuda_matmul_fp8(float* y, const float* x, const unsigned char* w, const float* scales, int S,
+                                      int I, int O, uint64_t key) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited || S < 1 || I < 1 || O < 1 || !y || !x || !w || !scales) return CZ_EARGS;
+    cudaSetDevice(g.dev);
+    const size_t xb = (size_t)S * I * sizeof(float);
+    const size_t wb = (size_t)O * I;
+    const size_t sb = nb(O) * nb(I) * sizeof(float);
+    const size_t yb = (size_t)S * O * sizeof(float);
+    if (!g.d_x.ensure(xb) || !g.d_y.ensure(yb)) return CZ_EALLOC;
+    if (cudaMemcpyAsync(g.d_x.p, x, xb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess) return CZ_EH2D;
+
+    const void* wdev = nullptr;
+    const void* sdev = nullptr;
+    if (key != 0 && g.budget != 0) {
+        auto it = g.keyed.find(key);
+        if (it != g.keyed.end() && it->second.wb == wb && it->second.sb == sb) {
+            g.hits++;
+            g.lru.splice(g.lru.begin(), g.lru, it->second.lru);
+            wdev = it->second.w;
+            sdev = it->second.s;
+        } else {
+            g.misses++;
+            if (it != g.keyed.end()) {  // same key, new shape: drop the stale copy
+                cudaFree(it->second.w);
+                cudaFree(it->second.s);
+                g.used -= it->second.wb + it->second.sb;
+                g.lru.erase(it->second.lru);
+                g.keyed.erase(it);
+            }
+            while (g.used + wb + sb > g.budget && !g.lru.empty()) evict_lru_one();
+            Keyed k;
+            if (g.used + wb + sb <= g.budget && cudaMalloc(&k.w, wb) == cudaSuccess) {
+                if (cudaMalloc(&k.s, sb) != cudaSuccess) {
+                    cudaFree(k.w);
+                    k.w = nullptr;
+                }
+            } else {
+                k.w = nullptr;
+            }
+            if (k.w) {
+                if (cudaMemcpyAsync(k.w, w, wb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess ||
+                    cudaMemcpyAsync(k.s, scales, sb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess) {
+                    cudaFree(k.w);
+                    cudaFree(k.s);
+                    return CZ_EH2D;
+                }
+                k.wb = wb;
+                k.sb = sb;
+                g.lru.push_front(key);
+                k.lru = g.lru.begin();
+                g.keyed[key] = k;
+                g.used += wb + sb;
+                g.uploaded += wb + sb;
+                wdev = k.w;
+                sdev = k.s;
+            }
+        }
+    }
+    if (!wdev) {  // uncached (key 0, budget 0, or no room): upload into scratch
+        if (!g.d_w.ensure(wb) || !g.d_s.ensure(sb)) return CZ_EALLOC;
+        if (cudaMemcpyAsync(g.d_w.p, w, wb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess) return CZ_EH2D;
+        if (cudaMemcpyAsync(g.d_s.p, scales, sb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess) return CZ_EH2D;
+        g.uploaded += wb + sb;
+        wdev = g.d_w.p;
+        sdev = g.d_s.p;
+    }
+    if (cz::fp8_matmul_launch(g.d_y.as<float>(), g.d_x.as<float>(), (const uint8_t*)wdev, (const float*)sdev, S, I,
+                              O, g.stream) != CZ_OK)
+        return CZ_ELAUNCH;
+    if (cudaMemcpyAsync(y, g.d_y.p, yb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess) return CZ_ED2H;
+    if (cudaStreamSynchronize(g.stream) != cudaSuccess) return CZ_ED2H;
+    return CZ_OK;
+}
+
+// ============================ Part 2 ============================
+
+CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_dims* dims, const float* router,
+                                              const colizig_moe_expert* experts, const colizig_moe_expert* shared,
+                                              const float* shared_gate, uint32_t flags) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited || !dims || !router || !experts) return CZ_EARGS;
+    const colizig_moe_dims d = *dims;
+    if (d.hidden == 0 || d.experts == 0 || d.topk == 0 || d.inter == 0 || d.topk > d.experts) return CZ_EARGS;
+    if (d.topk > (uint32_t)cz::kMaxTopk || d.experts > (uint32_t)cz::kMaxExperts) return CZ_ESHAPE;
+    if (d.hidden % 16 || d.inter % 16 || d.shared_inter % 16 || d.hidden > 16384 || d.inter > 32768 ||
+        d.shared_inter > 32768)
+        return CZ_ESHAPE;
+    if (d.shared_inter && (!shared || !shared_gate)) return CZ_EARGS;
+    cudaSetDevice(g.dev);
+    const cudaMemcpyKind kind = (flags & COLIZIG_PTR_DEVICE) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    const size_t H = d.hidden, E = d.experts, I = d.inter, SI = d.shared_inter;
+    const size_t wexp = I * H, sexp = nb(I) * nb(H) * 4;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off = align256(off + bytes);
+        return o;
+    };
+    const size_t o_router = take(E * H * 4), o_gw = take(E * wexp), o_uw = take(E * wexp), o_dw = take(E * wexp);
+    const size_t o_gs = take(E * sexp), o_us = take(E * sexp), o_ds = take(E * sexp);
+    size_t o_shgw = 0, o_shuw = 0, o_shdw = 0, o_shgs = 0, o_shus = 0, o_shds = 0, o_shg = 0;
+    if (SI) {
+        o_shgw = take(SI * H);
+        o_shuw = take(SI * H);
+        o_shdw = take(SI * H);
+        o_shgs = take(nb(SI) * nb(H) * 4);
+        o_shus = take(nb(SI) * nb(H) * 4);
+        o_shds = take(nb(H) * nb(SI) * 4);
+        o_shg = take(H * 4);
+    }
+    MoeLayer L;
+    L.d = d;
+    L.bytes = off;
+    if (cudaMalloc(&L.mem, off) != cudaSuccess) return CZ_EALLOC;
+    uint8_t* base = reinterpret_cast<uint8_t*>(L.mem);
+    L.router = reinterpret_cast<float*>(base + o_router);
+    L.gate_w = base + o_gw;
+    L.up_w = base + o_uw;
+    L.down_w = base + o_dw;
+    L.gate_s = reinterpret_cast<float*>(base + o_gs);
+    L.up_s = reinterpret_cast<float*>(base + o_us);
+    L.down_s = reinterpret_cast<float*>(base + o_ds);
+    int rc = CZ_OK;
+    if (cudaMemcpyAsync(L.router, router, E * H * 4, kind, g.stream) != cudaSuccess) rc = CZ_EH2D;
+    const int Ei = (int)E;
+    if (!rc) rc = gather_copy(L.gate_w, experts, Ei, wexp, &colizig_moe_expert::gate_w, kind);
+    if (!rc) rc = gather_copy(L.up_w, experts, Ei, wexp, &colizig_moe_expert::up_w, kind);
+    if (!rc) rc = gather_copy(L.down_w, experts, Ei, wexp, &colizig_moe_expert::down_w, kind);
+    if (!rc) rc = gather_copy(reinterpret_cast<uint8_t*>(L.gate_s), experts, Ei, sexp, &colizig_moe_expert::gate_s, kind);
+    if (!rc) rc = gather_copy(reinterpret_cast<uint8_t*>(L.up_s), experts, Ei, sexp, &colizig_moe_expert::up_s, kind);
+    if (!rc) rc = gather_copy(reinterpret_cast<uint8_t*>(L.down_s), experts, Ei, sexp, &colizig_moe_expert::down_s, kind);
+    if (!rc && SI) {
+        L.sh_gate_w = base + o_shgw;
+        L.sh_up_w = base + o_shuw;
+        L.sh_down_w = base + o_shdw;
+        L.sh_gate_s = reinterpret_cast<float*>(base + o_shgs);
+        L.sh_up_s = reinterpret_cast<float*>(base + o_shus);
+        L.sh_down_s = reinterpret_cast<float*>(base + o_shds);
+        L.sh_gate = reinterpret_cast<float*>(base + o_shg);
+        if (!shared->gate_w || !shared->up_w || !shared->down_w || !shared->gate_s || !shared->up_s ||
+            !shared->down_s)
+            rc = CZ_EARGS;
+        const struct {
+            void* dst;
+            const void* src;
+            size_t bytes;
+        } cp[] = {{L.sh_gate_w, shared->gate_w, SI * H},
+                  {L.sh_up_w, shared->up_w, SI * H},
+                  {L.sh_down_w, shared->down_w, SI * H},
+                  {L.sh_gate_s, shared->gate_s, nb(SI) * nb(H) * 4},
+                  {L.sh_up_s, shared->up_s, nb(SI) * nb(H) * 4},
+                  {L.sh_down_s, shared->down_s, nb(H) * nb(SI) * 4},
+                  {L.sh_gate, shared_gate, H * 4}};
+        for (const auto& c : cp)
+            if (!rc && cudaMemcpyAsync(c.dst, c.src, c.bytes, kind, g.stream) != cudaSuccess) rc = CZ_EH2D;
+    }
+    if (!rc && cudaStreamSynchronize(g.stream) != cudaSuccess) rc = CZ_EH2D;
+    if (rc) {
+        cudaStreamSynchronize(g.stream);
+        free_layer(L);
+        return rc;
+    }
+    auto it = g.layers.find(layer);
+    if (it != g.layers.end()) free_layer(it->second);
+    g.layers[layer] = L;
+    return CZ_OK;
+}
+
+CZ_EXPORT int colizig_cuda_moe_unregister_layer(uint32_t layer) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g.layers.find(layer);
+    if (it == g.layers.end()) return CZ_ENOLAYER;
+    cudaSetDevice(g.dev);
+    cudaDeviceSynchronize();
+    free_layer(it->second);
+    g.layers.erase(it);
+    return CZ_OK;
+}
+
+CZ_EXPORT int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtype, int T, float* out,
+                                       uint32_t* topk_idx, float* topk_gates, uint32_t flags, void* stream) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited || !x || !out || T < 0 || (x_dtype != COLIZIG_X_F32 && x_dtype != COLIZIG_X_BF16))
+        return CZ_EARGS;
+    auto it = g.layers.find(layer);
+    if (it == g.layers.end()) return CZ_ENOLAYER;
+    if (T == 0) return CZ_OK;
+    cudaSetDevice(g.dev);
+    const MoeLayer& L = it->second;
+    const size_t H = L.d.hidden, K = L.d.topk;
+    const int bf16 = x_dtype == COLIZIG_X_BF16;
+    const size_t xb = (size_t)T * H * (bf16 ? 2 : 4), ob = (size_t)T * H * 4, kb = (size_t)T * K * 4;
+    if (flags & COLIZIG_PTR_DEVICE) {
+        if (!aligned16(x) || !aligned16(out)) return CZ_EARGS;
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        return moe_run(L, x, bf16, T, out, topk_idx, topk_gates, nullptr, 0.f, nullptr, st);
+    }
+    // host pointers: synchronous on the library stream
+    if (!g.io_x.ensure(xb) || !g.io_out.ensure(ob)) return CZ_EALLOC;
+    if ((topk_idx && !g.io_idx.ensure(kb)) || (topk_gates && !g.io_gates.ensure(kb))) return CZ_EALLOC;
+    if (cudaMemcpyAsync(g.io_x.p, x, xb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess) return CZ_EH2D;
+    int rc = moe_run(L, g.io_x.p, bf16, T, g.io_out.as<float>(), topk_idx ? g.io_idx.as<uint32_t>() : nullptr,
+                     topk_gates ? g.io_gates.as<float>() : nullptr, nullptr, 0.f, nullptr, g.stream);
+    if (rc) {
+        cudaStreamSynchronize(g.stream);
+        return rc;
+    }
+    if (cudaMemcpyAsync(out, g.io_out.p, ob, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess) return CZ_ED2H;
+    if (topk_idx && cudaMemcpyAsync(topk_idx, g.io_idx.p, kb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess)
+        return CZ_ED2H;
+    if (topk_gates && cudaMemcpyAsync(topk_gates, g.io_gates.p, kb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess)
+        return CZ_ED2H;
+    return check_device_error(g.stream);
+}
+
+CZ_EXPORT int colizig_cuda_moe_stack_forward(uint32_t first_layer, uint32_t n_layers, const float* norm_w, float eps,
+                                             float* h, int T, uint32_t flags, void* stream) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited || !h || T < 0) return CZ_EARGS;
+    if (T == 0 || n_layers == 0) return CZ_OK;
+    std::vector<const MoeLayer*> Ls;
+    for (uint32_t l = 0; l < n_layers; ++l) {
+        auto it = g.layers.find(first_layer + l);
+        if (it == g.layers.end()) return CZ_ENOLAYER;
+        if (it->second.d.hidden != g.layers.find(first_layer)->second.d.hidden) return CZ_ESHAPE;
+        Ls.push_back(&it->second);
+    }
+    cudaSetDevice(g.dev);
+    const size_t H = Ls[0]->d.hidden;
+    const bool dev = flags & COLIZIG_PTR_DEVICE;
+    cudaStream_t st = dev ? reinterpret_cast<cudaStream_t>(stream) : g.stream;
+    // norm weights: caller's (device or host) or all ones
+    const float* nw = norm_w;
+    if (!nw || !dev) {
+        if (!g.ones.ensure((size_t)n_layers * H * 4)) return CZ_EALLOC;
+        if (!nw) {
+            std::vector<float> ones((size_t)n_layers * H, 1.0f);
+            if (cudaMemcpyAsync(g.ones.p, ones.data(), ones.size() * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+                cudaStreamSynchronize(st) != cudaSuccess)
+                return CZ_EH2D;
+        } else if (cudaMemcpyAsync(g.ones.p, nw, (size_t)n_layers * H * 4, cudaMemcpyHostToDevice, st) !=
+                   cudaSuccess) {
+            return CZ_EH2D;
+        }
+        nw = g.ones.as<float>();
+    }
+    float* hd = h;
+    if (!dev) {
+        if (!g.io_out.ensure((size_t)T * H * 4)) return CZ_EALLOC;
+        if (cudaMemcpyAsync(g.io_out.p, h, (size_t)T * H * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+            return CZ_EH2D;
+        hd = g.io_out.as<float>();
+    } else if (!aligned16(h)) {
+        return CZ_EARGS;
+    }
+    for (uint32_t l = 0; l < n_layers; ++l) {
+        const int rc = moe_run(*Ls[l], hd, 0, T, hd, nullptr, nullptr, nw + (size_t)l * H, eps, hd, st);
+        if (rc) {
+            cudaStreamSynchronize(st);
+            return rc;
+        }
+    }
+    if (!dev) {
+        if (cudaMemcpyAsync(h, hd, (size_t)T * H * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) return CZ_ED2H;
+        return check_device_error(st);
+    }
+    return CZ_OK;
+}
+
+CZ_EXPORT int colizig_cuda_moe_check(void* stream) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return CZ_EARGS;
+    cudaSetDevice(g.dev);
+    return check_device_error(stream ? reinterpret_cast<cudaStream_t>(stream) : g.stream);
+}
+
+CZ_EXPORT int colizig_cuda_debug_expf(const float* x_dev, float* y_dev, size_t n) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited || (!x_dev && n) || (!y_dev && n)) return CZ_EARGS;
+    cudaSetDevice(g.dev);
+    int rc = cz::debug_expf_launch(x_dev, y_dev, n, g.stream);
+    if (rc) return rc;
+    return cudaStreamSynchronize(g.stream) == cudaSuccess ? CZ_OK : CZ_ELAUNCH;
+}

@@ -1,0 +1,60 @@
+// Host/device shared definitions of the colizig B200 library (not part of the
+// public C ABI; see include/colizig_cuda.h for that).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace cz {
+
+constexpr int kDecodeMaxTokens = 32;  // tokens per decode launch (one lane per token)
+constexpr int kMaxTopk = 16;
+constexpr int kMaxExperts = 512;
+constexpr int kSyncRegionWords = 2 + kMaxExperts + 1 + 7;  // router, done, ready[groups], pad
+constexpr int kSyncWords = 2 + 2 * kSyncRegionWords;       // seq, err, two regions
+
+__host__ __device__ inline int cz_nblk(int x) { return (x + 127) / 128; }
+
+// Everything the decode kernel reads or writes; passed by value.
+struct DecodeParams {
+    const void* x;           // [T, H] f32 or bf16 (stack mode: h, f32)
+    int x_bf16;
+    int T;
+    const float* rms_w;      // stack mode: rmsnorm weight [H] (else null)
+    float eps;
+    const float* residual;   // stack mode: h (out = residual + moe) (else null)
+    float* out;              // [T, H] f32
+    uint32_t* topk_idx;      // [T, K] or null
+    float* topk_gates;       // [T, K] or null
+    const float* router;     // [E, H]
+    const uint8_t* gate_w;   // [E, I, H]
+    const uint8_t* up_w;     // [E, I, H]
+    const uint8_t* down_w;   // [E, H, I]
+    const float* gate_s;     // [E, nb(I), nb(H)]
+    const float* up_s;
+    const float* down_s;     // [E, nb(H), nb(I)]
+    const uint8_t* sh_gate_w;  // shared expert (SI > 0)
+    const uint8_t* sh_up_w;
+    const uint8_t* sh_down_w;
+    const float* sh_gate_s;
+    const float* sh_up_s;
+    const float* sh_down_s;
+    const float* sh_gate;    // [H]
+    int H, E, K, I, SI, norm_topk;
+    float* logits;           // scratch [T, E+1]
+    float* xf;               // scratch [T, H] f32 token copy (null: x is used directly)
+    float* hbuf;             // scratch [T*K + T, max(I, SI)]
+    uint32_t* sync;          // kSyncWords words, zeroed once at allocation
+};
+
+size_t decode_smem_bytes();
+int decode_launch(const DecodeParams& p, int num_sms, cudaStream_t stream);
+
+// Legacy per-matrix block-FP8 matmul (device pointers, stream-ordered).
+int fp8_matmul_launch(float* y, const float* x, const uint8_t* w, const float* scales, int S, int I, int O,
+                      cudaStream_t stream);
+
+int debug_expf_launch(const float* x, float* y, size_t n, cudaStream_t stream);
+
+}  // namespace cz

@@ -1,0 +1,205 @@
+"""Host-side mirror of src/qwen38/moe.zig for the B200 backend.
+
+``Dims`` is moe.zig:23-46.  ``Layer`` replaces moe.zig's ``Layer`` + the
+``ExpertCache`` LRU (moe.zig:141-249, 297-338): the router and every expert's
+block-FP8 weights are registered once into resident device memory.
+``forward`` is moe.zig:409-426 for T tokens; ``stack_forward`` is the per-layer
+caller loop of src/qwen3moe/model.zig:227-232 with attention as identity.
+
+Arrays may be numpy (host; the call is synchronous) or torch CUDA tensors
+(device; the call is stream-ordered on the current torch stream).  Weights are
+stacked over experts in the reference layout:
+  router [E, H] f32; gate_w / up_w [E, I, H] u8 (E4M3 bytes); gate_s / up_s
+  [E, nblk(I), nblk(H)] f32; down_w [E, H, I] u8; down_s [E, nblk(H), nblk(I)] f32.
+An optional always-on shared expert (``shared`` = dict of sh_gate_w, sh_gate_s,
+sh_up_w, sh_up_s, sh_down_w, sh_down_s) is scaled by sigmoid(x . sh_gate).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+
+from . import _abi, gpu
+
+try:
+    import torch
+except ImportError:  # pragma: no cover - torch is part of the image
+    torch = None
+
+
+@dataclass(frozen=True)
+class Dims:
+    hidden: int
+    experts: int
+    topk: int
+    inter: int
+    shared_inter: int = 0
+    norm_topk: bool = True
+
+    def has_shared(self) -> bool:
+        return self.shared_inter != 0
+
+    @staticmethod
+    def of(cfg: dict) -> "Dims":
+        """moe.zig:36-45 from a config mapping (config.zig field names)."""
+        return Dims(cfg["hidden"], cfg["experts"], cfg["topk"], cfg["inter"], cfg.get("shared_inter", 0),
+                    bool(cfg.get("norm_topk", True)))
+
+    def c(self) -> _abi.MoeDims:
+        return _abi.MoeDims(self.hidden, self.experts, self.topk, self.inter, self.shared_inter,
+                            int(self.norm_topk))
+
+
+def _is_cuda(a) -> bool:
+    return torch is not None and isinstance(a, torch.Tensor) and a.is_cuda
+
+
+def _ptr(a) -> int:
+    if torch is not None and isinstance(a, torch.Tensor):
+        if not a.is_contiguous():
+            raise ValueError("tensors must be contiguous")
+        return a.data_ptr()
+    if not a.flags["C_CONTIGUOUS"]:
+        raise ValueError("arrays must be C-contiguous")
+    return a.ctypes.data
+
+
+def _stream_handle(stream) -> int:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    return getattr(stream, "cuda_stream", stream)
+
+
+class Layer:
+    """A registered MoE layer (resident on the device)."""
+
+    def __init__(self, layer_id: int, dims: Dims, router, gate_w, gate_s, up_w, up_s, down_w, down_s,
+                 shared: Optional[dict] = None, shared_gate=None):
+        if not gpu.available():
+            gpu.init()
+        self.id = int(layer_id)
+        self.dims = dims
+        E, H, I = dims.experts, dims.hidden, dims.inter
+        arrays = [router, gate_w, gate_s, up_w, up_s, down_w, down_s]
+        device = _is_cuda(router)
+        if any(_is_cuda(a) != device for a in arrays):
+            raise ValueError("mix of host and device arrays")
+        if tuple(gate_w.shape) != (E, I, H) or tuple(down_w.shape) != (E, H, I) or tuple(router.shape) != (E, H):
+            raise ValueError("weight shapes do not match dims")
+        keep = [a for a in arrays]
+        experts = (_abi.MoeExpert * E)()
+        gw, gs, uw, us, dw, ds = (_ptr(a) for a in (gate_w, gate_s, up_w, up_s, down_w, down_s))
+        nbw = I * H
+        nbs = ((I + 127) // 128) * ((H + 127) // 128) * 4
+        for e in range(E):
+            experts[e] = _abi.MoeExpert(gw + e * nbw, gs + e * nbs, uw + e * nbw, us + e * nbs, dw + e * nbw,
+                                        ds + e * nbs)
+        sh_ptr = None
+        sg_ptr = None
+        if dims.has_shared():
+            if shared is None or shared_gate is None:
+                raise ValueError("dims.shared_inter > 0 needs shared weights and shared_gate")
+            sh = _abi.MoeExpert(_ptr(shared["sh_gate_w"]), _ptr(shared["sh_gate_s"]), _ptr(shared["sh_up_w"]),
+                                _ptr(shared["sh_up_s"]), _ptr(shared["sh_down_w"]), _ptr(shared["sh_down_s"]))
+            keep += list(shared.values()) + [shared_gate]
+            sh_ptr = ctypes.byref(sh)
+            sg_ptr = _ptr(shared_gate)
+        cd = dims.c()
+        flags = _abi.COLIZIG_PTR_DEVICE if device else 0
+        if device:
+            torch.cuda.synchronize()
+        rc = _abi.load().colizig_cuda_moe_register_layer(self.id, ctypes.byref(cd), _ptr(router), experts, sh_ptr,
+                                                         sg_ptr, flags)
+        del keep
+        _abi.check("colizig_cuda_moe_register_layer", rc)
+
+    @staticmethod
+    def from_weights(layer_id: int, dims: Dims, w: dict) -> "Layer":
+        shared = None
+        if dims.has_shared():
+            shared = {k: w[k] for k in ("sh_gate_w", "sh_gate_s", "sh_up_w", "sh_up_s", "sh_down_w", "sh_down_s")}
+        return Layer(layer_id, dims, w["router"], w["gate_w"], w["gate_s"], w["up_w"], w["up_s"], w["down_w"],
+                     w["down_s"], shared, w.get("sh_gate"))
+
+    def unregister(self) -> None:
+        _abi.check("colizig_cuda_moe_unregister_layer", _abi.load().colizig_cuda_moe_unregister_layer(self.id))
+
+    def forward(self, x, out=None, topk_idx=None, topk_gates=None, stream=None):
+        return forward(self, x, out, topk_idx, topk_gates, stream)
+
+
+def forward(layer: Layer, x, out=None, topk_idx=None, topk_gates=None, stream=None):
+    """moe.zig:409-426: out[T, H] = MoE(x[T, H]).  Returns (out, topk_idx, topk_gates);
+    the top-k arrays are allocated when not given."""
+    d = layer.dims
+    L = _abi.load()
+    if _is_cuda(x):
+        T = x.shape[0]
+        if x.dtype == torch.bfloat16:
+            dt = _abi.COLIZIG_X_BF16
+        elif x.dtype == torch.float32:
+            dt = _abi.COLIZIG_X_F32
+        else:
+            raise ValueError("x must be f32 or bf16")
+        if out is None:
+            out = torch.empty((T, d.hidden), dtype=torch.float32, device=x.device)
+        if topk_idx is None:
+            topk_idx = torch.empty((T, d.topk), dtype=torch.int32, device=x.device)
+        if topk_gates is None:
+            topk_gates = torch.empty((T, d.topk), dtype=torch.float32, device=x.device)
+        rc = L.colizig_cuda_moe_forward(layer.id, _ptr(x), dt, T, _ptr(out), _ptr(topk_idx), _ptr(topk_gates),
+                                        _abi.COLIZIG_PTR_DEVICE, _stream_handle(stream))
+        _abi.check("colizig_cuda_moe_forward", rc)
+        return out, topk_idx, topk_gates
+    # host path
+    if torch is not None and isinstance(x, torch.Tensor):
+        if x.dtype == torch.bfloat16:
+            xa = x.contiguous().view(torch.int16).numpy()
+            dt = _abi.COLIZIG_X_BF16
+        else:
+            xa = x.contiguous().float().numpy()
+            dt = _abi.COLIZIG_X_F32
+    else:
+        xa = np.ascontiguousarray(x, np.float32)
+        dt = _abi.COLIZIG_X_F32
+    if xa.ndim == 1:
+        xa = xa[None, :]
+    T = xa.shape[0]
+    if out is None:
+        out = np.empty((T, d.hidden), np.float32)
+    if topk_idx is None:
+        topk_idx = np.empty((T, d.topk), np.uint32)
+    if topk_gates is None:
+        topk_gates = np.empty((T, d.topk), np.float32)
+    rc = L.colizig_cuda_moe_forward(layer.id, _ptr(xa), dt, T, _ptr(out), _ptr(topk_idx), _ptr(topk_gates), 0,
+                                    None)
+    _abi.check("colizig_cuda_moe_forward", rc)
+    return out, topk_idx, topk_gates
+
+
+def stack_forward(first_layer: int, n_layers: int, h, norm_w=None, eps: float = 1e-6, stream=None):
+    """src/qwen3moe/model.zig:227-232 per layer (attention = identity):
+    n = rms(h, norm_w[l]); h += moe_l(n).  Updates h ([T, H] f32) in place."""
+    L = _abi.load()
+    if _is_cuda(h):
+        rc = L.colizig_cuda_moe_stack_forward(first_layer, n_layers, None if norm_w is None else _ptr(norm_w),
+                                              float(eps), _ptr(h), h.shape[0], _abi.COLIZIG_PTR_DEVICE,
+                                              _stream_handle(stream))
+    else:
+        if not (h.dtype == np.float32 and h.flags["C_CONTIGUOUS"]):
+            raise ValueError("h must be a C-contiguous f32 array")
+        nwa = None if norm_w is None else np.ascontiguousarray(norm_w, np.float32)
+        nw = None if nwa is None else _ptr(nwa)
+        rc = L.colizig_cuda_moe_stack_forward(first_layer, n_layers, nw, float(eps), _ptr(h), h.shape[0], 0, None)
+    _abi.check("colizig_cuda_moe_stack_forward", rc)
+    return h
+
+
+def check(stream=None) -> None:
+    """Raise if a device-side wait of an earlier asynchronous call gave up."""
+    h = None if stream is None else _stream_handle(stream)
+    _abi.check("colizig_cuda_moe_check", _abi.load().colizig_cuda_moe_check(h))

@@ -1,0 +1,147 @@
+/* colizig_cuda.h — C ABI of libcolizig_cuda.so, the B200 (sm_100a) backend for
+ * colizig's block-FP8 MoE expert path.
+ *
+ * Part 1 is the reference's runtime-loaded backend surface, the six symbols
+ * that src/backend/gpu.zig:84-89 resolves by name.  Each declaration names the
+ * reference function it replaces (src/backend/cuda/colizig_cuda.cu).  Names,
+ * argument meaning and return codes are kept; the CUDA runtime's habit of
+ * changing the host MXCSR is undone on every entry, as in the reference.
+ *
+ * Part 2 adds MoE-level entry points.  The reference only offers a per-matrix
+ * matmul, so its MoE layer (src/qwen38/moe.zig:409-426 forward) crosses the host
+ * boundary ~3*topk times per token.  These calls run the whole layer — router
+ * softmax/top-k, token-to-expert gather, gate/up with SiLU*mul, down, weighted
+ * combine — on resident weights in one call.
+ *
+ * Return codes (reference convention, colizig_cuda.cu:228-284, extended):
+ *    0 ok
+ *   -1 bad arguments / not initialised       -2 device allocation failed
+ *   -3 host->device copy failed              -4 kernel launch failed
+ *   -5 device->host copy failed              -6 layer not registered
+ *   -7 a device-side wait timed out (the kernel stopped early; the context is
+ *      still usable and the next call starts clean)
+ *   -8 shape not supported by this build     -9 NCCL / expert-parallel error
+ *
+ * Threading: one process-wide context, internally serialised by a mutex.
+ * Ownership: callers own every buffer they pass; no pointer is retained after
+ * a call returns, except that registered weights are copied into the
+ * library's resident device storage.
+ */
+#ifndef COLIZIG_CUDA_H
+#define COLIZIG_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- Part 1: the reference backend surface --------------------------- */
+
+/* colizig_cuda.cu:171-187 colizig_cuda_init.  Idempotent.  0 ok, -1 no device,
+ * -2 cudaSetDevice failed, -3 properties failed, -4 device setup failed. */
+int colizig_cuda_init(void);
+
+/* colizig_cuda_init on an explicit device ordinal (one process per GPU for
+ * expert parallelism).  No reference counterpart: the reference always uses
+ * device 0 (colizig_cuda.cu:176). */
+int colizig_cuda_init_device(int device);
+
+/* colizig_cuda.cu:189-191.  "<name> (sm_XY, N MiB)" or "" before init. */
+const char* colizig_cuda_device_name(void);
+
+/* colizig_cuda.cu:195-202.  Capacity, in bytes, of the keyed resident weight
+ * store used by colizig_cuda_matmul_fp8 (0 = keyed calls upload every time).
+ * Clamped to 7/8 of the free device memory. */
+void colizig_cuda_set_vram_budget(uint64_t bytes);
+
+/* colizig_cuda.cu:204-209.  Null-safe.  hits/misses of keyed lookups, MiB of
+ * weights uploaded host->device, and resident keyed matrices. */
+void colizig_cuda_stats(uint64_t* hits, uint64_t* misses, uint64_t* uploaded_mib, uint64_t* resident);
+
+/* colizig_cuda.cu:211-224.  Frees every device buffer (keyed store, MoE layers,
+ * scratch, expert-parallel state) and returns to the uninitialised state. */
+void colizig_cuda_shutdown(void);
+
+/* colizig_cuda.cu:228-284 colizig_cuda_matmul_fp8.  Synchronous, host pointers.
+ *   y[S,O] = x[S,I] @ (e4m3(w[O,I]) * scales[o/128, i/128])^T
+ * w row-major E4M3 bytes, scales row-major [ceil(O/128), ceil(I/128)] f32
+ * multipliers.  key 0 = upload w every call; otherwise the weights stay
+ * resident under `key` (the moe.zig:97-99 key scheme) within the budget. */
+int colizig_cuda_matmul_fp8(float* y, const float* x, const unsigned char* w, const float* scales, int S,
+                            int I, int O, uint64_t key);
+
+/* ---- Part 2: MoE layer entry points (no reference counterpart) ---------- */
+
+/* Mirrors moe.zig:23-30 Dims.  shared_inter == 0 -> no shared expert. */
+typedef struct colizig_moe_dims {
+    uint32_t hidden;
+    uint32_t experts;
+    uint32_t topk;
+    uint32_t inter;
+    uint32_t shared_inter;
+    uint32_t norm_topk;
+} colizig_moe_dims;
+
+/* One expert's three projections in the reference layout (moe.zig:50-117):
+ * gate/up u8 [inter, hidden] + f32 [nblk(inter), nblk(hidden)] scales, down
+ * u8 [hidden, inter] + f32 [nblk(hidden), nblk(inter)]. */
+typedef struct colizig_moe_expert {
+    const uint8_t* gate_w;
+    const float* gate_s;
+    const uint8_t* up_w;
+    const float* up_s;
+    const uint8_t* down_w;
+    const float* down_s;
+} colizig_moe_expert;
+
+/* flags */
+#define COLIZIG_PTR_DEVICE 1u /* every data pointer is a device pointer; the call is
+                                 asynchronous on `stream` (else: host pointers,
+                                 synchronous, like colizig_cuda_matmul_fp8) */
+
+/* x dtypes */
+#define COLIZIG_X_F32 0
+#define COLIZIG_X_BF16 1
+
+/* Register (or replace) MoE layer `layer`: copies the f32 router [experts,
+ * hidden] and every expert's E4M3 weights and scales into resident device
+ * memory (replaces moe.zig's ExpertCache / the VRAM LRU, colizig_cuda.cu:80-169).
+ * shared / shared_gate describe an always-on block-FP8 shared expert whose
+ * output is scaled by sigmoid(x . shared_gate) (moe.zig:467-479); both NULL
+ * when dims->shared_inter == 0.  hidden, inter and shared_inter must be
+ * multiples of 16; topk <= 16. */
+int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_dims* dims, const float* router,
+                                    const colizig_moe_expert* experts, const colizig_moe_expert* shared,
+                                    const float* shared_gate, uint32_t flags);
+
+int colizig_cuda_moe_unregister_layer(uint32_t layer);
+
+/* moe.zig:409-426 forward for T tokens: out[T, hidden] f32 =
+ * sum_k gate_k * down_k(silu(gate_k(x)) * up_k(x)) (+ shared expert).
+ * x is [T, hidden] f32 or bf16.  topk_idx / topk_gates (nullable) receive each
+ * token's router pick [T, topk] (u32 ids / f32 gates). */
+int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtype, int T, float* out, uint32_t* topk_idx,
+                             float* topk_gates, uint32_t flags, void* stream);
+
+/* The per-layer caller of the MoE (src/qwen3moe/model.zig:227-232) over layers
+ * first..first+n-1, with the attention sublayer as identity:
+ *   n = rms(h, norm_w[l]) ; h += moe_l(n)        (rmsnorm.zig:32-40, eps)
+ * h [T, hidden] f32 is updated in place; norm_w [n_layers, hidden] f32 or NULL
+ * (all ones). */
+int colizig_cuda_moe_stack_forward(uint32_t first_layer, uint32_t n_layers, const float* norm_w, float eps,
+                                   float* h, int T, uint32_t flags, void* stream);
+
+/* Device-side error word of the last asynchronous call(s) on the library's
+ * MoE scratch (0 = none); reading it synchronises `stream` and clears it. */
+int colizig_cuda_moe_check(void* stream);
+
+/* Diagnostics used by the parity tests: the router's exp (the reference's
+ * @exp(f32) restated in double precision) over n device floats. */
+int colizig_cuda_debug_expf(const float* x_dev, float* y_dev, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
