@@ -102,7 +102,7 @@ struct Ctx {
     uint64_t hits = 0, misses = 0, uploaded = 0;
     // MoE
     std::map<uint32_t, MoeLayer> layers;
-    DevBuf logits, xf, hbuf, io_x, io_out, io_idx, io_gates, ones;
+    DevBuf logits, hbuf, io_x, io_out, io_idx, io_gates, ones;
     uint32_t* sync = nullptr;
 };
 
@@ -151,7 +151,7 @@ void shutdown_locked() {
     g.lru.clear();
     for (auto& kv : g.layers) free_layer(kv.second);
     g.layers.clear();
-    for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.xf, &g.hbuf, &g.io_x, &g.io_out, &g.io_idx,
+    for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.hbuf, &g.io_x, &g.io_out, &g.io_idx,
                       &g.io_gates, &g.ones})
         b->release();
     if (g.sync) cudaFree(g.sync);
@@ -201,7 +201,6 @@ int ensure_decode_scratch(const colizig_moe_dims& d) {
     const size_t T = cz::kDecodeMaxTokens;
     const size_t HS = d.inter > d.shared_inter ? d.inter : d.shared_inter;
     if (!g.logits.ensure(T * (d.experts + 1) * sizeof(float))) return CZ_EALLOC;
-    if (!g.xf.ensure(T * d.hidden * sizeof(float))) return CZ_EALLOC;
     if (!g.hbuf.ensure(T * (d.topk + 1) * HS * sizeof(float))) return CZ_EALLOC;
     return ensure_sync();
 }
@@ -241,8 +240,11 @@ int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uin
     int rc = ensure_decode_scratch(L.d);
     if (rc) return rc;
     const size_t xelt = x_bf16 ? 2 : 4;
-    for (int t0 = 0; t0 < T; t0 += cz::kDecodeMaxTokens) {
-        const int n = T - t0 < cz::kDecodeMaxTokens ? T - t0 : cz::kDecodeMaxTokens;
+    const int tmax = cz::decode_max_tokens((int)L.d.hidden, (int)L.d.experts, (int)L.d.topk, (int)L.d.inter,
+                                           (int)L.d.shared_inter, x_bf16, g.num_sms);
+    if (tmax < 1) return CZ_ESHAPE;
+    for (int t0 = 0; t0 < T; t0 += tmax) {
+        const int n = T - t0 < tmax ? T - t0 : tmax;
         cz::DecodeParams p = make_params(L);
         p.x = reinterpret_cast<const uint8_t*>(x) + (size_t)t0 * L.d.hidden * xelt;
         p.x_bf16 = x_bf16;
@@ -253,8 +255,6 @@ int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uin
         p.out = out + (size_t)t0 * L.d.hidden;
         p.topk_idx = idx ? idx + (size_t)t0 * L.d.topk : nullptr;
         p.topk_gates = gates ? gates + (size_t)t0 * L.d.topk : nullptr;
-        // phase A reads f32 tokens: the caller's f32 x directly, else a converted copy
-        p.xf = (x_bf16 || rms_w) ? g.xf.as<float>() : nullptr;
         rc = cz::decode_launch(p, g.num_sms, st);
         if (rc) return rc;
     }

@@ -82,13 +82,17 @@ CZ_DEV float cz_expf(float x) {
     if (x > 100.0f) return __int_as_float(0x7f800000);
     if (x < -110.0f) return 0.0f;
     const double xd = (double)x;
-    const double kd = rint(__dmul_rn(xd, 0x1.71547652b82fep+0));
+    // k = round-to-nearest-even(x * log2(e)): adding and removing 1.5*2^52 is an
+    // exact RN-even rounding to an integer for |v| < 2^51.
+    const double kd = __dadd_rn(__dadd_rn(__dmul_rn(xd, 0x1.71547652b82fep+0), 0x1.8p52), -0x1.8p52);
     double r = __fma_rn(-kd, 0x1.62e42fefa3800p-1, xd);
     r = __fma_rn(-kd, 0x1.ef35793c76730p-45, r);
     double p = cz_inv_fact[13];
 #pragma unroll
     for (int n = 12; n >= 0; --n) p = __fma_rn(p, r, cz_inv_fact[n]);
-    return __double2float_rn(scalbn(p, (int)kd));
+    // * 2^k, exact (|k| < 160, the product stays a normal double)
+    const long long k = (long long)kd;
+    return __double2float_rn(__dmul_rn(p, __longlong_as_double((k + 1023) << 52)));
 }
 
 // activation.zig:8-20 (tolerance-checked path: CUDA's expf).

@@ -8,11 +8,11 @@
 
 namespace cz {
 
-constexpr int kDecodeMaxTokens = 32;  // tokens per decode launch (one lane per token)
+constexpr int kDecodeMaxTokens = 32;  // hard cap per decode launch (one lane per token)
 constexpr int kMaxTopk = 16;
 constexpr int kMaxExperts = 512;
-constexpr int kSyncRegionWords = 2 + kMaxExperts + 1 + 7;  // router, done, ready[groups], pad
-constexpr int kSyncWords = 2 + 2 * kSyncRegionWords;       // seq, err, two regions
+constexpr int kSyncRegionWords = 8;                   // router arrivals, done, gate/up done, pad
+constexpr int kSyncWords = 2 + 2 * kSyncRegionWords;  // seq, err, two regions
 
 __host__ __device__ inline int cz_nblk(int x) { return (x + 127) / 128; }
 
@@ -43,12 +43,14 @@ struct DecodeParams {
     const float* sh_gate;    // [H]
     int H, E, K, I, SI, norm_topk;
     float* logits;           // scratch [T, E+1]
-    float* xf;               // scratch [T, H] f32 token copy (null: x is used directly)
     float* hbuf;             // scratch [T*K + T, max(I, SI)]
     uint32_t* sync;          // kSyncWords words, zeroed once at allocation
 };
 
 size_t decode_smem_bytes();
+// Largest token count one decode launch takes for these dims (tokens and the
+// gate/up outputs must fit the kernel's shared staging area); 0 = unsupported.
+int decode_max_tokens(int H, int E, int K, int I, int SI, int x_bf16, int num_sms);
 int decode_launch(const DecodeParams& p, int num_sms, cudaStream_t stream);
 
 // Legacy per-matrix block-FP8 matmul (device pointers, stream-ordered).

@@ -619,10 +619,14 @@ int czref_moe_forward(const czref_layer* L, const czref_dims* d, const float* x,
     sc.r_idx = (uint32_t*)malloc(T * K * sizeof(uint32_t));
     sc.ord = (uint32_t*)malloc(T * K * sizeof(uint32_t));
     sc.r_gate = (float*)malloc(T * K * sizeof(float));
-    sc.xb = (float*)malloc(T * H * sizeof(float));
-    sc.bg = (float*)malloc(T * I * sizeof(float));
-    sc.bu = (float*)malloc(T * I * sizeof(float));
-    sc.bo = (float*)malloc(T * H * sizeof(float));
+    /* The reference sizes these [max_tokens, *] (moe.zig:353-361), which holds
+     * because a token never picks an expert twice.  When every logit is NaN the
+     * reference picks id 0 in every round (moe.zig:447-460) and one group gets
+     * S*K rows, overflowing that scratch; S*K rows keep the restatement defined. */
+    sc.xb = (float*)malloc(T * K * H * sizeof(float));
+    sc.bg = (float*)malloc(T * K * I * sizeof(float));
+    sc.bu = (float*)malloc(T * K * I * sizeof(float));
+    sc.bo = (float*)malloc(T * K * H * sizeof(float));
     if (S == 1)
         forward_dense(L, d, x, S, out, &sc, idx_out, gates_out);
     else
