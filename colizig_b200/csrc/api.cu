@@ -197,10 +197,31 @@ int gather_copy(uint8_t* dst, const colizig_moe_expert* ex, int count, size_t by
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+// Like gather_copy for block-scale tables: every item is `rows` rows of
+// `row_bytes`, written with a padded destination pitch (rows of the resident
+// tables start on 16-byte boundaries, so kernels can bulk-copy them).
+template <class T>
+int gather_copy_2d(uint8_t* dst, size_t dst_pitch, const colizig_moe_expert* ex, int count, size_t rows,
+                   size_t row_bytes, T colizig_moe_expert::*field, cudaMemcpyKind kind) {
+    const size_t item = rows * row_bytes;
+    int e = 0;
+    while (e < count) {
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(ex[e].*field);
+        if (!src) return CZ_EARGS;
+        int run = 1;
+        while (e + run < count && reinterpret_cast<const uint8_t*>(ex[e + run].*field) == src + run * item) ++run;
+        if (cudaMemcpy2DAsync(dst + (size_t)e * rows * dst_pitch, dst_pitch, src, row_bytes, row_bytes,
+                              (size_t)run * rows, kind, g.stream) != cudaSuccess)
+            return CZ_EH2D;
+        e += run;
+    }
+    return CZ_OK;
+}
+
 int ensure_decode_scratch(const colizig_moe_dims& d) {
     const size_t T = cz::kDecodeMaxTokens;
     const size_t HS = d.inter > d.shared_inter ? d.inter : d.shared_inter;
-    if (!g.logits.ensure(T * (d.experts + 1) * sizeof(float))) return CZ_EALLOC;
+    if (!g.logits.ensure(T * cz::logit_stride((int)d.experts) * sizeof(float))) return CZ_EALLOC;
     if (!g.hbuf.ensure(T * (d.topk + 1) * HS * sizeof(float))) return CZ_EALLOC;
     return ensure_sync();
 }
@@ -419,7 +440,9 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
     cudaSetDevice(g.dev);
     const cudaMemcpyKind kind = (flags & COLIZIG_PTR_DEVICE) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     const size_t H = d.hidden, E = d.experts, I = d.inter, SI = d.shared_inter;
-    const size_t wexp = I * H, sexp = nb(I) * nb(H) * 4;
+    const size_t wexp = I * H;
+    const size_t nbHp = (size_t)cz::cz_nbp((int)H), nbIp = (size_t)cz::cz_nbp((int)I), nbSIp = (size_t)cz::cz_nbp((int)SI);
+    const size_t sexp = nb(I) * nbHp * 4, dexp = nb(H) * nbIp * 4;  // padded scale tables
     size_t off = 0;
     auto take = [&](size_t bytes) {
         const size_t o = off;
@@ -427,15 +450,15 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
         return o;
     };
     const size_t o_router = take(E * H * 4), o_gw = take(E * wexp), o_uw = take(E * wexp), o_dw = take(E * wexp);
-    const size_t o_gs = take(E * sexp), o_us = take(E * sexp), o_ds = take(E * sexp);
+    const size_t o_gs = take(E * sexp), o_us = take(E * sexp), o_ds = take(E * dexp);
     size_t o_shgw = 0, o_shuw = 0, o_shdw = 0, o_shgs = 0, o_shus = 0, o_shds = 0, o_shg = 0;
     if (SI) {
         o_shgw = take(SI * H);
         o_shuw = take(SI * H);
         o_shdw = take(SI * H);
-        o_shgs = take(nb(SI) * nb(H) * 4);
-        o_shus = take(nb(SI) * nb(H) * 4);
-        o_shds = take(nb(H) * nb(SI) * 4);
+        o_shgs = take(nb(SI) * nbHp * 4);
+        o_shus = take(nb(SI) * nbHp * 4);
+        o_shds = take(nb(H) * nbSIp * 4);
         o_shg = take(H * 4);
     }
     MoeLayer L;
@@ -456,9 +479,15 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
     if (!rc) rc = gather_copy(L.gate_w, experts, Ei, wexp, &colizig_moe_expert::gate_w, kind);
     if (!rc) rc = gather_copy(L.up_w, experts, Ei, wexp, &colizig_moe_expert::up_w, kind);
     if (!rc) rc = gather_copy(L.down_w, experts, Ei, wexp, &colizig_moe_expert::down_w, kind);
-    if (!rc) rc = gather_copy(reinterpret_cast<uint8_t*>(L.gate_s), experts, Ei, sexp, &colizig_moe_expert::gate_s, kind);
-    if (!rc) rc = gather_copy(reinterpret_cast<uint8_t*>(L.up_s), experts, Ei, sexp, &colizig_moe_expert::up_s, kind);
-    if (!rc) rc = gather_copy(reinterpret_cast<uint8_t*>(L.down_s), experts, Ei, sexp, &colizig_moe_expert::down_s, kind);
+    if (!rc)
+        rc = gather_copy_2d(reinterpret_cast<uint8_t*>(L.gate_s), nbHp * 4, experts, Ei, nb(I), nb(H) * 4,
+                            &colizig_moe_expert::gate_s, kind);
+    if (!rc)
+        rc = gather_copy_2d(reinterpret_cast<uint8_t*>(L.up_s), nbHp * 4, experts, Ei, nb(I), nb(H) * 4,
+                            &colizig_moe_expert::up_s, kind);
+    if (!rc)
+        rc = gather_copy_2d(reinterpret_cast<uint8_t*>(L.down_s), nbIp * 4, experts, Ei, nb(H), nb(I) * 4,
+                            &colizig_moe_expert::down_s, kind);
     if (!rc && SI) {
         L.sh_gate_w = base + o_shgw;
         L.sh_up_w = base + o_shuw;
@@ -473,16 +502,18 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
         const struct {
             void* dst;
             const void* src;
-            size_t bytes;
-        } cp[] = {{L.sh_gate_w, shared->gate_w, SI * H},
-                  {L.sh_up_w, shared->up_w, SI * H},
-                  {L.sh_down_w, shared->down_w, SI * H},
-                  {L.sh_gate_s, shared->gate_s, nb(SI) * nb(H) * 4},
-                  {L.sh_up_s, shared->up_s, nb(SI) * nb(H) * 4},
-                  {L.sh_down_s, shared->down_s, nb(H) * nb(SI) * 4},
-                  {L.sh_gate, shared_gate, H * 4}};
+            size_t dpitch, rows, row_bytes;
+        } cp[] = {{L.sh_gate_w, shared->gate_w, SI * H, 1, SI * H},
+                  {L.sh_up_w, shared->up_w, SI * H, 1, SI * H},
+                  {L.sh_down_w, shared->down_w, SI * H, 1, SI * H},
+                  {L.sh_gate_s, shared->gate_s, nbHp * 4, nb(SI), nb(H) * 4},
+                  {L.sh_up_s, shared->up_s, nbHp * 4, nb(SI), nb(H) * 4},
+                  {L.sh_down_s, shared->down_s, nbSIp * 4, nb(H), nb(SI) * 4},
+                  {L.sh_gate, shared_gate, H * 4, 1, H * 4}};
         for (const auto& c : cp)
-            if (!rc && cudaMemcpyAsync(c.dst, c.src, c.bytes, kind, g.stream) != cudaSuccess) rc = CZ_EH2D;
+            if (!rc && cudaMemcpy2DAsync(c.dst, c.dpitch, c.src, c.row_bytes, c.row_bytes, c.rows, kind, g.stream) !=
+                           cudaSuccess)
+                rc = CZ_EH2D;
     }
     if (!rc && cudaStreamSynchronize(g.stream) != cudaSuccess) rc = CZ_EH2D;
     if (rc) {

@@ -8,13 +8,19 @@
 
 namespace cz {
 
-constexpr int kDecodeMaxTokens = 32;  // hard cap per decode launch (one lane per token)
+constexpr int kDecodeMaxTokens = 4;   // per decode launch: hi/lo of 4 tokens fill the MMA's 8 columns
 constexpr int kMaxTopk = 16;
 constexpr int kMaxExperts = 512;
-constexpr int kSyncRegionWords = 8;                   // router arrivals, done, gate/up done, pad
+constexpr int kSyncRegionWords = 8 + 4 * (kMaxTopk + 1);  // router, done, gate/up done, pad, max|h| per pair
 constexpr int kSyncWords = 2 + 2 * kSyncRegionWords;  // seq, err, two regions
 
 __host__ __device__ inline int cz_nblk(int x) { return (x + 127) / 128; }
+// Row stride (floats) of the router-logit scratch: E experts + the shared
+// expert's gate, rounded up to 4 floats (rows start on 16-byte boundaries).
+__host__ __device__ inline int logit_stride(int E) { return (E + 1 + 3) & ~3; }
+// Row length (floats) of a resident block-scale table: nblk rounded up to 4, so
+// every row starts on a 16-byte boundary.
+__host__ __device__ inline int cz_nbp(int x) { return (cz_nblk(x) + 3) & ~3; }
 
 // Everything the decode kernel reads or writes; passed by value.
 struct DecodeParams {
@@ -31,9 +37,9 @@ struct DecodeParams {
     const uint8_t* gate_w;   // [E, I, H]
     const uint8_t* up_w;     // [E, I, H]
     const uint8_t* down_w;   // [E, H, I]
-    const float* gate_s;     // [E, nb(I), nb(H)]
+    const float* gate_s;     // [E, nb(I), nbp(H)]  (rows padded to 4 floats)
     const float* up_s;
-    const float* down_s;     // [E, nb(H), nb(I)]
+    const float* down_s;     // [E, nb(H), nbp(I)]
     const uint8_t* sh_gate_w;  // shared expert (SI > 0)
     const uint8_t* sh_up_w;
     const uint8_t* sh_down_w;
@@ -42,7 +48,7 @@ struct DecodeParams {
     const float* sh_down_s;
     const float* sh_gate;    // [H]
     int H, E, K, I, SI, norm_topk;
-    float* logits;           // scratch [T, E+1]
+    float* logits;           // scratch [T, logit_stride(E)]
     float* hbuf;             // scratch [T*K + T, max(I, SI)]
     uint32_t* sync;          // kSyncWords words, zeroed once at allocation
 };
