@@ -31,6 +31,7 @@ MOE_SYMBOLS = (
     "colizig_cuda_moe_stack_forward",
     "colizig_cuda_moe_check",
     "colizig_cuda_debug_expf",
+    "colizig_cuda_moe_forward_noalloc",
 )
 
 COLIZIG_PTR_DEVICE = 1
@@ -122,6 +123,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         L.colizig_cuda_moe_stack_forward.argtypes = [u32, u32, vp, ctypes.c_float, vp, i32, u32, vp]
         L.colizig_cuda_moe_check.restype = i32
         L.colizig_cuda_moe_check.argtypes = [vp]
+        L.colizig_cuda_moe_forward_noalloc.restype = i32
+        L.colizig_cuda_moe_forward_noalloc.argtypes = [u32, vp, i32, i32, vp, vp, vp, vp, vp]
         L.colizig_cuda_debug_expf.restype = i32
         L.colizig_cuda_debug_expf.argtypes = [vp, vp, ctypes.c_size_t]
         _lib = L

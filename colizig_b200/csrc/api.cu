@@ -648,3 +648,89 @@ CZ_EXPORT int colizig_cuda_debug_expf(const float* x_dev, float* y_dev, size_t n
     if (rc) return rc;
     return cudaStreamSynchronize(g.stream) == cudaSuccess ? CZ_OK : CZ_ELAUNCH;
 }
+
+// ---- colizig_cuda_moe_forward_noalloc -------------------------------------
+// The device-pointer forward with its scratch in one static device array
+// instead of cudaMalloc'd buffers: [sync words][router logits][h].  Static
+// device storage is zero when the module loads, which is all the sync words
+// need (every launch zeroes the region the next launch uses, and the call
+// clears the error word); logits and h are written before they are read.
+namespace {
+
+constexpr int kNoAllocMaxInter = 2048;
+constexpr size_t kNoAllocSyncBytes = 768;
+constexpr size_t kNoAllocLogitBytes = 8448;
+constexpr size_t kNoAllocHBytes =
+    (size_t)cz::kDecodeMaxTokens * (cz::kMaxTopk + 1) * kNoAllocMaxInter * sizeof(float);
+constexpr size_t kNoAllocBytes = kNoAllocSyncBytes + kNoAllocLogitBytes + kNoAllocHBytes;
+static_assert(cz::kSyncWords * sizeof(uint32_t) <= kNoAllocSyncBytes, "sync words");
+static_assert((size_t)cz::kDecodeMaxTokens * ((cz::kMaxExperts + 1 + 3) & ~3) * sizeof(float) <= kNoAllocLogitBytes,
+              "logits");
+static_assert(kNoAllocBytes == 566272, "the size stated in colizig_cuda.h");
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+uint8_t* g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+// Address of the static scratch on device `dev`: looked up on the first call
+// for that device (set-up), cached afterwards.
+uint8_t* noalloc_scratch(int dev) {
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return nullptr;
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
+        g_noalloc_addr[dev] = static_cast<uint8_t*>(p);
+    }
+    return g_noalloc_addr[dev];
+}
+
+}  // namespace
+
+CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, int x_dtype, int T, float* out,
+                                               uint32_t* topk_idx, float* topk_gates, uint32_t* status,
+                                               void* stream) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited || !x || !out || T < 0 || (x_dtype != COLIZIG_X_F32 && x_dtype != COLIZIG_X_BF16))
+        return CZ_EARGS;
+    auto it = g.layers.find(layer);
+    if (it == g.layers.end()) return CZ_ENOLAYER;
+    const MoeLayer& L = it->second;
+    if (L.d.inter > (uint32_t)kNoAllocMaxInter || L.d.shared_inter > (uint32_t)kNoAllocMaxInter ||
+        L.d.experts > (uint32_t)cz::kMaxExperts || L.d.topk > (uint32_t)cz::kMaxTopk)
+        return CZ_ESHAPE;
+    if (!aligned16(x) || !aligned16(out)) return CZ_EARGS;
+    if (T == 0) return CZ_OK;
+    cudaSetDevice(g.dev);
+    uint8_t* base = noalloc_scratch(g.dev);
+    if (!base) return CZ_ELAUNCH;
+    uint32_t* sync = reinterpret_cast<uint32_t*>(base);
+    float* logits = reinterpret_cast<float*>(base + kNoAllocSyncBytes);
+    float* hbuf = reinterpret_cast<float*>(base + kNoAllocSyncBytes + kNoAllocLogitBytes);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int bf16 = x_dtype == COLIZIG_X_BF16;
+    const size_t xelt = bf16 ? 2 : 4;
+    const int tmax = cz::decode_max_tokens((int)L.d.hidden, (int)L.d.experts, (int)L.d.topk, (int)L.d.inter,
+                                           (int)L.d.shared_inter, bf16, g.num_sms);
+    if (tmax < 1) return CZ_ESHAPE;
+    for (int t0 = 0; t0 < T; t0 += tmax) {
+        const int n = T - t0 < tmax ? T - t0 : tmax;
+        cz::DecodeParams p = make_params(L);
+        p.logits = logits;
+        p.hbuf = hbuf;
+        p.sync = sync;
+        p.x = reinterpret_cast<const uint8_t*>(x) + (size_t)t0 * L.d.hidden * xelt;
+        p.x_bf16 = bf16;
+        p.T = n;
+        p.out = out + (size_t)t0 * L.d.hidden;
+        p.topk_idx = topk_idx ? topk_idx + (size_t)t0 * L.d.topk : nullptr;
+        p.topk_gates = topk_gates ? topk_gates + (size_t)t0 * L.d.topk : nullptr;
+        const int rc = cz::decode_launch(p, g.num_sms, st);
+        if (rc) return rc;
+    }
+    if (status && cudaMemcpyAsync(status, sync + 1, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return CZ_ELAUNCH;
+    if (cudaMemsetAsync(sync + 1, 0, sizeof(uint32_t), st) != cudaSuccess) return CZ_ELAUNCH;
+    return CZ_OK;
+}

@@ -181,6 +181,29 @@ def forward(layer: Layer, x, out=None, topk_idx=None, topk_gates=None, stream=No
     return out, topk_idx, topk_gates
 
 
+def forward_noalloc(layer: Layer, x, out, topk_idx=None, topk_gates=None, status=None, stream=None):
+    """``forward`` for device tensors through colizig_cuda_moe_forward_noalloc:
+    the library allocates nothing during the call (its scratch is a static
+    device array), and neither does this wrapper, so every output tensor is
+    the caller's.  ``status`` (optional int32 CUDA tensor of one element)
+    receives the call's device error word (0 = ok).  The first call on a device
+    does set-up; calls that overlap in time race on the shared scratch."""
+    if not (_is_cuda(x) and _is_cuda(out)):
+        raise ValueError("forward_noalloc takes CUDA tensors only")
+    if x.dtype == torch.bfloat16:
+        dt = _abi.COLIZIG_X_BF16
+    elif x.dtype == torch.float32:
+        dt = _abi.COLIZIG_X_F32
+    else:
+        raise ValueError("x must be f32 or bf16")
+    rc = _abi.load().colizig_cuda_moe_forward_noalloc(
+        layer.id, _ptr(x), dt, x.shape[0], _ptr(out), None if topk_idx is None else _ptr(topk_idx),
+        None if topk_gates is None else _ptr(topk_gates), None if status is None else _ptr(status),
+        _stream_handle(stream))
+    _abi.check("colizig_cuda_moe_forward_noalloc", rc)
+    return out
+
+
 def stack_forward(first_layer: int, n_layers: int, h, norm_w=None, eps: float = 1e-6, stream=None):
     """src/qwen3moe/model.zig:227-232 per layer (attention = identity):
     n = rms(h, norm_w[l]); h += moe_l(n).  Updates h ([T, H] f32) in place."""

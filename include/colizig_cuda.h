@@ -137,6 +137,28 @@ int colizig_cuda_moe_stack_forward(uint32_t first_layer, uint32_t n_layers, cons
  * MoE scratch (0 = none); reading it synchronises `stream` and clears it. */
 int colizig_cuda_moe_check(void* stream);
 
+/* No counterpart in the reference.  The same computation as
+ * colizig_cuda_moe_forward with COLIZIG_PTR_DEVICE (device pointers, async on
+ * `stream`), for callers that must not allocate device memory during a call:
+ * an engine that has already handed all of HBM to its own pool or to
+ * colizig_cuda_set_vram_budget, or a decode loop where a cudaMalloc/cudaFree
+ * (which synchronises the device) would stall every stream.  The scratch lives
+ * in one static device array of 566,272 bytes inside the library, so no call
+ * allocates.  Limits: inter and shared_inter <= 2048, experts <= 512,
+ * topk <= 16 (the same 4-token launches as colizig_cuda_moe_forward; larger T
+ * runs as several launches); a layer beyond them returns -8 before anything
+ * is launched.  The FIRST call on a device does set-up (it looks up the
+ * scratch address and configures the kernel), so make it before any stream
+ * capture.  The scratch is shared: calls whose executions overlap (two
+ * streams, two threads) race on it and give wrong results; serialise them.
+ * Only the scratch's sync words must start at zero; static storage is zero
+ * when the library loads and every call leaves them ready for the next.
+ * status (nullable, device u32): after the launches the call's device error
+ * word is copied there (0 = ok; non-zero = a bounded wait in the kernel gave
+ * up and the outputs are invalid), then cleared.  T == 0 launches nothing. */
+int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, int x_dtype, int T, float* out,
+                                     uint32_t* topk_idx, float* topk_gates, uint32_t* status, void* stream);
+
 /* Diagnostics used by the parity tests: the router's exp (the reference's
  * @exp(f32) restated in double precision) over n device floats. */
 int colizig_cuda_debug_expf(const float* x_dev, float* y_dev, size_t n);
