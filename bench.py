@@ -41,6 +41,12 @@ sys.path.insert(0, ROOT)
 EXPERT_BYTES = {}  # per config: bytes of one expert (3 projections + scales)
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
+# moe_decode_kernel launch, from an ncu capture of the same workload; other
+# (config, tokens) pairs report null until captured.
+NCU_TRAFFIC = {("c2", 1): 39.02e6}
+
+
 def expert_bytes(d) -> int:
     nb = lambda x: (x + 127) // 128
     return 3 * d.inter * d.hidden + 4 * (2 * nb(d.inter) * nb(d.hidden) + nb(d.hidden) * nb(d.inter))
@@ -349,7 +355,8 @@ def main():
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_block(args, d),
             "hbm_gbs": achieved_gbs,
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved_gbs / hbm_peak, "traffic": None,
+                         "frac": achieved_gbs / hbm_peak, "traffic": NCU_TRAFFIC.get((args.config, T)),
+                         "traffic_unit": "bytes per launch (ncu)",
                          "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6.65 TB/s",
                          "kernel": "moe_decode_kernel", "kernel_ms_avg": float(np.mean(kernel_ms)),
