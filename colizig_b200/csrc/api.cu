@@ -85,6 +85,8 @@ struct MoeLayer {
     uint8_t *sh_gate_w = nullptr, *sh_up_w = nullptr, *sh_down_w = nullptr;
     float *sh_gate_s = nullptr, *sh_up_s = nullptr, *sh_down_s = nullptr;
     float* sh_gate = nullptr;
+    CUtensorMap down_map{};     // TMA view of down_w: u8 [E*H][I]
+    CUtensorMap sh_down_map{};  // TMA view of sh_down_w: u8 [H][SI]
 };
 
 struct Ctx {
@@ -102,7 +104,7 @@ struct Ctx {
     uint64_t hits = 0, misses = 0, uploaded = 0;
     // MoE
     std::map<uint32_t, MoeLayer> layers;
-    DevBuf logits, hbuf, io_x, io_out, io_idx, io_gates, ones;
+    DevBuf logits, partial, io_x, io_out, io_idx, io_gates, ones;
     uint32_t* sync = nullptr;
 };
 
@@ -151,7 +153,7 @@ void shutdown_locked() {
     g.lru.clear();
     for (auto& kv : g.layers) free_layer(kv.second);
     g.layers.clear();
-    for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.hbuf, &g.io_x, &g.io_out, &g.io_idx,
+    for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.partial, &g.io_x, &g.io_out, &g.io_idx,
                       &g.io_gates, &g.ones})
         b->release();
     if (g.sync) cudaFree(g.sync);
@@ -220,9 +222,8 @@ int gather_copy_2d(uint8_t* dst, size_t dst_pitch, const colizig_moe_expert* ex,
 
 int ensure_decode_scratch(const colizig_moe_dims& d) {
     const size_t T = cz::kDecodeMaxTokens;
-    const size_t HS = d.inter > d.shared_inter ? d.inter : d.shared_inter;
     if (!g.logits.ensure(T * cz::logit_stride((int)d.experts) * sizeof(float))) return CZ_EALLOC;
-    if (!g.hbuf.ensure(T * (d.topk + 1) * HS * sizeof(float))) return CZ_EALLOC;
+    if (!g.partial.ensure((size_t)g.num_sms * T * d.hidden * sizeof(float))) return CZ_EALLOC;
     return ensure_sync();
 }
 
@@ -248,8 +249,10 @@ cz::DecodeParams make_params(const MoeLayer& L) {
     p.I = (int)L.d.inter;
     p.SI = (int)L.d.shared_inter;
     p.norm_topk = (int)L.d.norm_topk;
+    p.down_map = L.down_map;
+    p.sh_down_map = L.d.shared_inter ? L.sh_down_map : L.down_map;
     p.logits = g.logits.as<float>();
-    p.hbuf = g.hbuf.as<float>();
+    p.partial = g.partial.as<float>();
     p.sync = g.sync;
     return p;
 }
@@ -515,6 +518,8 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
                            cudaSuccess)
                 rc = CZ_EH2D;
     }
+    if (!rc && !cz::make_down_map(&L.down_map, L.down_w, E * H, I)) rc = CZ_ELAUNCH;
+    if (!rc && SI && !cz::make_down_map(&L.sh_down_map, L.sh_down_w, H, SI)) rc = CZ_ELAUNCH;
     if (!rc && cudaStreamSynchronize(g.stream) != cudaSuccess) rc = CZ_EH2D;
     if (rc) {
         cudaStreamSynchronize(g.stream);
@@ -651,22 +656,23 @@ CZ_EXPORT int colizig_cuda_debug_expf(const float* x_dev, float* y_dev, size_t n
 
 // ---- colizig_cuda_moe_forward_noalloc -------------------------------------
 // The device-pointer forward with its scratch in one static device array
-// instead of cudaMalloc'd buffers: [sync words][router logits][h].  Static
-// device storage is zero when the module loads, which is all the sync words
-// need (every launch zeroes the region the next launch uses, and the call
-// clears the error word); logits and h are written before they are read.
+// instead of cudaMalloc'd buffers: [sync words][router logits][per-CTA partial
+// sums].  Static device storage is zero when the module loads, which is all the
+// sync words need (every launch zeroes the region the next launch uses, and
+// the call clears the error word); logits and partial sums are written before
+// they are read.
 namespace {
 
-constexpr int kNoAllocMaxInter = 2048;
+constexpr int kNoAllocMaxHidden = 4096;
 constexpr size_t kNoAllocSyncBytes = 768;
 constexpr size_t kNoAllocLogitBytes = 8448;
-constexpr size_t kNoAllocHBytes =
-    (size_t)cz::kDecodeMaxTokens * (cz::kMaxTopk + 1) * kNoAllocMaxInter * sizeof(float);
-constexpr size_t kNoAllocBytes = kNoAllocSyncBytes + kNoAllocLogitBytes + kNoAllocHBytes;
+constexpr size_t kNoAllocPartialBytes =
+    (size_t)cz::kMaxGrid * cz::kDecodeMaxTokens * kNoAllocMaxHidden * sizeof(float);
+constexpr size_t kNoAllocBytes = kNoAllocSyncBytes + kNoAllocLogitBytes + kNoAllocPartialBytes;
 static_assert(cz::kSyncWords * sizeof(uint32_t) <= kNoAllocSyncBytes, "sync words");
 static_assert((size_t)cz::kDecodeMaxTokens * ((cz::kMaxExperts + 1 + 3) & ~3) * sizeof(float) <= kNoAllocLogitBytes,
               "logits");
-static_assert(kNoAllocBytes == 566272, "the size stated in colizig_cuda.h");
+static_assert(kNoAllocBytes == 10494976, "the size stated in colizig_cuda.h");
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 
@@ -697,8 +703,8 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
     auto it = g.layers.find(layer);
     if (it == g.layers.end()) return CZ_ENOLAYER;
     const MoeLayer& L = it->second;
-    if (L.d.inter > (uint32_t)kNoAllocMaxInter || L.d.shared_inter > (uint32_t)kNoAllocMaxInter ||
-        L.d.experts > (uint32_t)cz::kMaxExperts || L.d.topk > (uint32_t)cz::kMaxTopk)
+    if (L.d.hidden > (uint32_t)kNoAllocMaxHidden || L.d.experts > (uint32_t)cz::kMaxExperts ||
+        L.d.topk > (uint32_t)cz::kMaxTopk || g.num_sms > cz::kMaxGrid)
         return CZ_ESHAPE;
     if (!aligned16(x) || !aligned16(out)) return CZ_EARGS;
     if (T == 0) return CZ_OK;
@@ -707,7 +713,7 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
     if (!base) return CZ_ELAUNCH;
     uint32_t* sync = reinterpret_cast<uint32_t*>(base);
     float* logits = reinterpret_cast<float*>(base + kNoAllocSyncBytes);
-    float* hbuf = reinterpret_cast<float*>(base + kNoAllocSyncBytes + kNoAllocLogitBytes);
+    float* partial = reinterpret_cast<float*>(base + kNoAllocSyncBytes + kNoAllocLogitBytes);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int bf16 = x_dtype == COLIZIG_X_BF16;
     const size_t xelt = bf16 ? 2 : 4;
@@ -718,7 +724,7 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
         const int n = T - t0 < tmax ? T - t0 : tmax;
         cz::DecodeParams p = make_params(L);
         p.logits = logits;
-        p.hbuf = hbuf;
+        p.partial = partial;
         p.sync = sync;
         p.x = reinterpret_cast<const uint8_t*>(x) + (size_t)t0 * L.d.hidden * xelt;
         p.x_bf16 = bf16;

@@ -77,7 +77,7 @@ __device__ __constant__ double cz_inv_fact[14] = {
     0x1.a01a01a01a01ap-16, 0x1.71de3a556c734p-19, 0x1.27e4fb7789f5cp-22, 0x1.ae64567f544e4p-26,
     0x1.1eed8eff8d898p-29, 0x1.6124613a86d09p-33};
 
-CZ_DEV float cz_expf(float x) {
+static __device__ __noinline__ float cz_expf(float x) {
     if (x != x) return x;
     if (x > 100.0f) return __int_as_float(0x7f800000);
     if (x < -110.0f) return 0.0f;
@@ -141,7 +141,7 @@ CZ_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait on an mbarrier phase.  Returns false if it gave up, either after
 // CZ_SPIN_LIMIT polls or because *abort became non-zero.
-CZ_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+static __device__ __noinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, const volatile int* abort) {
     for (uint32_t it = 0; it < CZ_SPIN_LIMIT; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort) return false;
@@ -179,7 +179,7 @@ CZ_DEV void red_release_add_gpu(uint32_t* p, uint32_t v) {
 
 // Wait until *p >= target (acquire).  Gives up after CZ_SPIN_LIMIT polls, or
 // early when *err becomes non-zero (another CTA already gave up).
-CZ_DEV bool wait_geq_bounded(const uint32_t* p, uint32_t target, const uint32_t* err) {
+static __device__ __noinline__ bool wait_geq_bounded(const uint32_t* p, uint32_t target, const uint32_t* err) {
     for (uint32_t it = 0; it < CZ_SPIN_LIMIT; ++it) {
         if (ld_acquire_gpu(p) >= target) return true;
         if ((it & 63) == 63 && ld_relaxed_gpu(err) != 0) return false;

@@ -2,16 +2,18 @@
 // public C ABI; see include/colizig_cuda.h for that).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
 
 namespace cz {
 
-constexpr int kDecodeMaxTokens = 4;   // per decode launch: hi/lo of 4 tokens fill the MMA's 8 columns
+constexpr int kDecodeMaxTokens = 4;   // per decode launch
 constexpr int kMaxTopk = 16;
 constexpr int kMaxExperts = 512;
-constexpr int kSyncRegionWords = 8 + 4 * (kMaxTopk + 1);  // router, done, gate/up done, pad, max|h| per pair
+constexpr int kMaxGrid = 160;         // decode CTAs (one per SM) the partial-sum scratch is sized for
+constexpr int kSyncRegionWords = 8;   // router arrivals, CTAs done, partial sums written, pad
 constexpr int kSyncWords = 2 + 2 * kSyncRegionWords;  // seq, err, two regions
 
 __host__ __device__ inline int cz_nblk(int x) { return (x + 127) / 128; }
@@ -22,8 +24,11 @@ __host__ __device__ inline int logit_stride(int E) { return (E + 1 + 3) & ~3; }
 // every row starts on a 16-byte boundary.
 __host__ __device__ inline int cz_nbp(int x) { return (cz_nblk(x) + 3) & ~3; }
 
-// Everything the decode kernel reads or writes; passed by value.
-struct DecodeParams {
+// Everything the decode kernel reads or writes; passed by value (a
+// __grid_constant__ kernel parameter, so the tensor maps can be used in place).
+struct alignas(64) DecodeParams {
+    CUtensorMap down_map;     // down_w as 2D u8 [E*H rows][I cols], box 16 x 256
+    CUtensorMap sh_down_map;  // sh_down_w as 2D u8 [H rows][SI cols] (SI > 0)
     const void* x;           // [T, H] f32 or bf16 (stack mode: h, f32)
     int x_bf16;
     int T;
@@ -49,11 +54,15 @@ struct DecodeParams {
     const float* sh_gate;    // [H]
     int H, E, K, I, SI, norm_topk;
     float* logits;           // scratch [T, logit_stride(E)]
-    float* hbuf;             // scratch [T*K + T, max(I, SI)]
+    float* partial;          // scratch [grid][T][H]: each CTA's share of out
     uint32_t* sync;          // kSyncWords words, zeroed once at allocation
 };
 
-size_t decode_smem_bytes();
+// Down-weight tensor map for TMA: a 2D u8 tensor [rows][cols] (cols = the
+// expert's intermediate size, row pitch = cols bytes), box 16 cols x 256 rows.
+bool make_down_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64_t cols);
+
+size_t decode_smem_bytes(int T, int H, int x_bf16);
 // Largest token count one decode launch takes for these dims (tokens and the
 // gate/up outputs must fit the kernel's shared staging area); 0 = unsupported.
 int decode_max_tokens(int H, int E, int K, int I, int SI, int x_bf16, int num_sms);

@@ -5,13 +5,9 @@
 // (fp8.zig:165-257) -> silu(g)*u (activation.zig:8-20) -> down -> out += gate*eo,
 // plus the always-on shared expert (467-479).
 //
-// Grid = one CTA per SM: 5 consumer warps + 1 producer warp.  The weight stream
-// goes HBM -> shared memory through a ring of bulk-copy (TMA) stages, one slot
-// per consumer warp and one bulk copy per weight row into a padded row stride
-// (no bank conflicts when the rows of an MMA fragment are read together).  A
-// warp owns every stage it computes: no barrier or cross-warp reduction per
-// stage.  No global memory is read inside a compute loop: while HBM is
-// saturated by the weight stream, any other load would wait behind it.
+// Grid = one CTA per SM: 8 consumer warps + 1 producer warp.  The weights go
+// HBM -> shared memory through a ring of bulk-copy (TMA) stages filled by one
+// producer thread; no global memory is read inside a compute loop.
 //
 //   R  router logits.  CTA c owns router rows [c*E'/G, (c+1)*E'/G) (E' = E, +1
 //      for the shared expert's gate vector).  Rows and tokens are bulk-copied
@@ -19,33 +15,38 @@
 //      order (dotF32, matmul.zig:60-82: 32 FMA chains = one per lane, then the
 //      lane-ordered combine), so the top-k below is bit-identical to it.  In
 //      stack mode the tokens are rms-normalised in place first.  The tokens are
-//      then re-encoded for the MMA (below).  A grid-wide arrive counter closes
+//      then split into E4M3 terms (below).  A grid-wide arrive counter closes
 //      the phase.
 //   K  top-k.  Every CTA bulk-copies the logits, computes softmax/top-k for all
 //      tokens (identically) and groups the (token, slot) pairs by expert
-//      (ascending id, shared expert last).  The producer then bulk-copies the
-//      block scales this CTA needs.
-//   A  gate/up.  The flattened (group, row) list is split evenly over CTAs.  A
-//      stage holds up to 8 gate rows (MMA tile rows 0-7) and the same up rows
-//      (tile rows 8-15) of mma.sync m16n8k16 (f16 x f16 -> f32): E4M3 bytes
-//      become f16 exactly in registers (cvt.rn.f16x2.e4m3x2) and feed the A
-//      fragments directly.  The tokens are the B columns: each token, scaled by
-//      a power of two, is split into f16 hi + lo parts (columns t and t+4), so
-//      products keep ~22 bits.  Each 128-column block's partial is multiplied by
-//      its 128x128 scale.  h = silu(g)*u (f32) goes to HBM with the per-pair
-//      max |h|.
-//   B  down + combine.  CTA c owns output rows [c*H/G, (c+1)*H/G) of every
-//      group, as 16-row tiles; a down stage is one tile and up to 4 of the
-//      group's pairs.  The producer streams the down-weight rows as slots free
-//      up (they do not depend on h); once every CTA has finished phase A it adds
-//      the stage's h rows (one bulk copy per pair) on a second barrier of the
-//      slot.  The consumer splits them into per-pair 2^s-scaled f16 hi/lo in
-//      place and runs the tile with the pairs as columns; each warp adds
-//      gate * dot(h, w) into per-(row, token) registers, and the warps' sums are
-//      combined in a fixed order at the end (deterministic, no atomics).
+//      (ascending id, shared expert last).
+//   C  chunks.  Each group's intermediate rows are cut into chunks of 16; the
+//      flattened chunk list is split evenly over the CTAs (split-K: a chunk's
+//      gate, up AND down work stays on one SM, so h never leaves it).  A chunk
+//      is a sequence of ring stages: gate rows [r0, r0+16) x a 2048-column slab
+//      of H (one bulk copy per row), the same for up, then down columns
+//      [r0, r0+16) of 2048 output rows (2D TMA boxes of 16 x 256).  The
+//      consumer warps split every stage: K slabs by 128-column blocks for
+//      gate and up together, 16-row output tiles for down.  The weight copies
+//      carry an L2 evict-first hint: streamed once, they should not push the
+//      kernel's code, the router rows or the scratch out of L2.
+//
+// Arithmetic: mma.sync m16n8k32 E4M3 x E4M3 -> f32, which forms and sums the
+// exact products (checked on B200 to round like f32).  The weights enter as
+// their stored bytes.  The other operand is split exactly into E4M3 terms: a
+// token x (scaled by 2^s so that max|x| lies in [128, 256)) = t1 + t2 (+ t3),
+// every term a column of the MMA; a bf16 token is exact in 2 terms, an f32
+// token is kept to 12 bits in 3; h (per chunk and pair, scaled the same way)
+// to 16 bits in 4 terms.  Each 128-column block's sum is multiplied by its
+// 128x128 scale in f32.  Down sums go to a per-CTA [T][H] accumulator in
+// shared memory (every output row owned by one warp, chunks in a fixed order);
+// each CTA writes it out once, and after a grid-wide arrive counter CTA c adds
+// the G partial rows of its slice of out in a fixed order: deterministic, no
+// float atomics.
 //
 // Every wait is bounded; a CTA that gives up sets a bit in the device error
-// word, stops early (draining its in-flight copies) and the host returns -7.
+// word, stops issuing work (draining its in-flight copies) and the host
+// returns -7.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -55,137 +56,92 @@
 
 namespace cz {
 
-constexpr int NCW = 5;                    // consumer warps (one ring slot each)
+constexpr int NCW = 8;                    // consumer warps (2 per SM sub-partition)
 constexpr int NTHREADS = (NCW + 1) * 32;  // + 1 producer warp
-constexpr int STAGE_BYTES = 33 * 1024;    // 8 gate + 8 up rows of 2048 (+16 pad); 16 down rows + their h
-constexpr int NSTAGES = NCW;
-constexpr int RING_BYTES = STAGE_BYTES * NSTAGES;
-constexpr int XH_BYTES = 33 * 1024;       // tokens as f16 hi/lo columns (phase A)
+constexpr int CR = 16;                    // intermediate (h) rows per chunk
+constexpr int KS = 2048;                  // columns of a gate/up stage slab
+constexpr int OS = 2048;                  // output rows of a down stage
+constexpr int WPAD = 64;                  // row stride = 64 mod 128: rows g, g+1 of a fragment hit disjoint banks
+constexpr int GU_BYTES = CR * (KS + WPAD);
+constexpr int SC_BYTES = 2048;            // block scales carried with every stage
+constexpr int SLOT_BYTES = 35 * 1024;     // >= GU_BYTES + SC_BYTES; a down stage uses OS * 16
+constexpr int NSLOT = 4;
+constexpr int RING_BYTES = NSLOT * SLOT_BYTES;
+constexpr int BOX_ROWS = 256;             // down-weight TMA box: 16 bytes x 256 rows
+constexpr int JH = 4;                     // E4M3 terms of h
+constexpr int DB = 4;                     // down tiles per batch of one warp
+constexpr int MAXCH = 32;                 // chunks per CTA (h terms of all of them stay in shared memory)
 constexpr int MAXT = kDecodeMaxTokens;    // 4
 constexpr int MAXK = kMaxTopk;            // 16
 constexpr int MAXE = kMaxExperts;         // 512
 constexpr int MAXP = MAXT * (MAXK + 1);   // (token, slot) pairs incl. shared-expert pairs: 68
 constexpr int MAXG = MAXP;                // groups <= pairs
 constexpr int MAXM = MAXE / 32;           // router values per lane
-constexpr int SA_FLOATS = 1024;           // cached gate/up scale tables (phase A)
-constexpr int SB_FLOATS = 512;            // cached down scale rows (phase B)
-constexpr int MAXAG = 8;                  // groups cached for phase A
-constexpr int MAXBT = 4;                  // 16-row output tiles per CTA in phase B (rows per CTA <= 64)
-constexpr int RED_FLOATS = NCW * MAXBT * 16 * 4 * 2;
-constexpr int WPAD = 16;                  // bytes of padding after every staged weight row
-constexpr int HPAD = 32;                  // bytes of padding after every staged h row (down stages)
+constexpr int SMEM_LIMIT = 227 * 1024;
 
-struct __align__(128) DecodeSmem {
-    uint8_t ring[RING_BYTES];
-    uint8_t xh[XH_BYTES];
-    float sA[SA_FLOATS];
-    float sB[SB_FLOATS];
-    float red[RED_FLOATS];
-    uint64_t full[NSTAGES];   // a stage's weight rows landed
-    uint64_t hfull[NSTAGES];  // a down stage's h rows landed
-    uint64_t empty[NSTAGES];
+static_assert(GU_BYTES + SC_BYTES <= SLOT_BYTES, "slot");
+static_assert(OS * 16 <= GU_BYTES, "down stage");
+static_assert(SLOT_BYTES % 1024 == 0, "TMA destinations stay 1024-aligned");
+
+// Small shared state (after the large regions).
+struct __align__(16) DecodeMisc {
+    uint64_t full[NSLOT];
+    uint64_t empty[NSLOT];
     uint64_t rbar;
     uint64_t lbar;
-    uint64_t sbar;
     int abort;
-    int U, P;
-    int sA_ok, sB_ok, a_u0, a_u1;
-    int sA_off[MAXAG + 1];
+    int U, P, NC;
     uint32_t xmax[MAXT];  // max |x_t| (f32 bits)
-    int xexp[MAXT];       // s per token (tokens are stored * 2^s)
+    int xexp[MAXT];       // s per token (terms hold x_t * 2^s)
     float xscale[MAXT];   // 2^-s per token
+    float wq[MAXCH][4];   // per chunk and pair: gate * 2^-s_h
     int pe[MAXP];         // expert of pair p = t*K + z (shared: p = T*K + t -> E)
     float pg[MAXP];       // gate of pair p
     int order[MAXP];      // pairs sorted by (expert, pair)
     int g_expert[MAXG];
     int g_pair0[MAXG];
     int g_npairs[MAXG];
-    int g_rowA[MAXG + 1];
+    int g_chunk0[MAXG + 1];
 };
 
-static_assert(sizeof(DecodeSmem) + 1024 <= 227 * 1024, "decode smem too large");
+// Shared-memory map of one launch: [ring][x terms][acc][red][h terms][misc].
+struct Carve {
+    int JX, CS;  // E4M3 terms per token; byte stride of one term column
+    uint32_t xterm, acc, red, hterm, misc, total;
+};
+
+__host__ __device__ inline Carve carve(int T, int H, int x_bf16) {
+    Carve c;
+    c.JX = x_bf16 ? 2 : 3;
+    c.CS = ((H + 127) & ~127) + 64;  // column stride = 64 mod 128: lanes of 2 columns hit disjoint banks
+    uint32_t off = RING_BYTES;
+    c.xterm = off;
+    off += ((uint32_t)(T * c.JX * c.CS) + 127u) & ~127u;
+    c.acc = off;
+    off += ((uint32_t)(T * H * 4) + 127u) & ~127u;
+    c.red = off;
+    off += NCW * 2 * 16 * 16 * 4;
+    c.hterm = off;
+    off += MAXCH * 16 * 16;
+    c.misc = off;
+    off += ((uint32_t)sizeof(DecodeMisc) + 127u) & ~127u;
+    c.total = off;
+    return c;
+}
 
 // ---- sync words ------------------------------------------------------------
 // sync[0] = launch sequence number, sync[1] = error word, then two regions of
-// kSyncRegionWords: [0] router arrivals, [1] CTAs done, [2] CTAs done with
-// phase A, [8 + p] max |h| of pair p (f32 bits).  A launch uses region seq&1 and
-// zeroes the other one, so a launch that stopped early leaves nothing behind.
+// kSyncRegionWords: [0] router arrivals, [1] CTAs done, [2] partial sums
+// written.  A launch uses region seq&1 and zeroes the other one, so a launch
+// that stopped early leaves nothing behind.
 __device__ __forceinline__ uint32_t* region(uint32_t* sync, int par) { return sync + 2 + par * kSyncRegionWords; }
 
-struct Stage {
-    int phase;  // 0 = A (gate/up), 1 = B (down)
-    int u;      // group
-    int r0;     // A: first row within the group; B: first absolute output row (a 16-row tile)
-    int n;      // rows
-    int q0, nq; // B: the group's pairs q0 .. q0+nq-1 (at most 4: their h rides in the stage)
-};
-
-// Deterministic stage schedule shared by the producer and the consumers:
-// gate/up stages of this CTA's row range, then for every group (ascending),
-// every 16-row tile of this CTA's output rows, every batch of 4 pairs.
-struct StageIter {
-    int phase, u, a, a_hi, b_lo, b_hi, brow, bq, U, RA;
-    const int* rowA;
-    const int* npairs;
-
-    __device__ void init(const DecodeSmem& s, int a_lo, int a_hi_, int b_lo_, int b_hi_, int ra) {
-        phase = 0;
-        U = s.U;
-        rowA = s.g_rowA;
-        npairs = s.g_npairs;
-        a = a_lo;
-        a_hi = a_hi_;
-        b_lo = b_lo_;
-        b_hi = b_hi_;
-        brow = b_lo_;
-        bq = 0;
-        RA = ra;
-        u = 0;
-        while (u < U && rowA[u + 1] <= a) ++u;
-    }
-    __device__ bool next(Stage& st) {
-        if (phase == 0) {
-            if (a < a_hi) {
-                while (rowA[u + 1] <= a) ++u;
-                const int n = min(RA, min(rowA[u + 1] - a, a_hi - a));
-                st.phase = 0;
-                st.u = u;
-                st.r0 = a - rowA[u];
-                st.n = n;
-                st.q0 = 0;
-                st.nq = 0;
-                a += n;
-                return true;
-            }
-            phase = 1;
-            u = 0;
-            brow = b_lo;
-            bq = 0;
-        }
-        if (b_lo >= b_hi || u >= U) return false;
-        st.phase = 1;
-        st.u = u;
-        st.r0 = brow;
-        st.n = min(16, b_hi - brow);
-        st.q0 = bq;
-        st.nq = min(4, npairs[u] - bq);
-        bq += 4;
-        if (bq >= npairs[u]) {
-            bq = 0;
-            brow += st.n;
-            if (brow >= b_hi) {
-                brow = b_lo;
-                ++u;
-            }
-        }
-        return true;
-    }
-};
-
 struct GroupW {
-    const uint8_t *gw, *uw, *dw;
+    const uint8_t *gw, *uw;
     const float *gs, *us, *ds;
     int inter;
+    int down_row0;                // first row of this expert in its down tensor map
+    const CUtensorMap* dmap;
 };
 
 __device__ __forceinline__ GroupW group_w(const DecodeParams& p, int e) {
@@ -194,153 +150,127 @@ __device__ __forceinline__ GroupW group_w(const DecodeParams& p, int e) {
         g.inter = p.SI;
         g.gw = p.sh_gate_w;
         g.uw = p.sh_up_w;
-        g.dw = p.sh_down_w;
         g.gs = p.sh_gate_s;
         g.us = p.sh_up_s;
         g.ds = p.sh_down_s;
+        g.down_row0 = 0;
+        g.dmap = &p.sh_down_map;
     } else {
         g.inter = p.I;
         const size_t wsz = (size_t)p.I * p.H;
         g.gw = p.gate_w + (size_t)e * wsz;
         g.uw = p.up_w + (size_t)e * wsz;
-        g.dw = p.down_w + (size_t)e * wsz;
         const size_t ssz = (size_t)cz_nblk(p.I) * cz_nbp(p.H);
         g.gs = p.gate_s + (size_t)e * ssz;
         g.us = p.up_s + (size_t)e * ssz;
         g.ds = p.down_s + (size_t)e * cz_nblk(p.H) * cz_nbp(p.I);
+        g.down_row0 = e * p.H;
+        g.dmap = &p.down_map;
     }
     return g;
 }
 
-__device__ void set_error(uint32_t* err, DecodeSmem& s, uint32_t bit) {
+__device__ void set_error(uint32_t* err, DecodeMisc& s, uint32_t bit) {
     atomicOr(err, bit);
     s.abort = 1;
 }
 
-// 4 E4M3 bytes -> two f16x2 (bytes 0,1 and bytes 2,3), exact.
-__device__ __forceinline__ void cvt4(uint32_t w, uint32_t& lo, uint32_t& hi) {
-    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
-        "cvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
-        : "=r"(lo), "=r"(hi)
-        : "r"(w));
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
 }
 
-__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+// Bulk copy global -> shared with an L2 cache-policy hint (streamed weights).
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
+// One 2D TMA box (16 x 256 bytes) of a u8 tensor map -> shared memory (no multicast).
+__device__ __forceinline__ void tma_box_g2s(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_e4m3(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
     asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Power-of-two exponent s with max * 2^s in [2^13, 2^14) (0 for max == 0 or
-// non-finite): keeps the f16 hi/lo parts of every value inside f16's range.
+// Power-of-two exponent s with max * 2^s in [128, 256) (0 for max == 0 or
+// non-finite), so that the leading E4M3 term never saturates (max 448); read
+// off the exponent bits (mx in [2^(be-127), 2^(be-126)) for a normal mx), and
+// clamped to [-100, 100] so that 2^s and 2^-s are normal floats.
 __device__ __forceinline__ int prescale_exp(float mx) {
-    if (!(mx > 0.0f) || !(mx < 3.0e38f)) return 0;
-    int e;
-    frexpf(mx, &e);
-    return max(-100, min(14 - e, 100));
+    const int be = (int)(__float_as_uint(mx) >> 23);
+    if (!(mx > 0.0f) || be >= 255) return 0;
+    return max(-100, min(134 - be, 100));
 }
 
-// 2^e as a float, e in [-126, 127] (exact).
-__device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }
+// v * 2^e for e in [-126, 127] (exact while the product is a normal float).
+__device__ __forceinline__ float scale2(float v, int e) { return v * __int_as_float((127 + e) << 23); }
 
-// v * 2^e split into f16 hi + lo (the multiply by a power of two is exact
-// unless it leaves the f32 range; e is chosen so that it does not).
-__device__ __forceinline__ void split_f16(float v, int e, __half& hi, __half& lo) {
-    const float sv = e >= -126 && e <= 127 ? v * pow2f(e) : ldexpf(v, e);
-    hi = __float2half_rn(sv);
-    lo = __float2half_rn(sv - __half2float(hi));
+// silu with the fast exponential (relative error ~1e-6, far inside the
+// layer-output tolerance).
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// Two values -> their next E4M3 terms (round to nearest even; bytes lo = a,
+// hi = b) and the residuals a - term(a), b - term(b), which are exact.
+__device__ __forceinline__ uint16_t e4m3_term2(float& a, float& b) {
+    uint16_t d;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(d) : "f"(b), "f"(a));
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(d));
+    const __half2 hv = *reinterpret_cast<__half2*>(&h2);
+    a = __fsub_rn(a, __low2float(hv));
+    b = __fsub_rn(b, __high2float(hv));
+    return d;
 }
 
-// One 16-row x 8-column MMA tile over K (full K, one warp).  Lane (g, tq):
-// A rows g (top) and g+8 (bottom) start at `top` / `bot` in shared memory;
-// its B column starts at `bcol` (16-element chunks of 64 bytes: 16 hi halves
-// then 16 lo halves; `bcol` already points at the hi or lo half).  Each
-// 128-column block's partial is multiplied by stab[kb] / sbot[kb].
-// acc: C[g][2tq], C[g][2tq+1], C[g+8][2tq], C[g+8][2tq+1].
-__device__ __forceinline__ void tile_mma(const uint8_t* top, const uint8_t* bot, bool oktop, bool okbot,
-                                         const uint8_t* bcol, bool bok, int K, int tq, const float* stop,
-                                         const float* sbot, float* acc) {
-    const int nb = cz_nblk(K);
-    for (int kb = 0; kb < nb; ++kb) {
-        float cb[2][4] = {};
-#pragma unroll
-        for (int sb = 0; sb < 2; ++sb) {
-            const int kbase = kb * 128 + sb * 64;
-            if (kbase >= K) break;  // warp-uniform
-            const int k0 = kbase + 16 * tq;
-            const bool kin = k0 < K;  // lanes past the end feed zeros to the MMA
-            uint4 wa = make_uint4(0, 0, 0, 0), wb = wa, x0 = wa, x1 = wa;
-            if (oktop && kin) wa = *reinterpret_cast<const uint4*>(top + k0);
-            if (okbot && kin) wb = *reinterpret_cast<const uint4*>(bot + k0);
-            if (bok && kin) {
-                const uint4* xp = reinterpret_cast<const uint4*>(bcol + (size_t)(k0 >> 4) * 64);
-                x0 = xp[0];
-                x1 = xp[1];
-            }
-            const uint32_t A[4] = {wa.x, wa.y, wa.z, wa.w}, B[4] = {wb.x, wb.y, wb.z, wb.w};
-            const uint32_t X[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                uint32_t a0, a2, a1, a3;
-                cvt4(A[j], a0, a2);
-                cvt4(B[j], a1, a3);
-                mma16816(cb[j & 1], a0, a1, a2, a3, X[2 * j], X[2 * j + 1]);
-            }
-        }
-        const float st = oktop ? stop[kb] : 0.f, sbt = okbot ? sbot[kb] : 0.f;
-        acc[0] = __fmaf_rn(st, cb[0][0] + cb[1][0], acc[0]);
-        acc[1] = __fmaf_rn(st, cb[0][1] + cb[1][1], acc[1]);
-        acc[2] = __fmaf_rn(sbt, cb[0][2] + cb[1][2], acc[2]);
-        acc[3] = __fmaf_rn(sbt, cb[0][3] + cb[1][3], acc[3]);
-    }
-}
-
-// Router dot of one row with up to 4 tokens, in dotF32's exact order.
-// wrow / xs are shared memory.  Writes logits (lane 0).
-template <bool BF16>
-__device__ __forceinline__ void router_item(const float* __restrict__ wrow, const uint8_t* __restrict__ xs, int H,
-                                            int t0, int nt, int lane, float* __restrict__ logits, int lstride,
-                                            int col) {
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+// Router dot of one row with one token, in dotF32's exact order (lane l holds
+// chain l: elements l, l+32, ...; then the lane-ordered combine and the FMA
+// tail).  wrow / xs are shared memory.  Returns the logit in every lane.
+__device__ __forceinline__ float router_dot(const float* __restrict__ wrow, const uint8_t* __restrict__ xs, int H,
+                                            bool bf16, int lane) {
     const uint16_t* xb = reinterpret_cast<const uint16_t*>(xs);
     const float* xf = reinterpret_cast<const float*>(xs);
-    auto xv = [&](int t, int i) -> float {
-        if (BF16) return __uint_as_float((uint32_t)xb[(size_t)t * H + i] << 16);
-        return xf[(size_t)t * H + i];
-    };
+    float acc = 0.0f;
     int i = 0;
+#pragma unroll 2
     for (; i + 32 <= H; i += 32) {
-        const float w = wrow[i + lane];
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            if (q < nt) acc[q] = __fmaf_rn(xv(t0 + q, i + lane), w, acc[q]);
+        const float x = bf16 ? __uint_as_float((uint32_t)xb[i + lane] << 16) : xf[i + lane];
+        acc = __fmaf_rn(x, wrow[i + lane], acc);
     }
-    for (; i + 8 <= H; i += 8) {
+    for (; i + 8 <= H; i += 8) {  // a final 8-wide block: lanes 0..7 only
         if (lane < 8) {
-            const float w = wrow[i + lane];
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-                if (q < nt) acc[q] = __fmaf_rn(xv(t0 + q, i + lane), w, acc[q]);
+            const float x = bf16 ? __uint_as_float((uint32_t)xb[i + lane] << 16) : xf[i + lane];
+            acc = __fmaf_rn(x, wrow[i + lane], acc);
         }
     }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        // total[l] = (((0 + acc0[l]) + acc1[l]) + acc2[l]) + acc3[l]; chain k = lanes 8k..8k+7
-        const float a = acc[q];
-        const float a8 = __shfl_down_sync(0xffffffffu, a, 8);
-        const float a16 = __shfl_down_sync(0xffffffffu, a, 16);
-        const float a24 = __shfl_down_sync(0xffffffffu, a, 24);
-        const float tl = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, a), a8), a16), a24);
-        float sum = __shfl_sync(0xffffffffu, tl, 0);
-#pragma unroll
-        for (int l = 1; l < 8; ++l) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, tl, l));
-        if (q < nt) {
-            for (int ii = i; ii < H; ++ii) sum = __fmaf_rn(xv(t0 + q, ii), wrow[ii], sum);
-            if (lane == 0) logits[(size_t)(t0 + q) * lstride + col] = sum;
-        }
+    // total[l] = (((0 + acc0[l]) + acc1[l]) + acc2[l]) + acc3[l]; chain k = lanes 8k..8k+7
+    const float a8 = __shfl_down_sync(0xffffffffu, acc, 8);
+    const float a16 = __shfl_down_sync(0xffffffffu, acc, 16);
+    const float a24 = __shfl_down_sync(0xffffffffu, acc, 24);
+    const float tl = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, acc), a8), a16), a24);
+    float sum = __shfl_sync(0xffffffffu, tl, 0);
+#pragma unroll 1
+    for (int l = 1; l < 8; ++l) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, tl, l));
+    for (; i < H; ++i) {
+        const float x = bf16 ? __uint_as_float((uint32_t)xb[i] << 16) : xf[i];
+        sum = __fmaf_rn(x, wrow[i], sum);
     }
+    return sum;
 }
 
 // Top-k of one token (moe.zig:435-463) by one warp; lg = the token's logits in
@@ -350,26 +280,26 @@ __device__ __forceinline__ void router_item(const float* __restrict__ wrow, cons
 // among equal keys, the smallest id — the reference's strict-greater scan from
 // e = 0 with bv = -1.  A round without a candidate yields id 0, as in the
 // reference.
-__device__ void route_token(const float* __restrict__ lg, int E, int K, int norm_topk, int has_shared, int T, int t,
-                            int lane, DecodeSmem& s, uint32_t* topk_idx, float* topk_gates, bool write_out) {
-    float v[MAXM];
+template <int NM>
+__device__ __noinline__ void route_token(const float* __restrict__ lg, int E, int K, int norm_topk, int has_shared, int T, int t,
+                            int lane, DecodeMisc& s, uint32_t* topk_idx, float* topk_gates, bool write_out) {
+    float v[NM];
     float mx = __int_as_float(0xffc00000);  // NaN: fmaxf ignores it
-    const int nm = (E + 31) >> 5;
 #pragma unroll
-    for (int m = 0; m < MAXM; ++m) {
+    for (int m = 0; m < NM; ++m) {
         const int e = lane + 32 * m;
-        v[m] = (m < nm && e < E) ? lg[e] : __int_as_float(0xffc00000);
+        v[m] = (e < E) ? lg[e] : __int_as_float(0xffc00000);
         mx = fmaxf(mx, v[m]);
     }
     mx = warp_max(mx);
-    uint32_t key[MAXM];
+    uint32_t key[NM];
     double all = 0.0;
     float ex0 = 0.0f;
 #pragma unroll
-    for (int m = 0; m < MAXM; ++m) {
+    for (int m = 0; m < NM; ++m) {
         const int e = lane + 32 * m;
         key[m] = 0u;
-        if (m < nm && e < E) {
+        if (e < E) {
             const float ex = cz_expf(__fsub_rn(v[m], mx));
             all += (double)ex;
             if (ex > -1.0f) key[m] = __float_as_uint(ex) + 1u;
@@ -383,7 +313,7 @@ __device__ void route_token(const float* __restrict__ lg, int E, int K, int norm
         uint32_t lbest = 0u;
         int lid = 0x7fffffff;
 #pragma unroll
-        for (int m = 0; m < MAXM; ++m) {
+        for (int m = 0; m < NM; ++m) {
             if (key[m] > lbest) {
                 lbest = key[m];
                 lid = lane + 32 * m;
@@ -399,7 +329,7 @@ __device__ void route_token(const float* __restrict__ lg, int E, int K, int norm
             best = (int)redux_min_u32(lbest == kmax ? (uint32_t)lid : 0xffffffffu);
             bv = __uint_as_float(kmax - 1u);
 #pragma unroll
-            for (int m = 0; m < MAXM; ++m)
+            for (int m = 0; m < NM; ++m)
                 if (lane + 32 * m == best) key[m] = 0u;
         }
         top = __dadd_rn(top, (double)bv);
@@ -428,13 +358,18 @@ __device__ void route_token(const float* __restrict__ lg, int E, int K, int norm
 __device__ __forceinline__ int pair_token(int pr, int T, int K) { return pr < T * K ? pr / K : pr - T * K; }
 
 // Bounded wait of all lanes on an mbarrier phase; warp-uniform result.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, DecodeSmem& s) {
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, DecodeMisc& s) {
     return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, &s.abort));
 }
 
-__global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const DecodeParams p) {
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory"); }
+
+__global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_constant__ DecodeParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    DecodeSmem& s = *reinterpret_cast<DecodeSmem*>(smem_raw);
+    // 1024-aligned base as an offset into the __shared__ array itself, so every
+    // pointer below stays in the shared address space (plain LDS/STS, not
+    // generic accesses)
+    uint8_t* const sb = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, c = blockIdx.x;
     const int T = p.T, H = p.H, E = p.E, K = p.K;
@@ -442,24 +377,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const DecodePar
     const int Er = E + (SI ? 1 : 0);
     const int LS = logit_stride(E);
     const bool xbf = p.x_bf16 != 0;
+    const Carve cv = carve(T, H, p.x_bf16);
+    DecodeMisc& s = *reinterpret_cast<DecodeMisc*>(sb + cv.misc);
+    uint8_t* const ring = sb;
+    uint8_t* const xterm = sb + cv.xterm;
+    float* const acc = reinterpret_cast<float*>(sb + cv.acc);
+    float* const red = reinterpret_cast<float*>(sb + cv.red);
+    uint8_t* const hterm = sb + cv.hterm;
     uint32_t* const err = p.sync + 1;
 
     const uint32_t seq = ld_relaxed_gpu(p.sync);
     uint32_t* reg = region(p.sync, seq & 1);
     if (c == 0 && tid < kSyncRegionWords) region(p.sync, (seq & 1) ^ 1)[tid] = 0u;
     if (tid == 0) {
-        for (int i = 0; i < NSTAGES; ++i) {
+        for (int i = 0; i < NSLOT; ++i) {
             mbar_init(&s.full[i], 1);
-            mbar_init(&s.hfull[i], 1);
-            mbar_init(&s.empty[i], 1);
+            mbar_init(&s.empty[i], NCW);
         }
         mbar_init(&s.rbar, 1);
         mbar_init(&s.lbar, 1);
-        mbar_init(&s.sbar, 1);
         s.abort = 0;
         fence_mbarrier_init();
     }
     if (tid < MAXT) s.xmax[tid] = 0u;
+    for (int i = tid; i < T * H; i += NTHREADS) acc[i] = 0.0f;
     __syncthreads();
 
     // ---------------- phase R: router logits ----------------
@@ -468,9 +409,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const DecodePar
     const uint32_t xbytes = (uint32_t)T * H * (xbf ? 2u : 4u);
     const uint32_t rbytes = (uint32_t)nrows * H * 4u;
     // ring during phase R: [router rows][tokens][rms weight]
-    float* rows = reinterpret_cast<float*>(s.ring);
-    uint8_t* xs = s.ring + rbytes;
-    float* wnorm = reinterpret_cast<float*>(s.ring + rbytes + xbytes);
+    float* rows = reinterpret_cast<float*>(ring);
+    uint8_t* xs = ring + rbytes;
+    float* wnorm = reinterpret_cast<float*>(ring + rbytes + xbytes);
     if (tid == 0) {
         const uint32_t wbytes = p.rms_w ? (uint32_t)H * 4u : 0u;
         mbar_arrive_expect_tx(&s.rbar, xbytes + rbytes + wbytes);
@@ -513,15 +454,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const DecodePar
                    : reinterpret_cast<const float*>(xs)[k];
     };
     if (!s.abort) {
-        const int ntg = (T + 3) / 4;
-        for (int it = warp; it < nrows * ntg; it += NCW + 1) {
-            const int r = it / ntg, t0 = (it % ntg) * 4;
-            if (xbf)
-                router_item<true>(rows + (size_t)r * H, xs, H, t0, min(4, T - t0), lane, p.logits, LS, row_lo + r);
-            else
-                router_item<false>(rows + (size_t)r * H, xs, H, t0, min(4, T - t0), lane, p.logits, LS, row_lo + r);
+        for (int it = warp; it < nrows * T; it += NCW + 1) {
+            const int r = it / T, t = it - r * T;
+            const float v = router_dot(rows + (size_t)r * H, xs + (size_t)t * H * (xbf ? 2 : 4), H, xbf, lane);
+            if (lane == 0) p.logits[(size_t)t * LS + row_lo + r] = v;
         }
-        // max |x_t| for the per-token power-of-two prescale (register max, one atomic per warp)
+        // max |x_t| for the per-token power-of-two prescale (one atomic per warp)
         for (int t = 0; t < T; ++t) {
             float m = 0.0f;
             for (int i = tid; i < H; i += NTHREADS) {
@@ -536,22 +474,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const DecodePar
     if (tid < T) {
         const int e = prescale_exp(__uint_as_float(s.xmax[tid]));
         s.xexp[tid] = e;
-        s.xscale[tid] = ldexpf(1.0f, -e);
+        s.xscale[tid] = scale2(1.0f, -e);
     }
     __syncthreads();
-    // Tokens as MMA B columns: x_t * 2^s_t split into f16 hi/lo.  xh holds token
-    // rows of stride XQS bytes; 16-element chunk c of a row is 16 hi halves then
-    // 16 lo halves (64 bytes).  One thread per 2 elements (an f16x2 of each part).
-    const int XQS = H * 4 + 32;
+    // Tokens as MMA columns: x_t * 2^s_t = term 0 + term 1 (+ term 2), E4M3.
+    // Column (t, j) holds term j of token t, H bytes at xterm + (t*JX + j)*CS.
     if (!s.abort) {
-        for (int k = tid; k < (T * H) >> 1; k += NTHREADS) {
-            const int e2 = 2 * k, t = e2 / H, i = e2 - t * H;
-            __half h0, l0, h1, l1;
-            split_f16(xval(e2), s.xexp[t], h0, l0);
-            split_f16(xval(e2 + 1), s.xexp[t], h1, l1);
-            uint8_t* row = s.xh + (size_t)t * XQS + (size_t)(i >> 4) * 64 + (i & 15) * 2;
-            *reinterpret_cast<__half2*>(row) = __halves2half2(h0, h1);
-            *reinterpret_cast<__half2*>(row + 32) = __halves2half2(l0, l1);
+        for (int t = 0; t < T; ++t) {
+            const int sx = s.xexp[t];
+            uint8_t* col = xterm + (size_t)(t * cv.JX) * cv.CS;
+            for (int i = 2 * tid; i < H; i += 2 * NTHREADS) {
+                float a = scale2(xval(t * H + i), sx), b = scale2(xval(t * H + i + 1), sx);
+                for (int j = 0; j < cv.JX; ++j) {
+                    const uint16_t d = e4m3_term2(a, b);
+                    *reinterpret_cast<uint16_t*>(col + (size_t)j * cv.CS + i) = d;
+                }
+            }
         }
     }
     __syncthreads();
@@ -565,21 +503,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const DecodePar
             asm volatile("fence.proxy.async.global;" ::: "memory");
             const uint32_t lbytes = (uint32_t)T * LS * 4u;
             mbar_arrive_expect_tx(&s.lbar, lbytes);
-            bulk_g2s(s.ring, p.logits, lbytes, &s.lbar);
+            bulk_g2s(ring, p.logits, lbytes, &s.lbar);
         }
     }
     __syncthreads();
 
     // ---------------- phase K: top-k + grouping (every CTA) ----------------
-    if (s.abort) goto finish;  // uniform: settled before the barrier above
-    if (!mbar_wait_bounded(&s.lbar, 0, &s.abort) && lane == 0) set_error(err, s, CZ_DERR_FULL_WAIT);
+    if (!s.abort && !mbar_wait_bounded(&s.lbar, 0, &s.abort) && lane == 0) set_error(err, s, CZ_DERR_FULL_WAIT);
     __syncthreads();
-    if (s.abort) goto finish;
-    for (int t = warp; t < T; t += NCW + 1)
-        route_token(reinterpret_cast<const float*>(s.ring) + (size_t)t * LS, E, K, p.norm_topk, SI != 0, T, t, lane,
-                    s, p.topk_idx, p.topk_gates, c == 0);
+    if (!s.abort) {
+        for (int t = warp; t < T; t += NCW + 1) {
+            const float* lg = reinterpret_cast<const float*>(ring) + (size_t)t * LS;
+            if (E <= 128)
+                route_token<4>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates, c == 0);
+            else
+                route_token<MAXM>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates, c == 0);
+        }
+    }
     __syncthreads();
-    {
+    if (!s.abort) {
         const int P = T * K + (SI ? T : 0);
         // sort pairs by (expert, pair) with ranks: P <= 68
         for (int i = tid; i < P; i += NTHREADS) {
@@ -591,8 +533,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const DecodePar
             }
             s.order[r] = i;
         }
-        __syncthreads();
-        if (warp == 0) {
+    }
+    __syncthreads();
+    if (warp == 0) {
+        if (!s.abort) {
+            const int P = T * K + (SI ? T : 0);
             // group starts: positions where the expert changes
             int base = 0;
             for (int r0 = 0; r0 < P; r0 += 32) {
@@ -611,416 +556,411 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const DecodePar
                 const int end = (u + 1 < base) ? s.g_pair0[u + 1] : P;
                 s.g_npairs[u] = end - s.g_pair0[u];
             }
-            for (int u = lane; u <= base; u += 32) s.g_rowA[u] = u * Ir;  // routed groups: I rows each
             __syncwarp();
             if (lane == 0) {
-                if (base > 0 && s.g_expert[base - 1] == E) s.g_rowA[base] = (base - 1) * Ir + SI;  // shared: last
+                int nc = 0;
+                for (int u = 0; u < base; ++u) {
+                    s.g_chunk0[u] = nc;
+                    nc += (s.g_expert[u] == E ? SI : Ir) / CR;
+                }
+                s.g_chunk0[base] = nc;
                 s.U = base;
                 s.P = P;
+                s.NC = nc;
             }
+        } else if (lane == 0) {
+            s.U = 0;
+            s.NC = 0;
         }
-        __syncthreads();
     }
+    __syncthreads();
 
-    // ---------------- phases A and B ----------------
+    // ---------------- phase C: this CTA's chunks ----------------
     {
-        const int U = s.U;
-        const int NA = s.g_rowA[U];
-        const int a_lo = (int)((long long)c * NA / G), a_hi = (int)((long long)(c + 1) * NA / G);
-        const int b_lo = (int)((long long)c * H / G), b_hi = (int)((long long)(c + 1) * H / G);
-        const int WS = H + WPAD;
-        const int RA = min(8, STAGE_BYTES / (2 * WS));
-        const int HS = max(Ir, SI);
-        const int nbHp = cz_nbp(H), nbIrp = cz_nbp(Ir);
-        uint32_t* const adone = reg + 2;
-        uint32_t* const hmax = reg + 8;
-        const bool has_b = (b_lo < b_hi) && U > 0;
-        const int bb0 = b_lo >> 7, nbb = has_b ? ((b_hi - 1) >> 7) - bb0 + 1 : 0;
-
-        // block-scale tables this CTA needs (bulk-copied by the producer)
-        if (tid == 0) {
-            int u0 = 0;
-            while (u0 < U && s.g_rowA[u0 + 1] <= a_lo) ++u0;
-            int u1 = u0, need = 0;
-            s.sA_off[0] = 0;
-            while (u1 < U && s.g_rowA[u1] < a_hi && u1 - u0 < MAXAG) {
-                const int inter = s.g_expert[u1] == E ? SI : Ir;
-                need += 2 * cz_nblk(inter) * nbHp;
-                ++u1;
-                s.sA_off[u1 - u0] = need;
-            }
-            s.a_u0 = u0;
-            s.a_u1 = u1;
-            s.sA_ok = (need <= SA_FLOATS) && (u1 >= U || s.g_rowA[u1] >= a_hi);
-            const int nbSp = cz_nbp(SI ? SI : Ir);
-            const int needB = U > 0 ? (U - 1) * nbb * nbIrp + nbb * (s.g_expert[U - 1] == E ? nbSp : nbIrp) : 0;
-            s.sB_ok = needB <= SB_FLOATS;
-        }
-        __syncthreads();
+        const int NC = s.NC;
+        const int ch_lo = (int)((long long)c * NC / G), ch_hi = (int)((long long)(c + 1) * NC / G);
+        const int nks = (H + KS - 1) / KS;     // gate (and up) stages per chunk
+        const int nos = (H + OS - 1) / OS;     // down stages per chunk
+        const int spc = 2 * nks + nos;         // stages per chunk
+        const int nbpH = cz_nbp(H);
 
         if (warp == NCW) {
             // ---------------- producer (one thread) ----------------
             if (lane == 0) {
                 fence_proxy_async_smem();  // generic reads of the ring (logits) precede the async writes
-                uint32_t sbytes = 0;
-                if (s.sA_ok)
-                    for (int u = s.a_u0; u < s.a_u1; ++u)
-                        sbytes += 2u * (uint32_t)cz_nblk(s.g_expert[u] == E ? SI : Ir) * nbHp * 4u;
-                if (s.sB_ok && has_b)
-                    for (int u = 0; u < U; ++u) sbytes += (uint32_t)nbb * cz_nbp(s.g_expert[u] == E ? SI : Ir) * 4u;
-                mbar_arrive_expect_tx(&s.sbar, sbytes);
-                if (s.sA_ok) {
-                    for (int u = s.a_u0; u < s.a_u1; ++u) {
-                        const GroupW gwt = group_w(p, s.g_expert[u]);
-                        const uint32_t tb = (uint32_t)cz_nblk(gwt.inter) * nbHp * 4u;
-                        float* dst = s.sA + s.sA_off[u - s.a_u0];
-                        bulk_g2s(dst, gwt.gs, tb, &s.sbar);
-                        bulk_g2s(reinterpret_cast<uint8_t*>(dst) + tb, gwt.us, tb, &s.sbar);
-                    }
-                }
-                if (s.sB_ok && has_b) {
-                    for (int u = 0; u < U; ++u) {
-                        const GroupW gwt = group_w(p, s.g_expert[u]);
-                        const int nbIp = cz_nbp(gwt.inter);
-                        bulk_g2s(s.sB + u * nbb * nbIrp, gwt.ds + (size_t)bb0 * nbIp, (uint32_t)nbb * nbIp * 4u,
-                                 &s.sbar);
-                    }
-                }
-                StageIter itr;
-                itr.init(s, a_lo, a_hi, b_lo, b_hi, RA);
-                Stage st;
+                const uint64_t pol = l2_evict_first_policy();
                 int si = 0;
-                bool adone_seen = false;
-                // down stages whose h rows wait for every CTA to finish phase A
-                int pend_u[NSTAGES], pend_q0[NSTAGES], pend_nq[NSTAGES];
-#pragma unroll
-                for (int i = 0; i < NSTAGES; ++i) pend_nq[i] = 0;
-                auto issue_h = [&](int slot, int u, int q0, int nq) {
-                    const GroupW gwt = group_w(p, s.g_expert[u]);
-                    const int* pairs = s.order + s.g_pair0[u];
-                    uint8_t* hdst = s.ring + (size_t)slot * STAGE_BYTES + 16 * (gwt.inter + WPAD);
-                    mbar_arrive_expect_tx(&s.hfull[slot], (uint32_t)nq * gwt.inter * 4u);
-                    for (int q = 0; q < nq; ++q)
-                        bulk_g2s(hdst + (size_t)q * (gwt.inter * 4 + HPAD), p.hbuf + (size_t)pairs[q0 + q] * HS,
-                                 (uint32_t)gwt.inter * 4u, &s.hfull[slot]);
-                };
-                auto poll_adone = [&]() {
-                    if (adone_seen || !has_b || ld_acquire_gpu(adone) < (uint32_t)G) return;
-                    adone_seen = true;
-                    asm volatile("fence.proxy.async.global;" ::: "memory");
-#pragma unroll
-                    for (int i = 0; i < NSTAGES; ++i)
-                        if (pend_nq[i]) {
-                            issue_h(i, pend_u[i], pend_q0[i], pend_nq[i]);
-                            pend_nq[i] = 0;
-                        }
-                };
-                while (!s.abort && itr.next(st)) {
-                    const int slot = si % NSTAGES, round = si / NSTAGES;
-                    if (round > 0) {
-                        bool ok = false;
-                        for (uint32_t it = 0; it < CZ_SPIN_LIMIT && !ok && !s.abort; ++it) {
-                            ok = mbar_try_wait(&s.empty[slot], (round - 1) & 1);
-                            if (!ok) {
-                                poll_adone();
-                                if (it > 64) __nanosleep(64);
+                // stage order: gate/up slabs of every chunk, then the down stages of every chunk
+                for (int pass = 0; pass < 2; ++pass) {
+                    int u = 0;
+                    for (int ch = ch_lo; ch < ch_hi && !s.abort; ++ch) {
+                        while (s.g_chunk0[u + 1] <= ch) ++u;
+                        const GroupW gw = group_w(p, s.g_expert[u]);
+                        const int r0 = (ch - s.g_chunk0[u]) * CR;
+                        const int nbpI = cz_nbp(gw.inter);
+                        const int st_lo = pass == 0 ? 0 : 2 * nks, st_hi = pass == 0 ? 2 * nks : spc;
+                        for (int st = st_lo; st < st_hi && !s.abort; ++st, ++si) {
+                            const int slot = si % NSLOT, round = si / NSLOT;
+                            if (round > 0) {
+                                bool ok = false;
+                                for (uint32_t it = 0; it < CZ_SPIN_LIMIT && !ok && !s.abort; ++it) {
+                                    ok = mbar_try_wait(&s.empty[slot], (round - 1) & 1);
+                                    if (!ok && it > 64) __nanosleep(64);
+                                }
+                                if (!ok) {
+                                    if (!s.abort) set_error(err, s, CZ_DERR_EMPTY_WAIT);
+                                    break;
+                                }
+                            }
+                            uint8_t* dst = ring + (size_t)slot * SLOT_BYTES;
+                            float* sdst = reinterpret_cast<float*>(dst + GU_BYTES);
+                            if (st < 2 * nks) {
+                                // slab st/2: gate (st even) or up (st odd) rows [r0, r0+16), columns [k0, k0+L)
+                                const bool up = st & 1;
+                                const int k0 = (st >> 1) * KS, L = min(KS, H - k0);
+                                const uint8_t* src = (up ? gw.uw : gw.gw) + (size_t)r0 * H + k0;
+                                const float* ssrc = (up ? gw.us : gw.gs) + (size_t)(r0 >> 7) * nbpH;
+                                mbar_arrive_expect_tx(&s.full[slot], (uint32_t)(CR * L + nbpH * 4));
+                                for (int r = 0; r < CR; ++r)
+                                    bulk_g2s_hint(dst + (size_t)r * (KS + WPAD), src + (size_t)r * H, (uint32_t)L,
+                                                  &s.full[slot], pol);
+                                bulk_g2s(sdst, ssrc, (uint32_t)nbpH * 4u, &s.full[slot]);
+                            } else {
+                                // down columns [r0, r0+16) of output rows [o0, o0+OSl)
+                                const int o0 = (st - 2 * nks) * OS, OSl = min(OS, H - o0);
+                                const int nbox = (OSl + BOX_ROWS - 1) / BOX_ROWS;
+                                const int ob0 = o0 >> 7, nob = (OSl + 127) >> 7;
+                                mbar_arrive_expect_tx(&s.full[slot], (uint32_t)(nbox * BOX_ROWS * 16 + nob * nbpI * 4));
+                                for (int b = 0; b < nbox; ++b)
+                                    tma_box_g2s(dst + (size_t)b * BOX_ROWS * 16, gw.dmap, r0,
+                                                gw.down_row0 + o0 + b * BOX_ROWS, &s.full[slot], pol);
+                                bulk_g2s(sdst, gw.ds + (size_t)ob0 * nbpI, (uint32_t)(nob * nbpI * 4), &s.full[slot]);
                             }
                         }
-                        if (!ok) {
-                            if (!s.abort) set_error(err, s, CZ_DERR_EMPTY_WAIT);
-                            break;
-                        }
                     }
-                    const GroupW gwt = group_w(p, s.g_expert[st.u]);
-                    uint8_t* dst = s.ring + (size_t)slot * STAGE_BYTES;
-                    if (st.phase == 0) {
-                        // gate rows -> dst rows 0..n-1, up rows -> dst rows n..2n-1 (stride WS)
-                        mbar_arrive_expect_tx(&s.full[slot], 2u * st.n * H);
-                        for (int r = 0; r < st.n; ++r) {
-                            bulk_g2s(dst + (size_t)r * WS, gwt.gw + (size_t)(st.r0 + r) * H, (uint32_t)H, &s.full[slot]);
-                            bulk_g2s(dst + (size_t)(st.n + r) * WS, gwt.uw + (size_t)(st.r0 + r) * H, (uint32_t)H,
-                                     &s.full[slot]);
-                        }
-                    } else {
-                        const int IS = gwt.inter + WPAD;
-                        mbar_arrive_expect_tx(&s.full[slot], (uint32_t)st.n * gwt.inter);
-                        for (int r = 0; r < st.n; ++r)
-                            bulk_g2s(dst + (size_t)r * IS, gwt.dw + (size_t)(st.r0 + r) * gwt.inter, (uint32_t)gwt.inter,
-                                     &s.full[slot]);
-                        poll_adone();
-                        if (adone_seen) {
-                            issue_h(slot, st.u, st.q0, st.nq);
-                        } else {
-#pragma unroll
-                            for (int i = 0; i < NSTAGES; ++i)
-                                if (i == slot) {
-                                    pend_u[i] = st.u;
-                                    pend_q0[i] = st.q0;
-                                    pend_nq[i] = st.nq;
-                                }
-                        }
-                    }
-                    ++si;
                 }
-                bool pending = false;
-#pragma unroll
-                for (int i = 0; i < NSTAGES; ++i) pending |= pend_nq[i] != 0;
-                for (uint32_t it = 0; pending && !adone_seen && !s.abort && it < CZ_SPIN_LIMIT; ++it) {
-                    poll_adone();
-                    if (!adone_seen && it > 16) __nanosleep(128);
-                }
-                if (pending && !adone_seen && !s.abort) set_error(err, s, CZ_DERR_READY_WAIT);
                 // drain: no copy may land after this CTA exits (waiting on a phase
                 // that already completed returns at once)
-                for (int k = max(0, si - NSTAGES); k < si; ++k) {
+                for (int k = max(0, si - NSLOT); k < si; ++k) {
                     bool ok = false;
                     for (uint32_t it = 0; it < CZ_SPIN_LIMIT && !ok; ++it) {
-                        ok = mbar_try_wait(&s.full[k % NSTAGES], (k / NSTAGES) & 1);
+                        ok = mbar_try_wait(&s.full[k % NSLOT], (k / NSLOT) & 1);
                         if (!ok) __nanosleep(64);
                     }
                     if (!ok) atomicOr(err, CZ_DERR_DRAIN_WAIT);
                 }
-                bool ok = false;
-                for (uint32_t it = 0; it < CZ_SPIN_LIMIT && !ok; ++it) {
-                    ok = mbar_try_wait(&s.sbar, 0);
-                    if (!ok) __nanosleep(64);
-                }
-                if (!ok) atomicOr(err, CZ_DERR_DRAIN_WAIT);
-                // h copies: if one is still in flight, the consumer of that slot
-                // is waiting for it; the consumers drain them (below) before exit.
             }
             __syncwarp();
         } else {
-            // ---------------- consumers: warp w computes stages w, w+NCW, ... ----------------
-            const int g = lane >> 2, tq = lane & 3;  // MMA fragment coordinates
-            float bacc[MAXBT][2][4];                // phase B: [tile][row g / g+8][token]
-#pragma unroll
-            for (int a = 0; a < MAXBT; ++a)
-#pragma unroll
-                for (int b = 0; b < 2; ++b)
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) bacc[a][b][q] = 0.0f;
-            StageIter itr;
-            itr.init(s, a_lo, a_hi, b_lo, b_hi, RA);
-            Stage st;
-            int si = 0, hcnt = 0;
-            bool switched = false, hmax_seen = false;
-            // Every consumer warp runs this once, at the first down stage of the
-            // schedule (or at the end): all of this CTA's h rows and max |h| are
-            // stored, so the CTA counts itself done with phase A.
-            auto transition = [&]() {
-                switched = true;
-                asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
-                if (tid == 0) {
-                    __threadfence();
-                    red_release_add_gpu(adone, 1u);
-                }
-            };
-            if (!warp_wait(&s.sbar, 0, s) && lane == 0 && !s.abort) set_error(err, s, CZ_DERR_FULL_WAIT);
-            while (!s.abort && itr.next(st)) {
-                if (st.phase == 1 && !switched) transition();
-                if ((si % NCW) != warp) {
-                    ++si;
-                    continue;
-                }
-                const int slot = si % NSTAGES;
-                if (!warp_wait(&s.full[slot], (si / NSTAGES) & 1, s)) {
-                    if (lane == 0 && !s.abort) set_error(err, s, CZ_DERR_FULL_WAIT);
-                    break;
-                }
-                uint8_t* stage = s.ring + (size_t)slot * STAGE_BYTES;
-                const int u = st.u;
+            // ---------------- consumers ----------------
+            const int g = lane >> 2, t = lane & 3;  // MMA fragment coordinates
+            int si = 0;
+            int u = 0;
+            // ==== pass 1: gate/up and h of every chunk (h terms kept per chunk) ====
+            for (int ch = ch_lo; ch < ch_hi; ++ch) {
+                while (s.g_chunk0[u + 1] <= ch) ++u;
+                const int ci = ch - ch_lo;
                 const int np = s.g_npairs[u];
                 const int* pairs = s.order + s.g_pair0[u];
-                const GroupW gwt = group_w(p, s.g_expert[u]);
-                if (st.phase == 0) {
-                    // ---- gate/up: tile rows 0..7 = gate rows r0..r0+n-1, rows 8..15 = up rows ----
-                    const int n = st.n;
-                    const int nbI = cz_nblk(gwt.inter);
-                    const float* gtab = s.sA_ok ? s.sA + s.sA_off[u - s.a_u0] : gwt.gs;
-                    const float* utab = s.sA_ok ? gtab + nbI * nbHp : gwt.us;
-                    const bool rowok = g < n;
-                    const int rowblk = (st.r0 + min(g, n - 1)) >> 7;
-                    for (int q0 = 0; q0 < np; q0 += 4) {
-                        const int nq = min(4, np - q0);
-                        const int col_tok = (g & 3) < nq ? pair_token(pairs[q0 + (g & 3)], T, K) : -1;
-                        const uint8_t* xcol = s.xh + (size_t)max(col_tok, 0) * XQS + ((g >> 2) ? 32 : 0);
-                        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-                        tile_mma(stage + (size_t)g * WS, stage + (size_t)(n + g) * WS, rowok, rowok, xcol, col_tok >= 0,
-                                 H, tq, gtab + (size_t)rowblk * nbHp, utab + (size_t)rowblk * nbHp, acc);
-                        // hi (cols 0..3) + lo (cols 4..7, two lanes over)
-                        const float lo0 = __shfl_down_sync(0xffffffffu, acc[0], 2);
-                        const float lo1 = __shfl_down_sync(0xffffffffu, acc[1], 2);
-                        const float lo2 = __shfl_down_sync(0xffffffffu, acc[2], 2);
-                        const float lo3 = __shfl_down_sync(0xffffffffu, acc[3], 2);
-                        float mh[2] = {0.f, 0.f};
-                        if (tq < 2 && rowok) {
-                            const float gv[2] = {acc[0] + lo0, acc[1] + lo1};
-                            const float uv[2] = {acc[2] + lo2, acc[3] + lo3};
+                // columns of the gate/up MMAs: c = q*JX + j (pair q, term j); lane's column g of MMA m
+                const int ncolA = np * cv.JX, nmA = (ncolA + 7) >> 3;
+                const uint8_t* xcol[2];
+                bool xok[2];
 #pragma unroll
-                            for (int d = 0; d < 2; ++d) {
-                                const int q = 2 * tq + d;
-                                if (q < nq) {
-                                    const int pr = pairs[q0 + q];
-                                    const float xsc = s.xscale[pair_token(pr, T, K)];
-                                    const float hv = cz_silu(gv[d] * xsc) * (uv[d] * xsc);
-                                    p.hbuf[(size_t)pr * HS + st.r0 + g] = hv;
-                                    mh[d] = fabsf(hv);
-                                }
+                for (int m = 0; m < 2; ++m) {
+                    const int cc = 8 * m + g;
+                    xok[m] = cc < ncolA;
+                    const int q = xok[m] ? cc / cv.JX : 0, j = cc - q * cv.JX;
+                    const int tok = pair_token(pairs[q], T, K);
+                    xcol[m] = xterm + (size_t)(tok * cv.JX + (xok[m] ? j : 0)) * cv.CS;
+                }
+                float accg[2][4], accu[2][4];
+#pragma unroll
+                for (int m = 0; m < 2; ++m)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) accg[m][i] = accu[m][i] = 0.0f;
+
+                // ---- gate / up: slab k is the stage pair (gate, up); both tiles in one pass ----
+                for (int kq = 0; kq < nks; ++kq, si += 2) {
+                    const int slg = si % NSLOT, slu = (si + 1) % NSLOT;
+                    bool ok = !s.abort && warp_wait(&s.full[slg], (si / NSLOT) & 1, s);
+                    ok = ok && warp_wait(&s.full[slu], ((si + 1) / NSLOT) & 1, s);
+                    if (!ok) {
+                        if (lane == 0 && !s.abort) set_error(err, s, CZ_DERR_FULL_WAIT);
+                        continue;
+                    }
+                    const uint8_t* stg = ring + (size_t)slg * SLOT_BYTES;
+                    const uint8_t* stu = ring + (size_t)slu * SLOT_BYTES;
+                    const float* tg = reinterpret_cast<const float*>(stg + GU_BYTES);
+                    const float* tu = reinterpret_cast<const float*>(stu + GU_BYTES);
+                    const int k0 = kq * KS, L = min(KS, H - k0);
+                    const int nkb = (L + 127) >> 7;
+                    const int kb_lo = warp * nkb / NCW, kb_hi = (warp + 1) * nkb / NCW;
+                    float ag[2][4] = {}, au[2][4] = {};
+#pragma unroll 1
+                    for (int kb = kb_lo; kb < kb_hi; ++kb) {
+                        float cg[2][4] = {}, cu[2][4] = {};
+#pragma unroll
+                        for (int sg = 0; sg < 2; ++sg) {
+                            const int base = kb * 128 + sg * 64;
+                            if (base >= L) break;  // warp-uniform
+                            const int kk = base + 16 * t;
+                            const bool kin = kk < L;
+                            uint4 ga = make_uint4(0, 0, 0, 0), gb = ga, ua = ga, ub = ga, xb0 = ga, xb1 = ga;
+                            if (kin) {
+                                ga = *reinterpret_cast<const uint4*>(stg + (size_t)g * (KS + WPAD) + kk);
+                                gb = *reinterpret_cast<const uint4*>(stg + (size_t)(g + 8) * (KS + WPAD) + kk);
+                                ua = *reinterpret_cast<const uint4*>(stu + (size_t)g * (KS + WPAD) + kk);
+                                ub = *reinterpret_cast<const uint4*>(stu + (size_t)(g + 8) * (KS + WPAD) + kk);
+                                if (xok[0]) xb0 = *reinterpret_cast<const uint4*>(xcol[0] + k0 + kk);
+                                if (nmA > 1 && xok[1]) xb1 = *reinterpret_cast<const uint4*>(xcol[1] + k0 + kk);
+                            }
+                            mma_e4m3(cg[0], ga.x, gb.x, ga.y, gb.y, xb0.x, xb0.y);
+                            mma_e4m3(cu[0], ua.x, ub.x, ua.y, ub.y, xb0.x, xb0.y);
+                            mma_e4m3(cg[0], ga.z, gb.z, ga.w, gb.w, xb0.z, xb0.w);
+                            mma_e4m3(cu[0], ua.z, ub.z, ua.w, ub.w, xb0.z, xb0.w);
+                            if (nmA > 1) {  // warp-uniform
+                                mma_e4m3(cg[1], ga.x, gb.x, ga.y, gb.y, xb1.x, xb1.y);
+                                mma_e4m3(cu[1], ua.x, ub.x, ua.y, ub.y, xb1.x, xb1.y);
+                                mma_e4m3(cg[1], ga.z, gb.z, ga.w, gb.w, xb1.z, xb1.w);
+                                mma_e4m3(cu[1], ua.z, ub.z, ua.w, ub.w, xb1.z, xb1.w);
                             }
                         }
-                        // max |h| per pair over the tile rows (lanes g*4 + tq, same tq)
+                        const float scg = tg[(k0 >> 7) + kb], scu = tu[(k0 >> 7) + kb];
 #pragma unroll
-                        for (int d = 0; d < 2; ++d) {
-                            float m = mh[d];
-                            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-                            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
-                            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
-                            const int q = 2 * tq + d;
-                            if (g == 0 && tq < 2 && q < nq && m > 0.0f && m < 3.0e38f)
-                                atomicMax(hmax + pairs[q0 + q], __float_as_uint(m));
+                        for (int m = 0; m < 2; ++m)
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                ag[m][i] = __fmaf_rn(scg, cg[m][i], ag[m][i]);
+                                au[m][i] = __fmaf_rn(scu, cu[m][i], au[m][i]);
+                            }
+                    }
+#pragma unroll
+                    for (int m = 0; m < 2; ++m)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            accg[m][i] += ag[m][i];
+                            accu[m][i] += au[m][i];
                         }
-                    }
-                } else {
-                    // ---- down: tile = 16 of this CTA's output rows, columns = pairs q0.. of the group ----
-                    const int inter = gwt.inter;
-                    const int IS = inter + WPAD;
-                    const int nbIp = cz_nbp(inter);
-                    const int tile = (st.r0 - b_lo) >> 4;
-                    const int nq = st.nq;
-                    bool ok = warp_wait(&s.hfull[slot], hcnt & 1, s);
-                    if (ok) ++hcnt;
-                    if (ok && !hmax_seen) {  // every CTA's max |h| is visible once the count is (acquire)
-                        bool seen = true;
-                        if (lane == 0) seen = wait_geq_bounded(adone, (uint32_t)G, err);
-                        ok = __shfl_sync(0xffffffffu, seen, 0);
-                        hmax_seen = ok;
-                        __syncwarp();
-                    }
-                    if (!ok) {
-                        if (lane == 0 && !s.abort) set_error(err, s, CZ_DERR_READY_WAIT);
-                        break;
-                    }
-                    // this stage's h rows: f32 -> per-pair 2^s scaled f16 hi/lo chunks, in place
-                    uint8_t* hrows = stage + 16 * IS;
-                    const int HRS = inter * 4 + HPAD;
-                    int hexp[4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        hexp[q] = q < nq ? prescale_exp(__uint_as_float(ld_relaxed_gpu(hmax + pairs[st.q0 + q]))) : 0;
-                    const int nch = inter >> 4;
-                    for (int k = lane; k < nq * nch; k += 32) {
-                        const int q = k / nch, ch = k - q * nch;
-                        int e = hexp[0];
-#pragma unroll
-                        for (int qq = 1; qq < 4; ++qq)
-                            if (qq == q) e = hexp[qq];
-                        float4* cp = reinterpret_cast<float4*>(hrows + (size_t)q * HRS + ch * 64);
-                        float v[16];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const float4 f = cp[j];
-                            v[4 * j] = f.x;
-                            v[4 * j + 1] = f.y;
-                            v[4 * j + 2] = f.z;
-                            v[4 * j + 3] = f.w;
-                        }
-                        __align__(16) __half hv[32];
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) split_f16(v[j], e, hv[j], hv[16 + j]);
-                        const uint4* src = reinterpret_cast<const uint4*>(hv);
-                        uint4* dst = reinterpret_cast<uint4*>(cp);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) dst[j] = src[j];
-                    }
                     __syncwarp();
-                    const bool oka = g < st.n, okb = g + 8 < st.n;
-                    const int oa = st.r0 + min(g, st.n - 1), ob = st.r0 + min(g + 8, st.n - 1);
-                    const float* dtab = s.sB_ok ? s.sB + u * nbb * nbIrp : nullptr;
-                    const float* sa = dtab ? dtab + ((oa >> 7) - bb0) * nbIp : gwt.ds + (size_t)(oa >> 7) * nbIp;
-                    const float* sbr = dtab ? dtab + ((ob >> 7) - bb0) * nbIp : gwt.ds + (size_t)(ob >> 7) * nbIp;
-                    const int cq = g & 3;
-                    const uint8_t* hcol = hrows + (size_t)min(cq, max(nq - 1, 0)) * HRS + ((g >> 2) ? 32 : 0);
-                    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-                    tile_mma(stage + (size_t)g * IS, stage + (size_t)(g + 8) * IS, oka, okb, hcol, cq < nq, inter, tq,
-                             sa, sbr, acc);
-                    const float lo0 = __shfl_down_sync(0xffffffffu, acc[0], 2);
-                    const float lo1 = __shfl_down_sync(0xffffffffu, acc[1], 2);
-                    const float lo2 = __shfl_down_sync(0xffffffffu, acc[2], 2);
-                    const float lo3 = __shfl_down_sync(0xffffffffu, acc[3], 2);
-                    if (tq < 2) {
-                        const float va[2] = {acc[0] + lo0, acc[1] + lo1};
-                        const float vb[2] = {acc[2] + lo2, acc[3] + lo3};
+                    if (lane == 0) {
+                        mbar_arrive(&s.empty[slg]);
+                        mbar_arrive(&s.empty[slu]);
+                    }
+                }
+
+                // ---- h = silu(g) * u for the chunk's 16 rows x np pairs, then its E4M3 terms ----
+                // red[w][0 gate / 1 up][row][col]
+                {
+                    float* rg = red + (warp * 2 + 0) * 256;
+                    float* ru = red + (warp * 2 + 1) * 256;
 #pragma unroll
-                        for (int d = 0; d < 2; ++d) {
-                            const int q = 2 * tq + d;
-                            if (q < nq) {
-                                const int pr = pairs[st.q0 + q];
-                                const int tk = pair_token(pr, T, K);
-                                int e = hexp[0];
+                    for (int m = 0; m < 2; ++m) {
+                        const int col = 8 * m + 2 * t;
+                        rg[g * 16 + col] = accg[m][0];
+                        rg[g * 16 + col + 1] = accg[m][1];
+                        rg[(g + 8) * 16 + col] = accg[m][2];
+                        rg[(g + 8) * 16 + col + 1] = accg[m][3];
+                        ru[g * 16 + col] = accu[m][0];
+                        ru[g * 16 + col + 1] = accu[m][1];
+                        ru[(g + 8) * 16 + col] = accu[m][2];
+                        ru[(g + 8) * 16 + col + 1] = accu[m][3];
+                    }
+                }
+                consumers_sync();
+                if (tid < 64) {
+                    const int q = tid >> 4, r = tid & 15;
+                    const bool valid = q < np && !s.abort;
+                    float h = 0.0f;
+                    if (valid) {
+                        const int tok = pair_token(pairs[q], T, K);
+                        float gs = 0.0f, us = 0.0f;
+                        const float* rg = red + r * 16 + q * cv.JX;
 #pragma unroll
-                                for (int qq = 1; qq < 4; ++qq)
-                                    if (qq == q) e = hexp[qq];
-                                const float w = s.pg[pr] * ldexpf(1.0f, -e);
+                        for (int w = 0; w < NCW; ++w)
 #pragma unroll
-                                for (int tt = 0; tt < MAXBT; ++tt) {
-                                    if (tt != tile) continue;
+                            for (int j = 0; j < 3; ++j)
+                                if (j < cv.JX) {
+                                    gs += rg[w * 512 + j];
+                                    us += rg[w * 512 + 256 + j];
+                                }
+                        const float xsc = s.xscale[tok];
+                        h = silu_fast(gs * xsc) * (us * xsc);
+                    }
+                    // max |h| over the 16 rows of pair q (lanes of one half-warp)
+                    float mh = fabsf(h);
+                    if (!(mh < 3.0e38f)) mh = 0.0f;
 #pragma unroll
-                                    for (int t4 = 0; t4 < 4; ++t4) {
-                                        if (t4 != tk) continue;
-                                        bacc[tt][0][t4] = __fmaf_rn(w, va[d], bacc[tt][0][t4]);
-                                        bacc[tt][1][t4] = __fmaf_rn(w, vb[d], bacc[tt][1][t4]);
+                    for (int o = 8; o > 0; o >>= 1) mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
+                    const int sh = prescale_exp(mh);
+                    if (valid) {
+                        float a = scale2(h, sh), b = 0.0f;
+#pragma unroll
+                        for (int j = 0; j < JH; ++j) {
+                            const uint16_t d = e4m3_term2(a, b);
+                            hterm[ci * 256 + (q * JH + j) * 16 + r] = (uint8_t)(d & 0xff);
+                        }
+                        if (r == 0) s.wq[ci][q] = s.pg[pairs[q]] * scale2(1.0f, -sh);
+                    }
+                }
+                consumers_sync();
+            }
+            // ==== pass 2: down of every chunk into the per-CTA accumulator ====
+            u = 0;
+            for (int ch = ch_lo; ch < ch_hi; ++ch) {
+                while (s.g_chunk0[u + 1] <= ch) ++u;
+                const int ci = ch - ch_lo;
+                const int inter = s.g_expert[u] == E ? SI : Ir;
+                const int r0 = (ch - s.g_chunk0[u]) * CR;
+                const int np = s.g_npairs[u];
+                const int* pairs = s.order + s.g_pair0[u];
+                const int nbpI = cz_nbp(inter);
+                // ---- down stages: rows [o0, o0+OSl), columns = (pair, term) ----
+                const int ncolD = np * JH, nmD = (ncolD + 7) >> 3;
+                uint32_t bfr[2];
+                int tokq[2];
+                float wqv[2];
+#pragma unroll
+                for (int m = 0; m < 2; ++m) {
+                    const int cc = 8 * m + g;
+                    bfr[m] = cc < ncolD ? *reinterpret_cast<const uint32_t*>(hterm + ci * 256 + cc * 16 + 4 * t) : 0u;
+                    const int q = 2 * m + (t >> 1);
+                    tokq[m] = q < np ? pair_token(pairs[q], T, K) : 0;
+                    wqv[m] = q < np ? s.wq[ci][q] : 0.0f;
+                }
+                for (int st = 0; st < nos; ++st, ++si) {
+                    const int slot = si % NSLOT;
+                    const bool ok = !s.abort && warp_wait(&s.full[slot], (si / NSLOT) & 1, s);
+                    if (!ok) {
+                        if (lane == 0 && !s.abort) set_error(err, s, CZ_DERR_FULL_WAIT);
+                        continue;
+                    }
+                    const uint8_t* stage = ring + (size_t)slot * SLOT_BYTES;
+                    const float* stab = reinterpret_cast<const float*>(stage + GU_BYTES);
+                    const int o0 = st * OS, OSl = min(OS, H - o0);
+                    const int ntile = OSl >> 4;
+                    const int ib = r0 >> 7;
+                    // this warp's tiles tl = warp + NCW*v, in batches of DB: loads and MMAs
+                    // of a batch are independent; the accumulator update comes after all
+                    // of them (no store between two loads of a batch)
+                    for (int v0b = 0; warp + NCW * v0b < ntile; v0b += DB) {
+                        float r0[2][DB], r1[2][DB];
+                        float sdv[DB];
+#pragma unroll
+                        for (int v = 0; v < DB; ++v) {
+                            const int tl = warp + NCW * (v0b + v);
+                            const int ol = tl < ntile ? tl * 16 : 0;
+                            const uint32_t a0 = *reinterpret_cast<const uint32_t*>(stage + (size_t)(ol + g) * 16 + 4 * t);
+                            const uint32_t a1 =
+                                *reinterpret_cast<const uint32_t*>(stage + (size_t)(ol + g + 8) * 16 + 4 * t);
+                            sdv[v] = stab[(ol >> 7) * nbpI + ib];
+#pragma unroll
+                            for (int m = 0; m < 2; ++m) {
+                                float d[4] = {0.f, 0.f, 0.f, 0.f};
+                                if (m < nmD) mma_e4m3(d, a0, a1, 0u, 0u, bfr[m], 0u);
+                                r0[m][v] = d[0] + d[1];  // terms 2(t&1), 2(t&1)+1 of pair 2m + t/2
+                                r1[m][v] = d[2] + d[3];
+                            }
+                        }
+#pragma unroll
+                        for (int m = 0; m < 2; ++m)
+#pragma unroll
+                            for (int v = 0; v < DB; ++v) {  // the other two terms are one lane over
+                                r0[m][v] += __shfl_xor_sync(0xffffffffu, r0[m][v], 1);
+                                r1[m][v] += __shfl_xor_sync(0xffffffffu, r1[m][v], 1);
+                            }
+#pragma unroll
+                        for (int m = 0; m < 2; ++m) {
+                            if ((t & 1) == 0 && 2 * m + (t >> 1) < np) {
+                                float* arow = acc + (size_t)tokq[m] * H + o0 + g;
+                                float cur0[DB], cur1[DB];
+#pragma unroll
+                                for (int v = 0; v < DB; ++v) {
+                                    const int tl = warp + NCW * (v0b + v);
+                                    if (tl < ntile) {
+                                        cur0[v] = arow[tl * 16];
+                                        cur1[v] = arow[tl * 16 + 8];
+                                    }
+                                }
+#pragma unroll
+                                for (int v = 0; v < DB; ++v) {
+                                    const int tl = warp + NCW * (v0b + v);
+                                    if (tl < ntile) {
+                                        const float w = wqv[m] * sdv[v];
+                                        arow[tl * 16] = __fmaf_rn(w, r0[m][v], cur0[v]);
+                                        arow[tl * 16 + 8] = __fmaf_rn(w, r1[m][v], cur1[v]);
                                     }
                                 }
                             }
                         }
                     }
-                    // the in-place h writes precede the next bulk copy into this slot
-                    fence_proxy_async_smem();
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s.empty[slot]);
-                ++si;
-            }
-            if (!switched) transition();
-            // an h copy into this warp's slot may still be in flight after an early
-            // stop: wait (bounded) for every one the producer could have issued
-            if (s.abort) {
-                for (uint32_t it = 0; it < CZ_SPIN_LIMIT; ++it) {
-                    if (mbar_try_wait(&s.hfull[warp], hcnt & 1)) break;
-                    if (it > 16) __nanosleep(64);
-                    if (it > 4096) break;
-                }
-            }
-            // combine the warps' down sums in a fixed order and write the rows once
-            if (tq < 2) {
-#pragma unroll
-                for (int tt = 0; tt < MAXBT; ++tt)
-#pragma unroll
-                    for (int b = 0; b < 2; ++b)
-#pragma unroll
-                        for (int t4 = 0; t4 < 4; ++t4)
-                            s.red[((((warp * MAXBT + tt) * 16 + g + 8 * b) * 4 + t4) * 2) + tq] = bacc[tt][b][t4];
-            }
-            asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
-            if (!s.abort) {
-                for (int k = tid; k < (b_hi - b_lo) * 4; k += NCW * 32) {
-                    const int ol = k >> 2, tk = k & 3;
-                    if (tk >= T) continue;
-                    const int tt = ol >> 4, row = ol & 15;
-                    float v = 0.0f;
-                    for (int w = 0; w < NCW; ++w)
-                        for (int h2 = 0; h2 < 2; ++h2) v += s.red[((((w * MAXBT + tt) * 16 + row) * 4 + tk) * 2) + h2];
-                    const int o = b_lo + ol;
-                    if (p.residual) v = __fadd_rn(p.residual[(size_t)tk * H + o], v);
-                    p.out[(size_t)tk * H + o] = v;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s.empty[slot]);
                 }
             }
         }
     }
 
+    // ---------------- partial sums -> global, then this CTA's slice of out ----------------
+    __syncthreads();
+    {
+        float4* dst = reinterpret_cast<float4*>(p.partial + (size_t)c * T * H);
+        const float4* src = reinterpret_cast<const float4*>(acc);
+        for (int i = tid; i < (T * H) >> 2; i += NTHREADS) dst[i] = src[i];
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        red_release_add_gpu(&reg[2], 1u);
+        if (!wait_geq_bounded(&reg[2], (uint32_t)G, err)) set_error(err, s, CZ_DERR_READY_WAIT);
+    }
+    __syncthreads();
+    if (!s.abort) {
+        // CTA c owns output rows [c*RPC, (c+1)*RPC) (RPC a multiple of 4): items
+        // (t, 4 rows); thread (item, part) sums partials part, part+NP, ... in
+        // order, then the parts are added in order.
+        const int RPC = (((H + G - 1) / G) + 3) & ~3;
+        const int o_lo = c * RPC, o_hi = min(H, o_lo + RPC);
+        const int nq4 = o_hi > o_lo ? (o_hi - o_lo) >> 2 : 0;
+        const int nitem = T * nq4;
+        float4* part = reinterpret_cast<float4*>(red);  // [item][NPART]
+        const int NPART = nitem > 0 ? max(1, min(32, NTHREADS / nitem)) : 1;
+        const int it = tid / NPART, pt = tid - it * NPART;
+        if (nitem > 0 && it < nitem) {
+            const int tk = it / nq4, o = o_lo + 4 * (it - tk * nq4);
+            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int cc = pt; cc < G; cc += NPART) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(p.partial + ((size_t)cc * T + tk) * H + o));
+                sum.x += v.x;
+                sum.y += v.y;
+                sum.z += v.z;
+                sum.w += v.w;
+            }
+            part[it * NPART + pt] = sum;
+        }
+        __syncthreads();
+        if (nitem > 0 && tid < nitem) {
+            const int tk = tid / nq4, o = o_lo + 4 * (tid - tk * nq4);
+            float4 sum = part[tid * NPART];
+            for (int k = 1; k < NPART; ++k) {
+                const float4 v = part[tid * NPART + k];
+                sum.x += v.x;
+                sum.y += v.y;
+                sum.z += v.z;
+                sum.w += v.w;
+            }
+            if (p.residual) {
+                const float4 r = *reinterpret_cast<const float4*>(p.residual + (size_t)tk * H + o);
+                sum.x = __fadd_rn(r.x, sum.x);
+                sum.y = __fadd_rn(r.y, sum.y);
+                sum.z = __fadd_rn(r.z, sum.z);
+                sum.w = __fadd_rn(r.w, sum.w);
+            }
+            *reinterpret_cast<float4*>(p.out + (size_t)tk * H + o) = sum;
+        }
+    }
+
     // ---------------- completion: advance the launch sequence ----------------
-finish:
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -1033,35 +973,64 @@ finish:
 
 static bool g_attr_set = false;
 
-size_t decode_smem_bytes() { return sizeof(DecodeSmem) + 1024; }
+size_t decode_smem_bytes(int T, int H, int x_bf16) { return carve(T, H, x_bf16).total + 1024; }
 
 int decode_max_tokens(int H, int E, int K, int I, int SI, int x_bf16, int num_sms) {
     if (K < 1 || K > MAXK || E < K || E > MAXE || H % 16 || I % 16 || SI % 16 || H < 16 || I < 16) return 0;
-    const int rows_b = (H + num_sms - 1) / num_sms;  // output rows per CTA
-    if (rows_b > 16 * MAXBT) return 0;
-    if (2 * (H + WPAD) > STAGE_BYTES) return 0;  // >= 1 gate + 1 up row per stage
-    // a down stage: a 16-row tile + the h rows of 4 pairs
-    if (16 * (I + WPAD) + 4 * (4 * I + HPAD) > STAGE_BYTES || 16 * (SI + WPAD) + 4 * (4 * SI + HPAD) > STAGE_BYTES)
-        return 0;
+    if (num_sms > kMaxGrid) return 0;
+    if ((size_t)cz_nbp(H) * 4 > (size_t)SC_BYTES) return 0;  // gate/up scales of a row block
+    const int IM = I > SI ? I : SI;
+    if ((size_t)((OS + 127) / 128) * cz_nbp(IM) * 4 > (size_t)SC_BYTES) return 0;  // down scales of a stage
     const int max_rows = (E + (SI ? 1 : 0) + num_sms - 1) / num_sms;  // router rows staged per CTA
+    const int IM16 = (I > SI ? I : SI) / CR;  // chunks of the largest group
     int t = MAXT;
     while (t > 0) {
-        const size_t ring = (size_t)max_rows * H * 4 + (size_t)t * H * (x_bf16 ? 2 : 4) + (size_t)H * 4;
+        const int worst_chunks = (t * K + (SI ? t : 0)) * IM16;  // every pair its own group
+        if ((worst_chunks + num_sms - 1) / num_sms > MAXCH) {
+            --t;
+            continue;
+        }
+        const size_t stage_r = (size_t)max_rows * H * 4 + (size_t)t * H * (x_bf16 ? 2 : 4) + (size_t)H * 4;
         const size_t lg = (size_t)t * logit_stride(E) * 4;
-        const size_t xq = (size_t)t * (H * 4 + 32);
-        if (ring <= (size_t)RING_BYTES && lg <= (size_t)RING_BYTES && xq <= (size_t)XH_BYTES) break;
+        if (stage_r <= (size_t)RING_BYTES && lg <= (size_t)RING_BYTES && decode_smem_bytes(t, H, x_bf16) <= SMEM_LIMIT)
+            break;
         --t;
     }
     return t;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+bool make_down_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64_t cols) {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !f)
+            return false;
+        fn = reinterpret_cast<EncodeTiledFn>(f);
+    }
+    if (cols % 16 || rows == 0 || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols};
+    const cuuint32_t box[2] = {16, (cuuint32_t)BOX_ROWS};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int decode_launch(const DecodeParams& prm, int num_sms, cudaStream_t stream) {
     const int tmax = decode_max_tokens(prm.H, prm.E, prm.K, prm.I, prm.SI, prm.x_bf16, num_sms);
     if (prm.T < 1 || prm.T > tmax) return CZ_ESHAPE;
     if (prm.rms_w && prm.x_bf16) return CZ_EARGS;
-    const size_t smem = decode_smem_bytes();
     if (!g_attr_set) {
-        if (cudaFuncSetAttribute(moe_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        if (cudaFuncSetAttribute(moe_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT) !=
             cudaSuccess)
             return CZ_ELAUNCH;
         g_attr_set = true;
@@ -1069,7 +1038,7 @@ int decode_launch(const DecodeParams& prm, int num_sms, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);
     cfg.blockDim = dim3(NTHREADS);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = decode_smem_bytes(prm.T, prm.H, prm.x_bf16);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;

@@ -143,11 +143,11 @@ int colizig_cuda_moe_check(void* stream);
  * an engine that has already handed all of HBM to its own pool or to
  * colizig_cuda_set_vram_budget, or a decode loop where a cudaMalloc/cudaFree
  * (which synchronises the device) would stall every stream.  The scratch lives
- * in one static device array of 566,272 bytes inside the library, so no call
- * allocates.  Limits: inter and shared_inter <= 2048, experts <= 512,
- * topk <= 16 (the same 4-token launches as colizig_cuda_moe_forward; larger T
- * runs as several launches); a layer beyond them returns -8 before anything
- * is launched.  The FIRST call on a device does set-up (it looks up the
+ * in one static device array of 10,494,976 bytes inside the library, so no
+ * call allocates.  Limits: hidden <= 4096, experts <= 512, topk <= 16, a
+ * device of at most 160 SMs (the same launches of up to 4 tokens as
+ * colizig_cuda_moe_forward; larger T runs as several launches); a layer beyond
+ * them returns -8 before anything is launched.  The FIRST call on a device does set-up (it looks up the
  * scratch address and configures the kernel), so make it before any stream
  * capture.  The scratch is shared: calls whose executions overlap (two
  * streams, two threads) race on it and give wrong results; serialise them.

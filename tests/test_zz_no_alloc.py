@@ -71,7 +71,7 @@ def test_noalloc_matches_forward_two_calls_in_a_row(c2_layer, T, dtype):
 def test_noalloc_rejects_layer_beyond_static_scratch():
     torch.cuda.init()
     cz.gpu.init()
-    d = moe.Dims(hidden=256, experts=4, topk=2, inter=2064, shared_inter=0, norm_topk=True)
+    d = moe.Dims(hidden=4112, experts=4, topk=2, inter=16, shared_inter=0, norm_topk=True)
     layer = moe.Layer.from_weights(LAYER_BIG, d, synth.make_layer(d, seed=3, device="cuda"))
     try:
         x = synth.make_tokens(1, d.hidden, seed=5, device="cuda", dtype=torch.float32)
