@@ -16,8 +16,11 @@ between timed iterations.
 value = tokens/s over all ranks, device-timed (CUDA events on the launch
 stream, max over ranks), inputs resident in HBM.  e2e = the same metric through
 the C ABI with host buffers (pinned H2D of the tokens and D2H of the outputs
-inside the timed region).  --gpus N > 1 runs one process per GPU (torchrun), each
-rank an independent replica of the workload (weak scaling).
+inside the timed region).  --gpus N > 1 runs one process per GPU (torchrun) as
+expert parallelism: every layer's experts are partitioned over the GPUs, the
+router runs replicated, and the library sums the GPUs' outputs with one NCCL
+all-reduce per layer call; each GPU contributes --tokens tokens to the step's
+batch (N x --tokens tokens per step, weak scaling).
 
 --impl reference times the reference path's CPU implementation (the oracle's C
 restatement of the Zig AVX2 path, all host threads) on the same config.
@@ -188,12 +191,14 @@ def reference_arm(args):
 
 
 def config_block(args, d):
-    return {"workload": f"{args.config} MoE layer decode, {args.tokens} token(s)/step (BASELINE config 2)",
+    g = args.tokens * args.gpus
+    return {"workload": f"{args.config} MoE layer decode, {g} token(s)/step (BASELINE config 2)",
             "hidden": d.hidden, "experts": d.experts, "topk": d.topk, "moe_intermediate": d.inter,
-            "shared_intermediate": d.shared_inter, "tokens_per_step": args.tokens,
-            "global_batch": args.tokens * args.gpus, "layers_cycled": args.layers,
+            "shared_intermediate": d.shared_inter, "tokens_per_step": g, "tokens_per_gpu": args.tokens,
+            "global_batch": g, "layers_cycled": args.layers,
             "l2": "inputs larger than L2: steps cycle through distinct layers; L2 flushed once before the timed replay",
-            "parallelism": f"replicas x{args.gpus}" if args.gpus > 1 else "single GPU"}
+            "parallelism": (f"ep{args.gpus}: experts partitioned over the GPUs, router replicated, NCCL all-reduce "
+                            "of the layer output") if args.gpus > 1 else "single GPU"}
 
 
 def main():
@@ -230,14 +235,20 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
     cz.gpu.init(local)
+    if world > 1:
+        # expert parallelism: rank r holds experts [r*E/W, (r+1)*E/W) of every layer; the
+        # library sums the ranks' outputs with one NCCL all-reduce per layer call
+        from colizig_b200 import ep
+
+        ep.init()
     d = synth.CONFIGS[args.config]
-    T = args.tokens
+    T = args.tokens * world  # tokens per step over the whole job (each rank contributes --tokens)
     dev = torch.device("cuda", local)
 
     layers, host_layers = [], []
     for l in range(args.layers):
-        w = synth.make_layer(d, seed=1000 * rank + l, device=dev)
-        layers.append(moe.Layer.from_weights(l, d, w))
+        w = synth.make_layer(d, seed=l, device=dev)  # the same layer on every rank
+        layers.append(moe.Layer.from_weights(l, d, w, ep=world > 1))
         if rank == 0 and world == 1 and l < args.cpu_layers and not args.no_cpu:
             host_layers.append(synth.to_numpy_layer(w))
         del w
@@ -300,13 +311,14 @@ def main():
         tt = torch.tensor([elapsed_ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         elapsed_ms = float(tt.item())
-    value = world * args.steps * T / (elapsed_ms / 1e3)
+    value = args.steps * T / (elapsed_ms / 1e3)
     del graph
 
     # realised distinct experts per step -> algorithmic bytes
     ids = idx[args.warmup:].cpu().numpy()
     U = np.array([len(np.unique(ids[k])) for k in range(args.steps)], np.float64)
-    bytes_per = np.array([algorithmic_bytes(d, T, u) for u in U])
+    # whole-job algorithmic bytes (the router is read on every rank), per GPU on average
+    bytes_per = np.array([algorithmic_bytes(d, T, u) + (world - 1) * d.experts * d.hidden * 4 for u in U]) / world
     hbm_peak, tf_peak, peak_kind = load_peaks()
     achieved_gbs = float(bytes_per.sum() / (np.sum(kernel_ms) / 1e3) / 1e9)
 
@@ -335,7 +347,7 @@ def main():
         tt = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_s = float(tt.item())
-    e2e = {"value": world * args.steps * T / e2e_s, "unit": "tokens/s",
+    e2e = {"value": args.steps * T / e2e_s, "unit": "tokens/s",
            "h2d_bytes_per_step": T * d.hidden * 2, "d2h_bytes_per_step": T * d.hidden * 4 + T * d.topk * 8,
            "ms_per_step": e2e_s / args.steps * 1e3}
 
@@ -368,6 +380,10 @@ def main():
     for lay in layers:
         lay.unregister()
     if world > 1:
+        from colizig_b200 import ep
+
+        torch.cuda.synchronize()
+        ep.shutdown()
         dist.destroy_process_group()
 
 

@@ -10,12 +10,14 @@ the reference's host-side interfaces:
   fp8   src/ops/fp8.zig       nblk / matmul_fp8_keyed / matmul_fp8
   moe   src/qwen38/moe.zig    Dims / Layer / forward, plus stack_forward
                               (src/qwen3moe/model.zig:227-232)
+  ep    expert parallelism over the GPUs of one node (partition of moe.zig's
+        experts; NCCL all-reduce inside the library)
 
 There is no CPU fallback: if the library is missing or a call fails, an
 exception is raised.
 """
 
-from . import _abi, fp8, gpu, moe  # noqa: F401
+from . import _abi, ep, fp8, gpu, moe  # noqa: F401
 from ._abi import ColizigError  # noqa: F401
 
-__all__ = ["gpu", "fp8", "moe", "ColizigError"]
+__all__ = ["gpu", "fp8", "moe", "ep", "ColizigError"]

@@ -32,9 +32,13 @@ MOE_SYMBOLS = (
     "colizig_cuda_moe_check",
     "colizig_cuda_debug_expf",
     "colizig_cuda_moe_forward_noalloc",
+    "colizig_cuda_ep_unique_id",
+    "colizig_cuda_ep_init",
+    "colizig_cuda_ep_shutdown",
 )
 
 COLIZIG_PTR_DEVICE = 1
+COLIZIG_EP = 2
 COLIZIG_X_F32 = 0
 COLIZIG_X_BF16 = 1
 
@@ -125,6 +129,12 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         L.colizig_cuda_moe_check.argtypes = [vp]
         L.colizig_cuda_moe_forward_noalloc.restype = i32
         L.colizig_cuda_moe_forward_noalloc.argtypes = [u32, vp, i32, i32, vp, vp, vp, vp, vp]
+        L.colizig_cuda_ep_unique_id.restype = i32
+        L.colizig_cuda_ep_unique_id.argtypes = [vp]
+        L.colizig_cuda_ep_init.restype = i32
+        L.colizig_cuda_ep_init.argtypes = [i32, i32, vp]
+        L.colizig_cuda_ep_shutdown.restype = i32
+        L.colizig_cuda_ep_shutdown.argtypes = []
         L.colizig_cuda_debug_expf.restype = i32
         L.colizig_cuda_debug_expf.argtypes = [vp, vp, ctypes.c_size_t]
         _lib = L

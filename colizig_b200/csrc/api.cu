@@ -10,6 +10,8 @@
 // (colizig_cuda.cu:22-29): the CUDA runtime may turn on flush-to-zero on the
 // calling thread, which would silently change the caller's CPU float math.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 #include <stdint.h>
 #include <stdio.h>
 #include <string.h>
@@ -85,7 +87,10 @@ struct MoeLayer {
     uint8_t *sh_gate_w = nullptr, *sh_up_w = nullptr, *sh_down_w = nullptr;
     float *sh_gate_s = nullptr, *sh_up_s = nullptr, *sh_down_s = nullptr;
     float* sh_gate = nullptr;
-    CUtensorMap down_map{};     // TMA view of down_w: u8 [E*H][I]
+    int e_lo = 0, e_hi = 0;     // routed experts held here (all of them without expert parallelism)
+    int shared_here = 0;        // the shared expert's weights are held (and computed) here
+    bool ep = false;            // outputs are summed over the expert-parallel group after each forward
+    CUtensorMap down_map{};     // TMA view of down_w: u8 [(e_hi-e_lo)*H][I]
     CUtensorMap sh_down_map{};  // TMA view of sh_down_w: u8 [H][SI]
 };
 
@@ -106,7 +111,36 @@ struct Ctx {
     std::map<uint32_t, MoeLayer> layers;
     DevBuf logits, partial, io_x, io_out, io_idx, io_gates, ones;
     uint32_t* sync = nullptr;
+    // expert parallelism (one process per GPU)
+    bool ep_on = false;
+    int ep_rank = 0, ep_world = 1;
+    ncclComm_t ep_comm = nullptr;
 };
+
+// NCCL is resolved at run time (dlopen of libnccl.so.2): the library loads without
+// it, and a process that already loaded NCCL (torch does) shares that copy.
+struct NcclApi {
+    void* h = nullptr;
+    ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+    bool load() {
+        if (h) return true;
+        void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!lib) lib = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!lib) return false;
+        getUniqueId = reinterpret_cast<decltype(getUniqueId)>(dlsym(lib, "ncclGetUniqueId"));
+        commInitRank = reinterpret_cast<decltype(commInitRank)>(dlsym(lib, "ncclCommInitRank"));
+        allReduce = reinterpret_cast<decltype(allReduce)>(dlsym(lib, "ncclAllReduce"));
+        commDestroy = reinterpret_cast<decltype(commDestroy)>(dlsym(lib, "ncclCommDestroy"));
+        if (!getUniqueId || !commInitRank || !allReduce || !commDestroy) return false;
+        h = lib;
+        return true;
+    }
+};
+NcclApi nccl;
 
 Ctx g;
 std::mutex g_mu;
@@ -145,6 +179,11 @@ void shutdown_locked() {
     if (!g.inited) return;
     cudaSetDevice(g.dev);
     cudaDeviceSynchronize();
+    if (g.ep_comm) nccl.commDestroy(g.ep_comm);
+    g.ep_comm = nullptr;
+    g.ep_on = false;
+    g.ep_rank = 0;
+    g.ep_world = 1;
     for (auto& kv : g.keyed) {
         cudaFree(kv.second.w);
         cudaFree(kv.second.s);
@@ -249,8 +288,11 @@ cz::DecodeParams make_params(const MoeLayer& L) {
     p.I = (int)L.d.inter;
     p.SI = (int)L.d.shared_inter;
     p.norm_topk = (int)L.d.norm_topk;
+    p.e_lo = L.e_lo;
+    p.e_hi = L.e_hi;
+    p.shared_here = L.shared_here;
     p.down_map = L.down_map;
-    p.sh_down_map = L.d.shared_inter ? L.sh_down_map : L.down_map;
+    p.sh_down_map = L.shared_here ? L.sh_down_map : L.down_map;
     p.logits = g.logits.as<float>();
     p.partial = g.partial.as<float>();
     p.sync = g.sync;
@@ -275,12 +317,18 @@ int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uin
         p.T = n;
         p.rms_w = rms_w;
         p.eps = eps;
-        p.residual = residual ? residual + (size_t)t0 * L.d.hidden : nullptr;
+        // under expert parallelism the residual is added on rank 0 only (the all-reduce sums the ranks)
+        p.residual = residual && (!L.ep || g.ep_rank == 0) ? residual + (size_t)t0 * L.d.hidden : nullptr;
         p.out = out + (size_t)t0 * L.d.hidden;
         p.topk_idx = idx ? idx + (size_t)t0 * L.d.topk : nullptr;
         p.topk_gates = gates ? gates + (size_t)t0 * L.d.topk : nullptr;
         rc = cz::decode_launch(p, g.num_sms, st);
         if (rc) return rc;
+    }
+    if (L.ep && g.ep_world > 1) {
+        if (!g.ep_comm) return CZ_ENCCL;
+        if (nccl.allReduce(out, out, (size_t)T * L.d.hidden, ncclFloat, ncclSum, g.ep_comm, st) != ncclSuccess)
+            return CZ_ENCCL;
     }
     return CZ_OK;
 }
@@ -440,9 +488,18 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
         d.shared_inter > 32768)
         return CZ_ESHAPE;
     if (d.shared_inter && (!shared || !shared_gate)) return CZ_EARGS;
+    const bool ep = (flags & COLIZIG_EP) != 0;
+    if (ep && (!g.ep_on || (uint32_t)g.ep_world > d.experts)) return CZ_EARGS;
     cudaSetDevice(g.dev);
     const cudaMemcpyKind kind = (flags & COLIZIG_PTR_DEVICE) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
-    const size_t H = d.hidden, E = d.experts, I = d.inter, SI = d.shared_inter;
+    const size_t H = d.hidden, I = d.inter, SI = d.shared_inter;
+    // expert parallelism: rank r holds the contiguous experts [r*E/W, (r+1)*E/W); rank 0
+    // also holds the shared expert.  The router (and the shared gate vector) are replicated.
+    const int e_lo = ep ? (int)((uint64_t)g.ep_rank * d.experts / g.ep_world) : 0;
+    const int e_hi = ep ? (int)((uint64_t)(g.ep_rank + 1) * d.experts / g.ep_world) : (int)d.experts;
+    const int shared_here = SI && (!ep || g.ep_rank == 0);
+    const size_t ER = d.experts;          // router rows
+    const size_t E = (size_t)(e_hi - e_lo);  // experts held here
     const size_t wexp = I * H;
     const size_t nbHp = (size_t)cz::cz_nbp((int)H), nbIp = (size_t)cz::cz_nbp((int)I), nbSIp = (size_t)cz::cz_nbp((int)SI);
     const size_t sexp = nb(I) * nbHp * 4, dexp = nb(H) * nbIp * 4;  // padded scale tables
@@ -452,21 +509,25 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
         off = align256(off + bytes);
         return o;
     };
-    const size_t o_router = take(E * H * 4), o_gw = take(E * wexp), o_uw = take(E * wexp), o_dw = take(E * wexp);
+    const size_t o_router = take(ER * H * 4), o_gw = take(E * wexp), o_uw = take(E * wexp), o_dw = take(E * wexp);
     const size_t o_gs = take(E * sexp), o_us = take(E * sexp), o_ds = take(E * dexp);
     size_t o_shgw = 0, o_shuw = 0, o_shdw = 0, o_shgs = 0, o_shus = 0, o_shds = 0, o_shg = 0;
-    if (SI) {
+    if (shared_here) {
         o_shgw = take(SI * H);
         o_shuw = take(SI * H);
         o_shdw = take(SI * H);
         o_shgs = take(nb(SI) * nbHp * 4);
         o_shus = take(nb(SI) * nbHp * 4);
         o_shds = take(nb(H) * nbSIp * 4);
-        o_shg = take(H * 4);
     }
+    if (SI) o_shg = take(H * 4);
     MoeLayer L;
     L.d = d;
     L.bytes = off;
+    L.e_lo = e_lo;
+    L.e_hi = e_hi;
+    L.shared_here = shared_here;
+    L.ep = ep;
     if (cudaMalloc(&L.mem, off) != cudaSuccess) return CZ_EALLOC;
     uint8_t* base = reinterpret_cast<uint8_t*>(L.mem);
     L.router = reinterpret_cast<float*>(base + o_router);
@@ -477,8 +538,9 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
     L.up_s = reinterpret_cast<float*>(base + o_us);
     L.down_s = reinterpret_cast<float*>(base + o_ds);
     int rc = CZ_OK;
-    if (cudaMemcpyAsync(L.router, router, E * H * 4, kind, g.stream) != cudaSuccess) rc = CZ_EH2D;
+    if (cudaMemcpyAsync(L.router, router, ER * H * 4, kind, g.stream) != cudaSuccess) rc = CZ_EH2D;
     const int Ei = (int)E;
+    experts += e_lo;
     if (!rc) rc = gather_copy(L.gate_w, experts, Ei, wexp, &colizig_moe_expert::gate_w, kind);
     if (!rc) rc = gather_copy(L.up_w, experts, Ei, wexp, &colizig_moe_expert::up_w, kind);
     if (!rc) rc = gather_copy(L.down_w, experts, Ei, wexp, &colizig_moe_expert::down_w, kind);
@@ -492,13 +554,16 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
         rc = gather_copy_2d(reinterpret_cast<uint8_t*>(L.down_s), nbIp * 4, experts, Ei, nb(H), nb(I) * 4,
                             &colizig_moe_expert::down_s, kind);
     if (!rc && SI) {
+        L.sh_gate = reinterpret_cast<float*>(base + o_shg);
+        if (cudaMemcpyAsync(L.sh_gate, shared_gate, H * 4, kind, g.stream) != cudaSuccess) rc = CZ_EH2D;
+    }
+    if (!rc && shared_here) {
         L.sh_gate_w = base + o_shgw;
         L.sh_up_w = base + o_shuw;
         L.sh_down_w = base + o_shdw;
         L.sh_gate_s = reinterpret_cast<float*>(base + o_shgs);
         L.sh_up_s = reinterpret_cast<float*>(base + o_shus);
         L.sh_down_s = reinterpret_cast<float*>(base + o_shds);
-        L.sh_gate = reinterpret_cast<float*>(base + o_shg);
         if (!shared->gate_w || !shared->up_w || !shared->down_w || !shared->gate_s || !shared->up_s ||
             !shared->down_s)
             rc = CZ_EARGS;
@@ -511,15 +576,14 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
                   {L.sh_down_w, shared->down_w, SI * H, 1, SI * H},
                   {L.sh_gate_s, shared->gate_s, nbHp * 4, nb(SI), nb(H) * 4},
                   {L.sh_up_s, shared->up_s, nbHp * 4, nb(SI), nb(H) * 4},
-                  {L.sh_down_s, shared->down_s, nbSIp * 4, nb(H), nb(SI) * 4},
-                  {L.sh_gate, shared_gate, H * 4, 1, H * 4}};
+                  {L.sh_down_s, shared->down_s, nbSIp * 4, nb(H), nb(SI) * 4}};
         for (const auto& c : cp)
             if (!rc && cudaMemcpy2DAsync(c.dst, c.dpitch, c.src, c.row_bytes, c.row_bytes, c.rows, kind, g.stream) !=
                            cudaSuccess)
                 rc = CZ_EH2D;
     }
-    if (!rc && !cz::make_down_map(&L.down_map, L.down_w, E * H, I)) rc = CZ_ELAUNCH;
-    if (!rc && SI && !cz::make_down_map(&L.sh_down_map, L.sh_down_w, H, SI)) rc = CZ_ELAUNCH;
+    if (!rc && E && !cz::make_down_map(&L.down_map, L.down_w, E * H, I)) rc = CZ_ELAUNCH;
+    if (!rc && shared_here && !cz::make_down_map(&L.sh_down_map, L.sh_down_w, H, SI)) rc = CZ_ELAUNCH;
     if (!rc && cudaStreamSynchronize(g.stream) != cudaSuccess) rc = CZ_EH2D;
     if (rc) {
         cudaStreamSynchronize(g.stream);
@@ -654,6 +718,55 @@ CZ_EXPORT int colizig_cuda_debug_expf(const float* x_dev, float* y_dev, size_t n
     return cudaStreamSynchronize(g.stream) == cudaSuccess ? CZ_OK : CZ_ELAUNCH;
 }
 
+// ---- expert parallelism --------------------------------------------------
+
+CZ_EXPORT int colizig_cuda_ep_unique_id(void* id_out) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!id_out) return CZ_EARGS;
+    if (!nccl.load()) return CZ_ENCCL;
+    ncclUniqueId id;
+    if (nccl.getUniqueId(&id) != ncclSuccess) return CZ_ENCCL;
+    memcpy(id_out, &id, sizeof id);
+    return CZ_OK;
+}
+
+CZ_EXPORT int colizig_cuda_ep_init(int rank, int world, const void* id) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited || world < 1 || rank < 0 || rank >= world || (world > 1 && !id)) return CZ_EARGS;
+    if (g.ep_on) return CZ_EARGS;  // once per process (until colizig_cuda_ep_shutdown)
+    cudaSetDevice(g.dev);
+    if (world > 1) {
+        if (!nccl.load()) return CZ_ENCCL;
+        ncclUniqueId uid;
+        memcpy(&uid, id, sizeof uid);
+        ncclComm_t comm = nullptr;
+        if (nccl.commInitRank(&comm, world, uid, rank) != ncclSuccess) return CZ_ENCCL;
+        g.ep_comm = comm;
+    }
+    g.ep_rank = rank;
+    g.ep_world = world;
+    g.ep_on = true;
+    return CZ_OK;
+}
+
+CZ_EXPORT int colizig_cuda_ep_shutdown(void) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return CZ_OK;
+    cudaSetDevice(g.dev);
+    cudaDeviceSynchronize();
+    for (auto& kv : g.layers)
+        if (kv.second.ep) return CZ_EARGS;  // unregister the expert-parallel layers first
+    if (g.ep_comm) nccl.commDestroy(g.ep_comm);
+    g.ep_comm = nullptr;
+    g.ep_on = false;
+    g.ep_rank = 0;
+    g.ep_world = 1;
+    return CZ_OK;
+}
+
 // ---- colizig_cuda_moe_forward_noalloc -------------------------------------
 // The device-pointer forward with its scratch in one static device array
 // instead of cudaMalloc'd buffers: [sync words][router logits][per-CTA partial
@@ -703,6 +816,7 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
     auto it = g.layers.find(layer);
     if (it == g.layers.end()) return CZ_ENOLAYER;
     const MoeLayer& L = it->second;
+    if (L.ep) return CZ_EARGS;  // its all-reduce is not part of this entry point
     if (L.d.hidden > (uint32_t)kNoAllocMaxHidden || L.d.experts > (uint32_t)cz::kMaxExperts ||
         L.d.topk > (uint32_t)cz::kMaxTopk || g.num_sms > cz::kMaxGrid)
         return CZ_ESHAPE;

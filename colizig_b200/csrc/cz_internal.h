@@ -53,6 +53,8 @@ struct alignas(64) DecodeParams {
     const float* sh_down_s;
     const float* sh_gate;    // [H]
     int H, E, K, I, SI, norm_topk;
+    int e_lo, e_hi;          // routed experts held (and computed) here: [e_lo, e_hi); stacked from e_lo
+    int shared_here;         // the shared expert is computed here
     float* logits;           // scratch [T, logit_stride(E)]
     float* partial;          // scratch [grid][T][H]: each CTA's share of out
     uint32_t* sync;          // kSyncWords words, zeroed once at allocation

@@ -19,7 +19,9 @@
 //      the phase.
 //   K  top-k.  Every CTA bulk-copies the logits, computes softmax/top-k for all
 //      tokens (identically) and groups the (token, slot) pairs by expert
-//      (ascending id, shared expert last).
+//      (ascending id, shared expert last).  Under expert parallelism a GPU
+//      holds experts [e_lo, e_hi) only; the other groups get no chunks here and
+//      the GPUs' outputs are summed by one all-reduce after the launch.
 //   C  chunks.  Each group's intermediate rows are cut into chunks of 16; the
 //      flattened chunk list is split evenly over the CTAs (split-K: a chunk's
 //      gate, up AND down work stays on one SM, so h never leaves it).  A chunk
@@ -94,7 +96,9 @@ struct __align__(16) DecodeMisc {
     uint32_t xmax[MAXT];  // max |x_t| (f32 bits)
     int xexp[MAXT];       // s per token (terms hold x_t * 2^s)
     float xscale[MAXT];   // 2^-s per token
-    float wq[MAXCH][4];   // per chunk and pair: gate * 2^-s_h
+    float sdcol[64];      // down scales of the current chunk's column block, one per 128 output rows
+    float hmax[MAXT][64]; // max over chunks of |gate * h * down scale| per (token, 128-row block)
+    int hexp[MAXT][64];   // its power-of-two prescale
     int pe[MAXP];         // expert of pair p = t*K + z (shared: p = T*K + t -> E)
     float pg[MAXP];       // gate of pair p
     int order[MAXP];      // pairs sorted by (expert, pair)
@@ -104,10 +108,10 @@ struct __align__(16) DecodeMisc {
     int g_chunk0[MAXG + 1];
 };
 
-// Shared-memory map of one launch: [ring][x terms][acc][red][h terms][misc].
+// Shared-memory map of one launch: [ring][x terms][red][h of every chunk][misc].
 struct Carve {
     int JX, CS;  // E4M3 terms per token; byte stride of one term column
-    uint32_t xterm, acc, red, hterm, misc, total;
+    uint32_t xterm, red, hterm, misc, total;
 };
 
 __host__ __device__ inline Carve carve(int T, int H, int x_bf16) {
@@ -117,8 +121,6 @@ __host__ __device__ inline Carve carve(int T, int H, int x_bf16) {
     uint32_t off = RING_BYTES;
     c.xterm = off;
     off += ((uint32_t)(T * c.JX * c.CS) + 127u) & ~127u;
-    c.acc = off;
-    off += ((uint32_t)(T * H * 4) + 127u) & ~127u;
     c.red = off;
     off += NCW * 2 * 16 * 16 * 4;
     c.hterm = off;
@@ -157,6 +159,7 @@ __device__ __forceinline__ GroupW group_w(const DecodeParams& p, int e) {
         g.dmap = &p.sh_down_map;
     } else {
         g.inter = p.I;
+        e -= p.e_lo;  // experts are stacked from the first one held here
         const size_t wsz = (size_t)p.I * p.H;
         g.gw = p.gate_w + (size_t)e * wsz;
         g.uw = p.up_w + (size_t)e * wsz;
@@ -381,7 +384,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     DecodeMisc& s = *reinterpret_cast<DecodeMisc*>(sb + cv.misc);
     uint8_t* const ring = sb;
     uint8_t* const xterm = sb + cv.xterm;
-    float* const acc = reinterpret_cast<float*>(sb + cv.acc);
     float* const red = reinterpret_cast<float*>(sb + cv.red);
     uint8_t* const hterm = sb + cv.hterm;
     uint32_t* const err = p.sync + 1;
@@ -400,7 +402,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         fence_mbarrier_init();
     }
     if (tid < MAXT) s.xmax[tid] = 0u;
-    for (int i = tid; i < T * H; i += NTHREADS) acc[i] = 0.0f;
+    for (int i = tid; i < MAXT * 64; i += NTHREADS) (&s.hmax[0][0])[i] = 0.0f;
     __syncthreads();
 
     // ---------------- phase R: router logits ----------------
@@ -560,8 +562,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
             if (lane == 0) {
                 int nc = 0;
                 for (int u = 0; u < base; ++u) {
+                    // groups of experts held elsewhere (expert parallelism) get no chunks
+                    const int eu = s.g_expert[u];
+                    const bool here = eu == E ? p.shared_here != 0 : (eu >= p.e_lo && eu < p.e_hi);
                     s.g_chunk0[u] = nc;
-                    nc += (s.g_expert[u] == E ? SI : Ir) / CR;
+                    if (here) nc += (eu == E ? SI : Ir) / CR;
                 }
                 s.g_chunk0[base] = nc;
                 s.U = base;
@@ -580,9 +585,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         const int NC = s.NC;
         const int ch_lo = (int)((long long)c * NC / G), ch_hi = (int)((long long)(c + 1) * NC / G);
         const int nks = (H + KS - 1) / KS;     // gate (and up) stages per chunk
-        const int nos = (H + OS - 1) / OS;     // down stages per chunk
-        const int spc = 2 * nks + nos;         // stages per chunk
         const int nbpH = cz_nbp(H);
+        // down: tiles per warp (each warp's accumulators live in registers across
+        // all chunks) and the output rows of one slab
+        const int TPW = (T * JH <= 8) ? 16 : 8;
+        const int nmD = (T * JH + 7) >> 3;
+        const int OSr = TPW * 16 * NCW;
 
         if (warp == NCW) {
             // ---------------- producer (one thread) ----------------
@@ -590,53 +598,66 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 fence_proxy_async_smem();  // generic reads of the ring (logits) precede the async writes
                 const uint64_t pol = l2_evict_first_policy();
                 int si = 0;
-                // stage order: gate/up slabs of every chunk, then the down stages of every chunk
-                for (int pass = 0; pass < 2; ++pass) {
+                // wait until slot si % NSLOT is free again (bounded); false = stop
+                auto acquire_slot = [&](int slot, int round) -> bool {
+                    if (round == 0) return true;
+                    bool ok = false;
+                    for (uint32_t it = 0; it < CZ_SPIN_LIMIT && !ok && !s.abort; ++it) {
+                        ok = mbar_try_wait(&s.empty[slot], (round - 1) & 1);
+                        if (!ok && it > 64) __nanosleep(64);
+                    }
+                    if (!ok && !s.abort) set_error(err, s, CZ_DERR_EMPTY_WAIT);
+                    return ok;
+                };
+                // pass 1: gate/up slabs of every chunk
+                {
                     int u = 0;
                     for (int ch = ch_lo; ch < ch_hi && !s.abort; ++ch) {
                         while (s.g_chunk0[u + 1] <= ch) ++u;
                         const GroupW gw = group_w(p, s.g_expert[u]);
                         const int r0 = (ch - s.g_chunk0[u]) * CR;
                         const int nbpI = cz_nbp(gw.inter);
-                        const int st_lo = pass == 0 ? 0 : 2 * nks, st_hi = pass == 0 ? 2 * nks : spc;
-                        for (int st = st_lo; st < st_hi && !s.abort; ++st, ++si) {
-                            const int slot = si % NSLOT, round = si / NSLOT;
-                            if (round > 0) {
-                                bool ok = false;
-                                for (uint32_t it = 0; it < CZ_SPIN_LIMIT && !ok && !s.abort; ++it) {
-                                    ok = mbar_try_wait(&s.empty[slot], (round - 1) & 1);
-                                    if (!ok && it > 64) __nanosleep(64);
-                                }
-                                if (!ok) {
-                                    if (!s.abort) set_error(err, s, CZ_DERR_EMPTY_WAIT);
-                                    break;
-                                }
-                            }
+                        for (int st = 0; st < 2 * nks && !s.abort; ++st, ++si) {
+                            const int slot = si % NSLOT;
+                            if (!acquire_slot(slot, si / NSLOT)) break;
                             uint8_t* dst = ring + (size_t)slot * SLOT_BYTES;
                             float* sdst = reinterpret_cast<float*>(dst + GU_BYTES);
-                            if (st < 2 * nks) {
-                                // slab st/2: gate (st even) or up (st odd) rows [r0, r0+16), columns [k0, k0+L)
-                                const bool up = st & 1;
-                                const int k0 = (st >> 1) * KS, L = min(KS, H - k0);
-                                const uint8_t* src = (up ? gw.uw : gw.gw) + (size_t)r0 * H + k0;
-                                const float* ssrc = (up ? gw.us : gw.gs) + (size_t)(r0 >> 7) * nbpH;
-                                mbar_arrive_expect_tx(&s.full[slot], (uint32_t)(CR * L + nbpH * 4));
-                                for (int r = 0; r < CR; ++r)
-                                    bulk_g2s_hint(dst + (size_t)r * (KS + WPAD), src + (size_t)r * H, (uint32_t)L,
-                                                  &s.full[slot], pol);
-                                bulk_g2s(sdst, ssrc, (uint32_t)nbpH * 4u, &s.full[slot]);
-                            } else {
-                                // down columns [r0, r0+16) of output rows [o0, o0+OSl)
-                                const int o0 = (st - 2 * nks) * OS, OSl = min(OS, H - o0);
-                                const int nbox = (OSl + BOX_ROWS - 1) / BOX_ROWS;
-                                const int ob0 = o0 >> 7, nob = (OSl + 127) >> 7;
-                                mbar_arrive_expect_tx(&s.full[slot], (uint32_t)(nbox * BOX_ROWS * 16 + nob * nbpI * 4));
-                                for (int b = 0; b < nbox; ++b)
-                                    tma_box_g2s(dst + (size_t)b * BOX_ROWS * 16, gw.dmap, r0,
-                                                gw.down_row0 + o0 + b * BOX_ROWS, &s.full[slot], pol);
-                                bulk_g2s(sdst, gw.ds + (size_t)ob0 * nbpI, (uint32_t)(nob * nbpI * 4), &s.full[slot]);
-                            }
+                            // slab st/2: gate (st even) or up (st odd) rows [r0, r0+16), columns [k0, k0+L)
+                            const bool up = st & 1;
+                            const int k0 = (st >> 1) * KS, L = min(KS, H - k0);
+                            const uint8_t* src = (up ? gw.uw : gw.gw) + (size_t)r0 * H + k0;
+                            const float* ssrc = (up ? gw.us : gw.gs) + (size_t)(r0 >> 7) * nbpH;
+                            // the first up slab also carries the expert's down-scale table
+                            const uint32_t dsb = st == 1 ? (uint32_t)(cz_nblk(H) * nbpI * 4) : 0u;
+                            mbar_arrive_expect_tx(&s.full[slot], (uint32_t)(CR * L + nbpH * 4) + dsb);
+                            for (int r = 0; r < CR; ++r)
+                                bulk_g2s_hint(dst + (size_t)r * (KS + WPAD), src + (size_t)r * H, (uint32_t)L,
+                                              &s.full[slot], pol);
+                            bulk_g2s(sdst, ssrc, (uint32_t)nbpH * 4u, &s.full[slot]);
+                            if (dsb) bulk_g2s(sdst + nbpH, gw.ds, dsb, &s.full[slot]);
                         }
+                    }
+                }
+                // pass 2: for every slab of OSr output rows, the down columns of every chunk
+                for (int o0 = 0; o0 < H && !s.abort; o0 += OSr) {
+                    const int OSl = min(OSr, H - o0);
+                    const int nbox = (OSl + BOX_ROWS - 1) / BOX_ROWS;
+                    const int ob0 = o0 >> 7, nob = (OSl + 127) >> 7;
+                    int u = 0;
+                    for (int ch = ch_lo; ch < ch_hi && !s.abort; ++ch, ++si) {
+                        while (s.g_chunk0[u + 1] <= ch) ++u;
+                        const GroupW gw = group_w(p, s.g_expert[u]);
+                        const int r0 = (ch - s.g_chunk0[u]) * CR;
+                        const int nbpI = cz_nbp(gw.inter);
+                        const int slot = si % NSLOT;
+                        if (!acquire_slot(slot, si / NSLOT)) break;
+                        uint8_t* dst = ring + (size_t)slot * SLOT_BYTES;
+                        float* sdst = reinterpret_cast<float*>(dst + GU_BYTES);
+                        mbar_arrive_expect_tx(&s.full[slot], (uint32_t)(nbox * BOX_ROWS * 16 + nob * nbpI * 4));
+                        for (int b = 0; b < nbox; ++b)
+                            tma_box_g2s(dst + (size_t)b * BOX_ROWS * 16, gw.dmap, r0, gw.down_row0 + o0 + b * BOX_ROWS,
+                                        &s.full[slot], pol);
+                        bulk_g2s(sdst, gw.ds + (size_t)ob0 * nbpI, (uint32_t)(nob * nbpI * 4), &s.full[slot]);
                     }
                 }
                 // drain: no copy may land after this CTA exits (waiting on a phase
@@ -662,6 +683,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 const int ci = ch - ch_lo;
                 const int np = s.g_npairs[u];
                 const int* pairs = s.order + s.g_pair0[u];
+                const int ib = ((ch - s.g_chunk0[u]) * CR) >> 7;  // the chunk's 128-column block of down
+                const int nbpI = cz_nbp(s.g_expert[u] == E ? SI : Ir);
                 // columns of the gate/up MMAs: c = q*JX + j (pair q, term j); lane's column g of MMA m
                 const int ncolA = np * cv.JX, nmA = (ncolA + 7) >> 3;
                 const uint8_t* xcol[2];
@@ -742,6 +765,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                             accg[m][i] += ag[m][i];
                             accu[m][i] += au[m][i];
                         }
+                    if (kq == 0 && warp == 0) {  // down scales of column block ib, from the up slab
+                        const float* dtab = tu + nbpH;
+                        for (int ob = lane; ob < cz_nblk(H); ob += 32) s.sdcol[ob] = dtab[ob * nbpI + ib];
+                    }
                     __syncwarp();
                     if (lane == 0) {
                         mbar_arrive(&s.empty[slg]);
@@ -768,12 +795,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                     }
                 }
                 consumers_sync();
-                if (tid < 64) {
-                    const int q = tid >> 4, r = tid & 15;
-                    const bool valid = q < np && !s.abort;
-                    float h = 0.0f;
-                    if (valid) {
-                        const int tok = pair_token(pairs[q], T, K);
+                // hw = gate * silu(g) * u per (row r, token tk) of this chunk (0 for tokens
+                // not routed to its expert), and the running max of |hw * down scale| per
+                // (token, 128-row output block)
+                if (tid < 16 * MAXT) {
+                    const int tk = tid >> 4, r = tid & 15;
+                    int q = -1;
+                    for (int qq = 0; qq < np; ++qq)
+                        if (pair_token(pairs[qq], T, K) == tk) q = qq;
+                    float hw = 0.0f;
+                    if (q >= 0 && !s.abort) {
                         float gs = 0.0f, us = 0.0f;
                         const float* rg = red + r * 16 + q * cv.JX;
 #pragma unroll
@@ -784,51 +815,45 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                                     gs += rg[w * 512 + j];
                                     us += rg[w * 512 + 256 + j];
                                 }
-                        const float xsc = s.xscale[tok];
-                        h = silu_fast(gs * xsc) * (us * xsc);
+                        const float xsc = s.xscale[tk];
+                        hw = s.pg[pairs[q]] * (silu_fast(gs * xsc) * (us * xsc));
                     }
-                    // max |h| over the 16 rows of pair q (lanes of one half-warp)
-                    float mh = fabsf(h);
+                    reinterpret_cast<float*>(hterm)[ci * 64 + r * 4 + tk] = hw;
+                    float mh = fabsf(hw);
                     if (!(mh < 3.0e38f)) mh = 0.0f;
 #pragma unroll
                     for (int o = 8; o > 0; o >>= 1) mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
-                    const int sh = prescale_exp(mh);
-                    if (valid) {
-                        float a = scale2(h, sh), b = 0.0f;
-#pragma unroll
-                        for (int j = 0; j < JH; ++j) {
-                            const uint16_t d = e4m3_term2(a, b);
-                            hterm[ci * 256 + (q * JH + j) * 16 + r] = (uint8_t)(d & 0xff);
-                        }
-                        if (r == 0) s.wq[ci][q] = s.pg[pairs[q]] * scale2(1.0f, -sh);
-                    }
+                    if (q >= 0)
+                        for (int ob = r; ob < cz_nblk(H); ob += 16)
+                            s.hmax[tk][ob] = fmaxf(s.hmax[tk][ob], mh * fabsf(s.sdcol[ob]));
                 }
                 consumers_sync();
             }
-            // ==== pass 2: down of every chunk into the per-CTA accumulator ====
-            u = 0;
-            for (int ch = ch_lo; ch < ch_hi; ++ch) {
-                while (s.g_chunk0[u + 1] <= ch) ++u;
-                const int ci = ch - ch_lo;
-                const int inter = s.g_expert[u] == E ? SI : Ir;
-                const int r0 = (ch - s.g_chunk0[u]) * CR;
-                const int np = s.g_npairs[u];
-                const int* pairs = s.order + s.g_pair0[u];
-                const int nbpI = cz_nbp(inter);
-                // ---- down stages: rows [o0, o0+OSl), columns = (pair, term) ----
-                const int ncolD = np * JH, nmD = (ncolD + 7) >> 3;
-                uint32_t bfr[2];
-                int tokq[2];
-                float wqv[2];
+            // one power-of-two scale per (token, 128-row output block) for every chunk
+            for (int i = tid; i < MAXT * 64; i += NCW * 32) (&s.hexp[0][0])[i] = prescale_exp((&s.hmax[0][0])[i]);
+            consumers_sync();
+
+            // ==== pass 2: per slab of OSr output rows, down of every chunk ====
+            // Warp w owns tiles [w*TPW, (w+1)*TPW) of the slab; its accumulators stay in
+            // registers across the chunks (columns = (token, term) for every chunk).  The
+            // B operand of a chunk and 128-row block: the E4M3 terms of
+            // hw * down scale * 2^s(token, block).
+            for (int o0 = 0; o0 < H; o0 += OSr) {
+                const int OSl = min(OSr, H - o0);
+                const int ntile = OSl >> 4;
+                float accd[16][4];
 #pragma unroll
-                for (int m = 0; m < 2; ++m) {
-                    const int cc = 8 * m + g;
-                    bfr[m] = cc < ncolD ? *reinterpret_cast<const uint32_t*>(hterm + ci * 256 + cc * 16 + 4 * t) : 0u;
-                    const int q = 2 * m + (t >> 1);
-                    tokq[m] = q < np ? pair_token(pairs[q], T, K) : 0;
-                    wqv[m] = q < np ? s.wq[ci][q] : 0.0f;
-                }
-                for (int st = 0; st < nos; ++st, ++si) {
+                for (int i = 0; i < 16; ++i)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) accd[i][k] = 0.0f;
+                const int tw0 = warp * TPW;  // first tile of this warp in the slab
+                const int obw = (o0 >> 7) + ((tw0 * 16) >> 7);  // first 128-row block of those tiles
+                u = 0;
+                for (int ch = ch_lo; ch < ch_hi; ++ch, ++si) {
+                    while (s.g_chunk0[u + 1] <= ch) ++u;
+                    const int ci = ch - ch_lo;
+                    const int ib = ((ch - s.g_chunk0[u]) * CR) >> 7;
+                    const int nbpI = cz_nbp(s.g_expert[u] == E ? SI : Ir);
                     const int slot = si % NSLOT;
                     const bool ok = !s.abort && warp_wait(&s.full[slot], (si / NSLOT) & 1, s);
                     if (!ok) {
@@ -837,77 +862,72 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                     }
                     const uint8_t* stage = ring + (size_t)slot * SLOT_BYTES;
                     const float* stab = reinterpret_cast<const float*>(stage + GU_BYTES);
-                    const int o0 = st * OS, OSl = min(OS, H - o0);
-                    const int ntile = OSl >> 4;
-                    const int ib = r0 >> 7;
-                    // this warp's tiles tl = warp + NCW*v, in batches of DB: loads and MMAs
-                    // of a batch are independent; the accumulator update comes after all
-                    // of them (no store between two loads of a batch)
-                    for (int v0b = 0; warp + NCW * v0b < ntile; v0b += DB) {
-                        float r0[2][DB], r1[2][DB];
-                        float sdv[DB];
+                    // B fragments: lane column c = 8m + g = (token c/4, term c%4), rows 4t..4t+3
+                    uint32_t bf[2][2];
 #pragma unroll
-                        for (int v = 0; v < DB; ++v) {
-                            const int tl = warp + NCW * (v0b + v);
-                            const int ol = tl < ntile ? tl * 16 : 0;
+                    for (int ol = 0; ol < 2; ++ol)
+#pragma unroll
+                        for (int m = 0; m < 2; ++m) {
+                            const int cc = 8 * m + g, tk = cc >> 2, jt = cc & 3;
+                            const int ob = obw + ol;
+                            uint32_t word = 0u;
+                            if (m < nmD && tk < T && (ob << 7) < o0 + OSl) {
+                                const float f = stab[(ob - (o0 >> 7)) * nbpI + ib];
+                                const float sc = scale2(f, s.hexp[tk][ob]);
+                                const float* hv = reinterpret_cast<const float*>(hterm) + ci * 64 + (4 * t) * 4 + tk;
+                                float a0 = hv[0] * sc, b0 = hv[4] * sc, a1 = hv[8] * sc, b1 = hv[12] * sc;
+#pragma unroll
+                                for (int j = 0; j < JH; ++j) {
+                                    const uint32_t d0 = e4m3_term2(a0, b0), d1 = e4m3_term2(a1, b1);
+                                    if (j == jt) word = d0 | (d1 << 16);
+                                }
+                            }
+                            bf[ol][m] = word;
+                        }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        if (i < TPW && tw0 + i < ntile) {
+                            const int ol = (tw0 + i) * 16;
                             const uint32_t a0 = *reinterpret_cast<const uint32_t*>(stage + (size_t)(ol + g) * 16 + 4 * t);
                             const uint32_t a1 =
                                 *reinterpret_cast<const uint32_t*>(stage + (size_t)(ol + g + 8) * 16 + 4 * t);
-                            sdv[v] = stab[(ol >> 7) * nbpI + ib];
-#pragma unroll
-                            for (int m = 0; m < 2; ++m) {
-                                float d[4] = {0.f, 0.f, 0.f, 0.f};
-                                if (m < nmD) mma_e4m3(d, a0, a1, 0u, 0u, bfr[m], 0u);
-                                r0[m][v] = d[0] + d[1];  // terms 2(t&1), 2(t&1)+1 of pair 2m + t/2
-                                r1[m][v] = d[2] + d[3];
-                            }
-                        }
-#pragma unroll
-                        for (int m = 0; m < 2; ++m)
-#pragma unroll
-                            for (int v = 0; v < DB; ++v) {  // the other two terms are one lane over
-                                r0[m][v] += __shfl_xor_sync(0xffffffffu, r0[m][v], 1);
-                                r1[m][v] += __shfl_xor_sync(0xffffffffu, r1[m][v], 1);
-                            }
-#pragma unroll
-                        for (int m = 0; m < 2; ++m) {
-                            if ((t & 1) == 0 && 2 * m + (t >> 1) < np) {
-                                float* arow = acc + (size_t)tokq[m] * H + o0 + g;
-                                float cur0[DB], cur1[DB];
-#pragma unroll
-                                for (int v = 0; v < DB; ++v) {
-                                    const int tl = warp + NCW * (v0b + v);
-                                    if (tl < ntile) {
-                                        cur0[v] = arow[tl * 16];
-                                        cur1[v] = arow[tl * 16 + 8];
-                                    }
-                                }
-#pragma unroll
-                                for (int v = 0; v < DB; ++v) {
-                                    const int tl = warp + NCW * (v0b + v);
-                                    if (tl < ntile) {
-                                        const float w = wqv[m] * sdv[v];
-                                        arow[tl * 16] = __fmaf_rn(w, r0[m][v], cur0[v]);
-                                        arow[tl * 16 + 8] = __fmaf_rn(w, r1[m][v], cur1[v]);
-                                    }
-                                }
+                            const int obl = (i * 16) >> 7;
+                            if (nmD == 1) {
+                                mma_e4m3(accd[i], a0, a1, 0u, 0u, bf[obl][0], 0u);
+                            } else if (i < 8) {
+                                mma_e4m3(accd[2 * i], a0, a1, 0u, 0u, bf[obl][0], 0u);
+                                mma_e4m3(accd[2 * i + 1], a0, a1, 0u, 0u, bf[obl][1], 0u);
                             }
                         }
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&s.empty[slot]);
                 }
+                // slab done: combine the 4 terms of each token, undo the scale, write the
+                // CTA's partial rows (every (token, row) of the slab is written, zeros included)
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int tile = nmD == 1 ? i : (i >> 1), m = nmD == 1 ? 0 : (i & 1);
+                    if (tile < TPW) {
+                        float v0 = accd[i][0] + accd[i][1], v1 = accd[i][2] + accd[i][3];
+                        v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+                        v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+                        const int tk = 2 * m + (t >> 1);
+                        if (tw0 + tile < ntile && (t & 1) == 0 && tk < T) {
+                            const int o = o0 + (tw0 + tile) * 16 + g;
+                            const float us = scale2(1.0f, -s.hexp[tk][o >> 7]);
+                            float* dst = p.partial + ((size_t)c * T + tk) * H + o;
+                            dst[0] = v0 * us;
+                            dst[8] = v1 * us;
+                        }
+                    }
+                }
             }
         }
     }
 
-    // ---------------- partial sums -> global, then this CTA's slice of out ----------------
-    __syncthreads();
-    {
-        float4* dst = reinterpret_cast<float4*>(p.partial + (size_t)c * T * H);
-        const float4* src = reinterpret_cast<const float4*>(acc);
-        for (int i = tid; i < (T * H) >> 2; i += NTHREADS) dst[i] = src[i];
-    }
+    // ---------------- this CTA's slice of out: the G partial rows in a fixed order ----------------
+    __threadfence();  // this thread's partial rows before the arrive below
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -978,9 +998,12 @@ size_t decode_smem_bytes(int T, int H, int x_bf16) { return carve(T, H, x_bf16).
 int decode_max_tokens(int H, int E, int K, int I, int SI, int x_bf16, int num_sms) {
     if (K < 1 || K > MAXK || E < K || E > MAXE || H % 16 || I % 16 || SI % 16 || H < 16 || I < 16) return 0;
     if (num_sms > kMaxGrid) return 0;
-    if ((size_t)cz_nbp(H) * 4 > (size_t)SC_BYTES) return 0;  // gate/up scales of a row block
     const int IM = I > SI ? I : SI;
-    if ((size_t)((OS + 127) / 128) * cz_nbp(IM) * 4 > (size_t)SC_BYTES) return 0;  // down scales of a stage
+    if (cz_nblk(H) > 64) return 0;  // per-(token, 128-row block) scale tables
+    // scales carried with a stage: gate/up row block + (first up slab) the expert's down table;
+    // a down stage: its 128-row blocks of the down table
+    if ((size_t)(cz_nbp(H) + cz_nblk(H) * cz_nbp(IM)) * 4 > (size_t)SC_BYTES) return 0;
+    if ((size_t)(OS / 128) * cz_nbp(IM) * 4 > (size_t)SC_BYTES) return 0;
     const int max_rows = (E + (SI ? 1 : 0) + num_sms - 1) / num_sms;  // router rows staged per CTA
     const int IM16 = (I > SI ? I : SI) / CR;  // chunks of the largest group
     int t = MAXT;

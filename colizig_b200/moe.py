@@ -78,7 +78,9 @@ class Layer:
     """A registered MoE layer (resident on the device)."""
 
     def __init__(self, layer_id: int, dims: Dims, router, gate_w, gate_s, up_w, up_s, down_w, down_s,
-                 shared: Optional[dict] = None, shared_gate=None):
+                 shared: Optional[dict] = None, shared_gate=None, ep: bool = False):
+        """ep=True: hold only this rank's experts (after ep.init); every forward then
+        sums the ranks' outputs (one NCCL all-reduce)."""
         if not gpu.available():
             gpu.init()
         self.id = int(layer_id)
@@ -109,7 +111,8 @@ class Layer:
             sh_ptr = ctypes.byref(sh)
             sg_ptr = _ptr(shared_gate)
         cd = dims.c()
-        flags = _abi.COLIZIG_PTR_DEVICE if device else 0
+        flags = (_abi.COLIZIG_PTR_DEVICE if device else 0) | (_abi.COLIZIG_EP if ep else 0)
+        self.ep = bool(ep)
         if device:
             torch.cuda.synchronize()
         rc = _abi.load().colizig_cuda_moe_register_layer(self.id, ctypes.byref(cd), _ptr(router), experts, sh_ptr,
@@ -118,12 +121,12 @@ class Layer:
         _abi.check("colizig_cuda_moe_register_layer", rc)
 
     @staticmethod
-    def from_weights(layer_id: int, dims: Dims, w: dict) -> "Layer":
+    def from_weights(layer_id: int, dims: Dims, w: dict, ep: bool = False) -> "Layer":
         shared = None
         if dims.has_shared():
             shared = {k: w[k] for k in ("sh_gate_w", "sh_gate_s", "sh_up_w", "sh_up_s", "sh_down_w", "sh_down_s")}
         return Layer(layer_id, dims, w["router"], w["gate_w"], w["gate_s"], w["up_w"], w["up_s"], w["down_w"],
-                     w["down_s"], shared, w.get("sh_gate"))
+                     w["down_s"], shared, w.get("sh_gate"), ep=ep)
 
     def unregister(self) -> None:
         _abi.check("colizig_cuda_moe_unregister_layer", _abi.load().colizig_cuda_moe_unregister_layer(self.id))

@@ -101,6 +101,10 @@ typedef struct colizig_moe_expert {
                                  asynchronous on `stream` (else: host pointers,
                                  synchronous, like colizig_cuda_matmul_fp8) */
 
+#define COLIZIG_EP 2u /* register_layer: hold only this rank's experts (expert parallelism,
+                         after colizig_cuda_ep_init); every forward of the layer then sums
+                         the ranks' outputs with one NCCL all-reduce on `stream` */
+
 /* x dtypes */
 #define COLIZIG_X_F32 0
 #define COLIZIG_X_BF16 1
@@ -132,6 +136,17 @@ int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtype, int T, 
  * (all ones). */
 int colizig_cuda_moe_stack_forward(uint32_t first_layer, uint32_t n_layers, const float* norm_w, float eps,
                                    float* h, int T, uint32_t flags, void* stream);
+
+/* Expert parallelism over W GPUs of one node (one process per GPU), the
+ * partition of src/qwen38/moe.zig's experts that forwardGrouped (moe.zig:637-664)
+ * makes possible.  Rank r holds experts [r*E/W, (r+1)*E/W) (rank 0 also the
+ * shared expert); router and top-k run replicated.  colizig_cuda_ep_unique_id
+ * fills 128 bytes on one rank, the caller hands them to every rank, and every
+ * rank calls colizig_cuda_ep_init once (after colizig_cuda_init_device).
+ * Returns -9 when NCCL (libnccl.so.2) is unavailable or fails. */
+int colizig_cuda_ep_unique_id(void* id_out);
+int colizig_cuda_ep_init(int rank, int world, const void* id);
+int colizig_cuda_ep_shutdown(void);
 
 /* Device-side error word of the last asynchronous call(s) on the library's
  * MoE scratch (0 = none); reading it synchronises `stream` and clears it. */

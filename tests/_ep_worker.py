@@ -1,0 +1,65 @@
+"""One rank of the 2-GPU expert-parallel check (launched by tests/test_gpu_ep.py
+through torch.distributed.run).  Rank r holds experts [r*E/2, (r+1)*E/2) of
+every layer; the layer outputs (summed over ranks by the library's NCCL
+all-reduce) are compared with the CPU oracle (top-k bit-exact, outputs within
+the layer tolerance) and with the same layer run whole on one GPU."""
+
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import colizig_b200 as cz  # noqa: E402
+import oracle  # noqa: E402
+from colizig_b200 import ep, moe, synth  # noqa: E402
+from tests.util import OUT_TOL, rel_err  # noqa: E402
+
+
+def main() -> int:
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo")
+    cz.gpu.init(local)
+    ep.init()
+    oracle.set_threads(os.cpu_count() or 1)
+    ok = True
+    lid = 700
+    for cfg, Ts in (("c2", (1, 4, 16)), ("c5", (1, 5))):
+        d = synth.CONFIGS[cfg]
+        w = synth.make_layer(d, seed=11, device="cuda")
+        Lep = moe.Layer.from_weights(lid, d, w, ep=True)
+        Lfull = moe.Layer.from_weights(lid + 1, d, w)
+        lid += 2
+        wn = synth.to_numpy_layer(w) if rank == 0 else None
+        for T in Ts:
+            x = synth.make_tokens(T, d.hidden, 300 + T, device="cuda", dtype=torch.bfloat16)
+            out, idx, gates = moe.forward(Lep, x)
+            ref, ridx, rg = moe.forward(Lfull, x)
+            torch.cuda.synchronize()
+            moe.check()
+            if rank == 0:
+                ol = oracle.layer_from_dict(wn)
+                od = oracle.Dims(d.hidden, d.experts, d.topk, d.inter, d.shared_inter, d.norm_topk)
+                oo, oi, _ = oracle.moe_forward(ol, od, synth.tokens_f32(x.cpu()))
+                e_or = rel_err(out.cpu().numpy(), oo)
+                e_one = rel_err(out.cpu().numpy(), ref.cpu().numpy())
+                same = np.array_equal(idx.cpu().numpy().view(np.uint32), oi)
+                print(f"{cfg} T={T}: top-k exact {same}, vs oracle {e_or:.2e}, vs one GPU {e_one:.2e}", flush=True)
+                ok &= same and e_or <= OUT_TOL and e_one <= OUT_TOL and torch.equal(idx, ridx) and torch.equal(gates, rg)
+        Lep.unregister()
+        Lfull.unregister()
+    torch.cuda.synchronize()
+    ep.shutdown()
+    flag = torch.tensor([1 if ok else 0])
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    dist.destroy_process_group()
+    return 0 if int(flag.item()) == 1 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
