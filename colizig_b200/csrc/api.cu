@@ -91,6 +91,8 @@ struct MoeLayer {
     int shared_here = 0;        // the shared expert's weights are held (and computed) here
     bool ep = false;            // outputs are summed over the expert-parallel group after each forward
     CUtensorMap down_map{};     // TMA view of down_w: u8 [(e_hi-e_lo)*H][I]
+    cz::PrefillLayer pf{};      // the prefill kernels' view (tensor maps with 128-byte swizzle)
+    bool pf_ok = false;
     CUtensorMap sh_down_map{};  // TMA view of sh_down_w: u8 [H][SI]
 };
 
@@ -109,7 +111,7 @@ struct Ctx {
     uint64_t hits = 0, misses = 0, uploaded = 0;
     // MoE
     std::map<uint32_t, MoeLayer> layers;
-    DevBuf logits, partial, io_x, io_out, io_idx, io_gates, ones;
+    DevBuf logits, partial, io_x, io_out, io_idx, io_gates, ones, pf_scratch;
     uint32_t* sync = nullptr;
     // expert parallelism (one process per GPU)
     bool ep_on = false;
@@ -146,6 +148,10 @@ Ctx g;
 std::mutex g_mu;
 
 size_t nb(size_t x) { return (x + 127) / 128; }
+
+// Token batches of at least this size take the prefill path (grouped GEMMs on
+// tcgen05); smaller ones the decode kernel.
+constexpr int kPrefillMinTokens = 32;
 
 int ensure_sync() {
     if (g.sync) return CZ_OK;
@@ -192,7 +198,7 @@ void shutdown_locked() {
     g.lru.clear();
     for (auto& kv : g.layers) free_layer(kv.second);
     g.layers.clear();
-    for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.partial, &g.io_x, &g.io_out, &g.io_idx,
+    for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.partial, &g.pf_scratch, &g.io_x, &g.io_out, &g.io_idx,
                       &g.io_gates, &g.ones})
         b->release();
     if (g.sync) cudaFree(g.sync);
@@ -303,6 +309,22 @@ cz::DecodeParams make_params(const MoeLayer& L) {
 // of at most kDecodeMaxTokens tokens.
 int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uint32_t* idx, float* gates,
             const float* rms_w, float eps, const float* residual, cudaStream_t st) {
+    if (T >= kPrefillMinTokens && L.pf_ok) {
+        const size_t need = cz::prefill_scratch_bytes(T, (int)L.d.hidden, (int)L.d.experts, (int)L.d.topk,
+                                                      (int)L.d.inter, (int)L.d.shared_inter, g.num_sms);
+        if (!g.pf_scratch.ensure(need)) return CZ_EALLOC;
+        if (ensure_sync()) return CZ_EALLOC;
+        const float* res = residual && (!L.ep || g.ep_rank == 0) ? residual : nullptr;
+        int rc = cz::prefill_run(L.pf, x, x_bf16, T, rms_w, eps, res, out, idx, gates, g.pf_scratch.p,
+                                 g.pf_scratch.cap, g.sync + 1, g.num_sms, st);
+        if (rc) return rc;
+        if (L.ep && g.ep_world > 1) {
+            if (!g.ep_comm) return CZ_ENCCL;
+            if (nccl.allReduce(out, out, (size_t)T * L.d.hidden, ncclFloat, ncclSum, g.ep_comm, st) != ncclSuccess)
+                return CZ_ENCCL;
+        }
+        return CZ_OK;
+    }
     int rc = ensure_decode_scratch(L.d);
     if (rc) return rc;
     const size_t xelt = x_bf16 ? 2 : 4;
@@ -506,7 +528,7 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
     size_t off = 0;
     auto take = [&](size_t bytes) {
         const size_t o = off;
-        off = align256(off + bytes);
+        off = (off + bytes + 1023) & ~size_t(1023);  // 1024-aligned: swizzled TMA boxes need it
         return o;
     };
     const size_t o_router = take(ER * H * 4), o_gw = take(E * wexp), o_uw = take(E * wexp), o_dw = take(E * wexp);
@@ -584,6 +606,34 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
     }
     if (!rc && E && !cz::make_down_map(&L.down_map, L.down_w, E * H, I)) rc = CZ_ELAUNCH;
     if (!rc && shared_here && !cz::make_down_map(&L.sh_down_map, L.sh_down_w, H, SI)) rc = CZ_ELAUNCH;
+    if (!rc && E && cz::prefill_supported((int)H, (int)d.experts, (int)d.topk, (int)I, (int)SI)) {
+        cz::PrefillLayer& P = L.pf;
+        bool ok = cz::make_sw128_map(&P.gate_map, L.gate_w, E * I, H, 128) &&
+                  cz::make_sw128_map(&P.up_map, L.up_w, E * I, H, 128) &&
+                  cz::make_sw128_map(&P.down_map, L.down_w, E * H, I, 128);
+        if (ok && shared_here)
+            ok = cz::make_sw128_map(&P.sh_gate_map, L.sh_gate_w, SI, H, 128) &&
+                 cz::make_sw128_map(&P.sh_up_map, L.sh_up_w, SI, H, 128) &&
+                 cz::make_sw128_map(&P.sh_down_map, L.sh_down_w, H, SI, 128);
+        P.router = L.router;
+        P.sh_gate = L.sh_gate;
+        P.gate_s = L.gate_s;
+        P.up_s = L.up_s;
+        P.down_s = L.down_s;
+        P.sh_gate_s = L.sh_gate_s;
+        P.sh_up_s = L.sh_up_s;
+        P.sh_down_s = L.sh_down_s;
+        P.H = (int)H;
+        P.E = (int)d.experts;
+        P.K = (int)d.topk;
+        P.I = (int)I;
+        P.SI = (int)SI;
+        P.norm_topk = (int)d.norm_topk;
+        P.e_lo = e_lo;
+        P.e_hi = e_hi;
+        P.shared_here = shared_here;
+        L.pf_ok = ok;
+    }
     if (!rc && cudaStreamSynchronize(g.stream) != cudaSuccess) rc = CZ_EH2D;
     if (rc) {
         cudaStreamSynchronize(g.stream);

@@ -70,6 +70,34 @@ size_t decode_smem_bytes(int T, int H, int x_bf16);
 int decode_max_tokens(int H, int E, int K, int I, int SI, int x_bf16, int num_sms);
 int decode_launch(const DecodeParams& p, int num_sms, cudaStream_t stream);
 
+// ---- prefill: token batches on tcgen05 grouped GEMMs (moe_prefill.cu) ----
+
+// One layer's weights as the prefill kernels see them (experts [e_lo, e_hi)
+// held here, stacked from e_lo; the shared expert when shared_here).
+struct PrefillLayer {
+    CUtensorMap gate_map, up_map;  // u8 [(e_hi-e_lo)*I][H], box 128 x 128, 128-byte swizzle
+    CUtensorMap down_map;          // u8 [(e_hi-e_lo)*H][I], box 128 x 128, 128-byte swizzle
+    CUtensorMap sh_gate_map, sh_up_map, sh_down_map;  // shared expert (SI x H, H x SI)
+    const float *router, *sh_gate;
+    const float *gate_s, *up_s, *down_s;  // [EL][nb(I)][nbp(H)], [EL][nb(H)][nbp(I)]
+    const float *sh_gate_s, *sh_up_s, *sh_down_s;
+    int H, E, K, I, SI, norm_topk, e_lo, e_hi, shared_here;
+};
+
+// Whether the prefill path takes these dims (multiples of 128, sizes it was built for).
+bool prefill_supported(int H, int E, int K, int I, int SI);
+// Scratch bytes one prefill call of T tokens needs.
+size_t prefill_scratch_bytes(int T, int H, int E, int K, int I, int SI, int num_sms);
+// A u8 [rows][cols] tensor map, box 128 cols x box_rows rows, 128-byte swizzle.
+bool make_sw128_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+// out[T, H] (+ residual) = MoE(x) for a batch of T tokens; x f32 or bf16
+// (rms_w: x = rms(x, rms_w), eps).  topk_idx / topk_gates nullable.  err = the
+// device error word.  Stream-ordered; the scratch stays in use until the
+// stream reaches the end of the call.
+int prefill_run(const PrefillLayer& L, const void* x, int x_bf16, int T, const float* rms_w, float eps,
+                const float* residual, float* out, uint32_t* topk_idx, float* topk_gates, void* scratch,
+                size_t scratch_bytes, uint32_t* err, int num_sms, cudaStream_t st);
+
 // Legacy per-matrix block-FP8 matmul (device pointers, stream-ordered).
 int fp8_matmul_launch(float* y, const float* x, const uint8_t* w, const float* scales, int S, int I, int O,
                       cudaStream_t stream);
