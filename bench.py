@@ -62,6 +62,25 @@ def shared_bytes(d) -> int:
     return 3 * d.shared_inter * d.hidden + 4 * 3 * nb(d.shared_inter) * nb(d.hidden) + 4 * d.hidden
 
 
+PREFILL_MIN_TOKENS = 32  # the library's switch to the prefill path (grouped tcgen05 GEMMs)
+
+
+def gen_tokens(args, d, T, seed, device, synth, dtype=None):
+    import torch
+
+    dt = dtype or torch.bfloat16
+    if args.config == "c3":
+        return synth.zipf_tokens(T, d.hidden, seed, device=device, dtype=dt)
+    return synth.make_tokens(T, d.hidden, seed, device=device, dtype=dt)
+
+
+def gen_layer(args, d, seed, device, synth):
+    w = synth.make_layer(d, seed=seed, device=device)
+    if args.config == "c3":
+        synth.zipf_router(w, seed)
+    return w
+
+
 def algorithmic_bytes(d, T: int, U: float) -> float:
     """Bytes one layer call must move (survey 8d): U distinct experts' weights +
     scales, the f32 router, the shared expert, bf16 tokens in, f32 outputs out."""
@@ -124,7 +143,7 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_sample(d, layers_np, T, seconds, threads):
+def cpu_sample(args, d, layers_np, T, seconds, threads):
     """Time the CPU oracle (restatement of the reference AVX2 path) on a bounded
     sample of the workload: as many steps as fit in ~`seconds`."""
     import torch
@@ -136,7 +155,7 @@ def cpu_sample(d, layers_np, T, seconds, threads):
     oracle.set_threads(threads)
     od = oracle.Dims(d.hidden, d.experts, d.topk, d.inter, d.shared_inter, d.norm_topk)
     ols = [oracle_layer(w) for w in layers_np]
-    toks = [synth.tokens_f32(synth.make_tokens(T, d.hidden, 5000 + i, device="cpu")) for i in range(64)]
+    toks = [synth.tokens_f32(gen_tokens(args, d, T, 5000 + i, "cpu", synth)) for i in range(8 if T > 1 else 64)]
     oracle.moe_forward(ols[0], od, toks[0])  # warm-up
     n, t0 = 0, time.perf_counter()
     while True:
@@ -159,40 +178,51 @@ def reference_arm(args):
         return
     d = synth.CONFIGS[args.config]
     T = args.tokens
+    Ts = min(T, 64)  # each step: a bounded sample of the batch (prefill batches are thousands of tokens)
     cores = os.cpu_count() or 1
-    layers = [synth.to_numpy_layer(synth.make_layer(d, seed=i, device="cpu")) for i in range(args.cpu_layers)]
+    layers = [synth.to_numpy_layer(gen_layer(args, d, i, "cpu", synth)) for i in range(args.cpu_layers)]
     import oracle
 
     oracle_layer = oracle.layer_from_dict
     oracle.set_threads(cores)
     od = oracle.Dims(d.hidden, d.experts, d.topk, d.inter, d.shared_inter, d.norm_topk)
     ols = [oracle_layer(w) for w in layers]
-    toks = [synth.tokens_f32(synth.make_tokens(T, d.hidden, 9000 + i, device="cpu"))
-            for i in range(args.steps + args.warmup)]
+    toks = [synth.tokens_f32(gen_tokens(args, d, Ts, 9000 + i, "cpu", synth)) for i in range(args.steps + args.warmup)]
     for i in range(args.warmup):
         oracle.moe_forward(ols[i % len(ols)], od, toks[i])
     t0 = time.perf_counter()
     for i in range(args.steps):
         oracle.moe_forward(ols[i % len(ols)], od, toks[args.warmup + i])
     dt = time.perf_counter() - t0
-    value = args.steps * T / dt
+    value = args.steps * Ts / dt
     line = {
-        "impl": "reference", "metric": f"MoE-layer decode tokens/s ({args.config}, T={T})", "value": value,
+        "impl": "reference", "metric": metric_name(args, T), "value": value,
         "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_block(args, d),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} steps of the {args.config} T={T} layer forward over "
-                                   f"{args.cpu_layers} layers (C restatement of the reference AVX2 path)"},
+                         "sample": f"{args.steps} steps, each the {args.config} layer forward of {Ts} of the step's "
+                                   f"{T} tokens, over {args.cpu_layers} layers (C restatement of the reference AVX2 "
+                                   f"path, {cores} threads)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
+def metric_name(args, T):
+    mode = "prefill" if T >= PREFILL_MIN_TOKENS else "decode"
+    return f"MoE-layer {mode} tokens/s ({args.config}, T={T})"
+
+
 def config_block(args, d):
     g = args.tokens * args.gpus
-    return {"workload": f"{args.config} MoE layer decode, {g} token(s)/step (BASELINE config 2)",
+    if g >= PREFILL_MIN_TOKENS:
+        wl = (f"{args.config} MoE layer prefill, {g} tokens/step (BASELINE config 3: Zipf-skewed routing)"
+              if args.config == "c3" else f"{args.config} MoE layer prefill, {g} tokens/step")
+    else:
+        wl = f"{args.config} MoE layer decode, {g} token(s)/step (BASELINE config 2)"
+    return {"workload": wl,
             "hidden": d.hidden, "experts": d.experts, "topk": d.topk, "moe_intermediate": d.inter,
             "shared_intermediate": d.shared_inter, "tokens_per_step": g, "tokens_per_gpu": args.tokens,
             "global_batch": g, "layers_cycled": args.layers,
@@ -204,17 +234,25 @@ def config_block(args, d):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2")
-    ap.add_argument("--tokens", type=int, default=1)
-    ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--cpu-layers", type=int, default=4)
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    prefill_cfg = args.config == "c3"
+    if args.tokens is None:
+        args.tokens = 2048 if prefill_cfg else 1
+    big = args.tokens * args.gpus >= PREFILL_MIN_TOKENS
+    if args.steps is None:
+        args.steps = 20 if big else 200
+    if args.layers is None:
+        args.layers = 4 if big else 16
 
     if args.impl == "reference":
         reference_arm(args)
@@ -247,7 +285,7 @@ def main():
 
     layers, host_layers = [], []
     for l in range(args.layers):
-        w = synth.make_layer(d, seed=l, device=dev)  # the same layer on every rank
+        w = gen_layer(args, d, l, dev, synth)  # the same layer on every rank
         layers.append(moe.Layer.from_weights(l, d, w, ep=world > 1))
         if rank == 0 and world == 1 and l < args.cpu_layers and not args.no_cpu:
             host_layers.append(synth.to_numpy_layer(w))
@@ -255,7 +293,7 @@ def main():
     torch.cuda.empty_cache()
 
     n = args.warmup + args.steps
-    xs = [synth.make_tokens(T, d.hidden, 20000 + i, device=dev) for i in range(n)]
+    xs = [gen_tokens(args, d, T, 20000 + i, dev, synth) for i in range(n)]
     outs = torch.empty((n, T, d.hidden), dtype=torch.float32, device=dev)
     idx = torch.empty((n, T, d.topk), dtype=torch.int32, device=dev)
     gates = torch.empty((n, T, d.topk), dtype=torch.float32, device=dev)
@@ -354,19 +392,38 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cores = os.cpu_count() or 1
-        v, nsteps, dt = cpu_sample(d, host_layers, T, args.cpu_seconds, cores)
+        Tc = min(T, 64)  # bounded sample for prefill batches
+        v, nsteps, dt = cpu_sample(args, d, host_layers, Tc, args.cpu_seconds, cores)
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"{nsteps} layer forwards of {args.config} T={T} in {dt:.1f} s over {len(host_layers)} "
+               "sample": f"{nsteps} layer forwards of {args.config} T={Tc} in {dt:.1f} s over {len(host_layers)} "
                          f"layers (C restatement of the reference AVX2 path, {cores} threads)"}
 
+    prefill = T >= PREFILL_MIN_TOKENS
+    launches_per_step = 8 if prefill else -(-T // 4)
+    if prefill:
+        # tensor-bound: algorithmic FLOPs of the whole step (all its kernels) against the
+        # FP8 dense peak, taken as 2 x the measured cuBLAS bf16 throughput
+        tf = algorithmic_flops(d, T) * args.steps / (elapsed_ms / 1e3) / 1e12 / world
+        fp8_peak = 2.0 * tf_peak
+        roof = {"bound": "tensor", "achieved": tf, "peak": fp8_peak, "unit": "TFLOP/s", "frac": tf / fp8_peak,
+                "traffic": None,
+                "peak_kind": (f"FP8 dense = 2 x {peak_kind} bf16 (MEASURED_PEAKS.json bf16_tflops)"
+                              if peak_kind == "measured" else "FP8 dense = 2 x fallback 1.59 PFLOP/s"),
+                "kernel": "whole prefill step (route, grouping, dispatch, 2 tcgen05 grouped GEMMs, combine)",
+                "step_ms": elapsed_ms / args.steps, "flops_per_step": algorithmic_flops(d, T),
+                "distinct_experts_avg": float(U.mean()),
+                "top_expert_pairs_avg": float(np.mean([np.bincount(ids[k].ravel()).max() for k in range(args.steps)]))}
+    else:
+        roof = None
     if rank == 0:
         line = {
-            "metric": f"MoE-layer decode tokens/s ({args.config}, T={T})", "value": value, "unit": "tokens/s",
+            "metric": metric_name(args, T), "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_block(args, d),
+            "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32" if prefill else "f32", "data": "synthetic",
+            "config": config_block(args, d),
             "hbm_gbs": achieved_gbs,
-            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
+            "roofline": roof or {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved_gbs / hbm_peak, "traffic": NCU_TRAFFIC.get((args.config, T)),
                          "traffic_unit": "bytes per launch (ncu)",
                          "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
@@ -374,7 +431,7 @@ def main():
                          "kernel": "moe_decode_kernel", "kernel_ms_avg": float(np.mean(kernel_ms)),
                          "bytes_per_launch_avg": float(bytes_per.mean()), "distinct_experts_avg": float(U.mean())},
             "tflops": algorithmic_flops(d, T) * args.steps / (np.sum(kernel_ms) / 1e3) / 1e12,
-            "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": args.steps,
+            "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": args.steps * launches_per_step,
         }
         print(json.dumps(line), flush=True)
     for lay in layers:

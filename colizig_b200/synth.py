@@ -9,6 +9,10 @@ on generated data with the configured shapes and value distributions:
   * router: f32 N(0, 0.02) [experts, hidden];
   * shared-expert gate vector: f32 N(0, 0.02) [hidden];
   * tokens: bf16 (or f32) N(0, 1).
+Config 3's skewed routing (Zipf(1.1) over experts): the router has no bias, so
+the skew enters through a fixed unit vector u: router rows get beta_e * u and
+tokens get gamma * u, with beta_e * gamma = -1.1 * ln(1 + rank_e) for a seeded
+random rank order of the experts (see zipf_router / zipf_tokens).
 Generation runs with torch on the requested device (CUDA for full-size layers),
 in expert chunks so temporary f32 storage stays bounded.
 """
@@ -68,6 +72,41 @@ def make_layer(d: Dims, seed: int = 0, device="cpu") -> dict:
     return w
 
 
+ZIPF_S = 1.1
+ZIPF_GAMMA = 4.0
+
+
+def _zipf_dir(H: int, device) -> torch.Tensor:
+    gen = torch.Generator(device=device)
+    gen.manual_seed(12345)
+    u = torch.randn((H,), generator=gen, device=device, dtype=torch.float32)
+    return u / u.norm()
+
+
+def zipf_router(w: dict, seed: int = 0) -> dict:
+    """Skew a layer's routing: router row e += beta_e * u (in place)."""
+    E, H = w["router"].shape
+    dev = w["router"].device
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(int(seed) + 99)
+    rank = torch.randperm(E, generator=gen).to(dev, torch.float32)
+    beta = -ZIPF_S * torch.log1p(rank) / ZIPF_GAMMA
+    w["router"] += beta[:, None] * _zipf_dir(H, dev)[None, :]
+    return w
+
+
+def zipf_tokens(T: int, H: int, seed: int, device="cpu", dtype=torch.bfloat16) -> torch.Tensor:
+    """Tokens N(0, 1) + gamma * u (the routing skew's token side)."""
+    x = torch.randn((T, H), generator=_gen(seed, device), device=device, dtype=torch.float32)
+    return (x + ZIPF_GAMMA * _zipf_dir(H, x.device)[None, :]).to(dtype)
+
+
+def _gen(seed: int, device):
+    gen = torch.Generator(device=device)
+    gen.manual_seed(int(seed))
+    return gen
+
+
 def make_tokens(T: int, H: int, seed: int, device="cpu", dtype=torch.bfloat16) -> torch.Tensor:
     gen = torch.Generator(device=device)
     gen.manual_seed(int(seed))
@@ -88,5 +127,6 @@ def tokens_f32(x: torch.Tensor) -> np.ndarray:
 CONFIGS = {
     "c1": Dims(hidden=256, experts=16, topk=4, inter=128, shared_inter=0, norm_topk=True),
     "c2": Dims(hidden=2048, experts=128, topk=8, inter=768, shared_inter=0, norm_topk=True),
+    "c3": Dims(hidden=2048, experts=128, topk=8, inter=768, shared_inter=0, norm_topk=True),  # + Zipf routing
     "c5": Dims(hidden=4096, experts=512, topk=10, inter=1024, shared_inter=1024, norm_topk=True),
 }
