@@ -47,7 +47,7 @@ EXPERT_BYTES = {}  # per config: bytes of one expert (3 projections + scales)
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
 # moe_decode_kernel launch, from an ncu capture of the same workload; other
 # (config, tokens) pairs report null until captured.
-NCU_TRAFFIC = {("c2", 1): 39.02e6}
+NCU_TRAFFIC = {("c2", 1): 39.05e6, ("c3", 2048): 536.7e6}
 
 
 def expert_bytes(d) -> int:
@@ -316,6 +316,11 @@ def main():
 
     # The timed steps are captured once into a CUDA graph (one kernel node per
     # step) so the timing is not bounded by the host's launch rate.
+    prefill = T >= PREFILL_MIN_TOKENS
+    if prefill:
+        # event pairs around the grouped GEMM launches of every captured step, so the
+        # dominant kernel's own device time comes out of the timed replay itself
+        moe.kernel_timer(2 * args.steps)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=dev)):
         gs = torch.cuda.current_stream().cuda_stream
@@ -345,6 +350,11 @@ def main():
     moe.check()
     elapsed_ms = t_start.elapsed_time(t_end)
     kernel_ms = [elapsed_ms / args.steps] * args.steps  # one kernel per step, back to back
+    gemm_ms = {}
+    if prefill:
+        for kind, ms in moe.kernel_timer_read():
+            gemm_ms.setdefault(kind, []).append(ms)
+        moe.kernel_timer(0)
     if world > 1:
         tt = torch.tensor([elapsed_ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -398,19 +408,35 @@ def main():
                "sample": f"{nsteps} layer forwards of {args.config} T={Tc} in {dt:.1f} s over {len(host_layers)} "
                          f"layers (C restatement of the reference AVX2 path, {cores} threads)"}
 
-    prefill = T >= PREFILL_MIN_TOKENS
-    launches_per_step = 8 if prefill else -(-T // 4)
+    launches_per_step = 9 if prefill else -(-T // 4)  # prefill: logits, topk, count, place, tokpos, dispatch, 2 GEMMs, combine
     if prefill:
-        # tensor-bound: algorithmic FLOPs of the whole step (all its kernels) against the
-        # FP8 dense peak, taken as 2 x the measured cuBLAS bf16 throughput
-        tf = algorithmic_flops(d, T) * args.steps / (elapsed_ms / 1e3) / 1e12 / world
+        # tensor-bound.  Dominant kernel: the gate/up grouped GEMM.  Its algorithmic FLOPs
+        # (2 x pairs x H x 2I routed + 2 x T x H x 2SI shared, pairs on this rank's
+        # experts) over its own device time from the timer's event pairs, against the FP8
+        # dense peak taken as 2 x the measured cuBLAS bf16 throughput.
+        lo, hi = (0, d.experts) if world == 1 else ep.expert_range(rank, world, d.experts)
+        ids_t = idx[args.warmup:].cpu().numpy()
+        pairs_local = float(np.mean([((ids_t[k] >= lo) & (ids_t[k] < hi)).sum() for k in range(args.steps)]))
+        sh_t = T if (d.shared_inter and rank == 0) else 0
+        gu_flops = 2.0 * pairs_local * d.hidden * 2 * d.inter + 2.0 * sh_t * d.hidden * 2 * d.shared_inter
+        dn_flops = 2.0 * pairs_local * d.inter * d.hidden + 2.0 * sh_t * d.shared_inter * d.hidden
+        gu_ms = float(np.mean(gemm_ms[moe.TIMER_PREFILL_GATE_UP]))
+        dn_ms = float(np.mean(gemm_ms[moe.TIMER_PREFILL_DOWN]))
+        tf = gu_flops / (gu_ms / 1e3) / 1e12
+        step_tf = algorithmic_flops(d, T) * args.steps / (elapsed_ms / 1e3) / 1e12 / world
         fp8_peak = 2.0 * tf_peak
         roof = {"bound": "tensor", "achieved": tf, "peak": fp8_peak, "unit": "TFLOP/s", "frac": tf / fp8_peak,
-                "traffic": None,
+                "traffic": NCU_TRAFFIC.get((args.config, T)) if world == 1 else None,
+                "traffic_unit": "DRAM bytes per gate/up GEMM launch (ncu)",
                 "peak_kind": (f"FP8 dense = 2 x {peak_kind} bf16 (MEASURED_PEAKS.json bf16_tflops)"
                               if peak_kind == "measured" else "FP8 dense = 2 x fallback 1.59 PFLOP/s"),
-                "kernel": "whole prefill step (route, grouping, dispatch, 2 tcgen05 grouped GEMMs, combine)",
-                "step_ms": elapsed_ms / args.steps, "flops_per_step": algorithmic_flops(d, T),
+                "kernel": "pf_gemm_kernel (gate/up, tcgen05 grouped GEMM with the SiLU*up epilogue)",
+                "kernel_ms_avg": gu_ms, "flops_per_launch": gu_flops,
+                "down_gemm": {"kernel_ms_avg": dn_ms, "flops_per_launch": dn_flops,
+                              "achieved_tflops": dn_flops / (dn_ms / 1e3) / 1e12,
+                              "frac": dn_flops / (dn_ms / 1e3) / 1e12 / fp8_peak},
+                "step": {"ms": elapsed_ms / args.steps, "flops": algorithmic_flops(d, T) / world,
+                         "achieved_tflops": step_tf, "frac": step_tf / fp8_peak},
                 "distinct_experts_avg": float(U.mean()),
                 "top_expert_pairs_avg": float(np.mean([np.bincount(ids[k].ravel()).max() for k in range(args.steps)]))}
     else:

@@ -35,6 +35,8 @@ MOE_SYMBOLS = (
     "colizig_cuda_ep_unique_id",
     "colizig_cuda_ep_init",
     "colizig_cuda_ep_shutdown",
+    "colizig_cuda_kernel_timer",
+    "colizig_cuda_kernel_timer_read",
 )
 
 COLIZIG_PTR_DEVICE = 1
@@ -135,6 +137,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         L.colizig_cuda_ep_init.argtypes = [i32, i32, vp]
         L.colizig_cuda_ep_shutdown.restype = i32
         L.colizig_cuda_ep_shutdown.argtypes = []
+        L.colizig_cuda_kernel_timer.restype = i32
+        L.colizig_cuda_kernel_timer.argtypes = [i32]
+        L.colizig_cuda_kernel_timer_read.restype = i32
+        L.colizig_cuda_kernel_timer_read.argtypes = [vp, vp, i32]
         L.colizig_cuda_debug_expf.restype = i32
         L.colizig_cuda_debug_expf.argtypes = [vp, vp, ctypes.c_size_t]
         _lib = L

@@ -117,6 +117,11 @@ struct Ctx {
     bool ep_on = false;
     int ep_rank = 0, ep_world = 1;
     ncclComm_t ep_comm = nullptr;
+    // kernel timer (benchmarks): CUDA event pairs around the dominant launches
+    std::vector<cudaEvent_t> tm_ev;
+    std::vector<int> tm_kind;
+    int tm_n = 0;  // pairs recorded
+    bool tm_overflow = false;
 };
 
 // NCCL is resolved at run time (dlopen of libnccl.so.2): the library loads without
@@ -202,6 +207,7 @@ void shutdown_locked() {
                       &g.io_gates, &g.ones})
         b->release();
     if (g.sync) cudaFree(g.sync);
+    for (cudaEvent_t e : g.tm_ev) cudaEventDestroy(e);
     if (g.stream) cudaStreamDestroy(g.stream);
     g = Ctx{};
 }
@@ -305,6 +311,32 @@ cz::DecodeParams make_params(const MoeLayer& L) {
     return p;
 }
 
+// Kernel timer.  Kinds of the recorded launch pairs.
+constexpr int kTimerDecode = 1, kTimerPrefillGateUp = 2, kTimerPrefillDown = 3;
+
+// Reserves `pairs` consecutive begin/end event pairs of the timer (all of kind
+// `kind`); nullptr when the timer is off or full.  The events are recorded with
+// cudaEventRecordExternal, so a forward captured into a CUDA graph keeps them as
+// event-record nodes and every replay re-times the same launches.
+cudaEvent_t* timer_take(int kind, int pairs) {
+    if (g.tm_ev.empty()) return nullptr;
+    if ((size_t)(g.tm_n + pairs) * 2 > g.tm_ev.size()) {
+        g.tm_overflow = true;
+        return nullptr;
+    }
+    cudaEvent_t* ev = g.tm_ev.data() + (size_t)g.tm_n * 2;
+    for (int i = 0; i < pairs; ++i) g.tm_kind[g.tm_n++] = kind;
+    return ev;
+}
+
+void timer_free() {
+    for (cudaEvent_t e : g.tm_ev) cudaEventDestroy(e);
+    g.tm_ev.clear();
+    g.tm_kind.clear();
+    g.tm_n = 0;
+    g.tm_overflow = false;
+}
+
 // Runs one layer over T tokens (device pointers, stream-ordered), in launches
 // of at most kDecodeMaxTokens tokens.
 int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uint32_t* idx, float* gates,
@@ -315,8 +347,10 @@ int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uin
         if (!g.pf_scratch.ensure(need)) return CZ_EALLOC;
         if (ensure_sync()) return CZ_EALLOC;
         const float* res = residual && (!L.ep || g.ep_rank == 0) ? residual : nullptr;
+        cudaEvent_t* ev = timer_take(kTimerPrefillGateUp, 2);
+        if (ev) g.tm_kind[g.tm_n - 1] = kTimerPrefillDown;
         int rc = cz::prefill_run(L.pf, x, x_bf16, T, rms_w, eps, res, out, idx, gates, g.pf_scratch.p,
-                                 g.pf_scratch.cap, g.sync + 1, g.num_sms, st);
+                                 g.pf_scratch.cap, g.sync + 1, g.num_sms, st, ev);
         if (rc) return rc;
         if (L.ep && g.ep_world > 1) {
             if (!g.ep_comm) return CZ_ENCCL;
@@ -344,8 +378,11 @@ int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uin
         p.out = out + (size_t)t0 * L.d.hidden;
         p.topk_idx = idx ? idx + (size_t)t0 * L.d.topk : nullptr;
         p.topk_gates = gates ? gates + (size_t)t0 * L.d.topk : nullptr;
+        cudaEvent_t* ev = timer_take(kTimerDecode, 1);
+        if (ev && !cz::record_timer_event(ev[0], st)) return CZ_ELAUNCH;
         rc = cz::decode_launch(p, g.num_sms, st);
         if (rc) return rc;
+        if (ev && !cz::record_timer_event(ev[1], st)) return CZ_ELAUNCH;
     }
     if (L.ep && g.ep_world > 1) {
         if (!g.ep_comm) return CZ_ENCCL;
@@ -756,6 +793,52 @@ CZ_EXPORT int colizig_cuda_moe_check(void* stream) {
     if (!g.inited) return CZ_EARGS;
     cudaSetDevice(g.dev);
     return check_device_error(stream ? reinterpret_cast<cudaStream_t>(stream) : g.stream);
+}
+
+// Kernel timer for benchmarks (not in the reference surface).  capacity > 0
+// (re)arms it with room for `capacity` launch pairs and clears what it held;
+// capacity 0 turns it off.  While armed, colizig_cuda_moe_forward* record a CUDA
+// event pair around every decode kernel launch and around each of the two grouped
+// GEMM launches of a prefill forward, so that the launches' own device time can be
+// read back, also from inside a captured CUDA graph.
+CZ_EXPORT int colizig_cuda_kernel_timer(int capacity) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return CZ_EARGS;
+    if (capacity < 0 || capacity > (1 << 20)) return CZ_EARGS;
+    cudaSetDevice(g.dev);
+    timer_free();
+    g.tm_ev.resize((size_t)capacity * 2, nullptr);
+    g.tm_kind.assign((size_t)capacity, 0);
+    for (cudaEvent_t& e : g.tm_ev)
+        if (cudaEventCreate(&e) != cudaSuccess) {
+            e = nullptr;
+            timer_free();
+            return CZ_EALLOC;
+        }
+    return CZ_OK;
+}
+
+// Reads the timer: for up to max_n recorded pairs, their kind (1 decode kernel,
+// 2 prefill gate/up GEMM, 3 prefill down GEMM) and device time in ms.  Waits for
+// the recorded events.  Returns the number of pairs written, or a negative
+// result code (CZ_EALLOC when some pairs were dropped because the timer was full).
+CZ_EXPORT int colizig_cuda_kernel_timer_read(int* kinds, float* ms, int max_n) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return CZ_EARGS;
+    if (max_n < 0 || (max_n && (!kinds || !ms))) return CZ_EARGS;
+    if (g.tm_overflow) return CZ_EALLOC;
+    cudaSetDevice(g.dev);
+    const int n = g.tm_n < max_n ? g.tm_n : max_n;
+    for (int i = 0; i < n; ++i) {
+        if (cudaEventSynchronize(g.tm_ev[2 * i + 1]) != cudaSuccess) return CZ_ED2H;
+        float t = 0.f;
+        if (cudaEventElapsedTime(&t, g.tm_ev[2 * i], g.tm_ev[2 * i + 1]) != cudaSuccess) return CZ_ED2H;
+        kinds[i] = g.tm_kind[i];
+        ms[i] = t;
+    }
+    return n;
 }
 
 CZ_EXPORT int colizig_cuda_debug_expf(const float* x_dev, float* y_dev, size_t n) {

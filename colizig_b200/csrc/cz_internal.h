@@ -94,9 +94,20 @@ bool make_sw128_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64
 // (rms_w: x = rms(x, rms_w), eps).  topk_idx / topk_gates nullable.  err = the
 // device error word.  Stream-ordered; the scratch stays in use until the
 // stream reaches the end of the call.
+// Records a timer event on `st`: an external event-record node when the stream
+// is being captured into a CUDA graph (so every replay re-records it), a plain
+// record otherwise.
+inline bool record_timer_event(cudaEvent_t ev, cudaStream_t st) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) return false;
+    return (cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal)
+                                                : cudaEventRecord(ev, st)) == cudaSuccess;
+}
+
 int prefill_run(const PrefillLayer& L, const void* x, int x_bf16, int T, const float* rms_w, float eps,
                 const float* residual, float* out, uint32_t* topk_idx, float* topk_gates, void* scratch,
-                size_t scratch_bytes, uint32_t* err, int num_sms, cudaStream_t st);
+                size_t scratch_bytes, uint32_t* err, int num_sms, cudaStream_t st,
+                cudaEvent_t* gemm_ev = nullptr);
 
 // Legacy per-matrix block-FP8 matmul (device pointers, stream-ordered).
 int fp8_matmul_launch(float* y, const float* x, const uint8_t* w, const float* scales, int S, int I, int O,

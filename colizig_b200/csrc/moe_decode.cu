@@ -24,14 +24,17 @@
 //      the GPUs' outputs are summed by one all-reduce after the launch.
 //   C  chunks.  Each group's intermediate rows are cut into chunks of 16; the
 //      flattened chunk list is split evenly over the CTAs (split-K: a chunk's
-//      gate, up AND down work stays on one SM, so h never leaves it).  A chunk
-//      is a sequence of ring stages: gate rows [r0, r0+16) x a 2048-column slab
-//      of H (one bulk copy per row), the same for up, then down columns
-//      [r0, r0+16) of 2048 output rows (2D TMA boxes of 16 x 256).  The
-//      consumer warps split every stage: K slabs by 128-column blocks for
-//      gate and up together, 16-row output tiles for down.  The weight copies
-//      carry an L2 evict-first hint: streamed once, they should not push the
-//      kernel's code, the router rows or the scratch out of L2.
+//      gate, up AND down work stays on one SM, so h never leaves it).  Pass 1
+//      streams, per chunk, gate rows [r0, r0+16) x 2048-column slabs of H (one
+//      bulk copy per row) and the same for up; the consumer warps split the
+//      K blocks, reduce, and keep h = silu(gate)*up of every chunk in shared
+//      memory.  Pass 2 streams, per slab of output rows, the down columns
+//      [r0, r0+16) of every chunk of the CTA (2D TMA boxes of 16 x 256); each
+//      warp owns 16-row output tiles and accumulates all of the CTA's chunks
+//      into registers, then writes its rows of the CTA's partial [T][H] to
+//      global scratch once.  The weight copies carry an L2 evict-first hint:
+//      streamed once, they should not push the kernel's code, the router rows
+//      or the scratch out of L2.
 //
 // Arithmetic: mma.sync m16n8k32 E4M3 x E4M3 -> f32, which forms and sums the
 // exact products (checked on B200 to round like f32).  The weights enter as
@@ -40,11 +43,10 @@
 // every term a column of the MMA; a bf16 token is exact in 2 terms, an f32
 // token is kept to 12 bits in 3; h (per chunk and pair, scaled the same way)
 // to 16 bits in 4 terms.  Each 128-column block's sum is multiplied by its
-// 128x128 scale in f32.  Down sums go to a per-CTA [T][H] accumulator in
-// shared memory (every output row owned by one warp, chunks in a fixed order);
-// each CTA writes it out once, and after a grid-wide arrive counter CTA c adds
-// the G partial rows of its slice of out in a fixed order: deterministic, no
-// float atomics.
+// 128x128 scale in f32.  Down sums accumulate in registers (every output row
+// owned by one warp, chunks in a fixed order); each CTA writes its partial
+// [T][H] once, and after a grid-wide arrive counter CTA c adds the G partial
+// rows of its slice of out in a fixed order: deterministic, no float atomics.
 //
 // Every wait is bounded; a CTA that gives up sets a bit in the device error
 // word, stops issuing work (draining its in-flight copies) and the host

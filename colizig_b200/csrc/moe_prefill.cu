@@ -7,8 +7,9 @@
 //
 // Kernels, in stream order:
 //   rms       stack mode only: x = rms(h, w) (rmsnorm.zig:32-40)
-//   route     router logits in dotF32's exact f32 order (matmul.zig:60-82),
-//             softmax/top-k, per-token max |x|
+//   logits    router logits in dotF32's exact f32 order (matmul.zig:60-82) as
+//             a register-tiled CUDA-core GEMM (32 router rows x 16 tokens per CTA)
+//   topk      one warp per token: softmax/top-k (bit-exact), per-token max |x|
 //   count /   stable counting sort of the pairs by expert: positions padded to
 //   place     64 per group, the GEMM tile lists (prefix sums over groups)
 //   tokpos    each token's positions in ascending expert order (combine order)
@@ -1076,7 +1077,7 @@ static int launch_gemm(const pf::GemmParams& gp, int num_sms, cudaStream_t st) {
 
 int prefill_run(const PrefillLayer& L, const void* x, int x_bf16, int T, const float* rms_w, float eps,
                 const float* residual, float* out, uint32_t* topk_idx, float* topk_gates, void* scratch,
-                size_t scratch_bytes, uint32_t* err, int num_sms, cudaStream_t st) {
+                size_t scratch_bytes, uint32_t* err, int num_sms, cudaStream_t st, cudaEvent_t* gemm_ev) {
     using namespace pf;
     const int H = L.H, E = L.E, K = L.K, I = L.I, SI = L.SI;
     if (!prefill_supported(H, E, K, I, SI) || T < 1) return CZ_ESHAPE;
@@ -1185,8 +1186,10 @@ int prefill_run(const PrefillLayer& L, const void* x, int x_bf16, int T, const f
         q.ssc = L.sh_gate_s;
         q.ssc2 = L.sh_up_s;
         q.tpre = s.tpre_gu;
+        if (gemm_ev && !record_timer_event(gemm_ev[0], st)) return CZ_ELAUNCH;
         const int rc = JX == 2 ? launch_gemm<true, 2>(q, num_sms, st) : launch_gemm<true, 3>(q, num_sms, st);
         if (rc) return rc;
+        if (gemm_ev && !record_timer_event(gemm_ev[1], st)) return CZ_ELAUNCH;
     }
     // down
     {
@@ -1199,8 +1202,10 @@ int prefill_run(const PrefillLayer& L, const void* x, int x_bf16, int T, const f
         q.sc = L.down_s;
         q.ssc = L.sh_down_s;
         q.tpre = s.tpre_dn;
+        if (gemm_ev && !record_timer_event(gemm_ev[2], st)) return CZ_ELAUNCH;
         const int rc = launch_gemm<false, 3>(q, num_sms, st);
         if (rc) return rc;
+        if (gemm_ev && !record_timer_event(gemm_ev[3], st)) return CZ_ELAUNCH;
     }
     // combine
     {

@@ -229,3 +229,24 @@ def check(stream=None) -> None:
     """Raise if a device-side wait of an earlier asynchronous call gave up."""
     h = None if stream is None else _stream_handle(stream)
     _abi.check("colizig_cuda_moe_check", _abi.load().colizig_cuda_moe_check(h))
+
+
+TIMER_DECODE, TIMER_PREFILL_GATE_UP, TIMER_PREFILL_DOWN = 1, 2, 3
+
+
+def kernel_timer(capacity: int) -> None:
+    """Arm (capacity > 0 launch pairs) or disarm (0) the library's kernel timer:
+    CUDA event pairs around every decode kernel launch and around the two grouped
+    GEMM launches of each prefill forward, captured CUDA graphs included."""
+    _abi.check("colizig_cuda_kernel_timer", _abi.load().colizig_cuda_kernel_timer(int(capacity)))
+
+
+def kernel_timer_read(max_n: int = 1 << 16) -> list:
+    """[(kind, ms)] of the launch pairs recorded since the timer was armed (waits
+    for them).  kind is TIMER_DECODE, TIMER_PREFILL_GATE_UP or TIMER_PREFILL_DOWN."""
+    kinds = (ctypes.c_int * max_n)()
+    ms = (ctypes.c_float * max_n)()
+    n = _abi.load().colizig_cuda_kernel_timer_read(ctypes.addressof(kinds), ctypes.addressof(ms), max_n)
+    if n < 0:
+        _abi.check("colizig_cuda_kernel_timer_read", n)
+    return [(kinds[i], ms[i]) for i in range(n)]

@@ -174,6 +174,20 @@ int colizig_cuda_moe_check(void* stream);
 int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, int x_dtype, int T, float* out,
                                      uint32_t* topk_idx, float* topk_gates, uint32_t* status, void* stream);
 
+/* No counterpart in the reference: a kernel timer for benchmarks.
+ * colizig_cuda_kernel_timer(capacity > 0) arms it with room for `capacity`
+ * launch pairs (and clears it); capacity 0 turns it off.  While armed, every
+ * MoE forward records a CUDA event pair around each decode kernel launch and
+ * around each of the two grouped GEMM launches of a prefill forward; the
+ * records are external event nodes when the forward is captured into a CUDA
+ * graph, so graph replays are timed too.  colizig_cuda_kernel_timer_read waits
+ * for the events and writes, per recorded pair, its kind (1 decode kernel,
+ * 2 prefill gate/up GEMM, 3 prefill down GEMM) and device time in ms; it
+ * returns the number of pairs written, or -2 when pairs were dropped because
+ * the timer was full. */
+int colizig_cuda_kernel_timer(int capacity);
+int colizig_cuda_kernel_timer_read(int* kinds, float* ms, int max_n);
+
 /* Diagnostics used by the parity tests: the router's exp (the reference's
  * @exp(f32) restated in double precision) over n device floats. */
 int colizig_cuda_debug_expf(const float* x_dev, float* y_dev, size_t n);

@@ -72,3 +72,29 @@ def test_prefill_agrees_with_decode_kernel_c2_t512():
         assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) <= OUT_TOL
     finally:
         L.unregister()
+
+
+def test_kernel_timer_records_decode_and_prefill_gemms():
+    """The benchmark timer: one decode launch (T=3) gives one kind-1 pair, one
+    prefill forward (T=64) a kind-2 and a kind-3 pair, all with positive device
+    time; a full timer reports the dropped pairs instead of wrapping."""
+    d = synth.CONFIGS["c1"]
+    w = synth.make_layer(d, seed=5, device="cuda")
+    L = moe.Layer.from_weights(801, d, w)
+    try:
+        moe.kernel_timer(3)
+        moe.forward(L, synth.make_tokens(3, d.hidden, 1, device="cuda"))
+        moe.forward(L, synth.make_tokens(64, d.hidden, 2, device="cuda"))
+        rec = moe.kernel_timer_read()
+        assert [k for k, _ in rec] == [moe.TIMER_DECODE, moe.TIMER_PREFILL_GATE_UP, moe.TIMER_PREFILL_DOWN]
+        assert all(ms > 0 for _, ms in rec)
+        moe.forward(L, synth.make_tokens(3, d.hidden, 3, device="cuda"))  # no room left
+        with pytest.raises(cz.ColizigError):
+            moe.kernel_timer_read()
+        moe.kernel_timer(0)
+        moe.forward(L, synth.make_tokens(3, d.hidden, 4, device="cuda"))
+        assert moe.kernel_timer_read() == []
+        moe.check()
+    finally:
+        moe.kernel_timer(0)
+        L.unregister()
