@@ -94,6 +94,8 @@ struct MoeLayer {
     cz::PrefillLayer pf{};      // the prefill kernels' view (tensor maps with 128-byte swizzle)
     bool pf_ok = false;
     CUtensorMap sh_down_map{};  // TMA view of sh_down_w: u8 [H][SI]
+    CUtensorMap gate_map{}, up_map{}, sh_gate_map{}, sh_up_map{};  // decode views of the gate/up weights
+    int gu_kb = 0, dn_grp = 0, sh_dn_grp = 0;  // depth of those boxes (0 = 2D maps)
 };
 
 struct Ctx {
@@ -305,6 +307,14 @@ cz::DecodeParams make_params(const MoeLayer& L) {
     p.shared_here = L.shared_here;
     p.down_map = L.down_map;
     p.sh_down_map = L.shared_here ? L.sh_down_map : L.down_map;
+    p.gate_map = L.gate_map;
+    p.up_map = L.up_map;
+    p.sh_gate_map = L.shared_here ? L.sh_gate_map : L.gate_map;
+    p.sh_up_map = L.shared_here ? L.sh_up_map : L.up_map;
+    p.gu3d = L.gu_kb > 0;
+    p.gu_kb = L.gu_kb;
+    p.dn_grp = L.dn_grp;
+    p.sh_dn_grp = L.sh_dn_grp;
     p.logits = g.logits.as<float>();
     p.partial = g.partial.as<float>();
     p.sync = g.sync;
@@ -641,8 +651,25 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
                            cudaSuccess)
                 rc = CZ_EH2D;
     }
-    if (!rc && E && !cz::make_down_map(&L.down_map, L.down_w, E * H, I)) rc = CZ_ELAUNCH;
-    if (!rc && shared_here && !cz::make_down_map(&L.sh_down_map, L.sh_down_w, H, SI)) rc = CZ_ELAUNCH;
+    // decode tensor maps; every map of a layer gets the same box depth
+    if (!rc && E) {
+        int kb = 0, kb2 = 0, grp = 0;
+        if (!cz::make_down_map(&L.down_map, L.down_w, E * H, I, (int)H, &grp) ||
+            !cz::make_gu_map(&L.gate_map, L.gate_w, E * I, H, &kb) || !cz::make_gu_map(&L.up_map, L.up_w, E * I, H, &kb2) ||
+            kb != kb2)
+            rc = CZ_ELAUNCH;
+        L.gu_kb = kb;
+        L.dn_grp = grp;
+    }
+    if (!rc && shared_here) {
+        int kb = 0, kb2 = 0, grp = 0;
+        if (!cz::make_down_map(&L.sh_down_map, L.sh_down_w, H, SI, (int)H, &grp) ||
+            !cz::make_gu_map(&L.sh_gate_map, L.sh_gate_w, SI, H, &kb) ||
+            !cz::make_gu_map(&L.sh_up_map, L.sh_up_w, SI, H, &kb2) || kb != kb2 || (E && kb != L.gu_kb))
+            rc = CZ_ELAUNCH;
+        L.gu_kb = kb;
+        L.sh_dn_grp = grp;
+    }
     if (!rc && E && cz::prefill_supported((int)H, (int)d.experts, (int)d.topk, (int)I, (int)SI)) {
         cz::PrefillLayer& P = L.pf;
         bool ok = cz::make_sw128_map(&P.gate_map, L.gate_w, E * I, H, 128) &&

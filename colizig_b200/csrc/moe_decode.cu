@@ -61,16 +61,19 @@
 namespace cz {
 
 constexpr int NCW = 8;                    // consumer warps (2 per SM sub-partition)
-constexpr int NTHREADS = (NCW + 1) * 32;  // + 1 producer warp
+constexpr int PW = NCW;                   // producer warp
+constexpr int HW = NCW + 1;               // h warp
+constexpr int NWARPS = NCW + 2;
+constexpr int NTHREADS = NWARPS * 32;
 constexpr int CR = 16;                    // intermediate (h) rows per chunk
 constexpr int KS = 2048;                  // columns of a gate/up stage slab
 constexpr int OS = 2048;                  // output rows of a down stage
-constexpr int WPAD = 64;                  // row stride = 64 mod 128: rows g, g+1 of a fragment hit disjoint banks
-constexpr int GU_BYTES = CR * (KS + WPAD);
+constexpr int GU_BYTES = CR * KS;         // a gate/up stage: [K block][16 rows][128 B], 128-byte swizzled
 constexpr int SC_BYTES = 2048;            // block scales carried with every stage
-constexpr int SLOT_BYTES = 35 * 1024;     // >= GU_BYTES + SC_BYTES; a down stage uses OS * 16
-constexpr int NSLOT = 4;
-constexpr int RING_BYTES = NSLOT * SLOT_BYTES;
+constexpr int SLOT_BYTES = 34 * 1024;     // >= GU_BYTES + SC_BYTES; a down stage uses OS * 16
+constexpr int NSLOT = 4;                  // ring slots at least (more when shared memory allows)
+constexpr int MAXSLOT = 6;
+constexpr int RING_BYTES = NSLOT * SLOT_BYTES;  // the smallest ring (also stages phase R)
 constexpr int BOX_ROWS = 256;             // down-weight TMA box: 16 bytes x 256 rows
 constexpr int JH = 4;                     // E4M3 terms of h
 constexpr int DB = 4;                     // down tiles per batch of one warp
@@ -89,8 +92,8 @@ static_assert(SLOT_BYTES % 1024 == 0, "TMA destinations stay 1024-aligned");
 
 // Small shared state (after the large regions).
 struct __align__(16) DecodeMisc {
-    uint64_t full[NSLOT];
-    uint64_t empty[NSLOT];
+    uint64_t full[MAXSLOT];
+    uint64_t empty[MAXSLOT];
     uint64_t rbar;
     uint64_t lbar;
     int abort;
@@ -98,7 +101,7 @@ struct __align__(16) DecodeMisc {
     uint32_t xmax[MAXT];  // max |x_t| (f32 bits)
     int xexp[MAXT];       // s per token (terms hold x_t * 2^s)
     float xscale[MAXT];   // 2^-s per token
-    float sdcol[64];      // down scales of the current chunk's column block, one per 128 output rows
+    float sdcol[2][64];   // down scales of a chunk's column block, one per 128 output rows (chunk parity)
     float hmax[MAXT][64]; // max over chunks of |gate * h * down scale| per (token, 128-row block)
     int hexp[MAXT][64];   // its power-of-two prescale
     int pe[MAXP];         // expert of pair p = t*K + z (shared: p = T*K + t -> E)
@@ -113,6 +116,7 @@ struct __align__(16) DecodeMisc {
 // Shared-memory map of one launch: [ring][x terms][red][h of every chunk][misc].
 struct Carve {
     int JX, CS;  // E4M3 terms per token; byte stride of one term column
+    int ns;      // ring slots
     uint32_t xterm, red, hterm, misc, total;
 };
 
@@ -120,11 +124,16 @@ __host__ __device__ inline Carve carve(int T, int H, int x_bf16) {
     Carve c;
     c.JX = x_bf16 ? 2 : 3;
     c.CS = ((H + 127) & ~127) + 64;  // column stride = 64 mod 128: lanes of 2 columns hit disjoint banks
-    uint32_t off = RING_BYTES;
+    // the rest of the map decides how many slots fit
+    const uint32_t rest = (((uint32_t)(T * c.JX * c.CS) + 127u) & ~127u) + 2 * NCW * 2 * 16 * 16 * 4 +
+                          MAXCH * 16 * 16 + (((uint32_t)sizeof(DecodeMisc) + 127u) & ~127u);
+    const int fit = ((int)SMEM_LIMIT - 1024 - (int)rest) / SLOT_BYTES;
+    c.ns = fit < NSLOT ? NSLOT : (fit > MAXSLOT ? MAXSLOT : fit);
+    uint32_t off = (uint32_t)c.ns * SLOT_BYTES;
     c.xterm = off;
     off += ((uint32_t)(T * c.JX * c.CS) + 127u) & ~127u;
     c.red = off;
-    off += NCW * 2 * 16 * 16 * 4;
+    off += 2 * NCW * 2 * 16 * 16 * 4;  // two chunks in flight: [chunk parity][warp][gate/up][16 x 16]
     c.hterm = off;
     off += MAXCH * 16 * 16;
     c.misc = off;
@@ -145,7 +154,9 @@ struct GroupW {
     const float *gs, *us, *ds;
     int inter;
     int down_row0;                // first row of this expert in its down tensor map
-    const CUtensorMap* dmap;
+    int gu_row0;                  // first row of this expert in its gate/up tensor maps
+    int dgrp;                     // down boxes: groups of 256 rows per box (0 = 2D boxes)
+    const CUtensorMap *dmap, *gmap, *umap;
 };
 
 __device__ __forceinline__ GroupW group_w(const DecodeParams& p, int e) {
@@ -158,7 +169,11 @@ __device__ __forceinline__ GroupW group_w(const DecodeParams& p, int e) {
         g.us = p.sh_up_s;
         g.ds = p.sh_down_s;
         g.down_row0 = 0;
+        g.gu_row0 = 0;
+        g.dgrp = p.sh_dn_grp;
         g.dmap = &p.sh_down_map;
+        g.gmap = &p.sh_gate_map;
+        g.umap = &p.sh_up_map;
     } else {
         g.inter = p.I;
         e -= p.e_lo;  // experts are stacked from the first one held here
@@ -170,7 +185,11 @@ __device__ __forceinline__ GroupW group_w(const DecodeParams& p, int e) {
         g.us = p.up_s + (size_t)e * ssz;
         g.ds = p.down_s + (size_t)e * cz_nblk(p.H) * cz_nbp(p.I);
         g.down_row0 = e * p.H;
+        g.gu_row0 = e * p.I;
+        g.dgrp = p.dn_grp;
         g.dmap = &p.down_map;
+        g.gmap = &p.gate_map;
+        g.umap = &p.up_map;
     }
     return g;
 }
@@ -202,6 +221,16 @@ __device__ __forceinline__ void tma_box_g2s(void* dst, const CUtensorMap* map, i
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
         "{%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
+// One 3D TMA box of a u8 tensor map -> shared memory (no multicast).
+__device__ __forceinline__ void tma_box3_g2s(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar,
+                                             uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
 }
 
@@ -367,7 +396,13 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, Decode
     return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, &s.abort));
 }
 
-__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory"); }
+// Named barriers between the consumer warps and the h warp (288 threads each):
+// RED_FULL(b): the consumers' partial gate/up sums of a chunk of parity b are in
+// red[b]; RED_FREE(b): the h warp has read them; H_DONE: h, its maxima and
+// exponents of every chunk are in shared memory.
+constexpr int BAR_RED_FULL = 2, BAR_RED_FREE = 4, BAR_H_DONE = 6;
+__device__ __forceinline__ void bar_sync_n(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "n"((NCW + 1) * 32) : "memory"); }
+__device__ __forceinline__ void bar_arrive_n(int id) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "n"((NCW + 1) * 32) : "memory"); }
 
 __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_constant__ DecodeParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -394,7 +429,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     uint32_t* reg = region(p.sync, seq & 1);
     if (c == 0 && tid < kSyncRegionWords) region(p.sync, (seq & 1) ^ 1)[tid] = 0u;
     if (tid == 0) {
-        for (int i = 0; i < NSLOT; ++i) {
+        for (int i = 0; i < cv.ns; ++i) {
             mbar_init(&s.full[i], 1);
             mbar_init(&s.empty[i], NCW);
         }
@@ -433,7 +468,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         // stack mode: x = rms(h, w) in place (rmsnorm.zig:32-40): f64 sum of
         // squares, mean rounded to f32, r = 1/sqrt(mean + eps), v*r*w.
         float* xf = reinterpret_cast<float*>(xs);
-        for (int t = warp; t < T; t += NCW + 1) {
+        for (int t = warp; t < T; t += NWARPS) {
             double ss = 0.0;
             for (int i = lane; i < H; i += 32) {
                 const double v = (double)xf[(size_t)t * H + i];
@@ -458,7 +493,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                    : reinterpret_cast<const float*>(xs)[k];
     };
     if (!s.abort) {
-        for (int it = warp; it < nrows * T; it += NCW + 1) {
+        for (int it = warp; it < nrows * T; it += NWARPS) {
             const int r = it / T, t = it - r * T;
             const float v = router_dot(rows + (size_t)r * H, xs + (size_t)t * H * (xbf ? 2 : 4), H, xbf, lane);
             if (lane == 0) p.logits[(size_t)t * LS + row_lo + r] = v;
@@ -516,7 +551,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     if (!s.abort && !mbar_wait_bounded(&s.lbar, 0, &s.abort) && lane == 0) set_error(err, s, CZ_DERR_FULL_WAIT);
     __syncthreads();
     if (!s.abort) {
-        for (int t = warp; t < T; t += NCW + 1) {
+        for (int t = warp; t < T; t += NWARPS) {
             const float* lg = reinterpret_cast<const float*>(ring) + (size_t)t * LS;
             if (E <= 128)
                 route_token<4>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates, c == 0);
@@ -585,22 +620,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     // ---------------- phase C: this CTA's chunks ----------------
     {
         const int NC = s.NC;
+        const int NS = cv.ns;
         const int ch_lo = (int)((long long)c * NC / G), ch_hi = (int)((long long)(c + 1) * NC / G);
         const int nks = (H + KS - 1) / KS;     // gate (and up) stages per chunk
         const int nbpH = cz_nbp(H);
+        const int nkbH = cz_nblk(H);           // 128-column blocks of H
         // down: tiles per warp (each warp's accumulators live in registers across
         // all chunks) and the output rows of one slab
         const int TPW = (T * JH <= 8) ? 16 : 8;
         const int nmD = (T * JH + 7) >> 3;
         const int OSr = TPW * 16 * NCW;
 
-        if (warp == NCW) {
+        if (warp == PW) {
             // ---------------- producer (one thread) ----------------
             if (lane == 0) {
                 fence_proxy_async_smem();  // generic reads of the ring (logits) precede the async writes
                 const uint64_t pol = l2_evict_first_policy();
                 int si = 0;
-                // wait until slot si % NSLOT is free again (bounded); false = stop
+                // wait until slot si % NS is free again (bounded); false = stop
                 auto acquire_slot = [&](int slot, int round) -> bool {
                     if (round == 0) return true;
                     bool ok = false;
@@ -620,21 +657,27 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                         const int r0 = (ch - s.g_chunk0[u]) * CR;
                         const int nbpI = cz_nbp(gw.inter);
                         for (int st = 0; st < 2 * nks && !s.abort; ++st, ++si) {
-                            const int slot = si % NSLOT;
-                            if (!acquire_slot(slot, si / NSLOT)) break;
+                            const int slot = si % NS;
+                            if (!acquire_slot(slot, si / NS)) break;
                             uint8_t* dst = ring + (size_t)slot * SLOT_BYTES;
                             float* sdst = reinterpret_cast<float*>(dst + GU_BYTES);
-                            // slab st/2: gate (st even) or up (st odd) rows [r0, r0+16), columns [k0, k0+L)
+                            // slab st/2: gate (st even) or up (st odd) rows [r0, r0+16), column
+                            // blocks [kb0, kb0 + nkbs) as [block][row][128 B] (128-byte swizzle)
                             const bool up = st & 1;
-                            const int k0 = (st >> 1) * KS, L = min(KS, H - k0);
-                            const uint8_t* src = (up ? gw.uw : gw.gw) + (size_t)r0 * H + k0;
+                            const int kb0 = (st >> 1) * (KS / 128), nkbs = min(KS / 128, nkbH - kb0);
+                            const CUtensorMap* map = up ? gw.umap : gw.gmap;
                             const float* ssrc = (up ? gw.us : gw.gs) + (size_t)(r0 >> 7) * nbpH;
                             // the first up slab also carries the expert's down-scale table
                             const uint32_t dsb = st == 1 ? (uint32_t)(cz_nblk(H) * nbpI * 4) : 0u;
-                            mbar_arrive_expect_tx(&s.full[slot], (uint32_t)(CR * L + nbpH * 4) + dsb);
-                            for (int r = 0; r < CR; ++r)
-                                bulk_g2s_hint(dst + (size_t)r * (KS + WPAD), src + (size_t)r * H, (uint32_t)L,
-                                              &s.full[slot], pol);
+                            const uint32_t wb = (uint32_t)(CR * 128) * (uint32_t)(p.gu3d ? p.gu_kb : nkbs);
+                            mbar_arrive_expect_tx(&s.full[slot], wb + (uint32_t)(nbpH * 4) + dsb);
+                            if (p.gu3d) {
+                                tma_box3_g2s(dst, map, 0, gw.gu_row0 + r0, kb0, &s.full[slot], pol);
+                            } else {
+                                for (int kb = 0; kb < nkbs; ++kb)
+                                    tma_box_g2s(dst + (size_t)kb * CR * 128, map, (kb0 + kb) * 128, gw.gu_row0 + r0,
+                                                &s.full[slot], pol);
+                            }
                             bulk_g2s(sdst, ssrc, (uint32_t)nbpH * 4u, &s.full[slot]);
                             if (dsb) bulk_g2s(sdst + nbpH, gw.ds, dsb, &s.full[slot]);
                         }
@@ -651,38 +694,113 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                         const GroupW gw = group_w(p, s.g_expert[u]);
                         const int r0 = (ch - s.g_chunk0[u]) * CR;
                         const int nbpI = cz_nbp(gw.inter);
-                        const int slot = si % NSLOT;
-                        if (!acquire_slot(slot, si / NSLOT)) break;
+                        const int slot = si % NS;
+                        if (!acquire_slot(slot, si / NS)) break;
                         uint8_t* dst = ring + (size_t)slot * SLOT_BYTES;
                         float* sdst = reinterpret_cast<float*>(dst + GU_BYTES);
-                        mbar_arrive_expect_tx(&s.full[slot], (uint32_t)(nbox * BOX_ROWS * 16 + nob * nbpI * 4));
-                        for (int b = 0; b < nbox; ++b)
-                            tma_box_g2s(dst + (size_t)b * BOX_ROWS * 16, gw.dmap, r0, gw.down_row0 + o0 + b * BOX_ROWS,
-                                        &s.full[slot], pol);
+                        if (gw.dgrp) {
+                            // boxes of dgrp x 256 rows (3D map: [group][256 rows][cols])
+                            const int rows_b = BOX_ROWS * gw.dgrp, nb3 = (OSl + rows_b - 1) / rows_b;
+                            mbar_arrive_expect_tx(&s.full[slot], (uint32_t)(nb3 * rows_b * 16 + nob * nbpI * 4));
+                            for (int b = 0; b < nb3; ++b)
+                                tma_box3_g2s(dst + (size_t)b * rows_b * 16, gw.dmap, r0, 0,
+                                             (gw.down_row0 + o0) / BOX_ROWS + b * gw.dgrp, &s.full[slot], pol);
+                        } else {
+                            mbar_arrive_expect_tx(&s.full[slot], (uint32_t)(nbox * BOX_ROWS * 16 + nob * nbpI * 4));
+                            for (int b = 0; b < nbox; ++b)
+                                tma_box_g2s(dst + (size_t)b * BOX_ROWS * 16, gw.dmap, r0,
+                                            gw.down_row0 + o0 + b * BOX_ROWS, &s.full[slot], pol);
+                        }
                         bulk_g2s(sdst, gw.ds + (size_t)ob0 * nbpI, (uint32_t)(nob * nbpI * 4), &s.full[slot]);
                     }
                 }
                 // drain: no copy may land after this CTA exits (waiting on a phase
                 // that already completed returns at once)
-                for (int k = max(0, si - NSLOT); k < si; ++k) {
+                for (int k = max(0, si - NS); k < si; ++k) {
                     bool ok = false;
                     for (uint32_t it = 0; it < CZ_SPIN_LIMIT && !ok; ++it) {
-                        ok = mbar_try_wait(&s.full[k % NSLOT], (k / NSLOT) & 1);
+                        ok = mbar_try_wait(&s.full[k % NS], (k / NS) & 1);
                         if (!ok) __nanosleep(64);
                     }
                     if (!ok) atomicOr(err, CZ_DERR_DRAIN_WAIT);
                 }
             }
             __syncwarp();
+        } else if (warp == HW) {
+            // ---------------- h warp ----------------
+            // Per chunk, once the consumers' partial gate/up sums are in red[b]:
+            // hw = gate * silu(g) * u per (row r, token tk) (0 for tokens not routed
+            // to the chunk's expert) and the running max of |hw * down scale| per
+            // (token, 128-row output block).  Runs beside the next chunk's MMAs.
+            const int nch = ch_hi - ch_lo;
+            int u = 0;
+            for (int ch = ch_lo; ch < ch_hi; ++ch) {
+                while (s.g_chunk0[u + 1] <= ch) ++u;
+                const int ci = ch - ch_lo, b = ci & 1;
+                const int np = s.g_npairs[u];
+                const int* pairs = s.order + s.g_pair0[u];
+                bar_sync_n(BAR_RED_FULL + b);
+                const float* rb = red + b * (NCW * 2 * 256);
+#pragma unroll 1
+                for (int half = 0; half < (T + 1) / 2; ++half) {
+                    const int tk = 2 * half + (lane >> 4), r = lane & 15;
+                    int q = -1;
+                    for (int qq = 0; qq < np; ++qq)
+                        if (pair_token(pairs[qq], T, K) == tk) q = qq;
+                    float hw = 0.0f;
+                    if (q >= 0 && !s.abort) {
+                        float gs = 0.0f, us = 0.0f;
+                        const float* rg = rb + r * 16 + q * cv.JX;
+                        float gv[NCW][3], uv[NCW][3];
+#pragma unroll
+                        for (int w = 0; w < NCW; ++w)
+#pragma unroll
+                            for (int j = 0; j < 3; ++j) {
+                                gv[w][j] = j < cv.JX ? rg[w * 512 + j] : 0.0f;
+                                uv[w][j] = j < cv.JX ? rg[w * 512 + 256 + j] : 0.0f;
+                            }
+#pragma unroll
+                        for (int w = 0; w < NCW; ++w)
+#pragma unroll
+                            for (int j = 0; j < 3; ++j)
+                                if (j < cv.JX) {
+                                    gs += gv[w][j];
+                                    us += uv[w][j];
+                                }
+                        const float xsc = s.xscale[tk];
+                        hw = s.pg[pairs[q]] * (silu_fast(gs * xsc) * (us * xsc));
+                    }
+                    reinterpret_cast<float*>(hterm)[ci * 64 + r * 4 + tk] = hw;
+                    float mh = fabsf(hw);
+                    if (!(mh < 3.0e38f)) mh = 0.0f;
+#pragma unroll
+                    for (int o = 8; o > 0; o >>= 1) mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
+                    if (q >= 0)
+                        for (int ob = r; ob < cz_nblk(H); ob += 16)
+                            s.hmax[tk][ob] = fmaxf(s.hmax[tk][ob], mh * fabsf(s.sdcol[b][ob]));
+                }
+                __threadfence_block();
+                if (ci + 2 < nch) bar_arrive_n(BAR_RED_FREE + b);
+            }
+            // one power-of-two scale per (token, 128-row output block) for every chunk
+            __syncwarp();
+            for (int i = lane; i < MAXT * 64; i += 32) (&s.hexp[0][0])[i] = prescale_exp((&s.hmax[0][0])[i]);
+            __threadfence_block();
+            bar_arrive_n(BAR_H_DONE);
         } else {
             // ---------------- consumers ----------------
             const int g = lane >> 2, t = lane & 3;  // MMA fragment coordinates
+            // MMA rows g, g + 8 hold chunk rows rho, rho + 8: the two rows a quarter-warp
+            // reads then sit 4 apart in the swizzle pattern, so their chunks use disjoint banks
+            const int rho = (g >> 1) + 4 * (g & 1);
             int si = 0;
             int u = 0;
-            // ==== pass 1: gate/up and h of every chunk (h terms kept per chunk) ====
+            // ==== pass 1: gate/up of every chunk (h is formed by the h warp) ====
             for (int ch = ch_lo; ch < ch_hi; ++ch) {
                 while (s.g_chunk0[u + 1] <= ch) ++u;
-                const int ci = ch - ch_lo;
+                const int ci = ch - ch_lo, b = ci & 1;
+                // red[b] and sdcol[b] are reused: the h warp must be done with chunk ci-2
+                if (ci >= 2) bar_sync_n(BAR_RED_FREE + b);
                 const int np = s.g_npairs[u];
                 const int* pairs = s.order + s.g_pair0[u];
                 const int ib = ((ch - s.g_chunk0[u]) * CR) >> 7;  // the chunk's 128-column block of down
@@ -707,9 +825,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
 
                 // ---- gate / up: slab k is the stage pair (gate, up); both tiles in one pass ----
                 for (int kq = 0; kq < nks; ++kq, si += 2) {
-                    const int slg = si % NSLOT, slu = (si + 1) % NSLOT;
-                    bool ok = !s.abort && warp_wait(&s.full[slg], (si / NSLOT) & 1, s);
-                    ok = ok && warp_wait(&s.full[slu], ((si + 1) / NSLOT) & 1, s);
+                    const int slg = si % NS, slu = (si + 1) % NS;
+                    bool ok = !s.abort && warp_wait(&s.full[slg], (si / NS) & 1, s);
+                    ok = ok && warp_wait(&s.full[slu], ((si + 1) / NS) & 1, s);
                     if (!ok) {
                         if (lane == 0 && !s.abort) set_error(err, s, CZ_DERR_FULL_WAIT);
                         continue;
@@ -733,10 +851,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                             const bool kin = kk < L;
                             uint4 ga = make_uint4(0, 0, 0, 0), gb = ga, ua = ga, ub = ga, xb0 = ga, xb1 = ga;
                             if (kin) {
-                                ga = *reinterpret_cast<const uint4*>(stg + (size_t)g * (KS + WPAD) + kk);
-                                gb = *reinterpret_cast<const uint4*>(stg + (size_t)(g + 8) * (KS + WPAD) + kk);
-                                ua = *reinterpret_cast<const uint4*>(stu + (size_t)g * (KS + WPAD) + kk);
-                                ub = *reinterpret_cast<const uint4*>(stu + (size_t)(g + 8) * (KS + WPAD) + kk);
+                                // rows rho and rho + 8 of block kb; 16-byte chunk (kk/16)%8 is
+                                // stored at chunk ((kk/16)%8) ^ (rho%8)
+                                const uint32_t wo = (uint32_t)(kb * (CR * 128) + rho * 128) +
+                                                    (((uint32_t)(kk >> 4) & 7u) ^ (uint32_t)(rho & 7)) * 16u;
+                                ga = *reinterpret_cast<const uint4*>(stg + wo);
+                                gb = *reinterpret_cast<const uint4*>(stg + wo + 8 * 128);
+                                ua = *reinterpret_cast<const uint4*>(stu + wo);
+                                ub = *reinterpret_cast<const uint4*>(stu + wo + 8 * 128);
                                 if (xok[0]) xb0 = *reinterpret_cast<const uint4*>(xcol[0] + k0 + kk);
                                 if (nmA > 1 && xok[1]) xb1 = *reinterpret_cast<const uint4*>(xcol[1] + k0 + kk);
                             }
@@ -769,7 +891,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                         }
                     if (kq == 0 && warp == 0) {  // down scales of column block ib, from the up slab
                         const float* dtab = tu + nbpH;
-                        for (int ob = lane; ob < cz_nblk(H); ob += 32) s.sdcol[ob] = dtab[ob * nbpI + ib];
+                        for (int ob = lane; ob < cz_nblk(H); ob += 32) s.sdcol[b][ob] = dtab[ob * nbpI + ib];
                     }
                     __syncwarp();
                     if (lane == 0) {
@@ -778,62 +900,28 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                     }
                 }
 
-                // ---- h = silu(g) * u for the chunk's 16 rows x np pairs, then its E4M3 terms ----
-                // red[w][0 gate / 1 up][row][col]
+                // ---- this warp's partial gate/up sums of the chunk -> red[b] (h warp) ----
                 {
-                    float* rg = red + (warp * 2 + 0) * 256;
-                    float* ru = red + (warp * 2 + 1) * 256;
+                    float* rg = red + (b * NCW * 2 + warp * 2 + 0) * 256;
+                    float* ru = rg + 256;
 #pragma unroll
                     for (int m = 0; m < 2; ++m) {
                         const int col = 8 * m + 2 * t;
-                        rg[g * 16 + col] = accg[m][0];
-                        rg[g * 16 + col + 1] = accg[m][1];
-                        rg[(g + 8) * 16 + col] = accg[m][2];
-                        rg[(g + 8) * 16 + col + 1] = accg[m][3];
-                        ru[g * 16 + col] = accu[m][0];
-                        ru[g * 16 + col + 1] = accu[m][1];
-                        ru[(g + 8) * 16 + col] = accu[m][2];
-                        ru[(g + 8) * 16 + col + 1] = accu[m][3];
+                        rg[rho * 16 + col] = accg[m][0];
+                        rg[rho * 16 + col + 1] = accg[m][1];
+                        rg[(rho + 8) * 16 + col] = accg[m][2];
+                        rg[(rho + 8) * 16 + col + 1] = accg[m][3];
+                        ru[rho * 16 + col] = accu[m][0];
+                        ru[rho * 16 + col + 1] = accu[m][1];
+                        ru[(rho + 8) * 16 + col] = accu[m][2];
+                        ru[(rho + 8) * 16 + col + 1] = accu[m][3];
                     }
                 }
-                consumers_sync();
-                // hw = gate * silu(g) * u per (row r, token tk) of this chunk (0 for tokens
-                // not routed to its expert), and the running max of |hw * down scale| per
-                // (token, 128-row output block)
-                if (tid < 16 * MAXT) {
-                    const int tk = tid >> 4, r = tid & 15;
-                    int q = -1;
-                    for (int qq = 0; qq < np; ++qq)
-                        if (pair_token(pairs[qq], T, K) == tk) q = qq;
-                    float hw = 0.0f;
-                    if (q >= 0 && !s.abort) {
-                        float gs = 0.0f, us = 0.0f;
-                        const float* rg = red + r * 16 + q * cv.JX;
-#pragma unroll
-                        for (int w = 0; w < NCW; ++w)
-#pragma unroll
-                            for (int j = 0; j < 3; ++j)
-                                if (j < cv.JX) {
-                                    gs += rg[w * 512 + j];
-                                    us += rg[w * 512 + 256 + j];
-                                }
-                        const float xsc = s.xscale[tk];
-                        hw = s.pg[pairs[q]] * (silu_fast(gs * xsc) * (us * xsc));
-                    }
-                    reinterpret_cast<float*>(hterm)[ci * 64 + r * 4 + tk] = hw;
-                    float mh = fabsf(hw);
-                    if (!(mh < 3.0e38f)) mh = 0.0f;
-#pragma unroll
-                    for (int o = 8; o > 0; o >>= 1) mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
-                    if (q >= 0)
-                        for (int ob = r; ob < cz_nblk(H); ob += 16)
-                            s.hmax[tk][ob] = fmaxf(s.hmax[tk][ob], mh * fabsf(s.sdcol[ob]));
-                }
-                consumers_sync();
+                __threadfence_block();
+                bar_arrive_n(BAR_RED_FULL + b);
             }
-            // one power-of-two scale per (token, 128-row output block) for every chunk
-            for (int i = tid; i < MAXT * 64; i += NCW * 32) (&s.hexp[0][0])[i] = prescale_exp((&s.hmax[0][0])[i]);
-            consumers_sync();
+            // h, its maxima and the exponents of every chunk are ready
+            bar_sync_n(BAR_H_DONE);
 
             // ==== pass 2: per slab of OSr output rows, down of every chunk ====
             // Warp w owns tiles [w*TPW, (w+1)*TPW) of the slab; its accumulators stay in
@@ -850,60 +938,93 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                     for (int k = 0; k < 4; ++k) accd[i][k] = 0.0f;
                 const int tw0 = warp * TPW;  // first tile of this warp in the slab
                 const int obw = (o0 >> 7) + ((tw0 * 16) >> 7);  // first 128-row block of those tiles
+                // chunks in pairs: chunk A's 16 columns are the MMA's K values 0-15, chunk
+                // B's (the next stage) K values 16-31, so one MMA serves both
                 u = 0;
-                for (int ch = ch_lo; ch < ch_hi; ++ch, ++si) {
-                    while (s.g_chunk0[u + 1] <= ch) ++u;
-                    const int ci = ch - ch_lo;
-                    const int ib = ((ch - s.g_chunk0[u]) * CR) >> 7;
-                    const int nbpI = cz_nbp(s.g_expert[u] == E ? SI : Ir);
-                    const int slot = si % NSLOT;
-                    const bool ok = !s.abort && warp_wait(&s.full[slot], (si / NSLOT) & 1, s);
-                    if (!ok) {
-                        if (lane == 0 && !s.abort) set_error(err, s, CZ_DERR_FULL_WAIT);
-                        continue;
+                for (int ch = ch_lo; ch < ch_hi; ch += 2) {
+                    const int nh = ch + 1 < ch_hi ? 2 : 1;
+                    const uint8_t* stA = nullptr;
+                    const uint8_t* stB = nullptr;
+                    uint32_t bfA[2][2] = {}, bfB[2][2] = {};
+                    bool ok = !s.abort;
+#pragma unroll 1
+                    for (int hh = 0; hh < nh && ok; ++hh) {
+                        const int chh = ch + hh, sidx = si + hh;
+                        while (s.g_chunk0[u + 1] <= chh) ++u;
+                        const int ci = chh - ch_lo;
+                        const int ib = ((chh - s.g_chunk0[u]) * CR) >> 7;
+                        const int nbpI = cz_nbp(s.g_expert[u] == E ? SI : Ir);
+                        const int slot = sidx % NS;
+                        ok = warp_wait(&s.full[slot], (sidx / NS) & 1, s);
+                        if (!ok) break;
+                        const uint8_t* stage = ring + (size_t)slot * SLOT_BYTES;
+                        const float* stab = reinterpret_cast<const float*>(stage + GU_BYTES);
+                        // B fragments: lane column c = 8m + g = (token c/4, term c%4), rows 4t..4t+3
+                        uint32_t bw[2][2];
+#pragma unroll
+                        for (int ol = 0; ol < 2; ++ol)
+#pragma unroll
+                            for (int m = 0; m < 2; ++m) {
+                                const int cc = 8 * m + g, tk = cc >> 2, jt = cc & 3;
+                                const int ob = obw + ol;
+                                uint32_t word = 0u;
+                                if (m < nmD && tk < T && (ob << 7) < o0 + OSl) {
+                                    const float f = stab[(ob - (o0 >> 7)) * nbpI + ib];
+                                    const float sc = scale2(f, s.hexp[tk][ob]);
+                                    const float* hv = reinterpret_cast<const float*>(hterm) + ci * 64 + (4 * t) * 4 + tk;
+                                    float a0 = hv[0] * sc, b0 = hv[4] * sc, a1 = hv[8] * sc, b1 = hv[12] * sc;
+#pragma unroll
+                                    for (int j = 0; j < JH; ++j) {
+                                        const uint32_t d0 = e4m3_term2(a0, b0), d1 = e4m3_term2(a1, b1);
+                                        if (j == jt) word = d0 | (d1 << 16);
+                                    }
+                                }
+                                bw[ol][m] = word;
+                            }
+                        if (hh == 0) {
+                            stA = stage;
+#pragma unroll
+                            for (int ol = 0; ol < 2; ++ol)
+#pragma unroll
+                                for (int m = 0; m < 2; ++m) bfA[ol][m] = bw[ol][m];
+                        } else {
+                            stB = stage;
+#pragma unroll
+                            for (int ol = 0; ol < 2; ++ol)
+#pragma unroll
+                                for (int m = 0; m < 2; ++m) bfB[ol][m] = bw[ol][m];
+                        }
                     }
-                    const uint8_t* stage = ring + (size_t)slot * SLOT_BYTES;
-                    const float* stab = reinterpret_cast<const float*>(stage + GU_BYTES);
-                    // B fragments: lane column c = 8m + g = (token c/4, term c%4), rows 4t..4t+3
-                    uint32_t bf[2][2];
+                    if (ok) {
 #pragma unroll
-                    for (int ol = 0; ol < 2; ++ol)
-#pragma unroll
-                        for (int m = 0; m < 2; ++m) {
-                            const int cc = 8 * m + g, tk = cc >> 2, jt = cc & 3;
-                            const int ob = obw + ol;
-                            uint32_t word = 0u;
-                            if (m < nmD && tk < T && (ob << 7) < o0 + OSl) {
-                                const float f = stab[(ob - (o0 >> 7)) * nbpI + ib];
-                                const float sc = scale2(f, s.hexp[tk][ob]);
-                                const float* hv = reinterpret_cast<const float*>(hterm) + ci * 64 + (4 * t) * 4 + tk;
-                                float a0 = hv[0] * sc, b0 = hv[4] * sc, a1 = hv[8] * sc, b1 = hv[12] * sc;
-#pragma unroll
-                                for (int j = 0; j < JH; ++j) {
-                                    const uint32_t d0 = e4m3_term2(a0, b0), d1 = e4m3_term2(a1, b1);
-                                    if (j == jt) word = d0 | (d1 << 16);
+                        for (int i = 0; i < 16; ++i) {
+                            if (i < TPW && tw0 + i < ntile) {
+                                const size_t ra = (size_t)((tw0 + i) * 16 + g) * 16 + 4 * t;
+                                const uint32_t a0 = *reinterpret_cast<const uint32_t*>(stA + ra);
+                                const uint32_t a1 = *reinterpret_cast<const uint32_t*>(stA + ra + 8 * 16);
+                                uint32_t a2 = 0u, a3 = 0u;
+                                if (nh == 2) {
+                                    a2 = *reinterpret_cast<const uint32_t*>(stB + ra);
+                                    a3 = *reinterpret_cast<const uint32_t*>(stB + ra + 8 * 16);
+                                }
+                                const int obl = (i * 16) >> 7;
+                                if (nmD == 1) {
+                                    mma_e4m3(accd[i], a0, a1, a2, a3, bfA[obl][0], bfB[obl][0]);
+                                } else if (i < 8) {
+                                    mma_e4m3(accd[2 * i], a0, a1, a2, a3, bfA[obl][0], bfB[obl][0]);
+                                    mma_e4m3(accd[2 * i + 1], a0, a1, a2, a3, bfA[obl][1], bfB[obl][1]);
                                 }
                             }
-                            bf[ol][m] = word;
                         }
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        if (i < TPW && tw0 + i < ntile) {
-                            const int ol = (tw0 + i) * 16;
-                            const uint32_t a0 = *reinterpret_cast<const uint32_t*>(stage + (size_t)(ol + g) * 16 + 4 * t);
-                            const uint32_t a1 =
-                                *reinterpret_cast<const uint32_t*>(stage + (size_t)(ol + g + 8) * 16 + 4 * t);
-                            const int obl = (i * 16) >> 7;
-                            if (nmD == 1) {
-                                mma_e4m3(accd[i], a0, a1, 0u, 0u, bf[obl][0], 0u);
-                            } else if (i < 8) {
-                                mma_e4m3(accd[2 * i], a0, a1, 0u, 0u, bf[obl][0], 0u);
-                                mma_e4m3(accd[2 * i + 1], a0, a1, 0u, 0u, bf[obl][1], 0u);
-                            }
+                        __syncwarp();
+                        if (lane == 0) {
+                            mbar_arrive(&s.empty[si % NS]);
+                            if (nh == 2) mbar_arrive(&s.empty[(si + 1) % NS]);
                         }
+                    } else if (lane == 0 && !s.abort) {
+                        set_error(err, s, CZ_DERR_FULL_WAIT);
                     }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&s.empty[slot]);
+                    si += nh;
                 }
                 // slab done: combine the 4 terms of each token, undo the scale, write the
                 // CTA's partial rows (every (token, row) of the slab is written, zeros included)
@@ -951,12 +1072,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         if (nitem > 0 && it < nitem) {
             const int tk = it / nq4, o = o_lo + 4 * (it - tk * nq4);
             float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int cc = pt; cc < G; cc += NPART) {
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(p.partial + ((size_t)cc * T + tk) * H + o));
-                sum.x += v.x;
-                sum.y += v.y;
-                sum.z += v.z;
-                sum.w += v.w;
+            // batches of up to 8 loads in flight, added in order
+            for (int cc0 = pt; cc0 < G; cc0 += 8 * NPART) {
+                float4 v[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int cc = cc0 + k * NPART;
+                    v[k] = cc < G ? __ldcg(reinterpret_cast<const float4*>(p.partial + ((size_t)cc * T + tk) * H + o))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (cc0 + k * NPART < G) {
+                        sum.x += v[k].x;
+                        sum.y += v[k].y;
+                        sum.z += v[k].z;
+                        sum.w += v[k].w;
+                    }
             }
             part[it * NPART + pt] = sum;
         }
@@ -1030,23 +1162,71 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-bool make_down_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64_t cols) {
+static EncodeTiledFn encode_fn() {
     static EncodeTiledFn fn = nullptr;
     if (!fn) {
         void* f = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
             q != cudaDriverEntryPointSuccess || !f)
-            return false;
+            return nullptr;
         fn = reinterpret_cast<EncodeTiledFn>(f);
     }
-    if (cols % 16 || rows == 0 || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+    return fn;
+}
+
+bool make_down_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64_t cols, int H, int* grp) {
+    const EncodeTiledFn fn = encode_fn();
+    if (!fn || cols % 16 || rows == 0 || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (H % BOX_ROWS == 0 && rows % BOX_ROWS == 0) {
+        // [rows / 256][256][cols]: one box = 16 columns of up to 4 groups of 256 rows
+        const uint64_t ng = rows / BOX_ROWS;
+        const int g = (int)(ng < 4 ? ng : 4);
+        const cuuint64_t dims[3] = {cols, (cuuint64_t)BOX_ROWS, ng};
+        const cuuint64_t strides[2] = {cols, cols * BOX_ROWS};
+        const cuuint32_t box[3] = {16, (cuuint32_t)BOX_ROWS, (cuuint32_t)g};
+        if (fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+            *grp = g;
+            return true;
+        }
+    }
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {cols};
     const cuuint32_t box[2] = {16, (cuuint32_t)BOX_ROWS};
-    const cuuint32_t estr[2] = {1, 1};
+    *grp = 0;
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_gu_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64_t H, int* kb) {
+    const EncodeTiledFn fn = encode_fn();
+    if (!fn || H % 16 || rows == 0 || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (H % 128 == 0) {
+        // [H / 128 blocks][rows][128 bytes]: one box = 16 rows x up to 16 column blocks,
+        // laid out [block][row][128 B] in shared memory
+        const uint64_t nkb = H / 128;
+        const int d = (int)(nkb < (uint64_t)(KS / 128) ? nkb : (uint64_t)(KS / 128));
+        const cuuint64_t dims[3] = {128, rows, nkb};
+        const cuuint64_t strides[2] = {H, 128};
+        const cuuint32_t box[3] = {128, (cuuint32_t)CR, (cuuint32_t)d};
+        if (fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+            *kb = d;
+            return true;
+        }
+    }
+    const cuuint64_t dims[2] = {H, rows};
+    const cuuint64_t strides[1] = {H};
+    const cuuint32_t box[2] = {128, (cuuint32_t)CR};
+    *kb = 0;
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
