@@ -77,7 +77,7 @@ __device__ __constant__ double cz_inv_fact[14] = {
     0x1.a01a01a01a01ap-16, 0x1.71de3a556c734p-19, 0x1.27e4fb7789f5cp-22, 0x1.ae64567f544e4p-26,
     0x1.1eed8eff8d898p-29, 0x1.6124613a86d09p-33};
 
-static __device__ __noinline__ float cz_expf(float x) {
+__device__ __forceinline__ float cz_expf_inline(float x) {
     if (x != x) return x;
     if (x > 100.0f) return __int_as_float(0x7f800000);
     if (x < -110.0f) return 0.0f;
@@ -94,6 +94,9 @@ static __device__ __noinline__ float cz_expf(float x) {
     const long long k = (long long)kd;
     return __double2float_rn(__dmul_rn(p, __longlong_as_double((k + 1023) << 52)));
 }
+
+// Out-of-line copy for call sites where code size matters more than latency.
+static __device__ __noinline__ float cz_expf(float x) { return cz_expf_inline(x); }
 
 // activation.zig:8-20 (tolerance-checked path: CUDA's expf).
 CZ_DEV float cz_sigmoid(float x) {

@@ -274,24 +274,34 @@ __device__ __forceinline__ uint16_t e4m3_term2(float& a, float& b) {
 
 // Router dot of one row with one token, in dotF32's exact order (lane l holds
 // chain l: elements l, l+32, ...; then the lane-ordered combine and the FMA
-// tail).  wrow / xs are shared memory.  Returns the logit in every lane.
-__device__ __forceinline__ float router_dot(const float* __restrict__ wrow, const uint8_t* __restrict__ xs, int H,
-                                            bool bf16, int lane) {
-    const uint16_t* xb = reinterpret_cast<const uint16_t*>(xs);
-    const float* xf = reinterpret_cast<const float*>(xs);
+// tail).  wrow / xs are shared memory.  Returns the logit in every lane.  Kept
+// rolled and out of line: it runs once per launch, fetched cold.
+template <bool BF16>
+__device__ __noinline__ float router_dot(const float* __restrict__ wrow, const uint8_t* __restrict__ xs, int H,
+                                         int lane) {
+    auto xv = [&](int i) -> float {
+        return BF16 ? __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(xs)[i] << 16)
+                    : reinterpret_cast<const float*>(xs)[i];
+    };
     float acc = 0.0f;
     int i = 0;
-#pragma unroll 2
-    for (; i + 32 <= H; i += 32) {
-        const float x = bf16 ? __uint_as_float((uint32_t)xb[i + lane] << 16) : xf[i + lane];
-        acc = __fmaf_rn(x, wrow[i + lane], acc);
-    }
-    for (; i + 8 <= H; i += 8) {  // a final 8-wide block: lanes 0..7 only
-        if (lane < 8) {
-            const float x = bf16 ? __uint_as_float((uint32_t)xb[i + lane] << 16) : xf[i + lane];
-            acc = __fmaf_rn(x, wrow[i + lane], acc);
+    // batches of 16 elements per lane: the loads go out together, the FMAs keep the chain order
+#pragma unroll 1
+    for (; i + 512 <= H; i += 512) {
+        float xb[16], wb[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            xb[j] = xv(i + 32 * j + lane);
+            wb[j] = wrow[i + 32 * j + lane];
         }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc = __fmaf_rn(xb[j], wb[j], acc);
     }
+#pragma unroll 1
+    for (; i + 32 <= H; i += 32) acc = __fmaf_rn(xv(i + lane), wrow[i + lane], acc);
+#pragma unroll 1
+    for (; i + 8 <= H; i += 8)  // a final 8-wide block: lanes 0..7 only
+        if (lane < 8) acc = __fmaf_rn(xv(i + lane), wrow[i + lane], acc);
     // total[l] = (((0 + acc0[l]) + acc1[l]) + acc2[l]) + acc3[l]; chain k = lanes 8k..8k+7
     const float a8 = __shfl_down_sync(0xffffffffu, acc, 8);
     const float a16 = __shfl_down_sync(0xffffffffu, acc, 16);
@@ -300,58 +310,63 @@ __device__ __forceinline__ float router_dot(const float* __restrict__ wrow, cons
     float sum = __shfl_sync(0xffffffffu, tl, 0);
 #pragma unroll 1
     for (int l = 1; l < 8; ++l) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, tl, l));
-    for (; i < H; ++i) {
-        const float x = bf16 ? __uint_as_float((uint32_t)xb[i] << 16) : xf[i];
-        sum = __fmaf_rn(x, wrow[i], sum);
-    }
+#pragma unroll 1
+    for (; i < H; ++i) sum = __fmaf_rn(xv(i), wrow[i], sum);
     return sum;
 }
 
 // Top-k of one token (moe.zig:435-463) by one warp; lg = the token's logits in
-// shared memory.  Lane l holds experts l, l+32, ...  Keys are the f32 bits of
-// exp(v - max) + 1 (non-negative floats order like their bits; 0 = not a
-// candidate: chosen, NaN or beyond E).  Each round takes the largest key and,
-// among equal keys, the smallest id — the reference's strict-greater scan from
-// e = 0 with bv = -1.  A round without a candidate yields id 0, as in the
-// reference.
-template <int NM>
-__device__ __noinline__ void route_token(const float* __restrict__ lg, int E, int K, int norm_topk, int has_shared, int T, int t,
-                            int lane, DecodeMisc& s, uint32_t* topk_idx, float* topk_gates, bool write_out) {
-    float v[NM];
+// shared memory, key = E words of shared scratch.  Lane l owns experts l, l+32,
+// ...  Keys are the f32 bits of exp(v - max) + 1 (non-negative floats order like
+// their bits; 0 = not a candidate: chosen, NaN or beyond E).  Each round takes
+// the largest key and, among equal keys, the smallest id — the reference's
+// strict-greater scan from e = 0 with bv = -1.  A round without a candidate
+// yields id 0, as in the reference.  The loops are kept rolled: this code runs
+// once per launch, so its size (fetched cold) matters more than its trip count.
+__device__ __noinline__ void route_token(const float* __restrict__ lg, uint32_t* __restrict__ key, int E, int K,
+                                         int norm_topk, int has_shared, int T, int t, int lane, DecodeMisc& s,
+                                         uint32_t* topk_idx, float* topk_gates, bool write_out) {
     float mx = __int_as_float(0xffc00000);  // NaN: fmaxf ignores it
-#pragma unroll
-    for (int m = 0; m < NM; ++m) {
-        const int e = lane + 32 * m;
-        v[m] = (e < E) ? lg[e] : __int_as_float(0xffc00000);
-        mx = fmaxf(mx, v[m]);
-    }
+#pragma unroll 1
+    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
     mx = warp_max(mx);
-    uint32_t key[NM];
     double all = 0.0;
     float ex0 = 0.0f;
+    // four experts per lane at a time: their exp chains run side by side
+#pragma unroll 1
+    for (int e0 = lane; e0 < E; e0 += 128) {
+        float ex[4];
 #pragma unroll
-    for (int m = 0; m < NM; ++m) {
-        const int e = lane + 32 * m;
-        key[m] = 0u;
-        if (e < E) {
-            const float ex = cz_expf(__fsub_rn(v[m], mx));
-            all += (double)ex;
-            if (ex > -1.0f) key[m] = __float_as_uint(ex) + 1u;
-            if (m == 0) ex0 = ex;
+        for (int j = 0; j < 4; ++j) ex[j] = e0 + 32 * j < E ? cz_expf_inline(__fsub_rn(lg[e0 + 32 * j], mx)) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = e0 + 32 * j;
+            if (e < E) {
+                all += (double)ex[j];
+                key[e] = ex[j] > -1.0f ? __float_as_uint(ex[j]) + 1u : 0u;
+                if (e == 0) ex0 = ex[j];
+            }
         }
     }
     all = warp_sum_d(all);
     const float ex_e0 = __shfl_sync(0xffffffffu, ex0, 0);
+    __syncwarp();
     double top = 0.0;
+#pragma unroll 1
     for (int z = 0; z < K; ++z) {
         uint32_t lbest = 0u;
         int lid = 0x7fffffff;
+#pragma unroll 1
+        for (int e0 = lane; e0 < E; e0 += 128) {
+            uint32_t kk[4];
 #pragma unroll
-        for (int m = 0; m < NM; ++m) {
-            if (key[m] > lbest) {
-                lbest = key[m];
-                lid = lane + 32 * m;
-            }
+            for (int j = 0; j < 4; ++j) kk[j] = e0 + 32 * j < E ? key[e0 + 32 * j] : 0u;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (kk[j] > lbest) {
+                    lbest = kk[j];
+                    lid = e0 + 32 * j;
+                }
         }
         const uint32_t kmax = redux_max_u32(lbest);
         int best;
@@ -362,17 +377,16 @@ __device__ __noinline__ void route_token(const float* __restrict__ lg, int E, in
         } else {
             best = (int)redux_min_u32(lbest == kmax ? (uint32_t)lid : 0xffffffffu);
             bv = __uint_as_float(kmax - 1u);
-#pragma unroll
-            for (int m = 0; m < NM; ++m)
-                if (lane + 32 * m == best) key[m] = 0u;
         }
-        top = __dadd_rn(top, (double)bv);
+        __syncwarp();
         if (lane == 0) {
+            if (kmax != 0u) key[best] = 0u;
             s.pe[t * K + z] = best;
             s.pg[t * K + z] = bv;  // exp value for now; the gate is formed below
         }
+        __syncwarp();
+        top = __dadd_rn(top, (double)bv);
     }
-    __syncwarp();
     const double den = norm_topk ? top : all;
     if (lane < K) {
         const float g = __double2float_rn(__ddiv_rn((double)s.pg[t * K + lane], den));
@@ -404,6 +418,9 @@ constexpr int BAR_RED_FULL = 2, BAR_RED_FREE = 4, BAR_H_DONE = 6;
 __device__ __forceinline__ void bar_sync_n(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "n"((NCW + 1) * 32) : "memory"); }
 __device__ __forceinline__ void bar_arrive_n(int id) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "n"((NCW + 1) * 32) : "memory"); }
 
+// One instance per token count: loop trip counts, fragment shapes and slab sizes
+// become constants, so each launch runs a short, branch-free path.
+template <int TT>
 __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_constant__ DecodeParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-aligned base as an offset into the __shared__ array itself, so every
@@ -412,7 +429,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     uint8_t* const sb = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, c = blockIdx.x;
-    const int T = p.T, H = p.H, E = p.E, K = p.K;
+    constexpr int T = TT;
+    const int H = p.H, E = p.E, K = p.K;
     const int SI = p.SI, Ir = p.I;
     const int Er = E + (SI ? 1 : 0);
     const int LS = logit_stride(E);
@@ -495,7 +513,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     if (!s.abort) {
         for (int it = warp; it < nrows * T; it += NWARPS) {
             const int r = it / T, t = it - r * T;
-            const float v = router_dot(rows + (size_t)r * H, xs + (size_t)t * H * (xbf ? 2 : 4), H, xbf, lane);
+            const float* wr = rows + (size_t)r * H;
+            const float v = xbf ? router_dot<true>(wr, xs + (size_t)t * H * 2, H, lane)
+                                : router_dot<false>(wr, xs + (size_t)t * H * 4, H, lane);
             if (lane == 0) p.logits[(size_t)t * LS + row_lo + r] = v;
         }
         // max |x_t| for the per-token power-of-two prescale (one atomic per warp)
@@ -553,10 +573,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     if (!s.abort) {
         for (int t = warp; t < T; t += NWARPS) {
             const float* lg = reinterpret_cast<const float*>(ring) + (size_t)t * LS;
-            if (E <= 128)
-                route_token<4>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates, c == 0);
-            else
-                route_token<MAXM>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates, c == 0);
+            // keys of token t: shared scratch after the logits (the ring is idle until phase C)
+            uint32_t* key = reinterpret_cast<uint32_t*>(ring) + (size_t)MAXT * LS + (size_t)t * LS;
+            route_token(lg, key, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates, c == 0);
         }
     }
     __syncthreads();
@@ -1234,10 +1253,12 @@ int decode_launch(const DecodeParams& prm, int num_sms, cudaStream_t stream) {
     const int tmax = decode_max_tokens(prm.H, prm.E, prm.K, prm.I, prm.SI, prm.x_bf16, num_sms);
     if (prm.T < 1 || prm.T > tmax) return CZ_ESHAPE;
     if (prm.rms_w && prm.x_bf16) return CZ_EARGS;
+    static void (*const kern[MAXT])(DecodeParams) = {moe_decode_kernel<1>, moe_decode_kernel<2>,
+                                                      moe_decode_kernel<3>, moe_decode_kernel<4>};
     if (!g_attr_set) {
-        if (cudaFuncSetAttribute(moe_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT) !=
-            cudaSuccess)
-            return CZ_ELAUNCH;
+        for (int i = 0; i < MAXT; ++i)
+            if (cudaFuncSetAttribute(kern[i], cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT) != cudaSuccess)
+                return CZ_ELAUNCH;
         g_attr_set = true;
     }
     cudaLaunchConfig_t cfg = {};
@@ -1250,7 +1271,7 @@ int decode_launch(const DecodeParams& prm, int num_sms, cudaStream_t stream) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, moe_decode_kernel, prm) != cudaSuccess) return CZ_ELAUNCH;
+    if (cudaLaunchKernelEx(&cfg, kern[prm.T - 1], prm) != cudaSuccess) return CZ_ELAUNCH;
     return CZ_OK;
 }
 
