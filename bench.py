@@ -176,6 +176,9 @@ def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    if args.config == "c4":
+        reference_stack(args)
+        return
     d = synth.CONFIGS[args.config]
     T = args.tokens
     Ts = min(T, 64)  # each step: a bounded sample of the batch (prefill batches are thousands of tokens)
@@ -208,6 +211,223 @@ def reference_arm(args):
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def stack_metric(NL, T):
+    return f"MoE-stack ({NL} layers) {'prefill' if T >= PREFILL_MIN_TOKENS else 'decode'} tokens/s (c4, T={T})"
+
+
+def stack_config(args, d, NL, T, world):
+    return {"workload": f"c4: {NL} config-2 MoE layers, attention = identity, {T} f32 token(s)/step "
+                        "through colizig_cuda_moe_stack_forward (rms + MoE + residual per layer)",
+            "hidden": d.hidden, "experts": d.experts, "topk": d.topk, "moe_intermediate": d.inter,
+            "layers": NL, "tokens_per_step": T, "tokens_per_gpu": args.tokens, "global_batch": T,
+            "expert_weight_bytes": NL * d.experts * expert_bytes(d),
+            "l2": "inputs larger than L2: each step streams every layer's routed experts",
+            "parallelism": (f"ep{world}: experts partitioned over the GPUs, router replicated, NCCL "
+                            "all-reduce per layer") if world > 1 else "single GPU"}
+
+
+def reference_stack(args):
+    """--impl reference for config 4: the oracle's restatement of the reference's
+    per-layer caller (model.zig:227-232: n = rms(h, w); h += moe(n)) over the
+    stack, each step on a bounded sample of the batch (at most 64 tokens), the
+    layers cycling through --cpu-layers distinct weight sets."""
+    import torch
+
+    import oracle
+    from colizig_b200 import synth
+
+    d = synth.CONFIGS["c2"]
+    NL, T = args.layers, args.tokens * args.gpus
+    Ts = min(T, 64)
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    od = oracle.Dims(d.hidden, d.experts, d.topk, d.inter, d.shared_inter, d.norm_topk)
+    ols = [oracle.layer_from_dict(synth.to_numpy_layer(synth.make_layer(d, seed=l, device="cpu")))
+           for l in range(args.cpu_layers)]
+    g = torch.Generator(device="cpu").manual_seed(77)
+    norm_w = (1.0 + 0.05 * torch.randn(NL, d.hidden, generator=g)).numpy().astype(np.float32)
+
+    def run(h):
+        for l in range(NL):
+            out, _, _ = oracle.moe_forward(ols[l % len(ols)], od, oracle.rms(h, norm_w[l], 1e-6))
+            h = (h + out).astype(np.float32)
+        return h
+
+    toks = [synth.make_tokens(Ts, d.hidden, 30000 + i, device="cpu", dtype=torch.float32).numpy()
+            for i in range(4)]
+    for i in range(min(args.warmup, 3)):
+        run(toks[i % 4])
+    steps = max(1, min(args.steps, 5 if Ts > 1 else 20))  # bounded: a whole-stack step is 48 layer forwards
+    t0 = time.perf_counter()
+    for i in range(steps):
+        run(toks[i % 4])
+    dt = time.perf_counter() - t0
+    value = steps * Ts / dt
+    line = {
+        "impl": "reference", "metric": stack_metric(NL, T), "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": min(args.warmup, 3), "ms_per_step": dt / steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": stack_config(args, d, NL, T, args.gpus),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{steps} steps, each the {NL}-layer stack (rms + MoE + residual per layer) over "
+                                   f"{Ts} of the step's {T} tokens, layers cycling over {len(ols)} weight sets "
+                                   f"(C restatement of the reference AVX2 path, {cores} threads)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def stack_main(args, world, rank, local, torch, dist, cz, _abi, moe, synth):
+    """Config 4: the 48-layer stack of config-2 MoE layers (29 GB of E4M3 expert
+    weights), attention = identity, through colizig_cuda_moe_stack_forward: per
+    layer n = rms(h, w_l), h += moe_l(n) (model.zig:227-232).  One step = the
+    whole stack over one batch of `--tokens` tokens per GPU."""
+    d = synth.CONFIGS["c2"]
+    NL = args.layers
+    T = args.tokens * world
+    dev = torch.device("cuda", local)
+    layers = []
+    for l in range(NL):
+        w = synth.make_layer(d, seed=l, device=dev)
+        layers.append(moe.Layer.from_weights(l, d, w, ep=world > 1))
+        del w
+    torch.cuda.empty_cache()
+    g = torch.Generator(device="cpu").manual_seed(77)
+    norm_w = (1.0 + 0.05 * torch.randn(NL, d.hidden, generator=g)).to(dev)
+    n = args.warmup + args.steps
+    xs = [synth.make_tokens(T, d.hidden, 30000 + i, device=dev, dtype=torch.float32) for i in range(n)]
+    hs = torch.empty((n, T, d.hidden), dtype=torch.float32, device=dev)
+    L = _abi.load()
+    prefill = T >= PREFILL_MIN_TOKENS
+
+    def step(i, sh):
+        hs[i].copy_(xs[i])
+        rc = L.colizig_cuda_moe_stack_forward(0, NL, norm_w.data_ptr(), 1e-6, hs[i].data_ptr(), T,
+                                              _abi.COLIZIG_PTR_DEVICE, sh)
+        if rc:
+            raise cz.ColizigError("colizig_cuda_moe_stack_forward", rc)
+
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        step(i, stream.cuda_stream)
+    torch.cuda.synchronize()
+    moe.check()
+    if prefill:
+        moe.kernel_timer(2 * NL * args.steps)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=dev)):
+        gs = torch.cuda.current_stream()
+        for k in range(args.steps):
+            step(args.warmup + k, gs.cuda_stream)
+    graph.replay()
+    torch.cuda.synchronize()
+    moe.check()
+    sampler = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    t0e = torch.cuda.Event(enable_timing=True)
+    t1e = torch.cuda.Event(enable_timing=True)
+    t0e.record(stream)
+    graph.replay()
+    t1e.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    moe.check()
+    elapsed_ms = t0e.elapsed_time(t1e)
+    if world > 1:
+        tt = torch.tensor([elapsed_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(tt.item())
+    value = args.steps * T / (elapsed_ms / 1e3)
+    gemm = {}
+    if prefill:
+        for kind, ms in moe.kernel_timer_read():
+            gemm.setdefault(kind, []).append(ms)
+        moe.kernel_timer(0)
+    del graph
+
+    # end to end: host h (pinned), the C ABI copies it in and the result out each step
+    hh = [xs[i % 8].cpu().pin_memory() for i in range(min(n, 8))]
+
+    # host norm weights for the host-pointer call
+    nw_host = norm_w.cpu().contiguous()
+
+    def e2e_step_h(i):
+        rc = L.colizig_cuda_moe_stack_forward(0, NL, nw_host.data_ptr(), 1e-6, hh[i % len(hh)].data_ptr(), T, 0, None)
+        if rc:
+            raise cz.ColizigError("colizig_cuda_moe_stack_forward", rc)
+
+    ke = max(1, min(args.steps, 20))
+    for i in range(2):
+        e2e_step_h(i)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for k in range(ke):
+        e2e_step_h(k)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        tt = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_s = float(tt.item())
+    e2e = {"value": ke * T / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * d.hidden * 4 + NL * d.hidden * 4,
+           "d2h_bytes_per_step": T * d.hidden * 4, "ms_per_step": e2e_s / ke * 1e3}
+
+    hbm_peak, tf_peak, peak_kind = load_peaks()
+    step_ms = elapsed_ms / args.steps
+    if prefill:
+        fp8_peak = 2.0 * tf_peak
+        gu = float(np.mean(gemm[moe.TIMER_PREFILL_GATE_UP]))
+        dn = float(np.mean(gemm[moe.TIMER_PREFILL_DOWN]))
+        pairs = T * d.topk / world  # average pairs per rank and layer
+        gu_flops = 2.0 * pairs * d.hidden * 2 * d.inter
+        tf = gu_flops / (gu / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": tf, "peak": fp8_peak, "unit": "TFLOP/s", "frac": tf / fp8_peak,
+                "traffic": None, "kernel": "pf_gemm_kernel (gate/up), per layer", "kernel_ms_avg": gu,
+                "flops_per_launch": gu_flops,
+                "peak_kind": f"FP8 dense = 2 x {peak_kind} bf16 (MEASURED_PEAKS.json bf16_tflops)",
+                "down_gemm": {"kernel_ms_avg": dn, "achieved_tflops": gu_flops / 2 / (dn / 1e3) / 1e12},
+                "step": {"ms": step_ms, "flops": NL * algorithmic_flops(d, T) / world,
+                         "achieved_tflops": NL * algorithmic_flops(d, T) / world / (step_ms / 1e3) / 1e12}}
+    else:
+        # decode: every layer call moves its U = top-k distinct experts (T = 1) + router + token rows
+        U = float(d.topk) if T == 1 else float(min(d.experts, T * d.topk))
+        per_layer = algorithmic_bytes(d, T, U) + (world - 1) * d.experts * d.hidden * 4
+        gbs = NL * per_layer / world / (step_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                "traffic": NCU_TRAFFIC.get(("c2", T)) if world == 1 else None,
+                "traffic_unit": "DRAM bytes per moe_decode_kernel launch (ncu, config 2)",
+                "kernel": "moe_decode_kernel, one launch per layer (rms and residual fused)",
+                "kernel_ms_avg": step_ms / NL, "bytes_per_launch": per_layer / world,
+                "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cores = os.cpu_count() or 1
+        Tc = min(T, 64)
+        host_layers = [synth.to_numpy_layer(synth.make_layer(d, seed=l, device="cpu")) for l in range(args.cpu_layers)]
+        v, nsteps, dt = cpu_sample(args, d, host_layers, Tc, args.cpu_seconds, cores)
+        cpu = {"value": v / NL, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{nsteps} config-2 layer forwards of T={Tc} in {dt:.1f} s (C restatement of the reference "
+                         f"AVX2 path, {cores} threads); stack tokens/s = layer tokens/s / {NL} (rms and residual "
+                         "not timed)"}
+    if rank == 0:
+        line = {
+            "metric": stack_metric(NL, T),
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e4m3 x e4m3 -> f32", "data": "synthetic",
+            "config": stack_config(args, d, NL, T, world),
+            "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+            "gpu_launches": args.steps * NL * (9 if prefill else -(-args.tokens * world // 4)),
+        }
+        print(json.dumps(line), flush=True)
+    for lay in layers:
+        lay.unregister()
 
 
 def metric_name(args, T):
@@ -251,6 +471,8 @@ def main():
     big = args.tokens * args.gpus >= PREFILL_MIN_TOKENS
     if args.steps is None:
         args.steps = 20 if big else 200
+    if args.config == "c4":
+        args.layers = args.layers or 48
     if args.layers is None:
         args.layers = 4 if big else 16
 
@@ -279,6 +501,15 @@ def main():
         from colizig_b200 import ep
 
         ep.init()
+    if args.config == "c4":
+        stack_main(args, world, rank, local, torch, dist, cz, _abi, moe, synth)
+        if world > 1:
+            from colizig_b200 import ep
+
+            torch.cuda.synchronize()
+            ep.shutdown()
+            dist.destroy_process_group()
+        return
     d = synth.CONFIGS[args.config]
     T = args.tokens * world  # tokens per step over the whole job (each rank contributes --tokens)
     dev = torch.device("cuda", local)

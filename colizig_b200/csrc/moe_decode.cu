@@ -1069,7 +1069,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     }
 
     // ---------------- this CTA's slice of out: the G partial rows in a fixed order ----------------
-    __threadfence();  // this thread's partial rows before the arrive below
+    // the block barrier orders every thread's partial rows before thread 0's
+    // fence and release; the other CTAs acquire them through the counter
     __syncthreads();
     if (tid == 0) {
         __threadfence();
