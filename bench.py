@@ -423,7 +423,7 @@ def stack_main(args, world, rank, local, torch, dist, cz, _abi, moe, synth):
             "dtype": "e4m3 x e4m3 -> f32", "data": "synthetic",
             "config": stack_config(args, d, NL, T, world),
             "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
-            "gpu_launches": args.steps * NL * (9 if prefill else -(-args.tokens * world // 4)),
+            "gpu_launches": args.steps * NL * (10 if prefill else -(-args.tokens * world // 4)),
         }
         print(json.dumps(line), flush=True)
     for lay in layers:
@@ -639,7 +639,7 @@ def main():
                "sample": f"{nsteps} layer forwards of {args.config} T={Tc} in {dt:.1f} s over {len(host_layers)} "
                          f"layers (C restatement of the reference AVX2 path, {cores} threads)"}
 
-    launches_per_step = 9 if prefill else -(-T // 4)  # prefill: logits, topk, count, place, tokpos, dispatch, 2 GEMMs, combine
+    launches_per_step = 10 if prefill else -(-T // 4)  # prefill: logits, topk, count, scan, place, tokpos, dispatch, 2 GEMMs, combine
     if prefill:
         # tensor-bound.  Dominant kernel: the gate/up grouped GEMM.  Its algorithmic FLOPs
         # (2 x pairs x H x 2I routed + 2 x T x H x 2SI shared, pairs on this rank's

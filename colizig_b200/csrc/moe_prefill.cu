@@ -51,6 +51,7 @@ constexpr int NTH = 352;     // 11 warps: TMA, MMA, 8 epilogue, tables
 constexpr int MAXK = kMaxTopk;
 constexpr int MAXNKB = 32;   // K blocks per tile (H or I <= 4096)
 constexpr int HT = 3;        // E4M3 terms of h
+constexpr int GCH = 1024;    // pairs per chunk of the grouping kernels
 
 __host__ __device__ inline int pad64(int n) { return (n + TN - 1) / TN * TN; }
 
@@ -63,6 +64,7 @@ struct Scratch {
     float* sg;         // [T] shared-expert gate sigmoid(x . sh_gate)
     float* logits;     // [T][logit_stride(E)]
     int* cnt;          // [Eg]
+    int* ccnt;         // [nchunks][Eg] pairs of each group per chunk of GCH pairs, then the chunk's offset
     int* gbase;        // [Eg+1] first position of each group (padded to 64)
     int* tpre_gu;      // [Eg+1] tile prefix, gate/up
     int* tpre_dn;      // [Eg+1] tile prefix, down
@@ -98,6 +100,7 @@ Scratch carve_scratch(uint8_t* base, int T, int H, int E, int K, int I, int SI) 
     s.sg = (float*)take((size_t)T * 4);
     s.logits = (float*)take((size_t)T * logit_stride(E) * 4);
     s.cnt = (int*)take((size_t)s.Eg * 4);
+    s.ccnt = (int*)take((size_t)((s.P + GCH - 1) / GCH) * s.Eg * 4);
     s.gbase = (int*)take((size_t)(s.Eg + 1) * 4);
     s.tpre_gu = (int*)take((size_t)(s.Eg + 1) * 4);
     s.tpre_dn = (int*)take((size_t)(s.Eg + 1) * 4);
@@ -391,92 +394,110 @@ __device__ __forceinline__ int pair_group(const GroupParams& q, int p) {
     return p < q.T * q.K ? (int)q.idx[p] : q.E;
 }
 
+// Grouping = a stable counting sort of the pairs by group, in three launches:
+// count (per chunk of GCH pairs, a histogram of the held groups), scan (one
+// block: per-group totals, each chunk's offset inside its group, padded group
+// bases and the GEMM tile prefixes) and place (one warp per chunk: each pair's
+// rank among the chunk's pairs of its group, in pair order).  Pairs of groups
+// held elsewhere (expert parallelism) get position -1.
 __global__ void pf_count_kernel(const GroupParams q) {
-    const int g = blockIdx.x;
-    __shared__ int wsum[32];
-    int c = 0;
-    if (group_held(q, g))
-        for (int p = threadIdx.x; p < q.s.P; p += blockDim.x) c += pair_group(q, p) == g;
-    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < q.s.P; p += gridDim.x * blockDim.x)
-        q.s.pos_of_pair[p] = -1;
-    c = __reduce_add_sync(0xffffffffu, c);
-    if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = c;
+    extern __shared__ int hist[];  // [Eg]
+    const int Eg = q.s.Eg;
+    for (int g = threadIdx.x; g < Eg; g += blockDim.x) hist[g] = 0;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int tot = 0;
-        for (int k = 0; k < (int)(blockDim.x >> 5); ++k) tot += wsum[k];
-        q.s.cnt[g] = tot;
+    const int p0 = blockIdx.x * GCH, p1 = min(q.s.P, p0 + GCH);
+    for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
+        const int g = pair_group(q, p);
+        if (group_held(q, g)) atomicAdd(&hist[g], 1);
+    }
+    __syncthreads();
+    for (int g = threadIdx.x; g < Eg; g += blockDim.x) q.s.ccnt[(size_t)blockIdx.x * Eg + g] = hist[g];
+}
+
+// Exclusive scan of v over the block (blockDim.x a multiple of 32, <= 1024); returns the total.
+__device__ int block_exclusive_scan(int& v, int* wsum) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < nw ? wsum[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < nw) wsum[lane] = w;  // inclusive warp prefix
+    }
+    __syncthreads();
+    const int tot = wsum[nw - 1];
+    v = x - v + (warp ? wsum[warp - 1] : 0);
+    __syncthreads();
+    return tot;
+}
+
+// One block of 1024 threads; groups g = thread, thread + 1024, ... (Eg <= 1024 here).
+__global__ void pf_scan_kernel(const GroupParams q) {
+    __shared__ int wsum[32];
+    const int Eg = q.s.Eg, nch = (q.s.P + GCH - 1) / GCH, g = threadIdx.x;
+    int n = 0;
+    if (g < Eg) {
+        for (int b = 0; b < nch; ++b) {
+            int* c = q.s.ccnt + (size_t)b * Eg + g;
+            const int v = *c;
+            *c = n;
+            n += v;
+        }
+        q.s.cnt[g] = n;
+    }
+    const int np = pad64(n);
+    const int ig = g == q.E ? q.SI : q.I;
+    int base = np, tg = g < Eg ? (np / TN) * (ig / TM) : 0, td = g < Eg ? (np / TN) * (q.H / TM) : 0;
+    const int tot = block_exclusive_scan(base, wsum);
+    const int totg = block_exclusive_scan(tg, wsum);
+    const int totd = block_exclusive_scan(td, wsum);
+    if (g < Eg) {
+        q.s.gbase[g] = base;
+        q.s.tpre_gu[g] = tg;
+        q.s.tpre_dn[g] = td;
+        for (int r = n; r < np; ++r) q.s.pair_at_pos[base + r] = -1;
+    }
+    if (g == 0) {
+        q.s.gbase[Eg] = tot;
+        q.s.tpre_gu[Eg] = totg;
+        q.s.tpre_dn[Eg] = totd;
     }
 }
 
+// One warp per chunk of GCH pairs.
 __global__ void pf_place_kernel(const GroupParams q) {
-    const int g = blockIdx.x, Eg = q.s.Eg;
-    __shared__ int red[3][32];
-    __shared__ int wpre[33];
-    // this group's base position and tile prefixes (sums over the groups before it)
-    int b = 0, tg = 0, td = 0;
-    for (int k = threadIdx.x; k < g; k += blockDim.x) {
-        const int n = pad64(q.s.cnt[k]);
-        b += n;
-        const int ig = k == q.E ? q.SI : q.I;
-        tg += (n / TN) * (ig / TM);
-        td += (n / TN) * (q.H / TM);
-    }
-    b = __reduce_add_sync(0xffffffffu, b);
-    tg = __reduce_add_sync(0xffffffffu, tg);
-    td = __reduce_add_sync(0xffffffffu, td);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    if (lane == 0) {
-        red[0][warp] = b;
-        red[1][warp] = tg;
-        red[2][warp] = td;
-    }
-    __syncthreads();
-    int base = 0, tgu = 0, tdn = 0;
-    for (int k = 0; k < nw; ++k) {
-        base += red[0][k];
-        tgu += red[1][k];
-        tdn += red[2][k];
-    }
-    const int n = q.s.cnt[g], np = pad64(n);
-    if (threadIdx.x == 0) {
-        q.s.gbase[g] = base;
-        q.s.tpre_gu[g] = tgu;
-        q.s.tpre_dn[g] = tdn;
-        if (g == Eg - 1) {
-            const int ig = g == q.E ? q.SI : q.I;
-            q.s.gbase[Eg] = base + np;
-            q.s.tpre_gu[Eg] = tgu + (np / TN) * (ig / TM);
-            q.s.tpre_dn[Eg] = tdn + (np / TN) * (q.H / TM);
+    extern __shared__ int off[];  // [Eg] next position of each group for this chunk
+    const int Eg = q.s.Eg, lane = threadIdx.x;
+    for (int g = lane; g < Eg; g += 32) off[g] = q.s.gbase[g] + q.s.ccnt[(size_t)blockIdx.x * Eg + g];
+    __syncwarp();
+    const int p0 = blockIdx.x * GCH, p1 = min(q.s.P, p0 + GCH);
+    const uint32_t lt = (1u << lane) - 1u;
+    for (int pb = p0; pb < p1; pb += 32) {
+        const int p = pb + lane;
+        const int g = p < p1 ? pair_group(q, p) : -1;
+        const bool held = g >= 0 && group_held(q, g);
+        const uint32_t peers = __match_any_sync(0xffffffffu, held ? g : -2 - lane);
+        const int at = held ? off[g] : 0;
+        __syncwarp();
+        if (held) {
+            const int pos = at + __popc(peers & lt);
+            q.s.pos_of_pair[p] = pos;
+            q.s.pair_at_pos[pos] = p;
+            if ((peers & lt) == 0) off[g] = at + __popc(peers);
+        } else if (p < p1) {
+            q.s.pos_of_pair[p] = -1;
         }
-    }
-    for (int r = n + threadIdx.x; r < np; r += blockDim.x) q.s.pair_at_pos[base + r] = -1;
-    if (n == 0) return;
-    // stable placement: pairs of this group in pair order
-    int run = 0;
-    for (int p0 = 0; p0 < q.s.P; p0 += blockDim.x) {
-        const int p = p0 + threadIdx.x;
-        const bool f = p < q.s.P && pair_group(q, p) == g;
-        const uint32_t m = __ballot_sync(0xffffffffu, f);
-        if (lane == 0) wpre[warp] = __popc(m);
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            int acc = 0;
-            for (int k = 0; k < nw; ++k) {
-                const int c = wpre[k];
-                wpre[k] = acc;
-                acc += c;
-            }
-            wpre[32] = acc;
-        }
-        __syncthreads();
-        if (f) {
-            const int r = run + wpre[warp] + __popc(m & ((1u << lane) - 1u));
-            q.s.pos_of_pair[p] = base + r;
-            q.s.pair_at_pos[base + r] = p;
-        }
-        run += wpre[32];
-        __syncthreads();
+        __syncwarp();
     }
 }
 
@@ -1135,8 +1156,13 @@ int prefill_run(const PrefillLayer& L, const void* x, int x_bf16, int T, const f
     gq.e_hi = L.e_hi;
     gq.shared_here = L.shared_here;
     gq.s = s;
-    pf_count_kernel<<<s.Eg, 256, 0, st>>>(gq);
-    pf_place_kernel<<<s.Eg, 256, 0, st>>>(gq);
+    {
+        const int nch = (s.P + GCH - 1) / GCH;
+        const size_t hb = (size_t)s.Eg * sizeof(int);
+        pf_count_kernel<<<nch, 256, hb, st>>>(gq);
+        pf_scan_kernel<<<1, 1024, 0, st>>>(gq);
+        pf_place_kernel<<<nch, 32, hb, st>>>(gq);
+    }
     pf_tokpos_kernel<<<(T + 127) / 128, 128, 0, st>>>(gq);
     // dispatch
     {
