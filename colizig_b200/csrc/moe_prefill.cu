@@ -51,6 +51,7 @@ constexpr int NTH = 352;     // 11 warps: TMA, MMA, 8 epilogue, tables
 constexpr int MAXK = kMaxTopk;
 constexpr int MAXNKB = 32;   // K blocks per tile (H or I <= 4096)
 constexpr int HT = 3;        // E4M3 terms of h
+constexpr int TMD = 2 * TM;  // output rows of a down tile: two 128-row MMAs share the h operand
 constexpr int GCH = 1024;    // pairs per chunk of the grouping kernels
 
 __host__ __device__ inline int pad64(int n) { return (n + TN - 1) / TN * TN; }
@@ -457,7 +458,7 @@ __global__ void pf_scan_kernel(const GroupParams q) {
     }
     const int np = pad64(n);
     const int ig = g == q.E ? q.SI : q.I;
-    int base = np, tg = g < Eg ? (np / TN) * (ig / TM) : 0, td = g < Eg ? (np / TN) * (q.H / TM) : 0;
+    int base = np, tg = g < Eg ? (np / TN) * (ig / TM) : 0, td = g < Eg ? (np / TN) * (q.H / TMD) : 0;
     const int tot = block_exclusive_scan(base, wsum);
     const int totg = block_exclusive_scan(tg, wsum);
     const int totd = block_exclusive_scan(td, wsum);
@@ -654,9 +655,9 @@ struct GemmParams {
 
 template <bool DUAL, int NT>
 struct GemmCfg {
-    static constexpr int NA = DUAL ? 2 : 1;
+    static constexpr int NA = 2;  // gate + up, or the two 128-row halves of a down tile
     static constexpr int STAGE = NA * BA + NT * BB;
-    static constexpr int NSTAGE = DUAL ? 3 : 4;
+    static constexpr int NSTAGE = 3;
     static constexpr int NBUF = 4;  // TMEM accumulator buffers (K blocks in flight)
     static constexpr int EPI = DUAL ? HT * TN * TM : TN * TM * 4;
     // per-tile tables (weight scale per K block, gate/up column x scale or down pair gate,
@@ -701,7 +702,7 @@ template <bool DUAL, int NT>
 __global__ void __launch_bounds__(NTH, 1) pf_gemm_kernel(const __grid_constant__ GemmParams q) {
     using C = GemmCfg<DUAL, NT>;
     constexpr int TMEM_COLS = 512;
-    constexpr int BUFC = DUAL ? 2 * TN : TN;  // TMEM columns of one buffer
+    constexpr int BUFC = 2 * TN;  // TMEM columns of one buffer (two accumulators)
     extern __shared__ __align__(1024) uint8_t gsm_raw[];
     uint8_t* const sm = gsm_raw + ((1024u - (smem_u32(gsm_raw) & 1023u)) & 1023u);
     uint8_t* const stages = sm;
@@ -751,7 +752,7 @@ __global__ void __launch_bounds__(NTH, 1) pf_gemm_kernel(const __grid_constant__
             const int kdim = DUAL ? q.H : (sh ? q.SI : q.I);
             const int nkb = kdim / KB;
             const int pos0 = __ldg(q.gbase + g) + n * TN;
-            const bool inb = pos0 >= 0 && pos0 + TN <= q.PP && (m + 1) * TM <= (DUAL ? (sh ? q.SI : q.I) : q.H);
+            const bool inb = pos0 >= 0 && pos0 + TN <= q.PP && (DUAL ? (m + 1) * TM <= (sh ? q.SI : q.I) : (m + 1) * TMD <= q.H);
             const int slot = ti & 1;
             bool ok = true;
             if (ti >= 2) {
@@ -777,9 +778,11 @@ __global__ void __launch_bounds__(NTH, 1) pf_gemm_kernel(const __grid_constant__
                     wsA[k] = __ldg((sh ? q.ssc : q.sc) + rb + k);
                     wsB[k] = __ldg((sh ? q.ssc2 : q.sc2) + rb + k);
                 } else {
+                    // the two 128-row halves of the tile: row blocks 2m and 2m + 1
                     const int ig = sh ? q.SI : q.I, nbpI = cz_nbp(ig);
-                    const size_t rb = sh ? (size_t)m * nbpI : ((size_t)(g - q.e_lo) * cz_nblk(q.H) + m) * nbpI;
+                    const size_t rb = sh ? (size_t)(2 * m) * nbpI : ((size_t)(g - q.e_lo) * cz_nblk(q.H) + 2 * m) * nbpI;
                     wsA[k] = __ldg((sh ? q.ssc : q.sc) + rb + k);
+                    wsB[k] = __ldg((sh ? q.ssc : q.sc) + rb + nbpI + k);
                 }
             }
             for (int c = lane; c < TN; c += 32) {
@@ -809,8 +812,10 @@ __global__ void __launch_bounds__(NTH, 1) pf_gemm_kernel(const __grid_constant__
                 const int kdim = DUAL ? q.H : (sh ? q.SI : q.I);
                 const int nkb = kdim / KB;
                 const int pos0 = __ldg(q.gbase + g) + n * TN;
+                // gate/up: rows m*TM of gate and of up; down: rows m*TMD and m*TMD + TM of down
                 const int arow =
-                    DUAL ? (sh ? 0 : (g - q.e_lo) * q.I) + m * TM : (sh ? 0 : (g - q.e_lo) * q.H) + m * TM;
+                    DUAL ? (sh ? 0 : (g - q.e_lo) * q.I) + m * TM : (sh ? 0 : (g - q.e_lo) * q.H) + m * TMD;
+                const int arow2 = DUAL ? arow : arow + TM;
                 const CUtensorMap* a1 = sh ? &q.samap : &q.amap;
                 const CUtensorMap* a2 = sh ? &q.samap2 : &q.amap2;
                 for (int kb = 0; kb < nkb; ++kb, ++si) {
@@ -825,7 +830,7 @@ __global__ void __launch_bounds__(NTH, 1) pf_gemm_kernel(const __grid_constant__
                     const uint32_t dst = smem_u32(stages + (size_t)s * C::STAGE);
                     mbar_arrive_expect_tx(&B.full[s], (uint32_t)C::STAGE);
                     tma2d(dst, a1, kb * KB, arow, &B.full[s]);
-                    if (DUAL) tma2d(dst + BA, a2, kb * KB, arow, &B.full[s]);
+                    tma2d(dst + BA, a2, kb * KB, arow2, &B.full[s]);
 #pragma unroll
                     for (int j = 0; j < NT; ++j)
                         tma2d(dst + C::NA * BA + j * BB, &q.bmap, kb * KB, j * q.PP + pos0, &B.full[s]);
@@ -873,7 +878,7 @@ __global__ void __launch_bounds__(NTH, 1) pf_gemm_kernel(const __grid_constant__
                             const uint64_t bd = sdesc_sw128(sa + C::NA * BA + j * BB) + (uint64_t)(ks * 2);
                             const uint32_t acc = (ks | j) ? 1u : 0u;
                             umma(dg, sdesc_sw128(sa) + (uint64_t)(ks * 2), bd, id, acc);
-                            if (DUAL) umma(dg + TN, sdesc_sw128(sa + BA) + (uint64_t)(ks * 2), bd, id, acc);
+                            umma(dg + TN, sdesc_sw128(sa + BA) + (uint64_t)(ks * 2), bd, id, acc);
                         }
                     }
                     umma_commit(&B.empty[s]);
@@ -897,7 +902,7 @@ __global__ void __launch_bounds__(NTH, 1) pf_gemm_kernel(const __grid_constant__
             const int kdim = DUAL ? q.H : (sh ? q.SI : q.I);
             const int nkb = kdim / KB;
             const int pos0 = __ldg(q.gbase + g) + n * TN;
-            const bool inb = pos0 >= 0 && pos0 + TN <= q.PP && (m + 1) * TM <= (DUAL ? (sh ? q.SI : q.I) : q.H);
+            const bool inb = pos0 >= 0 && pos0 + TN <= q.PP && (DUAL ? (m + 1) * TM <= (sh ? q.SI : q.I) : (m + 1) * TMD <= q.H);
             const int slot = ti & 1;
             const bool tok = !*abort && bwait(&B.tabfull[slot], (ti >> 1) & 1, abort);
             if (!tok && lane == 0 && !*abort) {
@@ -909,9 +914,9 @@ __global__ void __launch_bounds__(NTH, 1) pf_gemm_kernel(const __grid_constant__
             const float* wsB = T + MAXNKB;
             const float* colt = T + 2 * MAXNKB;
             const float* colg = colt + MAXNKB * TN;
-            float acc[DUAL ? 2 : 1][32];
+            float acc[2][32];
 #pragma unroll
-            for (int a = 0; a < (DUAL ? 2 : 1); ++a)
+            for (int a = 0; a < 2; ++a)
 #pragma unroll
                 for (int c = 0; c < 32; ++c) acc[a][c] = 0.0f;
             for (int kb = 0; kb < nkb; ++kb, ++kbi) {
@@ -926,11 +931,10 @@ __global__ void __launch_bounds__(NTH, 1) pf_gemm_kernel(const __grid_constant__
                 }
                 tc_fence_after();
                 const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(bf * BUFC + chalf * 32);
-                uint32_t v0[32];
+                uint32_t v0[32], v1[32];
                 CZ_LD32(v0, ta);
+                CZ_LD32(v1, ta + TN);
                 if (DUAL) {
-                    uint32_t v1[32];
-                    CZ_LD32(v1, ta + TN);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                     tc_fence_before();
                     __syncwarp();
@@ -939,17 +943,20 @@ __global__ void __launch_bounds__(NTH, 1) pf_gemm_kernel(const __grid_constant__
 #pragma unroll
                     for (int c = 0; c < 32; ++c) {
                         acc[0][c] = __fmaf_rn(sa, __uint_as_float(v0[c]), acc[0][c]);
-                        acc[DUAL ? 1 : 0][c] = __fmaf_rn(sb, __uint_as_float(v1[c]), acc[DUAL ? 1 : 0][c]);
+                        acc[1][c] = __fmaf_rn(sb, __uint_as_float(v1[c]), acc[1][c]);
                     }
                 } else {
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&B.tempty[bf]);
-                    const float sa = wsA[kb];
+                    const float sa = wsA[kb], sb = wsB[kb];
                     const float* ct = colt + kb * TN + chalf * 32;
 #pragma unroll
-                    for (int c = 0; c < 32; ++c) acc[0][c] = __fmaf_rn(sa * ct[c], __uint_as_float(v0[c]), acc[0][c]);
+                    for (int c = 0; c < 32; ++c) {
+                        acc[0][c] = __fmaf_rn(sa * ct[c], __uint_as_float(v0[c]), acc[0][c]);
+                        acc[1][c] = __fmaf_rn(sb * ct[c], __uint_as_float(v1[c]), acc[1][c]);
+                    }
                 }
             }
             if (DUAL) {
@@ -959,7 +966,7 @@ __global__ void __launch_bounds__(NTH, 1) pf_gemm_kernel(const __grid_constant__
 #pragma unroll
                 for (int c = 0; c < 32; ++c) {
                     const float cs = colg[chalf * 32 + c];
-                    h[c] = silu_fast(acc[0][c] * cs) * (acc[DUAL ? 1 : 0][c] * cs);
+                    h[c] = silu_fast(acc[0][c] * cs) * (acc[1][c] * cs);
                     float a = fabsf(h[c]);
                     if (!(a < 3.0e38f)) a = 0.0f;
                     const uint32_t mx = redux_max_u32(__float_as_uint(a));
@@ -989,14 +996,20 @@ __global__ void __launch_bounds__(NTH, 1) pf_gemm_kernel(const __grid_constant__
                     colm[et] = 0.0f;
                 }
             } else {
-                float* Y = reinterpret_cast<float*>(epi);  // [TN][TM]
+                float* Y = reinterpret_cast<float*>(epi);  // [TN][TM], one half of the tile at a time
 #pragma unroll
-                for (int c = 0; c < 32; ++c) Y[(size_t)(chalf * 32 + c) * TM + row] = acc[0][c] * colg[chalf * 32 + c];
-                asm volatile("bar.sync 1, 256;" ::: "memory");
-                for (int k = et; inb && k < TN * (TM / 4); k += 256) {
-                    const int c = k / (TM / 4), seg = k - c * (TM / 4);
-                    const float4 v = *reinterpret_cast<const float4*>(Y + (size_t)c * TM + seg * 4);
-                    *reinterpret_cast<float4*>(q.y + (size_t)(pos0 + c) * q.H + (size_t)m * TM + seg * 4) = v;
+                for (int hf = 0; hf < 2; ++hf) {
+                    if (hf) asm volatile("bar.sync 1, 256;" ::: "memory");  // the first half is copied out
+#pragma unroll
+                    for (int c = 0; c < 32; ++c)
+                        Y[(size_t)(chalf * 32 + c) * TM + row] = acc[hf][c] * colg[chalf * 32 + c];
+                    asm volatile("bar.sync 1, 256;" ::: "memory");
+                    for (int k = et; inb && k < TN * (TM / 4); k += 256) {
+                        const int c = k / (TM / 4), seg = k - c * (TM / 4);
+                        const float4 v = *reinterpret_cast<const float4*>(Y + (size_t)c * TM + seg * 4);
+                        *reinterpret_cast<float4*>(q.y + (size_t)(pos0 + c) * q.H + (size_t)m * TMD + hf * TM +
+                                                   seg * 4) = v;
+                    }
                 }
             }
             asm volatile("bar.sync 1, 256;" ::: "memory");  // staging and tables free for the next tiles
@@ -1073,7 +1086,7 @@ bool make_sw128_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64
 }
 
 bool prefill_supported(int H, int E, int K, int I, int SI) {
-    return H % 128 == 0 && I % 128 == 0 && SI % 128 == 0 && H <= 4096 && I <= 4096 && SI <= 4096 && H >= 128 &&
+    return H % pf::TMD == 0 && I % 128 == 0 && SI % 128 == 0 && H <= 4096 && I <= 4096 && SI <= 4096 && H >= pf::TMD &&
            K >= 1 && K <= kMaxTopk && E >= K && E <= kMaxExperts;
 }
 
