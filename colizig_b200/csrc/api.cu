@@ -250,7 +250,6 @@ int gather_copy(uint8_t* dst, const colizig_moe_expert* ex, int count, size_t by
     return CZ_OK;
 }
 
-size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 // Like gather_copy for block-scale tables: every item is `rows` rows of
 // `row_bytes`, written with a padded destination pitch (rows of the resident
@@ -937,13 +936,14 @@ CZ_EXPORT int colizig_cuda_ep_shutdown(void) {
 namespace {
 
 constexpr int kNoAllocMaxHidden = 4096;
+constexpr int kNoAllocMaxTokens = 4;  // tokens per launch through the static scratch
 constexpr size_t kNoAllocSyncBytes = 768;
 constexpr size_t kNoAllocLogitBytes = 8448;
 constexpr size_t kNoAllocPartialBytes =
-    (size_t)cz::kMaxGrid * cz::kDecodeMaxTokens * kNoAllocMaxHidden * sizeof(float);
+    (size_t)cz::kMaxGrid * kNoAllocMaxTokens * kNoAllocMaxHidden * sizeof(float);
 constexpr size_t kNoAllocBytes = kNoAllocSyncBytes + kNoAllocLogitBytes + kNoAllocPartialBytes;
 static_assert(cz::kSyncWords * sizeof(uint32_t) <= kNoAllocSyncBytes, "sync words");
-static_assert((size_t)cz::kDecodeMaxTokens * ((cz::kMaxExperts + 1 + 3) & ~3) * sizeof(float) <= kNoAllocLogitBytes,
+static_assert((size_t)kNoAllocMaxTokens * ((cz::kMaxExperts + 1 + 3) & ~3) * sizeof(float) <= kNoAllocLogitBytes,
               "logits");
 static_assert(kNoAllocBytes == 10494976, "the size stated in colizig_cuda.h");
 
@@ -991,8 +991,9 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int bf16 = x_dtype == COLIZIG_X_BF16;
     const size_t xelt = bf16 ? 2 : 4;
-    const int tmax = cz::decode_max_tokens((int)L.d.hidden, (int)L.d.experts, (int)L.d.topk, (int)L.d.inter,
-                                           (int)L.d.shared_inter, bf16, g.num_sms);
+    int tmax = cz::decode_max_tokens((int)L.d.hidden, (int)L.d.experts, (int)L.d.topk, (int)L.d.inter,
+                                     (int)L.d.shared_inter, bf16, g.num_sms);
+    if (tmax > kNoAllocMaxTokens) tmax = kNoAllocMaxTokens;
     if (tmax < 1) return CZ_ESHAPE;
     for (int t0 = 0; t0 < T; t0 += tmax) {
         const int n = T - t0 < tmax ? T - t0 : tmax;

@@ -76,14 +76,12 @@ constexpr int MAXSLOT = 6;
 constexpr int RING_BYTES = NSLOT * SLOT_BYTES;  // the smallest ring (also stages phase R)
 constexpr int BOX_ROWS = 256;             // down-weight TMA box: 16 bytes x 256 rows
 constexpr int JH = 4;                     // E4M3 terms of h
-constexpr int DB = 4;                     // down tiles per batch of one warp
 constexpr int MAXCH = 32;                 // chunks per CTA (h terms of all of them stay in shared memory)
 constexpr int MAXT = kDecodeMaxTokens;    // 4
 constexpr int MAXK = kMaxTopk;            // 16
 constexpr int MAXE = kMaxExperts;         // 512
 constexpr int MAXP = MAXT * (MAXK + 1);   // (token, slot) pairs incl. shared-expert pairs: 68
 constexpr int MAXG = MAXP;                // groups <= pairs
-constexpr int MAXM = MAXE / 32;           // router values per lane
 constexpr int SMEM_LIMIT = 227 * 1024;
 
 static_assert(GU_BYTES + SC_BYTES <= SLOT_BYTES, "slot");
@@ -126,7 +124,7 @@ __host__ __device__ inline Carve carve(int T, int H, int x_bf16) {
     c.CS = ((H + 127) & ~127) + 64;  // column stride = 64 mod 128: lanes of 2 columns hit disjoint banks
     // the rest of the map decides how many slots fit
     const uint32_t rest = (((uint32_t)(T * c.JX * c.CS) + 127u) & ~127u) + 2 * NCW * 2 * 16 * 16 * 4 +
-                          MAXCH * 16 * 16 + (((uint32_t)sizeof(DecodeMisc) + 127u) & ~127u);
+                          MAXCH * 16 * MAXT * 4 + (((uint32_t)sizeof(DecodeMisc) + 127u) & ~127u);
     const int fit = ((int)SMEM_LIMIT - 1024 - (int)rest) / SLOT_BYTES;
     c.ns = fit < NSLOT ? NSLOT : (fit > MAXSLOT ? MAXSLOT : fit);
     uint32_t off = (uint32_t)c.ns * SLOT_BYTES;
@@ -135,7 +133,7 @@ __host__ __device__ inline Carve carve(int T, int H, int x_bf16) {
     c.red = off;
     off += 2 * NCW * 2 * 16 * 16 * 4;  // two chunks in flight: [chunk parity][warp][gate/up][16 x 16]
     c.hterm = off;
-    off += MAXCH * 16 * 16;
+    off += MAXCH * 16 * MAXT * 4;  // h of every chunk: [chunk][16 rows][MAXT tokens] f32
     c.misc = off;
     off += ((uint32_t)sizeof(DecodeMisc) + 127u) & ~127u;
     c.total = off;
@@ -646,8 +644,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         const int nkbH = cz_nblk(H);           // 128-column blocks of H
         // down: tiles per warp (each warp's accumulators live in registers across
         // all chunks) and the output rows of one slab
-        const int TPW = (T * JH <= 8) ? 16 : 8;
-        const int nmD = (T * JH + 7) >> 3;
+        // column groups of 8 (token, term) columns, and 16-row tiles per warp (NMD x TPW = 16 accumulators)
+        constexpr int NMD = T * JH <= 8 ? 1 : (T * JH <= 16 ? 2 : 4);
+        constexpr int TPW = 16 / NMD;
         const int OSr = TPW * 16 * NCW;
 
         if (warp == PW) {
@@ -789,7 +788,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                         const float xsc = s.xscale[tk];
                         hw = s.pg[pairs[q]] * (silu_fast(gs * xsc) * (us * xsc));
                     }
-                    reinterpret_cast<float*>(hterm)[ci * 64 + r * 4 + tk] = hw;
+                    reinterpret_cast<float*>(hterm)[(ci * 16 + r) * MAXT + tk] = hw;
                     float mh = fabsf(hw);
                     if (!(mh < 3.0e38f)) mh = 0.0f;
 #pragma unroll
@@ -964,7 +963,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                     const int nh = ch + 1 < ch_hi ? 2 : 1;
                     const uint8_t* stA = nullptr;
                     const uint8_t* stB = nullptr;
-                    uint32_t bfA[2][2] = {}, bfB[2][2] = {};
+                    uint32_t bfA[2][NMD] = {}, bfB[2][NMD] = {};
                     bool ok = !s.abort;
 #pragma unroll 1
                     for (int hh = 0; hh < nh && ok; ++hh) {
@@ -979,19 +978,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                         const uint8_t* stage = ring + (size_t)slot * SLOT_BYTES;
                         const float* stab = reinterpret_cast<const float*>(stage + GU_BYTES);
                         // B fragments: lane column c = 8m + g = (token c/4, term c%4), rows 4t..4t+3
-                        uint32_t bw[2][2];
+                        uint32_t bw[2][NMD];
 #pragma unroll
                         for (int ol = 0; ol < 2; ++ol)
 #pragma unroll
-                            for (int m = 0; m < 2; ++m) {
+                            for (int m = 0; m < NMD; ++m) {
                                 const int cc = 8 * m + g, tk = cc >> 2, jt = cc & 3;
                                 const int ob = obw + ol;
                                 uint32_t word = 0u;
-                                if (m < nmD && tk < T && (ob << 7) < o0 + OSl) {
+                                if (tk < T && (ob << 7) < o0 + OSl) {
                                     const float f = stab[(ob - (o0 >> 7)) * nbpI + ib];
                                     const float sc = scale2(f, s.hexp[tk][ob]);
-                                    const float* hv = reinterpret_cast<const float*>(hterm) + ci * 64 + (4 * t) * 4 + tk;
-                                    float a0 = hv[0] * sc, b0 = hv[4] * sc, a1 = hv[8] * sc, b1 = hv[12] * sc;
+                                    const float* hv = reinterpret_cast<const float*>(hterm) + (ci * 16 + 4 * t) * MAXT + tk;
+                                    float a0 = hv[0] * sc, b0 = hv[MAXT] * sc, a1 = hv[2 * MAXT] * sc, b1 = hv[3 * MAXT] * sc;
 #pragma unroll
                                     for (int j = 0; j < JH; ++j) {
                                         const uint32_t d0 = e4m3_term2(a0, b0), d1 = e4m3_term2(a1, b1);
@@ -1005,20 +1004,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
 #pragma unroll
                             for (int ol = 0; ol < 2; ++ol)
 #pragma unroll
-                                for (int m = 0; m < 2; ++m) bfA[ol][m] = bw[ol][m];
+                                for (int m = 0; m < NMD; ++m) bfA[ol][m] = bw[ol][m];
                         } else {
                             stB = stage;
 #pragma unroll
                             for (int ol = 0; ol < 2; ++ol)
 #pragma unroll
-                                for (int m = 0; m < 2; ++m) bfB[ol][m] = bw[ol][m];
+                                for (int m = 0; m < NMD; ++m) bfB[ol][m] = bw[ol][m];
                         }
                     }
                     if (ok) {
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            if (i < TPW && tw0 + i < ntile) {
-                                const size_t ra = (size_t)((tw0 + i) * 16 + g) * 16 + 4 * t;
+                        for (int it = 0; it < TPW; ++it) {
+                            if (tw0 + it < ntile) {
+                                const size_t ra = (size_t)((tw0 + it) * 16 + g) * 16 + 4 * t;
                                 const uint32_t a0 = *reinterpret_cast<const uint32_t*>(stA + ra);
                                 const uint32_t a1 = *reinterpret_cast<const uint32_t*>(stA + ra + 8 * 16);
                                 uint32_t a2 = 0u, a3 = 0u;
@@ -1026,13 +1025,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                                     a2 = *reinterpret_cast<const uint32_t*>(stB + ra);
                                     a3 = *reinterpret_cast<const uint32_t*>(stB + ra + 8 * 16);
                                 }
-                                const int obl = (i * 16) >> 7;
-                                if (nmD == 1) {
-                                    mma_e4m3(accd[i], a0, a1, a2, a3, bfA[obl][0], bfB[obl][0]);
-                                } else if (i < 8) {
-                                    mma_e4m3(accd[2 * i], a0, a1, a2, a3, bfA[obl][0], bfB[obl][0]);
-                                    mma_e4m3(accd[2 * i + 1], a0, a1, a2, a3, bfA[obl][1], bfB[obl][1]);
-                                }
+                                const int obl = (it * 16) >> 7;
+#pragma unroll
+                                for (int m = 0; m < NMD; ++m)
+                                    mma_e4m3(accd[it * NMD + m], a0, a1, a2, a3, bfA[obl][m], bfB[obl][m]);
                             }
                         }
                         __syncwarp();
@@ -1049,8 +1045,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 // CTA's partial rows (every (token, row) of the slab is written, zeros included)
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const int tile = nmD == 1 ? i : (i >> 1), m = nmD == 1 ? 0 : (i & 1);
-                    if (tile < TPW) {
+                    const int tile = i / NMD, m = i % NMD;
+                    {
                         float v0 = accd[i][0] + accd[i][1], v1 = accd[i][2] + accd[i][3];
                         v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
                         v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
@@ -1162,6 +1158,11 @@ int decode_max_tokens(int H, int E, int K, int I, int SI, int x_bf16, int num_sm
     const int IM16 = (I > SI ? I : SI) / CR;  // chunks of the largest group
     int t = MAXT;
     while (t > 0) {
+        // gate/up MMA columns: a group holds at most t pairs, each as JX E4M3 term columns (<= 16)
+        if (t * (x_bf16 ? 2 : 3) > 16) {
+            --t;
+            continue;
+        }
         const int worst_chunks = (t * K + (SI ? t : 0)) * IM16;  // every pair its own group
         if ((worst_chunks + num_sms - 1) / num_sms > MAXCH) {
             --t;
@@ -1254,8 +1255,9 @@ int decode_launch(const DecodeParams& prm, int num_sms, cudaStream_t stream) {
     const int tmax = decode_max_tokens(prm.H, prm.E, prm.K, prm.I, prm.SI, prm.x_bf16, num_sms);
     if (prm.T < 1 || prm.T > tmax) return CZ_ESHAPE;
     if (prm.rms_w && prm.x_bf16) return CZ_EARGS;
-    static void (*const kern[MAXT])(DecodeParams) = {moe_decode_kernel<1>, moe_decode_kernel<2>,
-                                                      moe_decode_kernel<3>, moe_decode_kernel<4>};
+    static_assert(MAXT == 4, "one kernel instance per token count");
+    static void (*const kern[MAXT])(DecodeParams) = {moe_decode_kernel<1>, moe_decode_kernel<2>, moe_decode_kernel<3>,
+                                                      moe_decode_kernel<4>};
     if (!g_attr_set) {
         for (int i = 0; i < MAXT; ++i)
             if (cudaFuncSetAttribute(kern[i], cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT) != cudaSuccess)

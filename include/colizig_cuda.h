@@ -160,8 +160,8 @@ int colizig_cuda_moe_check(void* stream);
  * (which synchronises the device) would stall every stream.  The scratch lives
  * in one static device array of 10,494,976 bytes inside the library, so no
  * call allocates.  Limits: hidden <= 4096, experts <= 512, topk <= 16, a
- * device of at most 160 SMs (the same launches of up to 4 tokens as
- * colizig_cuda_moe_forward; larger T runs as several launches); a layer beyond
+ * device of at most 160 SMs (launches of up to 4 tokens; larger T runs as
+ * several launches); a layer beyond
  * them returns -8 before anything is launched.  The FIRST call on a device does set-up (it looks up the
  * scratch address and configures the kernel), so make it before any stream
  * capture.  The scratch is shared: calls whose executions overlap (two

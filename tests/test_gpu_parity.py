@@ -176,7 +176,7 @@ def test_moe_c2_decode_full_size():
 
 def test_moe_c2_chunked_and_odd_token_counts():
     d, w, L = _device_layer("c2", 1, 201)
-    _check_layer(d, w, L, [3, 32, 33, 70], seed0=77, bf16=False)
+    _check_layer(d, w, L, [3, 5, 32, 33, 70], seed0=77, bf16=False)
     L.unregister()
 
 
