@@ -590,8 +590,9 @@ __global__ void pf_dispatch_kernel(const DispatchParams q) {
 #pragma unroll
         for (int j = 0; j < 3; ++j) out[j] = make_uint4(words[j][0], words[j][1], words[j][2], words[j][3]);
     }
-    for (int j = 0; j < q.JX; ++j)
-        *reinterpret_cast<uint4*>(q.s.X + ((size_t)j * q.s.PP + r) * q.H + (size_t)c16 * 16) = out[j];
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+        if (j < q.JX) *reinterpret_cast<uint4*>(q.s.X + ((size_t)j * q.s.PP + r) * q.H + (size_t)c16 * 16) = out[j];
 }
 
 // ============================ tcgen05 GEMM ============================
