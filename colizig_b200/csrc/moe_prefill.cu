@@ -51,7 +51,7 @@ constexpr int MAXK = kMaxTopk;
 constexpr int MAXNKB = 32;   // K blocks per tile (H or I <= 4096)
 constexpr int HT = 3;        // E4M3 terms of h
 constexpr int TMD = 2 * TM;  // output rows of a down tile: two 128-row MMAs share the h operand
-constexpr int GCH = 1024;    // pairs per chunk of the grouping kernels
+constexpr int GCH = 256;     // pairs per chunk of the grouping kernels
 
 __host__ __device__ inline int pad64(int n) { return (n + TN - 1) / TN * TN; }
 
@@ -396,9 +396,10 @@ __device__ __forceinline__ int pair_group(const GroupParams& q, int p) {
 
 // Grouping = a stable counting sort of the pairs by group, in three launches:
 // count (per chunk of GCH pairs, a histogram of the held groups), scan (one
-// block: per-group totals, each chunk's offset inside its group, padded group
-// bases and the GEMM tile prefixes) and place (one warp per chunk: each pair's
-// rank among the chunk's pairs of its group, in pair order).  Pairs of groups
+// block: per-group totals and each chunk's offset inside its group, a warp per
+// group scanning over the chunks, then the padded group bases and the GEMM tile
+// prefixes) and place (one warp per chunk: each pair's rank among the chunk's
+// pairs of its group, in pair order).  Pairs of groups
 // held elsewhere (expert parallelism) get position -1.
 __global__ void pf_count_kernel(const GroupParams q) {
     extern __shared__ int hist[];  // [Eg]
@@ -444,17 +445,30 @@ __device__ int block_exclusive_scan(int& v, int* wsum) {
 // One block of 1024 threads; groups g = thread, thread + 1024, ... (Eg <= 1024 here).
 __global__ void pf_scan_kernel(const GroupParams q) {
     __shared__ int wsum[32];
+    __shared__ int gtot[1024];
     const int Eg = q.s.Eg, nch = (q.s.P + GCH - 1) / GCH, g = threadIdx.x;
-    int n = 0;
-    if (g < Eg) {
-        for (int b = 0; b < nch; ++b) {
-            int* c = q.s.ccnt + (size_t)b * Eg + g;
-            const int v = *c;
-            *c = n;
-            n += v;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // per group (one warp each): exclusive prefix of its counts over the chunks, in chunk order
+    for (int gg = warp; gg < Eg; gg += 32) {
+        int run = 0;
+        for (int b0 = 0; b0 < nch; b0 += 32) {
+            const int b = b0 + lane;
+            int* c = q.s.ccnt + (size_t)b * Eg + gg;
+            const int v = b < nch ? *c : 0;
+            int x = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
+            }
+            if (b < nch) *c = run + x - v;
+            run += __shfl_sync(0xffffffffu, x, 31);
         }
-        q.s.cnt[g] = n;
+        if (lane == 0) gtot[gg] = run;
     }
+    __syncthreads();
+    const int n = g < Eg ? gtot[g] : 0;
+    if (g < Eg) q.s.cnt[g] = n;
     const int np = pad64(n);
     const int ig = g == q.E ? q.SI : q.I;
     // gate/up tiles span 2*TN positions (a 64-position tail when np is an odd multiple of TN), down tiles TN
