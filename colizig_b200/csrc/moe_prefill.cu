@@ -246,96 +246,90 @@ __device__ void pf_route_token(const float* __restrict__ lg, const RouteParams& 
 // Router logits as a tiled CUDA-core GEMM that keeps dotF32's exact order:
 // lane c of a warp runs chain c (elements c, c+32, c+64, ... in order) for an
 // 8-row x 8-token register tile; the CTA (8 warps) covers 32 router rows x 16
-// tokens, with x and router rows staged in shared memory in K chunks (double
-// buffered through registers).  The 32 chains of every (row, token) are then
-// combined in the reference's order (per chain group of 8 lanes, then across
-// the groups) through shared memory.
-constexpr int LG_R = 32, LG_T = 16, LG_KC = 256;
+// tokens.  x and the router rows stream through a 3-stage shared-memory ring
+// of 128-column chunks with cp.async (no staging registers, so two CTAs fit an
+// SM).  The 32 chains of every (row, token) are then combined in the
+// reference's order (per chain group of 8 lanes, then across the groups)
+// through shared memory.  H is a multiple of 128 on this path.
+constexpr int LG_R = 32, LG_T = 16, LG_KC = 128, LG_ST = 3;
+constexpr int LG_STAGE_F = (LG_T + LG_R) * LG_KC;  // floats per stage (x as f32 or bf16 pairs, then w)
+constexpr int LG_SMEM = LG_ST * LG_STAGE_F * 4 > 8 * 64 * 33 * 4 ? LG_ST * LG_STAGE_F * 4 : 8 * 64 * 33 * 4;
 
-__global__ void __launch_bounds__(256) pf_logits_kernel(const RouteParams q) {
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(256, 2) pf_logits_kernel(const RouteParams q) {
     extern __shared__ __align__(16) float lgsm[];
-    float (*xs)[LG_T][LG_KC] = reinterpret_cast<float (*)[LG_T][LG_KC]>(lgsm);                    // [2][16][256]
-    float (*ws)[LG_R][LG_KC] = reinterpret_cast<float (*)[LG_R][LG_KC]>(lgsm + 2 * LG_T * LG_KC);  // [2][32][256]
     const int H = q.H, E = q.E, LS = logit_stride(E);
     const int Er = E + (q.SI ? 1 : 0);
     const int t0 = blockIdx.x * LG_T, r0 = blockIdx.y * LG_R;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rg = warp & 3, tg = warp >> 2;  // rows rg*8.., tokens tg*8..
-    // this thread's share of a chunk: x 16 x 256 (4 float4 each), w 32 x 256 (8 float4 each)
-    auto load_chunk = [&](int k0, int kc, float4 (&xr)[4], float4 (&wr)[8]) {
+    const bool xbf = q.x_bf16 != 0;
+    // stage s: x [16][128] (f32, or bf16 in the first half), then w [32][128] f32
+    auto issue = [&](int st, int k0) {
+        float* xs = lgsm + st * LG_STAGE_F;
+        float* ws = xs + LG_T * LG_KC;
+        if (xbf) {  // 16 x 128 bf16 = 256 pieces of 16 bytes: one per thread
+            const int t = tid >> 4, k8 = (tid & 15) * 8;
+            const bool v = t0 + t < q.T;
+            const uint16_t* src = reinterpret_cast<const uint16_t*>(q.x) + (size_t)(v ? t0 + t : 0) * H + k0 + k8;
+            cp_async16(reinterpret_cast<uint16_t*>(xs) + t * LG_KC + k8, src, v);
+        } else {  // 16 x 128 f32 = 512 pieces
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int f = tid + 256 * u;  // float4 index in [16][64]
-            const int t = f >> 6, k4 = (f & 63) * 4;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t0 + t < q.T && k4 < kc) {
-                const size_t gi = (size_t)(t0 + t) * H + k0 + k4;
-                if (q.x_bf16) {
-                    const uint2 raw = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(q.x) + gi);
-                    v = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
-                                    __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u));
-                } else {
-                    v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(q.x) + gi);
-                }
+            for (int u = 0; u < 2; ++u) {
+                const int f = tid + 256 * u, t = f >> 5, k4 = (f & 31) * 4;
+                const bool v = t0 + t < q.T;
+                const float* src = reinterpret_cast<const float*>(q.x) + (size_t)(v ? t0 + t : 0) * H + k0 + k4;
+                cp_async16(xs + t * LG_KC + k4, src, v);
             }
-            xr[u] = v;
         }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int f = tid + 256 * u;  // float4 index in [32][64]
-            const int r = f >> 6, k4 = (f & 63) * 4;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int u = 0; u < 4; ++u) {  // 32 x 128 f32 = 1024 pieces
+            const int f = tid + 256 * u, r = f >> 5, k4 = (f & 31) * 4;
             const int e = r0 + r;
-            if (e < Er && k4 < kc) {
-                const float* wr0 = e < E ? q.router + (size_t)e * H : q.sh_gate;
-                v = __ldg(reinterpret_cast<const float4*>(wr0 + k0 + k4));
-            }
-            wr[u] = v;
+            const bool v = e < Er;
+            const float* row = !v ? q.router : (e < E ? q.router + (size_t)e * H : q.sh_gate);
+            cp_async16(ws + r * LG_KC + k4, row + k0 + k4, v);
         }
-    };
-    auto store_chunk = [&](int b, const float4 (&xr)[4], const float4 (&wr)[8]) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int f = tid + 256 * u;
-            *reinterpret_cast<float4*>(&xs[b][f >> 6][(f & 63) * 4]) = xr[u];
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int f = tid + 256 * u;
-            *reinterpret_cast<float4*>(&ws[b][f >> 6][(f & 63) * 4]) = wr[u];
-        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
     };
     float acc[8][8];
 #pragma unroll
     for (int r = 0; r < 8; ++r)
 #pragma unroll
         for (int t = 0; t < 8; ++t) acc[r][t] = 0.0f;
-    float4 xr[4], wr[8];
-    load_chunk(0, min(LG_KC, H), xr, wr);
-    store_chunk(0, xr, wr);
-    __syncthreads();
-    int b = 0;
-    for (int k0 = 0; k0 < H; k0 += LG_KC) {
-        const int kc = min(LG_KC, H - k0);
-        const bool more = k0 + LG_KC < H;
-        if (more) load_chunk(k0 + LG_KC, min(LG_KC, H - k0 - LG_KC), xr, wr);
-        for (int j = 0; j < kc / 32; ++j) {
+    const int nkc = H / LG_KC;
+    issue(0, 0);
+    if (nkc > 1) issue(1, LG_KC);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int kc = 0; kc < nkc; ++kc) {
+        asm volatile("cp.async.wait_group 1;" ::: "memory");  // chunk kc has landed (kc + 1 may be in flight)
+        __syncthreads();                                      // ... for every thread; stage (kc + 2) % 3 is free
+        if (kc + 2 < nkc) issue((kc + 2) % LG_ST, (kc + 2) * LG_KC);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        const float* xs = lgsm + (kc % LG_ST) * LG_STAGE_F;
+        const float* ws = xs + LG_T * LG_KC;
+        const uint16_t* xh = reinterpret_cast<const uint16_t*>(xs);
+#pragma unroll
+        for (int j = 0; j < LG_KC / 32; ++j) {
             const int k = j * 32 + lane;
             float wv[8], xv[8];
 #pragma unroll
-            for (int r = 0; r < 8; ++r) wv[r] = ws[b][rg * 8 + r][k];
+            for (int r = 0; r < 8; ++r) wv[r] = ws[(rg * 8 + r) * LG_KC + k];
 #pragma unroll
-            for (int t = 0; t < 8; ++t) xv[t] = xs[b][tg * 8 + t][k];
+            for (int t = 0; t < 8; ++t)
+                xv[t] = xbf ? __uint_as_float((uint32_t)xh[(tg * 8 + t) * LG_KC + k] << 16) : xs[(tg * 8 + t) * LG_KC + k];
 #pragma unroll
             for (int r = 0; r < 8; ++r)
 #pragma unroll
                 for (int t = 0; t < 8; ++t) acc[r][t] = __fmaf_rn(xv[t], wv[r], acc[r][t]);
         }
-        __syncthreads();
-        if (more) store_chunk(b ^ 1, xr, wr);
-        __syncthreads();
-        b ^= 1;
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // the staging is reused below
     // combine the 32 chains of each (row, token) in the reference's order:
     // total[l] = (((0 + acc0[l]) + acc1[l]) + acc2[l]) + acc3[l] (chain k*8 + l), then sum over l
     float* cs = lgsm + warp * (64 * 33);  // this warp's [64 pairs][33] (staging reused)
@@ -1206,7 +1200,7 @@ int prefill_run(const PrefillLayer& L, const void* x, int x_bf16, int T, const f
         q.xexp = s.xexp;
         q.sg = s.sg;
         const int Er = E + (SI ? 1 : 0);
-        const int smem = 2 * (LG_T + LG_R) * LG_KC * 4;
+        const int smem = LG_SMEM;
         static bool attr = false;
         if (!attr) {
             if (cudaFuncSetAttribute(pf_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
