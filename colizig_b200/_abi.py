@@ -41,6 +41,7 @@ MOE_SYMBOLS = (
 
 COLIZIG_PTR_DEVICE = 1
 COLIZIG_EP = 2
+COLIZIG_EP_SHARDED = 4
 COLIZIG_X_F32 = 0
 COLIZIG_X_BF16 = 1
 

@@ -119,6 +119,9 @@ struct Ctx {
     bool ep_on = false;
     int ep_rank = 0, ep_world = 1;
     ncclComm_t ep_comm = nullptr;
+    // sharded expert parallelism (prefill): routing of this rank's tokens, exchange buffers
+    DevBuf sh_idx, sh_gates, sh_xn, sh_slot, sh_counts, sh_allc, sh_tmp, sh_send, sh_recv, sh_x, sh_ridx, sh_rgates,
+        sh_part, sh_back;
     // kernel timer (benchmarks): CUDA event pairs around the dominant launches
     std::vector<cudaEvent_t> tm_ev;
     std::vector<int> tm_kind;
@@ -135,6 +138,11 @@ struct NcclApi {
     ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
     ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*allGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*groupStart)() = nullptr;
+    ncclResult_t (*groupEnd)() = nullptr;
     bool load() {
         if (h) return true;
         void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
@@ -144,7 +152,14 @@ struct NcclApi {
         commInitRank = reinterpret_cast<decltype(commInitRank)>(dlsym(lib, "ncclCommInitRank"));
         allReduce = reinterpret_cast<decltype(allReduce)>(dlsym(lib, "ncclAllReduce"));
         commDestroy = reinterpret_cast<decltype(commDestroy)>(dlsym(lib, "ncclCommDestroy"));
-        if (!getUniqueId || !commInitRank || !allReduce || !commDestroy) return false;
+        allGather = reinterpret_cast<decltype(allGather)>(dlsym(lib, "ncclAllGather"));
+        send = reinterpret_cast<decltype(send)>(dlsym(lib, "ncclSend"));
+        recv = reinterpret_cast<decltype(recv)>(dlsym(lib, "ncclRecv"));
+        groupStart = reinterpret_cast<decltype(groupStart)>(dlsym(lib, "ncclGroupStart"));
+        groupEnd = reinterpret_cast<decltype(groupEnd)>(dlsym(lib, "ncclGroupEnd"));
+        if (!getUniqueId || !commInitRank || !allReduce || !commDestroy || !allGather || !send || !recv ||
+            !groupStart || !groupEnd)
+            return false;
         h = lib;
         return true;
     }
@@ -206,7 +221,8 @@ void shutdown_locked() {
     for (auto& kv : g.layers) free_layer(kv.second);
     g.layers.clear();
     for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.partial, &g.pf_scratch, &g.io_x, &g.io_out, &g.io_idx,
-                      &g.io_gates, &g.ones})
+                      &g.io_gates, &g.ones, &g.sh_idx, &g.sh_gates, &g.sh_xn, &g.sh_slot, &g.sh_counts, &g.sh_allc,
+                      &g.sh_tmp, &g.sh_send, &g.sh_recv, &g.sh_x, &g.sh_ridx, &g.sh_rgates, &g.sh_part, &g.sh_back})
         b->release();
     if (g.sync) cudaFree(g.sync);
     for (cudaEvent_t e : g.tm_ev) cudaEventDestroy(e);
@@ -398,6 +414,139 @@ int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uin
         if (nccl.allReduce(out, out, (size_t)T * L.d.hidden, ncclFloat, ncclSum, g.ep_comm, st) != ncclSuccess)
             return CZ_ENCCL;
     }
+    return CZ_OK;
+}
+
+// Expert parallelism with sharded tokens (prefill): every rank passes its own
+// T tokens (T may differ between ranks, 0 included) and gets their outputs.
+// Each rank routes its tokens, sends every token row once to each rank holding
+// one of its top-k experts (row + the token's ids and gates), runs the grouped
+// pipeline on the rows it receives (pairs of experts held elsewhere are
+// skipped), returns each row's partial sum, and adds its tokens' partials in
+// ascending rank order (+ residual).  The exchanges are NCCL send/recv groups
+// sized from one all-gather of the per-destination row counts (the host reads
+// the counts, so this path synchronises the stream once per call).
+int moe_run_sharded(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uint32_t* idx_out,
+                    float* gates_out, const float* rms_w, float eps, const float* residual, cudaStream_t st) {
+    if (!L.ep || g.ep_world < 2 || !g.ep_comm) return CZ_EARGS;
+    if (L.d.shared_inter || !L.pf_ok) return CZ_ESHAPE;  // the same verdict on every rank (same layer)
+    const int W = g.ep_world, me = g.ep_rank;
+    const int K = (int)L.d.topk, E = (int)L.d.experts, H = (int)L.d.hidden;
+    // Until the first collective, a failure here is only recorded: the rank still takes
+    // part in the all-gather below (flagging itself), so its peers never wait for it.
+    int local_rc = ensure_sync() ? CZ_EALLOC : CZ_OK;
+    // 1. routing of this rank's tokens
+    const size_t tk = (size_t)(T > 0 ? T : 1);
+    if (!g.sh_idx.ensure(tk * K * 4) || !g.sh_gates.ensure(tk * K * 4) || !g.sh_slot.ensure(tk * W * 4) ||
+        !g.sh_tmp.ensure(tk * 4) || (rms_w && !g.sh_xn.ensure(tk * H * 4)))
+        local_rc = CZ_EALLOC;
+    if (!g.sh_counts.ensure((size_t)(W + 2) * 4) || !g.sh_allc.ensure((size_t)W * (W + 2) * 4))
+        return CZ_EALLOC;  // (a few bytes; without them there is nothing to exchange at all)
+    if (!local_rc && T > 0) {
+        const size_t need = cz::prefill_scratch_bytes(T, H, E, K, (int)L.d.inter, 0, g.num_sms);
+        local_rc = g.pf_scratch.ensure(need)
+                       ? cz::prefill_route(L.pf, x, x_bf16, T, rms_w, eps, g.sh_idx.as<uint32_t>(),
+                                           g.sh_gates.as<float>(), rms_w ? g.sh_xn.as<float>() : nullptr,
+                                           g.pf_scratch.p, g.pf_scratch.cap, st)
+                       : CZ_EALLOC;
+    }
+    const void* xs = rms_w ? g.sh_xn.p : x;
+    const int xbf = rms_w ? 0 : x_bf16;
+    const size_t xrow = (size_t)H * (xbf ? 2 : 4);
+    const size_t rs = (xrow + (size_t)8 * K + 15) & ~(size_t)15;
+    // 2. destinations and row counts; 3. every rank's counts
+    if (!local_rc)
+        local_rc = cz::ep_plan(g.sh_idx.as<uint32_t>(), T, K, E, W, g.sh_slot.as<int>(), g.sh_counts.as<int>(),
+                               g.sh_tmp.p, g.sh_tmp.cap, st);
+    if (local_rc && cudaMemsetAsync(g.sh_counts.p, 0, (size_t)W * 4, st) != cudaSuccess) return local_rc;
+    int rc = CZ_OK;
+    // each rank's row: W counts, its row stride and its hidden size, so that every rank
+    // can check that all of them will exchange rows of the same size
+    const int meta[2] = {local_rc ? -1 : (int)rs, H};  // -1: this rank failed, every rank stops
+    if (cudaMemcpyAsync(g.sh_counts.as<int>() + W, meta, sizeof meta, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return CZ_EH2D;
+    const int CW = W + 2;
+    if (nccl.allGather(g.sh_counts.p, g.sh_allc.p, (size_t)CW, ncclInt32, g.ep_comm, st) != ncclSuccess) return CZ_ENCCL;
+    std::vector<int> allc((size_t)W * CW);
+    if (cudaMemcpyAsync(allc.data(), g.sh_allc.p, allc.size() * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return CZ_ED2H;
+    for (int r = 0; r < W; ++r)  // the same verdict on every rank: no exchange of mismatched sizes
+        if (allc[(size_t)r * CW + W] != (int)rs || allc[(size_t)r * CW + W + 1] != H)
+            return local_rc ? local_rc : CZ_EARGS;
+    std::vector<size_t> scnt(W), rcnt(W), soff(W + 1, 0), roff(W + 1, 0);
+    for (int d = 0; d < W; ++d) {
+        scnt[d] = (size_t)allc[(size_t)me * CW + d];
+        rcnt[d] = (size_t)allc[(size_t)d * CW + me];
+        soff[d + 1] = soff[d] + scnt[d];
+        roff[d + 1] = roff[d] + rcnt[d];
+    }
+    const size_t S = soff[W], R = roff[W];
+    // every buffer of the exchange, then one all-reduce (min) of the ranks' verdicts, so that
+    // no rank enters a send/recv its peers will not match
+    const bool bufs_ok =
+        g.sh_send.ensure((S ? S : 1) * rs) && g.sh_recv.ensure((R ? R : 1) * rs) &&
+        g.sh_x.ensure((R ? R : 1) * xrow) && g.sh_ridx.ensure((R ? R : 1) * K * 4) &&
+        g.sh_rgates.ensure((R ? R : 1) * K * 4) && g.sh_part.ensure((R ? R : 1) * (size_t)H * 4) &&
+        g.sh_back.ensure((S ? S : 1) * (size_t)H * 4) &&
+        (R == 0 || g.pf_scratch.ensure(cz::prefill_scratch_bytes((int)R, H, E, K, (int)L.d.inter, 0, g.num_sms)));
+    {
+        const int v = bufs_ok ? 1 : 0;
+        int all = 0;
+        int* dv = g.sh_tmp.as<int>();
+        if (cudaMemcpyAsync(dv, &v, 4, cudaMemcpyHostToDevice, st) != cudaSuccess) return CZ_EH2D;
+        if (nccl.allReduce(dv, dv, 1, ncclInt32, ncclMin, g.ep_comm, st) != ncclSuccess) return CZ_ENCCL;
+        if (cudaMemcpyAsync(&all, dv, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess)
+            return CZ_ED2H;
+        if (!all) return CZ_EALLOC;
+    }
+    // 4. pack; 5. exchange the rows
+    rc = cz::ep_pack(xs, xrow, g.sh_idx.as<uint32_t>(), g.sh_gates.as<float>(), T, K, W, g.sh_slot.as<int>(),
+                     g.sh_send.as<uint8_t>(), rs, st);
+    if (rc) return rc;
+    if (nccl.groupStart() != ncclSuccess) return CZ_ENCCL;
+    for (int d = 0; d < W; ++d) {
+        if (scnt[d] && nccl.send(g.sh_send.as<uint8_t>() + soff[d] * rs, scnt[d] * rs, ncclUint8, d, g.ep_comm, st) !=
+                           ncclSuccess)
+            rc = CZ_ENCCL;
+        if (rcnt[d] && nccl.recv(g.sh_recv.as<uint8_t>() + roff[d] * rs, rcnt[d] * rs, ncclUint8, d, g.ep_comm, st) !=
+                           ncclSuccess)
+            rc = CZ_ENCCL;
+    }
+    if (nccl.groupEnd() != ncclSuccess || rc) return CZ_ENCCL;
+    // 6. the experts held here over the received rows
+    if (R) {
+        rc = cz::ep_unpack(g.sh_recv.as<uint8_t>(), rs, (int)R, xrow, K, g.sh_x.p, g.sh_ridx.as<uint32_t>(),
+                           g.sh_rgates.as<float>(), st);
+        if (rc) return rc;
+        cudaEvent_t* ev = timer_take(kTimerPrefillGateUp, 2);
+        if (ev) g.tm_kind[g.tm_n - 1] = kTimerPrefillDown;
+        rc = cz::prefill_run(L.pf, g.sh_x.p, xbf, (int)R, nullptr, 0.f, nullptr, g.sh_part.as<float>(), nullptr, nullptr,
+                             g.pf_scratch.p, g.pf_scratch.cap, g.sync + 1, g.num_sms, st, ev, g.sh_ridx.as<uint32_t>(),
+                             g.sh_rgates.as<float>());
+        if (rc) return rc;
+    }
+    // 7. partial sums back to the rows' ranks
+    if (nccl.groupStart() != ncclSuccess) return CZ_ENCCL;
+    for (int d = 0; d < W; ++d) {
+        if (rcnt[d] && nccl.send(g.sh_part.as<float>() + roff[d] * H, rcnt[d] * H, ncclFloat, d, g.ep_comm, st) !=
+                           ncclSuccess)
+            rc = CZ_ENCCL;
+        if (scnt[d] && nccl.recv(g.sh_back.as<float>() + soff[d] * H, scnt[d] * H, ncclFloat, d, g.ep_comm, st) !=
+                           ncclSuccess)
+            rc = CZ_ENCCL;
+    }
+    if (nccl.groupEnd() != ncclSuccess || rc) return CZ_ENCCL;
+    // 8. this rank's tokens: ranks in ascending order (+ residual)
+    rc = cz::ep_combine(g.sh_back.as<float>(), g.sh_slot.as<int>(), T, W, H, residual, out, st);
+    if (rc) return rc;
+    if (T > 0 && idx_out &&
+        cudaMemcpyAsync(idx_out, g.sh_idx.p, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return CZ_ELAUNCH;
+    if (T > 0 && gates_out &&
+        cudaMemcpyAsync(gates_out, g.sh_gates.p, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return CZ_ELAUNCH;
     return CZ_OK;
 }
 
@@ -725,35 +874,41 @@ CZ_EXPORT int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtyp
                                        uint32_t* topk_idx, float* topk_gates, uint32_t flags, void* stream) {
     CsrGuard _csr;
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g.inited || !x || !out || T < 0 || (x_dtype != COLIZIG_X_F32 && x_dtype != COLIZIG_X_BF16))
+    if (!g.inited || T < 0 || (T > 0 && (!x || !out)) || (x_dtype != COLIZIG_X_F32 && x_dtype != COLIZIG_X_BF16))
         return CZ_EARGS;
     auto it = g.layers.find(layer);
     if (it == g.layers.end()) return CZ_ENOLAYER;
-    if (T == 0) return CZ_OK;
+    const bool sharded = flags & COLIZIG_EP_SHARDED;
+    if (sharded && !it->second.ep) return CZ_EARGS;
+    if (T == 0 && !sharded) return CZ_OK;  // a sharded call takes part in the exchange even without tokens
     cudaSetDevice(g.dev);
     const MoeLayer& L = it->second;
     const size_t H = L.d.hidden, K = L.d.topk;
     const int bf16 = x_dtype == COLIZIG_X_BF16;
     const size_t xb = (size_t)T * H * (bf16 ? 2 : 4), ob = (size_t)T * H * 4, kb = (size_t)T * K * 4;
+    auto run = [&](const void* xd, float* od, uint32_t* id, float* gd, cudaStream_t st) {
+        return sharded ? moe_run_sharded(L, xd, bf16, T, od, id, gd, nullptr, 0.f, nullptr, st)
+                       : moe_run(L, xd, bf16, T, od, id, gd, nullptr, 0.f, nullptr, st);
+    };
     if (flags & COLIZIG_PTR_DEVICE) {
-        if (!aligned16(x) || !aligned16(out)) return CZ_EARGS;
+        if (T > 0 && (!aligned16(x) || !aligned16(out))) return CZ_EARGS;
         cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-        return moe_run(L, x, bf16, T, out, topk_idx, topk_gates, nullptr, 0.f, nullptr, st);
+        return run(x, out, topk_idx, topk_gates, st);
     }
     // host pointers: synchronous on the library stream
     if (!g.io_x.ensure(xb) || !g.io_out.ensure(ob)) return CZ_EALLOC;
     if ((topk_idx && !g.io_idx.ensure(kb)) || (topk_gates && !g.io_gates.ensure(kb))) return CZ_EALLOC;
-    if (cudaMemcpyAsync(g.io_x.p, x, xb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess) return CZ_EH2D;
-    int rc = moe_run(L, g.io_x.p, bf16, T, g.io_out.as<float>(), topk_idx ? g.io_idx.as<uint32_t>() : nullptr,
-                     topk_gates ? g.io_gates.as<float>() : nullptr, nullptr, 0.f, nullptr, g.stream);
+    if (xb && cudaMemcpyAsync(g.io_x.p, x, xb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess) return CZ_EH2D;
+    int rc = run(g.io_x.p, g.io_out.as<float>(), topk_idx ? g.io_idx.as<uint32_t>() : nullptr,
+                 topk_gates ? g.io_gates.as<float>() : nullptr, g.stream);
     if (rc) {
         cudaStreamSynchronize(g.stream);
         return rc;
     }
-    if (cudaMemcpyAsync(out, g.io_out.p, ob, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess) return CZ_ED2H;
-    if (topk_idx && cudaMemcpyAsync(topk_idx, g.io_idx.p, kb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess)
+    if (ob && cudaMemcpyAsync(out, g.io_out.p, ob, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess) return CZ_ED2H;
+    if (kb && topk_idx && cudaMemcpyAsync(topk_idx, g.io_idx.p, kb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess)
         return CZ_ED2H;
-    if (topk_gates && cudaMemcpyAsync(topk_gates, g.io_gates.p, kb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess)
+    if (kb && topk_gates && cudaMemcpyAsync(topk_gates, g.io_gates.p, kb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess)
         return CZ_ED2H;
     return check_device_error(g.stream);
 }

@@ -119,7 +119,25 @@ inline bool record_timer_event(cudaEvent_t ev, cudaStream_t st) {
 int prefill_run(const PrefillLayer& L, const void* x, int x_bf16, int T, const float* rms_w, float eps,
                 const float* residual, float* out, uint32_t* topk_idx, float* topk_gates, void* scratch,
                 size_t scratch_bytes, uint32_t* err, int num_sms, cudaStream_t st,
-                cudaEvent_t* gemm_ev = nullptr);
+                cudaEvent_t* gemm_ev = nullptr, const uint32_t* pre_idx = nullptr, const float* pre_gates = nullptr);
+// The routing part alone: idx/gates [T][K] of T tokens (stack mode: xn = rms(x, rms_w), f32 [T][H]).
+int prefill_route(const PrefillLayer& L, const void* x, int x_bf16, int T, const float* rms_w, float eps,
+                  uint32_t* idx, float* gates, float* xn, void* scratch, size_t scratch_bytes, cudaStream_t st);
+
+// Expert parallelism with sharded tokens (moe_ep.cu).  Rank r holds experts
+// [r*E/W, (r+1)*E/W).  ep_plan: per token the W destination slots (-1 = not sent)
+// in a send buffer ordered by destination then token, and the W row counts.
+int ep_plan(const uint32_t* idx, int T, int K, int E, int W, int* slot, int* counts, void* tmp, size_t tmp_bytes,
+            cudaStream_t st);
+// Rows of the send buffer: [H x elt bytes of the token row][K u32 ids][K f32 gates], stride rs bytes.
+int ep_pack(const void* x, size_t xrow_bytes, const uint32_t* idx, const float* gates, int T, int K, int W,
+            const int* slot, uint8_t* send, size_t rs, cudaStream_t st);
+// Received rows -> contiguous x [R][H], idx [R][K], gates [R][K].
+int ep_unpack(const uint8_t* recv, size_t rs, int R, size_t xrow_bytes, int K, void* x, uint32_t* idx, float* gates,
+              cudaStream_t st);
+// out[t] = residual[t] + sum over destinations d (ascending) of back[slot[t][d]] (f32 [.][H]).
+int ep_combine(const float* back, const int* slot, int T, int W, int H, const float* residual, float* out,
+               cudaStream_t st);
 
 // Legacy per-matrix block-FP8 matmul (device pointers, stream-ordered).
 int fp8_matmul_launch(float* y, const float* x, const uint8_t* w, const float* scales, int S, int I, int O,

@@ -64,7 +64,7 @@ struct Scratch {
     float* sg;         // [T] shared-expert gate sigmoid(x . sh_gate)
     float* logits;     // [T][logit_stride(E)]
     int* cnt;          // [Eg]
-    int* ccnt;         // [nchunks][Eg] pairs of each group per chunk of GCH pairs, then the chunk's offset
+    int* ccnt;         // [Eg][nchunks] pairs of each group per chunk of GCH pairs, then the chunk's offset
     int* gbase;        // [Eg+1] first position of each group (padded to 64)
     int* tpre_gu;      // [Eg+1] tile prefix, gate/up
     int* tpre_dn;      // [Eg+1] tile prefix, down
@@ -406,7 +406,8 @@ __global__ void pf_count_kernel(const GroupParams q) {
         if (group_held(q, g)) atomicAdd(&hist[g], 1);
     }
     __syncthreads();
-    for (int g = threadIdx.x; g < Eg; g += blockDim.x) q.s.ccnt[(size_t)blockIdx.x * Eg + g] = hist[g];
+    const int nch = gridDim.x;
+    for (int g = threadIdx.x; g < Eg; g += blockDim.x) q.s.ccnt[(size_t)g * nch + blockIdx.x] = hist[g];
 }
 
 // Exclusive scan of v over the block (blockDim.x a multiple of 32, <= 1024); returns the total.
@@ -447,7 +448,7 @@ __global__ void pf_scan_kernel(const GroupParams q) {
         int run = 0;
         for (int b0 = 0; b0 < nch; b0 += 32) {
             const int b = b0 + lane;
-            int* c = q.s.ccnt + (size_t)b * Eg + gg;
+            int* c = q.s.ccnt + (size_t)gg * nch + b;  // coalesced over the chunks
             const int v = b < nch ? *c : 0;
             int x = v;
 #pragma unroll
@@ -488,7 +489,7 @@ __global__ void pf_scan_kernel(const GroupParams q) {
 __global__ void pf_place_kernel(const GroupParams q) {
     extern __shared__ int off[];  // [Eg] next position of each group for this chunk
     const int Eg = q.s.Eg, lane = threadIdx.x;
-    for (int g = lane; g < Eg; g += 32) off[g] = q.s.gbase[g] + q.s.ccnt[(size_t)blockIdx.x * Eg + g];
+    for (int g = lane; g < Eg; g += 32) off[g] = q.s.gbase[g] + q.s.ccnt[(size_t)g * gridDim.x + blockIdx.x];
     __syncwarp();
     const int p0 = blockIdx.x * GCH, p1 = min(q.s.P, p0 + GCH);
     const uint32_t lt = (1u << lane) - 1u;
@@ -537,6 +538,23 @@ __global__ void pf_tokpos_kernel(const GroupParams q) {
             ps[j - 1] = bpos;
         }
     for (int i = 0; i < K + 1; ++i) q.s.tokpos[(size_t)t * (K + 1) + i] = i < n ? ps[i] : -1;
+}
+
+// Per-row power-of-two exponent of the x terms (the part of pf_topk_kernel that
+// does not depend on the routing), for rows whose routing was done elsewhere.
+__global__ void __launch_bounds__(256) pf_xexp_kernel(const void* x, int x_bf16, int T, int H, int* xexp) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + warp;
+    if (t >= T) return;
+    float m = 0.0f;
+    for (int i = lane; i < H; i += 32) {
+        const float v = x_bf16 ? __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(x)[(size_t)t * H + i] << 16)
+                               : reinterpret_cast<const float*>(x)[(size_t)t * H + i];
+        const float a = fabsf(v);
+        if (a < 3.0e38f) m = fmaxf(m, a);
+    }
+    m = warp_max(m);
+    if (lane == 0) xexp[t] = prescale_exp(m);
 }
 
 // ============================ dispatch ============================
@@ -1163,23 +1181,76 @@ static int launch_gemm(const pf::GemmParams& gp, int num_sms, cudaStream_t st) {
     return cudaGetLastError() == cudaSuccess ? CZ_OK : CZ_ELAUNCH;
 }
 
+int prefill_route(const PrefillLayer& L, const void* x, int x_bf16, int T, const float* rms_w, float eps,
+                  uint32_t* idx, float* gates, float* xn, void* scratch, size_t scratch_bytes, cudaStream_t st) {
+    using namespace pf;
+    const int H = L.H, E = L.E, K = L.K, SI = L.SI;
+    if (!prefill_supported(H, E, K, L.I, SI)) return CZ_ESHAPE;
+    if (T == 0) return CZ_OK;
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(scratch) + 1023) & ~uintptr_t(1023));
+    Scratch s = carve_scratch(base, T, H, E, K, L.I, SI);
+    if (s.bytes + 1024 > scratch_bytes) return CZ_EALLOC;
+    if (rms_w && x_bf16) return CZ_EARGS;
+    if (rms_w) {
+        pf_rms_kernel<<<T, 256, 0, st>>>(reinterpret_cast<const float*>(x), rms_w, eps, T, H, xn);
+        x = xn;
+    }
+    RouteParams q{};
+    q.x = x;
+    q.x_bf16 = x_bf16;
+    q.router = L.router;
+    q.sh_gate = L.sh_gate;
+    q.T = T;
+    q.H = H;
+    q.E = E;
+    q.K = K;
+    q.SI = SI;
+    q.norm_topk = L.norm_topk;
+    q.TT = LG_T;
+    q.logits = s.logits;
+    q.idx = idx;
+    q.gates = gates;
+    q.xexp = s.xexp;
+    q.sg = s.sg;
+    const int Er = E + (SI ? 1 : 0);
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(pf_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LG_SMEM) != cudaSuccess)
+            return CZ_ELAUNCH;
+        attr = true;
+    }
+    pf_logits_kernel<<<dim3((T + LG_T - 1) / LG_T, (Er + LG_R - 1) / LG_R), 256, LG_SMEM, st>>>(q);
+    pf_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(q);
+    return cudaGetLastError() == cudaSuccess ? CZ_OK : CZ_ELAUNCH;
+}
+
 int prefill_run(const PrefillLayer& L, const void* x, int x_bf16, int T, const float* rms_w, float eps,
                 const float* residual, float* out, uint32_t* topk_idx, float* topk_gates, void* scratch,
-                size_t scratch_bytes, uint32_t* err, int num_sms, cudaStream_t st, cudaEvent_t* gemm_ev) {
+                size_t scratch_bytes, uint32_t* err, int num_sms, cudaStream_t st, cudaEvent_t* gemm_ev,
+                const uint32_t* pre_idx, const float* pre_gates) {
     using namespace pf;
-    const int H = L.H, E = L.E, K = L.K, I = L.I, SI = L.SI;
-    if (!prefill_supported(H, E, K, I, SI) || T < 1) return CZ_ESHAPE;
+    const int H = L.H, E = L.E, K = L.K, I = L.I;
+    // rows routed elsewhere (pre_idx): no shared-expert slot of their own
+    const int SI = pre_idx ? 0 : L.SI;
+    if (!prefill_supported(H, E, K, I, L.SI) || T < 1) return CZ_ESHAPE;
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(scratch) + 1023) & ~uintptr_t(1023));
     Scratch s = carve_scratch(base, T, H, E, K, I, SI);
     if (s.bytes + 1024 > scratch_bytes) return CZ_EALLOC;
     if (rms_w && x_bf16) return CZ_EARGS;
+    if (pre_idx) {
+        if (rms_w) return CZ_EARGS;
+        if (cudaMemcpyAsync(s.idx, pre_idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(s.gates, pre_gates, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+            return CZ_ELAUNCH;
+        pf_xexp_kernel<<<(T + 7) / 8, 256, 0, st>>>(x, x_bf16, T, H, s.xexp);
+    }
     if (rms_w) {
         pf_rms_kernel<<<T, 256, 0, st>>>(reinterpret_cast<const float*>(x), rms_w, eps, T, H, s.xn);
         x = s.xn;
     }
     const int JX = x_bf16 ? 2 : 3;
     // route
-    {
+    if (!pre_idx) {
         RouteParams q{};
         q.x = x;
         q.x_bf16 = x_bf16;

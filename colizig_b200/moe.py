@@ -135,11 +135,14 @@ class Layer:
         return forward(self, x, out, topk_idx, topk_gates, stream)
 
 
-def forward(layer: Layer, x, out=None, topk_idx=None, topk_gates=None, stream=None):
+def forward(layer: Layer, x, out=None, topk_idx=None, topk_gates=None, stream=None, sharded: bool = False):
     """moe.zig:409-426: out[T, H] = MoE(x[T, H]).  Returns (out, topk_idx, topk_gates);
-    the top-k arrays are allocated when not given."""
+    the top-k arrays are allocated when not given.  sharded=True (a layer registered
+    with ep=True): x holds this rank's own tokens and the ranks exchange rows with
+    NCCL send/recv (expert-parallel prefill); every rank must make the call."""
     d = layer.dims
     L = _abi.load()
+    sh = _abi.COLIZIG_EP_SHARDED if sharded else 0
     if _is_cuda(x):
         T = x.shape[0]
         if x.dtype == torch.bfloat16:
@@ -155,7 +158,7 @@ def forward(layer: Layer, x, out=None, topk_idx=None, topk_gates=None, stream=No
         if topk_gates is None:
             topk_gates = torch.empty((T, d.topk), dtype=torch.float32, device=x.device)
         rc = L.colizig_cuda_moe_forward(layer.id, _ptr(x), dt, T, _ptr(out), _ptr(topk_idx), _ptr(topk_gates),
-                                        _abi.COLIZIG_PTR_DEVICE, _stream_handle(stream))
+                                        _abi.COLIZIG_PTR_DEVICE | sh, _stream_handle(stream))
         _abi.check("colizig_cuda_moe_forward", rc)
         return out, topk_idx, topk_gates
     # host path
@@ -178,7 +181,7 @@ def forward(layer: Layer, x, out=None, topk_idx=None, topk_gates=None, stream=No
         topk_idx = np.empty((T, d.topk), np.uint32)
     if topk_gates is None:
         topk_gates = np.empty((T, d.topk), np.float32)
-    rc = L.colizig_cuda_moe_forward(layer.id, _ptr(xa), dt, T, _ptr(out), _ptr(topk_idx), _ptr(topk_gates), 0,
+    rc = L.colizig_cuda_moe_forward(layer.id, _ptr(xa), dt, T, _ptr(out), _ptr(topk_idx), _ptr(topk_gates), sh,
                                     None)
     _abi.check("colizig_cuda_moe_forward", rc)
     return out, topk_idx, topk_gates

@@ -2,7 +2,9 @@
 through torch.distributed.run).  Rank r holds experts [r*E/2, (r+1)*E/2) of
 every layer; the layer outputs (summed over ranks by the library's NCCL
 all-reduce) are compared with the CPU oracle (top-k bit-exact, outputs within
-the layer tolerance) and with the same layer run whole on one GPU."""
+the layer tolerance) and with the same layer run whole on one GPU.  Then the
+sharded-token path (each rank its own batch, rows exchanged with NCCL
+send/recv), the batches together against the oracle and the one-GPU layer."""
 
 import os
 import sys
@@ -53,6 +55,36 @@ def main() -> int:
                 ok &= same and e_or <= OUT_TOL and e_one <= OUT_TOL and torch.equal(idx, ridx) and torch.equal(gates, rg)
         Lep.unregister()
         Lfull.unregister()
+    # sharded tokens (prefill): each rank its own batch (one rank may have none); the
+    # batches together against the oracle and against the whole layer on one GPU
+    d = synth.CONFIGS["c2"]
+    w = synth.make_layer(d, seed=13, device="cuda")
+    Lep = moe.Layer.from_weights(lid, d, w, ep=True)
+    Lfull = moe.Layer.from_weights(lid + 1, d, w)
+    wn = synth.to_numpy_layer(w) if rank == 0 else None
+    for Ts in ((40, 72), (48, 0), (3, 5)):
+        xs = [synth.make_tokens(t, d.hidden, 900 + 17 * i + t, device="cuda", dtype=torch.bfloat16)
+              for i, t in enumerate(Ts)]
+        xall = torch.cat(xs)
+        out, idx, gates = moe.forward(Lep, xs[rank], sharded=True)
+        torch.cuda.synchronize()
+        moe.check()
+        parts = [None] * world
+        dist.all_gather_object(parts, (out.cpu(), idx.cpu(), gates.cpu()))
+        if rank == 0:
+            o = torch.cat([p[0] for p in parts]).numpy()
+            i_ = torch.cat([p[1] for p in parts]).numpy().view(np.uint32)
+            ref, ridx, _ = moe.forward(Lfull, xall)
+            ol = oracle.layer_from_dict(wn)
+            od = oracle.Dims(d.hidden, d.experts, d.topk, d.inter, d.shared_inter, d.norm_topk)
+            oo, oi, _ = oracle.moe_forward(ol, od, synth.tokens_f32(xall.cpu()))
+            same = np.array_equal(i_, oi)
+            e_or = rel_err(o, oo)
+            e_one = rel_err(o, ref.cpu().numpy())
+            print(f"sharded c2 T={Ts}: top-k exact {same}, vs oracle {e_or:.2e}, vs one GPU {e_one:.2e}", flush=True)
+            ok &= same and e_or <= OUT_TOL and e_one <= OUT_TOL
+    Lep.unregister()
+    Lfull.unregister()
     torch.cuda.synchronize()
     ep.shutdown()
     flag = torch.tensor([1 if ok else 0])
