@@ -430,6 +430,152 @@ def stack_main(args, world, rank, local, torch, dist, cz, _abi, moe, synth):
         lay.unregister()
 
 
+def sharded_main(args, world, rank, local, torch, dist, cz, _abi, moe, synth):
+    """Expert-parallel prefill with sharded tokens (N > 1): every rank routes its own
+    --tokens rows, sends each row to the ranks holding its experts, runs the grouped
+    GEMMs on the rows it receives and adds the partial sums of its own tokens.  The
+    library reads the exchange's row counts on the host, so the steps are issued one
+    by one (no CUDA graph) and timed with CUDA events around all of them."""
+    from colizig_b200 import ep
+
+    d = synth.CONFIGS[args.config]
+    Tr = args.tokens
+    T = Tr * world
+    dev = torch.device("cuda", local)
+    layers = []
+    for l in range(args.layers):
+        w = gen_layer(args, d, l, dev, synth)  # the same layer on every rank
+        layers.append(moe.Layer.from_weights(l, d, w, ep=True))
+        del w
+    torch.cuda.empty_cache()
+    n = args.warmup + args.steps
+    # rank r's rows of step i: rows [r*Tr, (r+1)*Tr) of that step's job-wide batch
+    xs = [gen_tokens(args, d, T, 20000 + i, dev, synth)[rank * Tr:(rank + 1) * Tr].contiguous() for i in range(n)]
+    outs = torch.empty((n, Tr, d.hidden), dtype=torch.float32, device=dev)
+    idx = torch.empty((n, Tr, d.topk), dtype=torch.int32, device=dev)
+    gates = torch.empty((n, Tr, d.topk), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+    L = _abi.load()
+    sh = stream.cuda_stream
+    flags = _abi.COLIZIG_PTR_DEVICE | _abi.COLIZIG_EP_SHARDED
+
+    def step(i):
+        lay = layers[i % len(layers)]
+        rc = L.colizig_cuda_moe_forward(lay.id, xs[i].data_ptr(), _abi.COLIZIG_X_BF16, Tr, outs[i].data_ptr(),
+                                        idx[i].data_ptr(), gates[i].data_ptr(), flags, sh)
+        if rc:
+            raise cz.ColizigError("colizig_cuda_moe_forward", rc)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    moe.check()
+    moe.kernel_timer(2 * args.steps)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush.fill_(1)
+    del flush
+    sampler = ClockSampler(local)
+    dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for k in range(args.steps):
+        step(args.warmup + k)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    dist.barrier()
+    moe.check()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    gemm_ms = {}
+    for kind, ms in moe.kernel_timer_read():
+        gemm_ms.setdefault(kind, []).append(ms)
+    moe.kernel_timer(0)
+    tt = torch.tensor([elapsed_ms], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(tt.item())
+    value = args.steps * T / (elapsed_ms / 1e3)
+
+    # pairs this rank's GEMMs processed: every rank's (token, expert) pairs on its experts
+    lo, hi = ep.expert_range(rank, world, d.experts)
+    hist = torch.stack([torch.bincount(idx[args.warmup + k].reshape(-1).long(), minlength=d.experts)
+                        for k in range(args.steps)]).to(torch.float64)
+    dist.all_reduce(hist)
+    hist = hist.cpu().numpy()
+    pairs_local = float(hist[:, lo:hi].sum(axis=1).mean())
+    gu_flops = 2.0 * pairs_local * d.hidden * 2 * d.inter
+    dn_flops = 2.0 * pairs_local * d.inter * d.hidden
+    gu_ms = float(np.mean(gemm_ms.get(moe.TIMER_PREFILL_GATE_UP, [float("nan")])))
+    dn_ms = float(np.mean(gemm_ms.get(moe.TIMER_PREFILL_DOWN, [float("nan")])))
+    hbm_peak, tf_peak, peak_kind = load_peaks()
+    fp8_peak = 2.0 * tf_peak
+    tf = gu_flops / (gu_ms / 1e3) / 1e12
+    step_tf = algorithmic_flops(d, T) * args.steps / (elapsed_ms / 1e3) / 1e12 / world
+    U = (hist > 0).sum(axis=1)
+
+    # end to end: this rank's rows from pinned host memory, outputs back to host memory
+    xh = [x.cpu().pin_memory() for x in xs[:min(n, 64)]]
+    oh = torch.empty((Tr, d.hidden), dtype=torch.float32).pin_memory()
+    ih = torch.empty((Tr, d.topk), dtype=torch.int32).pin_memory()
+    gh = torch.empty((Tr, d.topk), dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        lay = layers[i % len(layers)]
+        rc = L.colizig_cuda_moe_forward(lay.id, xh[i % len(xh)].data_ptr(), _abi.COLIZIG_X_BF16, Tr, oh.data_ptr(),
+                                        ih.data_ptr(), gh.data_ptr(), _abi.COLIZIG_EP_SHARDED, None)
+        if rc:
+            raise cz.ColizigError("colizig_cuda_moe_forward", rc)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    dist.barrier()
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        e2e_step(args.warmup + k)
+    e2e_s = time.perf_counter() - t0
+    tt = torch.tensor([e2e_s], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    e2e_s = float(tt.item())
+    e2e = {"value": args.steps * T / e2e_s, "unit": "tokens/s",
+           "h2d_bytes_per_step": Tr * d.hidden * 2, "d2h_bytes_per_step": Tr * d.hidden * 4 + Tr * d.topk * 8,
+           "bytes_are": "per rank (each rank copies its own rows)", "ms_per_step": e2e_s / args.steps * 1e3}
+
+    if rank == 0:
+        cfg = config_block(args, d)
+        cfg["parallelism"] = (f"ep{world}, sharded tokens: each rank routes its own {Tr} rows, rows go to the ranks "
+                              "holding their experts and partial sums come back over NCCL send/recv")
+        cfg["l2"] = "inputs larger than L2: steps cycle through distinct layers; L2 flushed once before the timed steps"
+        roof = {"bound": "tensor", "achieved": tf, "peak": fp8_peak, "unit": "TFLOP/s", "frac": tf / fp8_peak,
+                "traffic": None, "traffic_unit": "DRAM bytes per gate/up GEMM launch (ncu; captured on one GPU only)",
+                "peak_kind": (f"FP8 dense = 2 x {peak_kind} bf16 (MEASURED_PEAKS.json bf16_tflops)"
+                              if peak_kind == "measured" else "FP8 dense = 2 x fallback 1.59 PFLOP/s"),
+                "kernel": "pf_gemm_kernel (gate/up, tcgen05 grouped GEMM with the SiLU*up epilogue), rank 0",
+                "kernel_ms_avg": gu_ms, "flops_per_launch": gu_flops,
+                "down_gemm": {"kernel_ms_avg": dn_ms, "flops_per_launch": dn_flops,
+                              "achieved_tflops": dn_flops / (dn_ms / 1e3) / 1e12,
+                              "frac": dn_flops / (dn_ms / 1e3) / 1e12 / fp8_peak},
+                "step": {"ms": elapsed_ms / args.steps, "flops": algorithmic_flops(d, T) / world,
+                         "achieved_tflops": step_tf, "frac": step_tf / fp8_peak},
+                "distinct_experts_avg": float(U.mean())}
+        line = {
+            "metric": metric_name(args, T), "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32", "data": "synthetic",
+            "config": cfg, "roofline": roof, "tflops": step_tf * world,
+            "e2e": e2e, "cpu_baseline": None, "clocks": clocks,
+            # route (logits, top-k), plan (mask, slots), pack, unpack, xexp, count, scan, place,
+            # tokpos, dispatch, 2 GEMMs, combine, ep_combine (NCCL's own kernels not counted)
+            "gpu_launches": args.steps * 16,
+        }
+        print(json.dumps(line), flush=True)
+    for lay in layers:
+        lay.unregister()
+
+
 def metric_name(args, T):
     mode = "prefill" if T >= PREFILL_MIN_TOKENS else "decode"
     return f"MoE-layer {mode} tokens/s ({args.config}, T={T})"
@@ -509,6 +655,14 @@ def main():
             torch.cuda.synchronize()
             ep.shutdown()
             dist.destroy_process_group()
+        return
+    if world > 1 and args.tokens >= PREFILL_MIN_TOKENS:
+        sharded_main(args, world, rank, local, torch, dist, cz, _abi, moe, synth)
+        from colizig_b200 import ep
+
+        torch.cuda.synchronize()
+        ep.shutdown()
+        dist.destroy_process_group()
         return
     d = synth.CONFIGS[args.config]
     T = args.tokens * world  # tokens per step over the whole job (each rank contributes --tokens)

@@ -16,6 +16,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
+#include <climits>
 #include <list>
 #include <map>
 #include <mutex>
@@ -440,7 +442,7 @@ int moe_run_sharded(const MoeLayer& L, const void* x, int x_bf16, int T, float* 
     if (!g.sh_idx.ensure(tk * K * 4) || !g.sh_gates.ensure(tk * K * 4) || !g.sh_slot.ensure(tk * W * 4) ||
         !g.sh_tmp.ensure(tk * 4) || (rms_w && !g.sh_xn.ensure(tk * H * 4)))
         local_rc = CZ_EALLOC;
-    if (!g.sh_counts.ensure((size_t)(W + 2) * 4) || !g.sh_allc.ensure((size_t)W * (W + 2) * 4))
+    if (!g.sh_counts.ensure((size_t)(W + 5) * 4) || !g.sh_allc.ensure((size_t)W * (W + 5) * 4))
         return CZ_EALLOC;  // (a few bytes; without them there is nothing to exchange at all)
     if (!local_rc && T > 0) {
         const size_t need = cz::prefill_scratch_bytes(T, H, E, K, (int)L.d.inter, 0, g.num_sms);
@@ -460,12 +462,30 @@ int moe_run_sharded(const MoeLayer& L, const void* x, int x_bf16, int T, float* 
                                g.sh_tmp.p, g.sh_tmp.cap, st);
     if (local_rc && cudaMemsetAsync(g.sh_counts.p, 0, (size_t)W * 4, st) != cudaSuccess) return local_rc;
     int rc = CZ_OK;
-    // each rank's row: W counts, its row stride and its hidden size, so that every rank
-    // can check that all of them will exchange rows of the same size
-    const int meta[2] = {local_rc ? -1 : (int)rs, H};  // -1: this rank failed, every rank stops
+    // each rank's row: W counts, its row stride and its hidden size (so that every rank can
+    // check that all of them will exchange rows of the same size), and the rows its current
+    // buffers hold without allocating: receive side (exchange buffers, grouped-pipeline
+    // scratch) and send side
+    const auto rows_of = [](const DevBuf& b, size_t row) {
+        return (int)std::min<size_t>(b.p ? b.cap / row : 0, (size_t)INT_MAX);
+    };
+    const int rbuf = std::min({rows_of(g.sh_recv, rs), rows_of(g.sh_x, xrow), rows_of(g.sh_ridx, (size_t)K * 4),
+                               rows_of(g.sh_rgates, (size_t)K * 4), rows_of(g.sh_part, (size_t)H * 4)});
+    int rpf = 0;  // largest R whose grouped-pipeline scratch fits (the size grows with R)
+    for (int lo = 1, hi = rbuf; g.pf_scratch.p && lo <= hi;) {
+        const int mid = lo + (hi - lo) / 2;
+        if (cz::prefill_scratch_bytes(mid, H, E, K, (int)L.d.inter, 0, g.num_sms) <= g.pf_scratch.cap) {
+            rpf = mid;
+            lo = mid + 1;
+        } else {
+            hi = mid - 1;
+        }
+    }
+    const int sbuf = std::min(rows_of(g.sh_send, rs), rows_of(g.sh_back, (size_t)H * 4));
+    const int meta[5] = {local_rc ? -1 : (int)rs, H, rbuf, rpf, sbuf};  // rs -1: this rank failed, every rank stops
     if (cudaMemcpyAsync(g.sh_counts.as<int>() + W, meta, sizeof meta, cudaMemcpyHostToDevice, st) != cudaSuccess)
         return CZ_EH2D;
-    const int CW = W + 2;
+    const int CW = W + 5;
     if (nccl.allGather(g.sh_counts.p, g.sh_allc.p, (size_t)CW, ncclInt32, g.ep_comm, st) != ncclSuccess) return CZ_ENCCL;
     std::vector<int> allc((size_t)W * CW);
     if (cudaMemcpyAsync(allc.data(), g.sh_allc.p, allc.size() * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
@@ -482,15 +502,28 @@ int moe_run_sharded(const MoeLayer& L, const void* x, int x_bf16, int T, float* 
         roff[d + 1] = roff[d] + rcnt[d];
     }
     const size_t S = soff[W], R = roff[W];
-    // every buffer of the exchange, then one all-reduce (min) of the ranks' verdicts, so that
-    // no rank enters a send/recv its peers will not match
+    // Does any rank have to allocate?  Every rank evaluates the same table, so all of them
+    // take the same branch: without growth nothing below can fail and the exchange follows
+    // directly; with growth every buffer is sized, then one all-reduce (min) of the ranks'
+    // verdicts, so that no rank enters a send/recv its peers will not match.
+    bool grow = false;
+    for (int r = 0; r < W; ++r) {
+        size_t Rr = 0, Sr = 0;
+        for (int d = 0; d < W; ++d) {
+            Rr += (size_t)allc[(size_t)d * CW + r];
+            Sr += (size_t)allc[(size_t)r * CW + d];
+        }
+        const int* mr = &allc[(size_t)r * CW + W];
+        grow |= std::max<size_t>(Rr, 1) > (size_t)mr[2] || (Rr > 0 && Rr > (size_t)mr[3]) ||
+                std::max<size_t>(Sr, 1) > (size_t)mr[4];
+    }
     const bool bufs_ok =
         g.sh_send.ensure((S ? S : 1) * rs) && g.sh_recv.ensure((R ? R : 1) * rs) &&
         g.sh_x.ensure((R ? R : 1) * xrow) && g.sh_ridx.ensure((R ? R : 1) * K * 4) &&
         g.sh_rgates.ensure((R ? R : 1) * K * 4) && g.sh_part.ensure((R ? R : 1) * (size_t)H * 4) &&
         g.sh_back.ensure((S ? S : 1) * (size_t)H * 4) &&
         (R == 0 || g.pf_scratch.ensure(cz::prefill_scratch_bytes((int)R, H, E, K, (int)L.d.inter, 0, g.num_sms)));
-    {
+    if (grow) {
         const int v = bufs_ok ? 1 : 0;
         int all = 0;
         int* dv = g.sh_tmp.as<int>();
@@ -918,7 +951,8 @@ CZ_EXPORT int colizig_cuda_moe_stack_forward(uint32_t first_layer, uint32_t n_la
     CsrGuard _csr;
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g.inited || !h || T < 0) return CZ_EARGS;
-    if (T == 0 || n_layers == 0) return CZ_OK;
+    const bool sharded = flags & COLIZIG_EP_SHARDED;
+    if (n_layers == 0 || (T == 0 && !sharded)) return CZ_OK;  // sharded: every rank takes part in every layer
     std::vector<const MoeLayer*> Ls;
     for (uint32_t l = 0; l < n_layers; ++l) {
         auto it = g.layers.find(first_layer + l);
@@ -955,7 +989,8 @@ CZ_EXPORT int colizig_cuda_moe_stack_forward(uint32_t first_layer, uint32_t n_la
         return CZ_EARGS;
     }
     for (uint32_t l = 0; l < n_layers; ++l) {
-        const int rc = moe_run(*Ls[l], hd, 0, T, hd, nullptr, nullptr, nw + (size_t)l * H, eps, hd, st);
+        const int rc = sharded ? moe_run_sharded(*Ls[l], hd, 0, T, hd, nullptr, nullptr, nw + (size_t)l * H, eps, hd, st)
+                               : moe_run(*Ls[l], hd, 0, T, hd, nullptr, nullptr, nw + (size_t)l * H, eps, hd, st);
         if (rc) {
             cudaStreamSynchronize(st);
             return rc;

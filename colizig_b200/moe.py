@@ -210,20 +210,24 @@ def forward_noalloc(layer: Layer, x, out, topk_idx=None, topk_gates=None, status
     return out
 
 
-def stack_forward(first_layer: int, n_layers: int, h, norm_w=None, eps: float = 1e-6, stream=None):
+def stack_forward(first_layer: int, n_layers: int, h, norm_w=None, eps: float = 1e-6, stream=None,
+                  sharded: bool = False):
     """src/qwen3moe/model.zig:227-232 per layer (attention = identity):
-    n = rms(h, norm_w[l]); h += moe_l(n).  Updates h ([T, H] f32) in place."""
+    n = rms(h, norm_w[l]); h += moe_l(n).  Updates h ([T, H] f32) in place.
+    sharded=True (layers registered with ep=True): h holds this rank's own tokens and
+    every layer exchanges rows with the other ranks, as forward(..., sharded=True)."""
     L = _abi.load()
+    sh = _abi.COLIZIG_EP_SHARDED if sharded else 0
     if _is_cuda(h):
         rc = L.colizig_cuda_moe_stack_forward(first_layer, n_layers, None if norm_w is None else _ptr(norm_w),
-                                              float(eps), _ptr(h), h.shape[0], _abi.COLIZIG_PTR_DEVICE,
+                                              float(eps), _ptr(h), h.shape[0], _abi.COLIZIG_PTR_DEVICE | sh,
                                               _stream_handle(stream))
     else:
         if not (h.dtype == np.float32 and h.flags["C_CONTIGUOUS"]):
             raise ValueError("h must be a C-contiguous f32 array")
         nwa = None if norm_w is None else np.ascontiguousarray(norm_w, np.float32)
         nw = None if nwa is None else _ptr(nwa)
-        rc = L.colizig_cuda_moe_stack_forward(first_layer, n_layers, nw, float(eps), _ptr(h), h.shape[0], 0, None)
+        rc = L.colizig_cuda_moe_stack_forward(first_layer, n_layers, nw, float(eps), _ptr(h), h.shape[0], sh, None)
     _abi.check("colizig_cuda_moe_stack_forward", rc)
     return h
 

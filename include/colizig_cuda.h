@@ -105,12 +105,13 @@ typedef struct colizig_moe_expert {
                          after colizig_cuda_ep_init); every forward of the layer then sums
                          the ranks' outputs with one NCCL all-reduce on `stream` */
 
+#define COLIZIG_EP_SHARDED 4u /* moe_forward / moe_stack_forward on COLIZIG_EP layers: x (h)
+    holds this rank's own tokens (T may differ between ranks, 0 included) and
+    out/topk are for them; the ranks exchange token rows and partial sums with
+    NCCL send/recv (expert-parallel prefill).  Every rank of the group makes the
+    call.  Layers with a shared expert are not supported here (-8). */
+
 /* x dtypes */
-#define COLIZIG_EP_SHARDED 4u /* moe_forward on a COLIZIG_EP layer: x holds this rank's own
-    tokens (T may differ between ranks, 0 included) and out/topk are for them;
-    the ranks exchange token rows and partial sums with NCCL send/recv
-    (expert-parallel prefill).  Every rank of the group makes the call.  Layers
-    with a shared expert are not supported here (-8). */
 #define COLIZIG_X_F32 0
 #define COLIZIG_X_BF16 1
 

@@ -4,7 +4,8 @@ every layer; the layer outputs (summed over ranks by the library's NCCL
 all-reduce) are compared with the CPU oracle (top-k bit-exact, outputs within
 the layer tolerance) and with the same layer run whole on one GPU.  Then the
 sharded-token path (each rank its own batch, rows exchanged with NCCL
-send/recv), the batches together against the oracle and the one-GPU layer."""
+send/recv), the batches together against the oracle and the one-GPU layer,
+and the same for a two-layer sharded stack (rms + MoE + residual per layer)."""
 
 import os
 import sys
@@ -85,6 +86,49 @@ def main() -> int:
             ok &= same and e_or <= OUT_TOL and e_one <= OUT_TOL
     Lep.unregister()
     Lfull.unregister()
+    # the sharded stack (rms + MoE + residual per layer, rows exchanged in every layer),
+    # teacher-forced per layer against the oracle and the one-GPU layer on the same input
+    # (a chain of layers amplifies rounding differences through later top-k picks)
+    lid += 2
+    NL = 2
+    ws = [synth.make_layer(d, seed=60 + l, device="cuda") for l in range(NL)]
+    eps_l = [moe.Layer.from_weights(lid + l, d, ws[l], ep=True) for l in range(NL)]
+    full_l = [moe.Layer.from_weights(lid + 10 + l, d, ws[l]) for l in range(NL)]
+    rng = np.random.default_rng(5)
+    norm_w = (1.0 + 0.05 * rng.standard_normal((NL, d.hidden))).astype(np.float32)
+    Ts = (40, 24)
+    h0 = [rng.standard_normal((t, d.hidden)).astype(np.float32) for t in Ts]
+    od = oracle.Dims(d.hidden, d.experts, d.topk, d.inter, d.shared_inter, d.norm_topk)
+    h = h0[rank].copy()
+    for l in range(NL):
+        h_in = [None] * world
+        dist.all_gather_object(h_in, h)
+        h = moe.stack_forward(lid + l, 1, h.copy(), norm_w[l:l + 1], 1e-6, sharded=True)
+        h_out = [None] * world
+        dist.all_gather_object(h_out, h)
+        if rank == 0:
+            hi, ho = np.concatenate(h_in), np.concatenate(h_out)
+            ref = moe.stack_forward(lid + 10 + l, 1, hi.copy(), norm_w[l:l + 1], 1e-6)
+            b, _, _ = oracle.moe_forward(oracle.layer_from_dict(synth.to_numpy_layer(ws[l])), od,
+                                         oracle.rms(hi, norm_w[l], 1e-6))
+            # h + b is rounded to f32: allow the layer tolerance plus one rounding of the
+            # residual add (two for the GPU-vs-GPU comparison)
+            want = (hi + b).astype(np.float32)
+            ulp = np.spacing(np.maximum(np.abs(hi), np.abs(want))).astype(np.float64)
+            e_or = float(np.max((np.abs(ho.astype(np.float64) - want) - ulp) / (OUT_TOL * np.abs(b).max())))
+            e_one = float(np.max((np.abs(ho.astype(np.float64) - ref) - 2 * ulp) /
+                                 (OUT_TOL * np.abs(ref.astype(np.float64) - hi).max())))
+            print(f"sharded c2 stack layer {l} T={Ts}: error / bound vs one GPU {e_one:.2e}, vs oracle {e_or:.2e}",
+                  flush=True)
+            ok &= e_one <= 1.0 and e_or <= 1.0
+    # the two-layer call equals the chain of one-layer calls on every rank
+    h2 = moe.stack_forward(lid, NL, h0[rank].copy(), norm_w, 1e-6, sharded=True)
+    same = bool(np.array_equal(h2, h))
+    if not same:
+        print(f"rank {rank}: sharded stack of {NL} differs from its layer-by-layer chain", flush=True)
+    ok &= same
+    for lay in eps_l + full_l:
+        lay.unregister()
     torch.cuda.synchronize()
     ep.shutdown()
     flag = torch.tensor([1 if ok else 0])
