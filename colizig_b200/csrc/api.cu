@@ -92,12 +92,10 @@ struct MoeLayer {
     int e_lo = 0, e_hi = 0;     // routed experts held here (all of them without expert parallelism)
     int shared_here = 0;        // the shared expert's weights are held (and computed) here
     bool ep = false;            // outputs are summed over the expert-parallel group after each forward
-    CUtensorMap down_map{};     // TMA view of down_w: u8 [(e_hi-e_lo)*H][I]
     cz::PrefillLayer pf{};      // the prefill kernels' view (tensor maps with 128-byte swizzle)
     bool pf_ok = false;
-    CUtensorMap sh_down_map{};  // TMA view of sh_down_w: u8 [H][SI]
     CUtensorMap gate_map{}, up_map{}, sh_gate_map{}, sh_up_map{};  // decode views of the gate/up weights
-    int gu_kb = 0, dn_grp = 0, sh_dn_grp = 0;  // depth of those boxes (0 = 2D maps)
+    int gu_kb = 0;              // depth of those boxes (0 = 2D maps)
 };
 
 struct Ctx {
@@ -293,7 +291,8 @@ int gather_copy_2d(uint8_t* dst, size_t dst_pitch, const colizig_moe_expert* ex,
 int ensure_decode_scratch(const colizig_moe_dims& d) {
     const size_t T = cz::kDecodeMaxTokens;
     if (!g.logits.ensure(T * cz::logit_stride((int)d.experts) * sizeof(float))) return CZ_EALLOC;
-    if (!g.partial.ensure((size_t)g.num_sms * T * d.hidden * sizeof(float))) return CZ_EALLOC;
+    const size_t im = d.inter > d.shared_inter ? d.inter : d.shared_inter;
+    if (!g.partial.ensure(T * (d.topk + 1) * im * sizeof(float))) return CZ_EALLOC;
     return ensure_sync();
 }
 
@@ -322,16 +321,12 @@ cz::DecodeParams make_params(const MoeLayer& L) {
     p.e_lo = L.e_lo;
     p.e_hi = L.e_hi;
     p.shared_here = L.shared_here;
-    p.down_map = L.down_map;
-    p.sh_down_map = L.shared_here ? L.sh_down_map : L.down_map;
     p.gate_map = L.gate_map;
     p.up_map = L.up_map;
     p.sh_gate_map = L.shared_here ? L.sh_gate_map : L.gate_map;
     p.sh_up_map = L.shared_here ? L.sh_up_map : L.up_map;
     p.gu3d = L.gu_kb > 0;
     p.gu_kb = L.gu_kb;
-    p.dn_grp = L.dn_grp;
-    p.sh_dn_grp = L.sh_dn_grp;
     p.logits = g.logits.as<float>();
     p.partial = g.partial.as<float>();
     p.sync = g.sync;
@@ -832,24 +827,20 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
                            cudaSuccess)
                 rc = CZ_EH2D;
     }
-    // decode tensor maps; every map of a layer gets the same box depth
+    // decode tensor maps (gate/up); every map of a layer gets the same box depth
     if (!rc && E) {
-        int kb = 0, kb2 = 0, grp = 0;
-        if (!cz::make_down_map(&L.down_map, L.down_w, E * H, I, (int)H, &grp) ||
-            !cz::make_gu_map(&L.gate_map, L.gate_w, E * I, H, &kb) || !cz::make_gu_map(&L.up_map, L.up_w, E * I, H, &kb2) ||
+        int kb = 0, kb2 = 0;
+        if (!cz::make_gu_map(&L.gate_map, L.gate_w, E * I, H, &kb) || !cz::make_gu_map(&L.up_map, L.up_w, E * I, H, &kb2) ||
             kb != kb2)
             rc = CZ_ELAUNCH;
         L.gu_kb = kb;
-        L.dn_grp = grp;
     }
     if (!rc && shared_here) {
-        int kb = 0, kb2 = 0, grp = 0;
-        if (!cz::make_down_map(&L.sh_down_map, L.sh_down_w, H, SI, (int)H, &grp) ||
-            !cz::make_gu_map(&L.sh_gate_map, L.sh_gate_w, SI, H, &kb) ||
+        int kb = 0, kb2 = 0;
+        if (!cz::make_gu_map(&L.sh_gate_map, L.sh_gate_w, SI, H, &kb) ||
             !cz::make_gu_map(&L.sh_up_map, L.sh_up_w, SI, H, &kb2) || kb != kb2 || (E && kb != L.gu_kb))
             rc = CZ_ELAUNCH;
         L.gu_kb = kb;
-        L.sh_dn_grp = grp;
     }
     if (!rc && E && cz::prefill_supported((int)H, (int)d.experts, (int)d.topk, (int)I, (int)SI)) {
         cz::PrefillLayer& P = L.pf;
@@ -1185,6 +1176,8 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
                                      (int)L.d.shared_inter, bf16, g.num_sms);
     if (tmax > kNoAllocMaxTokens) tmax = kNoAllocMaxTokens;
     if (tmax < 1) return CZ_ESHAPE;
+    const size_t im = L.d.inter > L.d.shared_inter ? L.d.inter : L.d.shared_inter;
+    if ((size_t)kNoAllocMaxTokens * (L.d.topk + 1) * im * sizeof(float) > kNoAllocPartialBytes) return CZ_ESHAPE;
     for (int t0 = 0; t0 < T; t0 += tmax) {
         const int n = T - t0 < tmax ? T - t0 : tmax;
         cz::DecodeParams p = make_params(L);

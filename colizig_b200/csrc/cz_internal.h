@@ -12,8 +12,8 @@ namespace cz {
 constexpr int kDecodeMaxTokens = 4;   // per decode launch (more tokens cost more slabs of the down pass than a second launch)
 constexpr int kMaxTopk = 16;
 constexpr int kMaxExperts = 512;
-constexpr int kMaxGrid = 160;         // decode CTAs (one per SM) the partial-sum scratch is sized for
-constexpr int kSyncRegionWords = 8;   // router arrivals, CTAs done, partial sums written, pad
+constexpr int kMaxGrid = 160;         // decode CTAs (one per SM) the no-allocation scratch is sized for
+constexpr int kSyncRegionWords = 8;   // router arrivals, CTAs done, h rows written, pad
 constexpr int kSyncWords = 2 + 2 * kSyncRegionWords;  // seq, err, two regions
 
 __host__ __device__ inline int cz_nblk(int x) { return (x + 127) / 128; }
@@ -27,14 +27,11 @@ __host__ __device__ inline int cz_nbp(int x) { return (cz_nblk(x) + 3) & ~3; }
 // Everything the decode kernel reads or writes; passed by value (a
 // __grid_constant__ kernel parameter, so the tensor maps can be used in place).
 struct alignas(64) DecodeParams {
-    CUtensorMap down_map;     // down_w u8 [E*H rows][I cols]: boxes of 16 columns x 256 (x grp) rows
-    CUtensorMap sh_down_map;  // sh_down_w u8 [H rows][SI cols] (SI > 0), the same boxes
     CUtensorMap gate_map;     // gate_w u8 [E*I rows][H]: boxes of 16 rows x 128 columns (x gu_kb blocks), 128-byte swizzle
     CUtensorMap up_map;
     CUtensorMap sh_gate_map;  // shared expert [SI rows][H] (SI > 0)
     CUtensorMap sh_up_map;
     int gu3d, gu_kb;          // gate/up boxes span gu_kb 128-column blocks (3D map) or one (2D map)
-    int dn_grp, sh_dn_grp;    // down boxes span dn_grp groups of 256 rows (3D maps) or one (0: 2D maps)
     const void* x;           // [T, H] f32 or bf16 (stack mode: h, f32)
     int x_bf16;
     int T;
@@ -62,18 +59,13 @@ struct alignas(64) DecodeParams {
     int e_lo, e_hi;          // routed experts held (and computed) here: [e_lo, e_hi); stacked from e_lo
     int shared_here;         // the shared expert is computed here
     float* logits;           // scratch [T, logit_stride(E)]
-    float* partial;          // scratch [grid][T][H]: each CTA's share of out
+    float* partial;          // scratch [T*(K+1)][max(I, SI)] f32: the h row of every (token, expert) pair
     uint32_t* sync;          // kSyncWords words, zeroed once at allocation
 };
 
-// Down-weight tensor map for TMA: a 2D u8 tensor [rows][cols] (cols = the
-// expert's intermediate size, row pitch = cols bytes), box 16 cols x 256 rows.
-// Decode-kernel tensor maps.  down: u8 [rows][cols] in boxes of 16 columns x
-// 256 rows, grouped 4 deep (one box = 1024 rows) when H % 256 == 0 (*grp = 4 or
-// fewer for small H, else 0 = 2D).  gate/up: u8 [rows][H] in 128-byte-swizzled
+// Decode-kernel tensor map of gate/up weights: u8 [rows][H] in 128-byte-swizzled
 // boxes of 16 rows x 128 columns, up to 16 column blocks deep when H % 128 == 0
 // (*kb = depth, else 0 = 2D).
-bool make_down_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64_t cols, int H, int* grp);
 bool make_gu_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64_t H, int* kb);
 
 size_t decode_smem_bytes(int T, int H, int x_bf16);

@@ -5,9 +5,10 @@
 // (fp8.zig:165-257) -> silu(g)*u (activation.zig:8-20) -> down -> out += gate*eo,
 // plus the always-on shared expert (467-479).
 //
-// Grid = one CTA per SM: 8 consumer warps + 1 producer warp.  The weights go
-// HBM -> shared memory through a ring of bulk-copy (TMA) stages filled by one
-// producer thread; no global memory is read inside a compute loop.
+// Grid = one CTA per SM: 8 consumer warps, 1 producer warp, 1 h warp.  The
+// weights go HBM -> shared memory through a ring of bulk-copy (TMA) stages
+// filled by one producer thread; no weight is read from global memory inside a
+// compute loop.
 //
 //   R  router logits.  CTA c owns router rows [c*E'/G, (c+1)*E'/G) (E' = E, +1
 //      for the shared expert's gate vector).  Rows and tokens are bulk-copied
@@ -20,33 +21,36 @@
 //   K  top-k.  Every CTA bulk-copies the logits, computes softmax/top-k for all
 //      tokens (identically) and groups the (token, slot) pairs by expert
 //      (ascending id, shared expert last).  Under expert parallelism a GPU
-//      holds experts [e_lo, e_hi) only; the other groups get no chunks here and
+//      holds experts [e_lo, e_hi) only; the other groups get no work here and
 //      the GPUs' outputs are summed by one all-reduce after the launch.
-//   C  chunks.  Each group's intermediate rows are cut into chunks of 16; the
-//      flattened chunk list is split evenly over the CTAs (split-K: a chunk's
-//      gate, up AND down work stays on one SM, so h never leaves it).  Pass 1
-//      streams, per chunk, gate rows [r0, r0+16) x 2048-column slabs of H (one
-//      bulk copy per row) and the same for up; the consumer warps split the
-//      K blocks, reduce, and keep h = silu(gate)*up of every chunk in shared
-//      memory.  Pass 2 streams, per slab of output rows, the down columns
-//      [r0, r0+16) of every chunk of the CTA (2D TMA boxes of 16 x 256); each
-//      warp owns 16-row output tiles and accumulates all of the CTA's chunks
-//      into registers, then writes its rows of the CTA's partial [T][H] to
-//      global scratch once.  The weight copies carry an L2 evict-first hint:
-//      streamed once, they should not push the kernel's code, the router rows
-//      or the scratch out of L2.
+//   C  gate/up.  Each group's intermediate rows are cut into chunks of 16; the
+//      flattened chunk list is split evenly over the CTAs.  Per chunk the
+//      producer streams gate rows [r0, r0+16) x 2048-column slabs of H and the
+//      same for up; the consumer warps split the K blocks and reduce, and the
+//      h warp writes hw = gate * silu(g) * u of every routed token to the
+//      pair's h row in global scratch.  A grid-wide arrive counter closes the
+//      phase (the producer keeps streaming meanwhile, see D).
+//   D  down.  CTA c owns output rows [c*H/G, (c+1)*H/G).  While C still runs,
+//      the producer streams those rows of every group's down matrix (with their
+//      128 x 128 scales), packed several groups to a ring stage.  After the
+//      counter, consumer warp j takes pairs j, j+8, ...: the pair's h row
+//      (from L2) becomes f16 hi/lo terms, and f16 MMAs against the down rows
+//      give one partial per (pair, row).  Out = residual + each token's pair
+//      partials in ascending expert order: no second reduction over CTAs.
+//      The weight copies carry an L2 evict-first hint: streamed once, they
+//      should not push the kernel's code, the router rows or the scratch out
+//      of L2.
 //
-// Arithmetic: mma.sync m16n8k32 E4M3 x E4M3 -> f32, which forms and sums the
-// exact products (checked on B200 to round like f32).  The weights enter as
-// their stored bytes.  The other operand is split exactly into E4M3 terms: a
-// token x (scaled by 2^s so that max|x| lies in [128, 256)) = t1 + t2 (+ t3),
-// every term a column of the MMA; a bf16 token is exact in 2 terms, an f32
-// token is kept to 12 bits in 3; h (per chunk and pair, scaled the same way)
-// to 16 bits in 4 terms.  Each 128-column block's sum is multiplied by its
-// 128x128 scale in f32.  Down sums accumulate in registers (every output row
-// owned by one warp, chunks in a fixed order); each CTA writes its partial
-// [T][H] once, and after a grid-wide arrive counter CTA c adds the G partial
-// rows of its slice of out in a fixed order: deterministic, no float atomics.
+// Arithmetic.  Gate/up: mma.sync m16n8k32 E4M3 x E4M3 -> f32, which forms and
+// sums the exact products (checked on B200 to round like f32).  The weights
+// enter as their stored bytes.  The token is split exactly into E4M3 terms: x
+// (scaled by 2^s so that max|x| lies in [128, 256)) = t1 + t2 (+ t3), every
+// term a column of the MMA; a bf16 token is exact in 2 terms, an f32 token is
+// kept to 12 bits in 3.  Down: mma.sync m16n8k16 f16 x f16 -> f32 with the
+// E4M3 weights converted exactly to f16 and h (scaled by a power of two per
+// pair into the f16 range) as hi + lo f16 terms (22 bits).  Each 128-column
+// block's sum is multiplied by its 128 x 128 scale in f32.  Every sum has a
+// fixed order: deterministic, no float atomics.
 //
 // Every wait is bounded; a CTA that gives up sets a bit in the device error
 // word, stops issuing work (draining its in-flight copies) and the host
@@ -67,17 +71,15 @@ constexpr int NWARPS = NCW + 2;
 constexpr int NTHREADS = NWARPS * 32;
 constexpr int CR = 16;                    // intermediate (h) rows per chunk
 constexpr int KS = 2048;                  // columns of a gate/up stage slab
-constexpr int OS = 2048;                  // output rows of a down stage
 constexpr int GU_BYTES = CR * KS;         // a gate/up stage: [K block][16 rows][128 B], 128-byte swizzled
 constexpr int SC_BYTES = 2048;            // block scales carried with every stage
-constexpr int SLOT_BYTES = 34 * 1024;     // >= GU_BYTES + SC_BYTES; a down stage uses OS * 16
+constexpr int SLOT_BYTES = 34 * 1024;     // >= GU_BYTES + SC_BYTES; also one pack of down rows
 constexpr int NSLOT = 4;                  // ring slots at least (more when shared memory allows)
 constexpr int MAXSLOT = 6;
 constexpr int RING_BYTES = NSLOT * SLOT_BYTES;  // the smallest ring (also stages phase R)
-constexpr int BOX_ROWS = 256;             // down-weight TMA box: 16 bytes x 256 rows
-constexpr int JH = 4;                     // E4M3 terms of h
-constexpr int MAXCH = 32;                 // chunks per CTA (h terms of all of them stay in shared memory)
 constexpr int MAXT = kDecodeMaxTokens;    // 4
+constexpr int DHW = 1024;                 // phase D: words of a warp's f16 h terms (intermediate <= 1024)
+constexpr int DMR = 32;                   // phase D: output rows per CTA at most
 constexpr int MAXK = kMaxTopk;            // 16
 constexpr int MAXE = kMaxExperts;         // 512
 constexpr int MAXP = MAXT * (MAXK + 1);   // (token, slot) pairs incl. shared-expert pairs: 68
@@ -85,7 +87,6 @@ constexpr int MAXG = MAXP;                // groups <= pairs
 constexpr int SMEM_LIMIT = 227 * 1024;
 
 static_assert(GU_BYTES + SC_BYTES <= SLOT_BYTES, "slot");
-static_assert(OS * 16 <= GU_BYTES, "down stage");
 static_assert(SLOT_BYTES % 1024 == 0, "TMA destinations stay 1024-aligned");
 
 // Small shared state (after the large regions).
@@ -99,9 +100,6 @@ struct __align__(16) DecodeMisc {
     uint32_t xmax[MAXT];  // max |x_t| (f32 bits)
     int xexp[MAXT];       // s per token (terms hold x_t * 2^s)
     float xscale[MAXT];   // 2^-s per token
-    float sdcol[2][64];   // down scales of a chunk's column block, one per 128 output rows (chunk parity)
-    float hmax[MAXT][64]; // max over chunks of |gate * h * down scale| per (token, 128-row block)
-    int hexp[MAXT][64];   // its power-of-two prescale
     int pe[MAXP];         // expert of pair p = t*K + z (shared: p = T*K + t -> E)
     float pg[MAXP];       // gate of pair p
     int order[MAXP];      // pairs sorted by (expert, pair)
@@ -109,13 +107,17 @@ struct __align__(16) DecodeMisc {
     int g_pair0[MAXG];
     int g_npairs[MAXG];
     int g_chunk0[MAXG + 1];
+    int g_pack[MAXG];     // phase D: the pack (ring stage) holding the group's down rows (-1: not held here)
+    int g_poff[MAXG];     // byte offset of the group's rows in its pack
+    int npk;              // packs of this CTA
+    int rtok[MAXP];       // token of sorted pair r when its group is held here, else -1
 };
 
-// Shared-memory map of one launch: [ring][x terms][red][h of every chunk][misc].
+// Shared-memory map of one launch: [ring][x terms][red][misc].
 struct Carve {
     int JX, CS;  // E4M3 terms per token; byte stride of one term column
     int ns;      // ring slots
-    uint32_t xterm, red, hterm, misc, total;
+    uint32_t xterm, red, dsum, misc, total;
 };
 
 __host__ __device__ inline Carve carve(int T, int H, int x_bf16) {
@@ -124,16 +126,16 @@ __host__ __device__ inline Carve carve(int T, int H, int x_bf16) {
     c.CS = ((H + 127) & ~127) + 64;  // column stride = 64 mod 128: lanes of 2 columns hit disjoint banks
     // the rest of the map decides how many slots fit
     const uint32_t rest = (((uint32_t)(T * c.JX * c.CS) + 127u) & ~127u) + 2 * NCW * 2 * 16 * 16 * 4 +
-                          MAXCH * 16 * MAXT * 4 + (((uint32_t)sizeof(DecodeMisc) + 127u) & ~127u);
+                          MAXP * DMR * 4 + (((uint32_t)sizeof(DecodeMisc) + 127u) & ~127u);
     const int fit = ((int)SMEM_LIMIT - 1024 - (int)rest) / SLOT_BYTES;
     c.ns = fit < NSLOT ? NSLOT : (fit > MAXSLOT ? MAXSLOT : fit);
     uint32_t off = (uint32_t)c.ns * SLOT_BYTES;
     c.xterm = off;
     off += ((uint32_t)(T * c.JX * c.CS) + 127u) & ~127u;
     c.red = off;
-    off += 2 * NCW * 2 * 16 * 16 * 4;  // two chunks in flight: [chunk parity][warp][gate/up][16 x 16]
-    c.hterm = off;
-    off += MAXCH * 16 * MAXT * 4;  // h of every chunk: [chunk][16 rows][MAXT tokens] f32
+    off += 2 * NCW * 2 * 16 * 16 * 4;  // two chunks in flight: [chunk parity][warp][gate/up][16 x 16]; then phase D h terms
+    c.dsum = off;
+    off += MAXP * DMR * 4;             // phase D: [sorted pair][output row] sums
     c.misc = off;
     off += ((uint32_t)sizeof(DecodeMisc) + 127u) & ~127u;
     c.total = off;
@@ -142,7 +144,7 @@ __host__ __device__ inline Carve carve(int T, int H, int x_bf16) {
 
 // ---- sync words ------------------------------------------------------------
 // sync[0] = launch sequence number, sync[1] = error word, then two regions of
-// kSyncRegionWords: [0] router arrivals, [1] CTAs done, [2] partial sums
+// kSyncRegionWords: [0] router arrivals, [1] CTAs done, [2] h rows
 // written.  A launch uses region seq&1 and zeroes the other one, so a launch
 // that stopped early leaves nothing behind.
 __device__ __forceinline__ uint32_t* region(uint32_t* sync, int par) { return sync + 2 + par * kSyncRegionWords; }
@@ -151,10 +153,8 @@ struct GroupW {
     const uint8_t *gw, *uw;
     const float *gs, *us, *ds;
     int inter;
-    int down_row0;                // first row of this expert in its down tensor map
     int gu_row0;                  // first row of this expert in its gate/up tensor maps
-    int dgrp;                     // down boxes: groups of 256 rows per box (0 = 2D boxes)
-    const CUtensorMap *dmap, *gmap, *umap;
+    const CUtensorMap *gmap, *umap;
 };
 
 __device__ __forceinline__ GroupW group_w(const DecodeParams& p, int e) {
@@ -166,10 +166,7 @@ __device__ __forceinline__ GroupW group_w(const DecodeParams& p, int e) {
         g.gs = p.sh_gate_s;
         g.us = p.sh_up_s;
         g.ds = p.sh_down_s;
-        g.down_row0 = 0;
         g.gu_row0 = 0;
-        g.dgrp = p.sh_dn_grp;
-        g.dmap = &p.sh_down_map;
         g.gmap = &p.sh_gate_map;
         g.umap = &p.sh_up_map;
     } else {
@@ -182,10 +179,7 @@ __device__ __forceinline__ GroupW group_w(const DecodeParams& p, int e) {
         g.gs = p.gate_s + (size_t)e * ssz;
         g.us = p.up_s + (size_t)e * ssz;
         g.ds = p.down_s + (size_t)e * cz_nblk(p.H) * cz_nbp(p.I);
-        g.down_row0 = e * p.H;
         g.gu_row0 = e * p.I;
-        g.dgrp = p.dn_grp;
-        g.dmap = &p.down_map;
         g.gmap = &p.gate_map;
         g.umap = &p.up_map;
     }
@@ -230,6 +224,21 @@ __device__ __forceinline__ void tma_box3_g2s(void* dst, const CUtensorMap* map, 
         "{%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
+}
+
+// Two E4M3 bytes (low byte = element 0) -> f16x2, exactly.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v) {
+    uint32_t h;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"((uint16_t)v));
+    return h;
+}
+
+__device__ __forceinline__ void mma_f16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ void mma_e4m3(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -314,83 +323,77 @@ __device__ __noinline__ float router_dot(const float* __restrict__ wrow, const u
 }
 
 // Top-k of one token (moe.zig:435-463) by one warp; lg = the token's logits in
-// shared memory, key = E words of shared scratch.  Lane l owns experts l, l+32,
-// ...  Keys are the f32 bits of exp(v - max) + 1 (non-negative floats order like
+// shared memory.  Lane l owns experts l, l+32, ... (NKL of them, in registers).
+// Keys are the f32 bits of exp(v - max) + 1 (non-negative floats order like
 // their bits; 0 = not a candidate: chosen, NaN or beyond E).  Each round takes
 // the largest key and, among equal keys, the smallest id — the reference's
 // strict-greater scan from e = 0 with bv = -1.  A round without a candidate
-// yields id 0, as in the reference.  The loops are kept rolled: this code runs
-// once per launch, so its size (fetched cold) matters more than its trip count.
-__device__ __noinline__ void route_token(const float* __restrict__ lg, uint32_t* __restrict__ key, int E, int K,
-                                         int norm_topk, int has_shared, int T, int t, int lane, DecodeMisc& s,
-                                         uint32_t* topk_idx, float* topk_gates, bool write_out) {
+// yields id 0, as in the reference.  One round = two warp reductions: the
+// largest key, then the smallest id holding it.
+template <int NKL>
+__device__ __noinline__ void route_token(const float* __restrict__ lg, int E, int K, int norm_topk, int has_shared,
+                                         int T, int t, int lane, DecodeMisc& s, uint32_t* topk_idx,
+                                         float* topk_gates, bool write_out) {
     float mx = __int_as_float(0xffc00000);  // NaN: fmaxf ignores it
-#pragma unroll 1
-    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
-    mx = warp_max(mx);
-    double all = 0.0;
-    float ex0 = 0.0f;
-    // four experts per lane at a time: their exp chains run side by side
-#pragma unroll 1
-    for (int e0 = lane; e0 < E; e0 += 128) {
-        float ex[4];
+    float lv[NKL];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) ex[j] = e0 + 32 * j < E ? cz_expf_inline(__fsub_rn(lg[e0 + 32 * j], mx)) : 0.0f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int e = e0 + 32 * j;
-            if (e < E) {
-                all += (double)ex[j];
-                key[e] = ex[j] > -1.0f ? __float_as_uint(ex[j]) + 1u : 0u;
-                if (e == 0) ex0 = ex[j];
-            }
-        }
+    for (int j = 0; j < NKL; ++j) {
+        lv[j] = 32 * j + lane < E ? lg[32 * j + lane] : __int_as_float(0xffc00000);
+        mx = fmaxf(mx, lv[j]);
     }
-    all = warp_sum_d(all);
-    const float ex_e0 = __shfl_sync(0xffffffffu, ex0, 0);
-    __syncwarp();
+    mx = warp_max(mx);
+    uint32_t kk[NKL];
+    double all = 0.0;
+#pragma unroll
+    for (int j = 0; j < NKL; ++j) {
+        const float ex = 32 * j + lane < E ? cz_expf_inline(__fsub_rn(lv[j], mx)) : 0.0f;
+        kk[j] = (32 * j + lane < E && ex > -1.0f) ? __float_as_uint(ex) + 1u : 0u;
+        if (!norm_topk && 32 * j + lane < E) all += (double)ex;
+        lv[j] = ex;
+    }
+    if (!norm_topk) all = warp_sum_d(all);
+    const float ex_e0 = __shfl_sync(0xffffffffu, lv[0], 0);
     double top = 0.0;
+    int my_e = 0;
+    float my_v = 0.0f;
 #pragma unroll 1
     for (int z = 0; z < K; ++z) {
-        uint32_t lbest = 0u;
-        int lid = 0x7fffffff;
-#pragma unroll 1
-        for (int e0 = lane; e0 < E; e0 += 128) {
-            uint32_t kk[4];
+        uint32_t lb = 0u;
+        int lj = 0;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) kk[j] = e0 + 32 * j < E ? key[e0 + 32 * j] : 0u;
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                if (kk[j] > lbest) {
-                    lbest = kk[j];
-                    lid = e0 + 32 * j;
-                }
-        }
-        const uint32_t kmax = redux_max_u32(lbest);
+        for (int j = 0; j < NKL; ++j)
+            if (kk[j] > lb) {
+                lb = kk[j];
+                lj = j;
+            }
+        const uint32_t kmax = redux_max_u32(lb);
         int best;
         float bv;
         if (kmax == 0u) {
             best = 0;
             bv = ex_e0;
         } else {
-            best = (int)redux_min_u32(lbest == kmax ? (uint32_t)lid : 0xffffffffu);
+            best = (int)redux_min_u32(lb == kmax ? (uint32_t)(32 * lj + lane) : 0xffffffffu);
             bv = __uint_as_float(kmax - 1u);
+            if ((best & 31) == lane) {
+#pragma unroll
+                for (int j = 0; j < NKL; ++j)
+                    if (j == (best >> 5)) kk[j] = 0u;
+            }
         }
-        __syncwarp();
-        if (lane == 0) {
-            if (kmax != 0u) key[best] = 0u;
-            s.pe[t * K + z] = best;
-            s.pg[t * K + z] = bv;  // exp value for now; the gate is formed below
+        if (lane == z) {
+            my_e = best;
+            my_v = bv;
         }
-        __syncwarp();
         top = __dadd_rn(top, (double)bv);
     }
     const double den = norm_topk ? top : all;
     if (lane < K) {
-        const float g = __double2float_rn(__ddiv_rn((double)s.pg[t * K + lane], den));
+        const float g = __double2float_rn(__ddiv_rn((double)my_v, den));
+        s.pe[t * K + lane] = my_e;
         s.pg[t * K + lane] = g;
         if (write_out) {
-            if (topk_idx) topk_idx[(size_t)t * K + lane] = (uint32_t)s.pe[t * K + lane];
+            if (topk_idx) topk_idx[(size_t)t * K + lane] = (uint32_t)my_e;
             if (topk_gates) topk_gates[(size_t)t * K + lane] = g;
         }
     }
@@ -410,11 +413,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, Decode
 
 // Named barriers between the consumer warps and the h warp (288 threads each):
 // RED_FULL(b): the consumers' partial gate/up sums of a chunk of parity b are in
-// red[b]; RED_FREE(b): the h warp has read them; H_DONE: h, its maxima and
-// exponents of every chunk are in shared memory.
-constexpr int BAR_RED_FULL = 2, BAR_RED_FREE = 4, BAR_H_DONE = 6;
+// red[b]; RED_FREE(b): the h warp has read them; H_WRITTEN: every h row of this
+// CTA is in global scratch.  D_GO (consumers only): the grid-wide h barrier has
+// passed.  The producer warp takes part in none of them: it may still be waiting
+// for ring slots that only phase D frees.
+constexpr int BAR_RED_FULL = 2, BAR_RED_FREE = 4, BAR_H_WRITTEN = 6, BAR_D_GO = 7;
 __device__ __forceinline__ void bar_sync_n(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "n"((NCW + 1) * 32) : "memory"); }
 __device__ __forceinline__ void bar_arrive_n(int id) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "n"((NCW + 1) * 32) : "memory"); }
+__device__ __forceinline__ void bar_sync_c(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "n"(NCW * 32) : "memory"); }
 
 // One instance per token count: loop trip counts, fragment shapes and slab sizes
 // become constants, so each launch runs a short, branch-free path.
@@ -438,7 +444,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     uint8_t* const ring = sb;
     uint8_t* const xterm = sb + cv.xterm;
     float* const red = reinterpret_cast<float*>(sb + cv.red);
-    uint8_t* const hterm = sb + cv.hterm;
     uint32_t* const err = p.sync + 1;
 
     const uint32_t seq = ld_relaxed_gpu(p.sync);
@@ -455,7 +460,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         fence_mbarrier_init();
     }
     if (tid < MAXT) s.xmax[tid] = 0u;
-    for (int i = tid; i < MAXT * 64; i += NTHREADS) (&s.hmax[0][0])[i] = 0.0f;
     __syncthreads();
 
     // ---------------- phase R: router logits ----------------
@@ -571,9 +575,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     if (!s.abort) {
         for (int t = warp; t < T; t += NWARPS) {
             const float* lg = reinterpret_cast<const float*>(ring) + (size_t)t * LS;
-            // keys of token t: shared scratch after the logits (the ring is idle until phase C)
-            uint32_t* key = reinterpret_cast<uint32_t*>(ring) + (size_t)MAXT * LS + (size_t)t * LS;
-            route_token(lg, key, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates, c == 0);
+            if (E <= 32)
+                route_token<1>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates, c == 0);
+            else if (E <= 128)
+                route_token<4>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates, c == 0);
+            else
+                route_token<MAXE / 32>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates,
+                                       c == 0);
         }
     }
     __syncthreads();
@@ -613,28 +621,59 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 s.g_npairs[u] = end - s.g_pair0[u];
             }
             __syncwarp();
+            for (int u = lane; u < base; u += 32) {  // token of every sorted pair of a group held here
+                const int eu = s.g_expert[u];
+                const bool here = eu == E ? p.shared_here != 0 : (eu >= p.e_lo && eu < p.e_hi);
+                for (int q = 0; q < s.g_npairs[u]; ++q)
+                    s.rtok[s.g_pair0[u] + q] = here ? pair_token(s.order[s.g_pair0[u] + q], T, K) : -1;
+            }
             if (lane == 0) {
-                int nc = 0;
+                // phase D packs: this CTA's output rows of every group held here, groups in
+                // order, as many per ring stage as fit
+                const int o_lo = (int)((long long)c * H / G), o_hi = (int)((long long)(c + 1) * H / G);
+                const int drows = o_hi - o_lo;
+                const int nrb = drows > 0 ? ((o_hi - 1) >> 7) - (o_lo >> 7) + 1 : 0;
+                int nc = 0, npk = 0, fill = SLOT_BYTES;
                 for (int u = 0; u < base; ++u) {
                     // groups of experts held elsewhere (expert parallelism) get no chunks
                     const int eu = s.g_expert[u];
                     const bool here = eu == E ? p.shared_here != 0 : (eu >= p.e_lo && eu < p.e_hi);
+                    const int iu = eu == E ? SI : Ir;
                     s.g_chunk0[u] = nc;
-                    if (here) nc += (eu == E ? SI : Ir) / CR;
+                    s.g_pack[u] = -1;
+                    if (here) {
+                        nc += iu / CR;
+                        if (drows > 0) {
+                            const int bytes = drows * iu + nrb * cz_nbp(iu) * 4;
+                            if (fill + bytes > SLOT_BYTES) {
+                                ++npk;
+                                fill = 0;
+                            }
+                            s.g_pack[u] = npk - 1;
+                            s.g_poff[u] = fill;
+                            fill += bytes;
+                        }
+                    }
                 }
                 s.g_chunk0[base] = nc;
                 s.U = base;
                 s.P = P;
                 s.NC = nc;
+                s.npk = npk;
             }
         } else if (lane == 0) {
             s.U = 0;
             s.NC = 0;
+            s.npk = 0;
         }
     }
     __syncthreads();
 
-    // ---------------- phase C: this CTA's chunks ----------------
+    // ---------------- phase C: this CTA's chunks; phase D: this CTA's output rows ----------------
+    const int o_lo = (int)((long long)c * H / G), o_hi = (int)((long long)(c + 1) * H / G);
+    const int drows = o_hi - o_lo;
+    const int ldh = Ir > SI ? Ir : SI;  // row stride of the h rows in global scratch
+    float* const dsum = reinterpret_cast<float*>(sb + cv.dsum);  // phase D: [sorted pair][row] sums
     {
         const int NC = s.NC;
         const int NS = cv.ns;
@@ -642,12 +681,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         const int nks = (H + KS - 1) / KS;     // gate (and up) stages per chunk
         const int nbpH = cz_nbp(H);
         const int nkbH = cz_nblk(H);           // 128-column blocks of H
-        // down: tiles per warp (each warp's accumulators live in registers across
-        // all chunks) and the output rows of one slab
-        // column groups of 8 (token, term) columns, and 16-row tiles per warp (NMD x TPW = 16 accumulators)
-        constexpr int NMD = T * JH <= 8 ? 1 : (T * JH <= 16 ? 2 : 4);
-        constexpr int TPW = 16 / NMD;
-        const int OSr = TPW * 16 * NCW;
 
         if (warp == PW) {
             // ---------------- producer (one thread) ----------------
@@ -666,14 +699,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                     if (!ok && !s.abort) set_error(err, s, CZ_DERR_EMPTY_WAIT);
                     return ok;
                 };
-                // pass 1: gate/up slabs of every chunk
+                // phase C: gate/up slabs of every chunk
                 {
                     int u = 0;
                     for (int ch = ch_lo; ch < ch_hi && !s.abort; ++ch) {
                         while (s.g_chunk0[u + 1] <= ch) ++u;
                         const GroupW gw = group_w(p, s.g_expert[u]);
                         const int r0 = (ch - s.g_chunk0[u]) * CR;
-                        const int nbpI = cz_nbp(gw.inter);
                         for (int st = 0; st < 2 * nks && !s.abort; ++st, ++si) {
                             const int slot = si % NS;
                             if (!acquire_slot(slot, si / NS)) break;
@@ -685,10 +717,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                             const int kb0 = (st >> 1) * (KS / 128), nkbs = min(KS / 128, nkbH - kb0);
                             const CUtensorMap* map = up ? gw.umap : gw.gmap;
                             const float* ssrc = (up ? gw.us : gw.gs) + (size_t)(r0 >> 7) * nbpH;
-                            // the first up slab also carries the expert's down-scale table
-                            const uint32_t dsb = st == 1 ? (uint32_t)(cz_nblk(H) * nbpI * 4) : 0u;
                             const uint32_t wb = (uint32_t)(CR * 128) * (uint32_t)(p.gu3d ? p.gu_kb : nkbs);
-                            mbar_arrive_expect_tx(&s.full[slot], wb + (uint32_t)(nbpH * 4) + dsb);
+                            mbar_arrive_expect_tx(&s.full[slot], wb + (uint32_t)(nbpH * 4));
                             if (p.gu3d) {
                                 tma_box3_g2s(dst, map, 0, gw.gu_row0 + r0, kb0, &s.full[slot], pol);
                             } else {
@@ -697,39 +727,42 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                                                 &s.full[slot], pol);
                             }
                             bulk_g2s(sdst, ssrc, (uint32_t)nbpH * 4u, &s.full[slot]);
-                            if (dsb) bulk_g2s(sdst + nbpH, gw.ds, dsb, &s.full[slot]);
                         }
                     }
                 }
-                // pass 2: for every slab of OSr output rows, the down columns of every chunk
-                for (int o0 = 0; o0 < H && !s.abort; o0 += OSr) {
-                    const int OSl = min(OSr, H - o0);
-                    const int nbox = (OSl + BOX_ROWS - 1) / BOX_ROWS;
-                    const int ob0 = o0 >> 7, nob = (OSl + 127) >> 7;
+                // phase D: the packs of down rows [o_lo, o_hi) (+ their 128 x 128 scales) of
+                // every group held here; they stream in while phase C still runs
+                if (drows > 0) {
+                    const int rb0 = o_lo >> 7, nrb = ((o_hi - 1) >> 7) - rb0 + 1;
                     int u = 0;
-                    for (int ch = ch_lo; ch < ch_hi && !s.abort; ++ch, ++si) {
-                        while (s.g_chunk0[u + 1] <= ch) ++u;
-                        const GroupW gw = group_w(p, s.g_expert[u]);
-                        const int r0 = (ch - s.g_chunk0[u]) * CR;
-                        const int nbpI = cz_nbp(gw.inter);
+                    for (int j = 0; j < s.npk && !s.abort; ++j, ++si) {
+                        while (u < s.U && s.g_pack[u] != j) ++u;
+                        int u1 = u;
+                        uint32_t bytes = 0;  // what the copies below deliver (rows x iu is a multiple of 16)
+                        for (; u1 < s.U && (s.g_pack[u1] == j || s.g_pack[u1] < 0); ++u1) {
+                            if (s.g_pack[u1] < 0) continue;
+                            const int iu = s.g_expert[u1] == E ? SI : Ir;
+                            bytes += (uint32_t)(drows * iu + nrb * cz_nbp(iu) * 4);
+                        }
                         const int slot = si % NS;
                         if (!acquire_slot(slot, si / NS)) break;
                         uint8_t* dst = ring + (size_t)slot * SLOT_BYTES;
-                        float* sdst = reinterpret_cast<float*>(dst + GU_BYTES);
-                        if (gw.dgrp) {
-                            // boxes of dgrp x 256 rows (3D map: [group][256 rows][cols])
-                            const int rows_b = BOX_ROWS * gw.dgrp, nb3 = (OSl + rows_b - 1) / rows_b;
-                            mbar_arrive_expect_tx(&s.full[slot], (uint32_t)(nb3 * rows_b * 16 + nob * nbpI * 4));
-                            for (int b = 0; b < nb3; ++b)
-                                tma_box3_g2s(dst + (size_t)b * rows_b * 16, gw.dmap, r0, 0,
-                                             (gw.down_row0 + o0) / BOX_ROWS + b * gw.dgrp, &s.full[slot], pol);
-                        } else {
-                            mbar_arrive_expect_tx(&s.full[slot], (uint32_t)(nbox * BOX_ROWS * 16 + nob * nbpI * 4));
-                            for (int b = 0; b < nbox; ++b)
-                                tma_box_g2s(dst + (size_t)b * BOX_ROWS * 16, gw.dmap, r0,
-                                            gw.down_row0 + o0 + b * BOX_ROWS, &s.full[slot], pol);
+                        mbar_arrive_expect_tx(&s.full[slot], bytes);
+                        for (int v = u; v < u1; ++v) {
+                            if (s.g_pack[v] < 0) continue;
+                            const int ev = s.g_expert[v];
+                            const bool sh = ev == E;
+                            const int iu = sh ? SI : Ir;
+                            const uint8_t* wsrc = sh ? p.sh_down_w + (size_t)o_lo * SI
+                                                     : p.down_w + ((size_t)(ev - p.e_lo) * H + o_lo) * Ir;
+                            const float* ssrc = sh ? p.sh_down_s + (size_t)rb0 * cz_nbp(SI)
+                                                   : p.down_s + ((size_t)(ev - p.e_lo) * nkbH + rb0) * cz_nbp(Ir);
+                            uint8_t* d = dst + s.g_poff[v];
+                            const uint32_t wbytes = (uint32_t)drows * (uint32_t)iu;  // a multiple of 16
+                            bulk_g2s_hint(d, wsrc, wbytes, &s.full[slot], pol);
+                            bulk_g2s(d + wbytes, ssrc, (uint32_t)(nrb * cz_nbp(iu) * 4), &s.full[slot]);
                         }
-                        bulk_g2s(sdst, gw.ds + (size_t)ob0 * nbpI, (uint32_t)(nob * nbpI * 4), &s.full[slot]);
+                        u = u1;
                     }
                 }
                 // drain: no copy may land after this CTA exits (waiting on a phase
@@ -747,9 +780,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         } else if (warp == HW) {
             // ---------------- h warp ----------------
             // Per chunk, once the consumers' partial gate/up sums are in red[b]:
-            // hw = gate * silu(g) * u per (row r, token tk) (0 for tokens not routed
-            // to the chunk's expert) and the running max of |hw * down scale| per
-            // (token, 128-row output block).  Runs beside the next chunk's MMAs.
+            // hw = gate * silu(g) * u per (row r, routed token) into the pair's h row in
+            // global scratch.  Runs beside the next chunk's MMAs.
             const int nch = ch_hi - ch_lo;
             int u = 0;
             for (int ch = ch_lo; ch < ch_hi; ++ch) {
@@ -757,6 +789,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 const int ci = ch - ch_lo, b = ci & 1;
                 const int np = s.g_npairs[u];
                 const int* pairs = s.order + s.g_pair0[u];
+                const int r0 = (ch - s.g_chunk0[u]) * CR;
                 bar_sync_n(BAR_RED_FULL + b);
                 const float* rb = red + b * (NCW * 2 * 256);
 #pragma unroll 1
@@ -765,7 +798,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                     int q = -1;
                     for (int qq = 0; qq < np; ++qq)
                         if (pair_token(pairs[qq], T, K) == tk) q = qq;
-                    float hw = 0.0f;
                     if (q >= 0 && !s.abort) {
                         float gs = 0.0f, us = 0.0f;
                         const float* rg = rb + r * 16 + q * cv.JX;
@@ -786,25 +818,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                                     us += uv[w][j];
                                 }
                         const float xsc = s.xscale[tk];
-                        hw = s.pg[pairs[q]] * (silu_fast(gs * xsc) * (us * xsc));
+                        p.partial[(size_t)pairs[q] * ldh + r0 + r] =
+                            s.pg[pairs[q]] * (silu_fast(gs * xsc) * (us * xsc));
                     }
-                    reinterpret_cast<float*>(hterm)[(ci * 16 + r) * MAXT + tk] = hw;
-                    float mh = fabsf(hw);
-                    if (!(mh < 3.0e38f)) mh = 0.0f;
-#pragma unroll
-                    for (int o = 8; o > 0; o >>= 1) mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
-                    if (q >= 0)
-                        for (int ob = r; ob < cz_nblk(H); ob += 16)
-                            s.hmax[tk][ob] = fmaxf(s.hmax[tk][ob], mh * fabsf(s.sdcol[b][ob]));
                 }
                 __threadfence_block();
                 if (ci + 2 < nch) bar_arrive_n(BAR_RED_FREE + b);
             }
-            // one power-of-two scale per (token, 128-row output block) for every chunk
-            __syncwarp();
-            for (int i = lane; i < MAXT * 64; i += 32) (&s.hexp[0][0])[i] = prescale_exp((&s.hmax[0][0])[i]);
-            __threadfence_block();
-            bar_arrive_n(BAR_H_DONE);
         } else {
             // ---------------- consumers ----------------
             const int g = lane >> 2, t = lane & 3;  // MMA fragment coordinates
@@ -813,16 +833,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
             const int rho = (g >> 1) + 4 * (g & 1);
             int si = 0;
             int u = 0;
-            // ==== pass 1: gate/up of every chunk (h is formed by the h warp) ====
+            // ==== phase C: gate/up of every chunk (h is formed by the h warp) ====
             for (int ch = ch_lo; ch < ch_hi; ++ch) {
                 while (s.g_chunk0[u + 1] <= ch) ++u;
                 const int ci = ch - ch_lo, b = ci & 1;
-                // red[b] and sdcol[b] are reused: the h warp must be done with chunk ci-2
+                // red[b] is reused: the h warp must be done with chunk ci-2
                 if (ci >= 2) bar_sync_n(BAR_RED_FREE + b);
                 const int np = s.g_npairs[u];
                 const int* pairs = s.order + s.g_pair0[u];
-                const int ib = ((ch - s.g_chunk0[u]) * CR) >> 7;  // the chunk's 128-column block of down
-                const int nbpI = cz_nbp(s.g_expert[u] == E ? SI : Ir);
                 // columns of the gate/up MMAs: c = q*JX + j (pair q, term j); lane's column g of MMA m
                 const int ncolA = np * cv.JX, nmA = (ncolA + 7) >> 3;
                 const uint8_t* xcol[2];
@@ -907,10 +925,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                             accg[m][i] += ag[m][i];
                             accu[m][i] += au[m][i];
                         }
-                    if (kq == 0 && warp == 0) {  // down scales of column block ib, from the up slab
-                        const float* dtab = tu + nbpH;
-                        for (int ob = lane; ob < cz_nblk(H); ob += 32) s.sdcol[b][ob] = dtab[ob * nbpI + ib];
-                    }
                     __syncwarp();
                     if (lane == 0) {
                         mbar_arrive(&s.empty[slg]);
@@ -938,195 +952,151 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 __threadfence_block();
                 bar_arrive_n(BAR_RED_FULL + b);
             }
-            // h, its maxima and the exponents of every chunk are ready
-            bar_sync_n(BAR_H_DONE);
-
-            // ==== pass 2: per slab of OSr output rows, down of every chunk ====
-            // Warp w owns tiles [w*TPW, (w+1)*TPW) of the slab; its accumulators stay in
-            // registers across the chunks (columns = (token, term) for every chunk).  The
-            // B operand of a chunk and 128-row block: the E4M3 terms of
-            // hw * down scale * 2^s(token, block).
-            for (int o0 = 0; o0 < H; o0 += OSr) {
-                const int OSl = min(OSr, H - o0);
-                const int ntile = OSl >> 4;
-                float accd[16][4];
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) accd[i][k] = 0.0f;
-                const int tw0 = warp * TPW;  // first tile of this warp in the slab
-                const int obw = (o0 >> 7) + ((tw0 * 16) >> 7);  // first 128-row block of those tiles
-                // chunks in pairs: chunk A's 16 columns are the MMA's K values 0-15, chunk
-                // B's (the next stage) K values 16-31, so one MMA serves both
-                u = 0;
-                for (int ch = ch_lo; ch < ch_hi; ch += 2) {
-                    const int nh = ch + 1 < ch_hi ? 2 : 1;
-                    const uint8_t* stA = nullptr;
-                    const uint8_t* stB = nullptr;
-                    uint32_t bfA[2][NMD] = {}, bfB[2][NMD] = {};
-                    bool ok = !s.abort;
-#pragma unroll 1
-                    for (int hh = 0; hh < nh && ok; ++hh) {
-                        const int chh = ch + hh, sidx = si + hh;
-                        while (s.g_chunk0[u + 1] <= chh) ++u;
-                        const int ci = chh - ch_lo;
-                        const int ib = ((chh - s.g_chunk0[u]) * CR) >> 7;
-                        const int nbpI = cz_nbp(s.g_expert[u] == E ? SI : Ir);
-                        const int slot = sidx % NS;
-                        ok = warp_wait(&s.full[slot], (sidx / NS) & 1, s);
-                        if (!ok) break;
-                        const uint8_t* stage = ring + (size_t)slot * SLOT_BYTES;
-                        const float* stab = reinterpret_cast<const float*>(stage + GU_BYTES);
-                        // B fragments: lane column c = 8m + g = (token c/4, term c%4), rows 4t..4t+3
-                        uint32_t bw[2][NMD];
-#pragma unroll
-                        for (int ol = 0; ol < 2; ++ol)
-#pragma unroll
-                            for (int m = 0; m < NMD; ++m) {
-                                const int cc = 8 * m + g, tk = cc >> 2, jt = cc & 3;
-                                const int ob = obw + ol;
-                                uint32_t word = 0u;
-                                if (tk < T && (ob << 7) < o0 + OSl) {
-                                    const float f = stab[(ob - (o0 >> 7)) * nbpI + ib];
-                                    const float sc = scale2(f, s.hexp[tk][ob]);
-                                    const float* hv = reinterpret_cast<const float*>(hterm) + (ci * 16 + 4 * t) * MAXT + tk;
-                                    float a0 = hv[0] * sc, b0 = hv[MAXT] * sc, a1 = hv[2 * MAXT] * sc, b1 = hv[3 * MAXT] * sc;
-#pragma unroll
-                                    for (int j = 0; j < JH; ++j) {
-                                        const uint32_t d0 = e4m3_term2(a0, b0), d1 = e4m3_term2(a1, b1);
-                                        if (j == jt) word = d0 | (d1 << 16);
-                                    }
-                                }
-                                bw[ol][m] = word;
-                            }
-                        if (hh == 0) {
-                            stA = stage;
-#pragma unroll
-                            for (int ol = 0; ol < 2; ++ol)
-#pragma unroll
-                                for (int m = 0; m < NMD; ++m) bfA[ol][m] = bw[ol][m];
-                        } else {
-                            stB = stage;
-#pragma unroll
-                            for (int ol = 0; ol < 2; ++ol)
-#pragma unroll
-                                for (int m = 0; m < NMD; ++m) bfB[ol][m] = bw[ol][m];
-                        }
-                    }
-                    if (ok) {
-#pragma unroll
-                        for (int it = 0; it < TPW; ++it) {
-                            if (tw0 + it < ntile) {
-                                const size_t ra = (size_t)((tw0 + it) * 16 + g) * 16 + 4 * t;
-                                const uint32_t a0 = *reinterpret_cast<const uint32_t*>(stA + ra);
-                                const uint32_t a1 = *reinterpret_cast<const uint32_t*>(stA + ra + 8 * 16);
-                                uint32_t a2 = 0u, a3 = 0u;
-                                if (nh == 2) {
-                                    a2 = *reinterpret_cast<const uint32_t*>(stB + ra);
-                                    a3 = *reinterpret_cast<const uint32_t*>(stB + ra + 8 * 16);
-                                }
-                                const int obl = (it * 16) >> 7;
-#pragma unroll
-                                for (int m = 0; m < NMD; ++m)
-                                    mma_e4m3(accd[it * NMD + m], a0, a1, a2, a3, bfA[obl][m], bfB[obl][m]);
-                            }
-                        }
-                        __syncwarp();
-                        if (lane == 0) {
-                            mbar_arrive(&s.empty[si % NS]);
-                            if (nh == 2) mbar_arrive(&s.empty[(si + 1) % NS]);
-                        }
-                    } else if (lane == 0 && !s.abort) {
-                        set_error(err, s, CZ_DERR_FULL_WAIT);
-                    }
-                    si += nh;
-                }
-                // slab done: combine the 4 terms of each token, undo the scale, write the
-                // CTA's partial rows (every (token, row) of the slab is written, zeros included)
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int tile = i / NMD, m = i % NMD;
-                    {
-                        float v0 = accd[i][0] + accd[i][1], v1 = accd[i][2] + accd[i][3];
-                        v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
-                        v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
-                        const int tk = 2 * m + (t >> 1);
-                        if (tw0 + tile < ntile && (t & 1) == 0 && tk < T) {
-                            const int o = o0 + (tw0 + tile) * 16 + g;
-                            const float us = scale2(1.0f, -s.hexp[tk][o >> 7]);
-                            float* dst = p.partial + ((size_t)c * T + tk) * H + o;
-                            dst[0] = v0 * us;
-                            dst[8] = v1 * us;
-                        }
-                    }
-                }
-            }
         }
     }
 
-    // ---------------- this CTA's slice of out: the G partial rows in a fixed order ----------------
-    // the block barrier orders every thread's partial rows before thread 0's
-    // fence and release; the other CTAs acquire them through the counter
-    __syncthreads();
+    // ---------------- every h row of every CTA is written ----------------
+    // H_WRITTEN orders the h warp's global writes before thread 0's fence and release;
+    // the other CTAs acquire them through the counter.  The producer keeps issuing the
+    // phase D packs meanwhile (it joins the block again at the end).
+    if (warp < NCW || warp == HW) bar_sync_n(BAR_H_WRITTEN);
     if (tid == 0) {
         __threadfence();
         red_release_add_gpu(&reg[2], 1u);
         if (!wait_geq_bounded(&reg[2], (uint32_t)G, err)) set_error(err, s, CZ_DERR_READY_WAIT);
     }
-    __syncthreads();
-    if (!s.abort) {
-        // CTA c owns output rows [c*RPC, (c+1)*RPC) (RPC a multiple of 4): items
-        // (t, 4 rows); thread (item, part) sums partials part, part+NP, ... in
-        // order, then the parts are added in order.
-        const int RPC = (((H + G - 1) / G) + 3) & ~3;
-        const int o_lo = c * RPC, o_hi = min(H, o_lo + RPC);
-        const int nq4 = o_hi > o_lo ? (o_hi - o_lo) >> 2 : 0;
-        const int nitem = T * nq4;
-        float4* part = reinterpret_cast<float4*>(red);  // [item][NPART]
-        const int NPART = nitem > 0 ? max(1, min(32, NTHREADS / nitem)) : 1;
-        const int it = tid / NPART, pt = tid - it * NPART;
-        if (nitem > 0 && it < nitem) {
-            const int tk = it / nq4, o = o_lo + 4 * (it - tk * nq4);
-            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-            // batches of up to 8 loads in flight, added in order
-            for (int cc0 = pt; cc0 < G; cc0 += 8 * NPART) {
-                float4 v[8];
+    if (warp < NCW) bar_sync_c(BAR_D_GO);
+
+    // ---------------- phase D: output rows [o_lo, o_hi) over every pair held here ----------------
+    // Pair j (in group order) goes to consumer warp j % NCW.  For one pair and one row:
+    // sum over 128-column blocks of scale(row block, column block) x (down row . h row),
+    // lanes on 8-column pieces.  Every warp waits for and releases every pack in order.
+    if (warp < NCW && drows > 0) {
+        const int NS = cv.ns;
+        const int nch = s.NC;
+        const int si0 = 2 * ((H + KS - 1) / KS) * ((int)((long long)(c + 1) * nch / G) - (int)((long long)c * nch / G));
+        const int rb0 = o_lo >> 7;
+        int pk_done = 0;   // packs waited for and released by this warp
+        bool ok = !s.abort;
+        auto release_to = [&](int j_end) {  // wait for and release packs [pk_done, j_end)
+            for (; pk_done < j_end; ++pk_done) {
+                const int sidx = si0 + pk_done;
+                if (ok) ok = warp_wait(&s.full[sidx % NS], (sidx / NS) & 1, s);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s.empty[sidx % NS]);
+            }
+        };
+        int jp = 0;  // running index of held pairs
+        for (int u = 0; u < s.U; ++u) {
+            const int pk = s.g_pack[u];
+            if (pk < 0) continue;
+            const int np = s.g_npairs[u];
+            const bool sh = s.g_expert[u] == E;
+            const int iu = sh ? SI : Ir, nbpI = cz_nbp(iu);
+            for (int q = 0; q < np; ++q, ++jp) {
+                if (jp % NCW != warp) continue;
+                // the pair's h row (loads in flight while the pack is waited for); below it becomes,
+                // x 2^e (max |h| x 2^e in [2^14, 2^15), inside the f16 range), f16 pairs of hi and lo
+                // terms (22 bits) in this warp's share of the idle reduction buffer: words [0, iu/2)
+                // hi, [iu/2, iu) lo
+                const int pr = s.order[s.g_pair0[u] + q];
+                const float2* hrow = reinterpret_cast<const float2*>(p.partial + (size_t)pr * ldh);
+                uint32_t* hb = reinterpret_cast<uint32_t*>(red) + warp * DHW;
+                const int nw2 = iu >> 1;
+                float2 hv[DHW / 64];
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const int cc = cc0 + k * NPART;
-                    v[k] = cc < G ? __ldcg(reinterpret_cast<const float4*>(p.partial + ((size_t)cc * T + tk) * H + o))
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int j = 0; j < DHW / 64; ++j)
+                    hv[j] = lane + 32 * j < nw2 ? __ldcg(hrow + lane + 32 * j) : make_float2(0.f, 0.f);
+                release_to(pk);  // every earlier pack is done for this warp
+                const int sidx = si0 + pk;
+                if (ok) ok = warp_wait(&s.full[sidx % NS], (sidx / NS) & 1, s);
+                if (!ok) {
+                    if (lane == 0 && !s.abort) set_error(err, s, CZ_DERR_FULL_WAIT);
+                    continue;
                 }
+                const uint8_t* wr = ring + (size_t)(sidx % NS) * SLOT_BYTES + s.g_poff[u];
+                const float* sc = reinterpret_cast<const float*>(wr + (size_t)drows * iu);
+                float hm = 0.0f;
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    if (cc0 + k * NPART < G) {
-                        sum.x += v[k].x;
-                        sum.y += v[k].y;
-                        sum.z += v[k].z;
-                        sum.w += v[k].w;
+                for (int j = 0; j < DHW / 64; ++j) hm = fmaxf(hm, fmaxf(fabsf(hv[j].x), fabsf(hv[j].y)));
+                hm = warp_max(hm);
+                const int he = !(hm < 3.0e38f) ? 0 : prescale_exp(hm) + 7;  // [128, 256) x 2^7
+                const float hs = scale2(1.0f, he), hsi = scale2(1.0f, -he);
+#pragma unroll
+                for (int j = 0; j < DHW / 64; ++j)
+                    if (lane + 32 * j < nw2) {
+                        const float ax = hv[j].x * hs, ay = hv[j].y * hs;
+                        const __half2 hi = __floats2half2_rn(ax, ay);
+                        const float2 back = __half22float2(hi);
+                        const __half2 lo = __floats2half2_rn(ax - back.x, ay - back.y);
+                        hb[lane + 32 * j] = *reinterpret_cast<const uint32_t*>(&hi);
+                        hb[nw2 + lane + 32 * j] = *reinterpret_cast<const uint32_t*>(&lo);
                     }
+                __syncwarp();
+                // f16 MMAs m16n8k16: A = 16 of the pack's down rows (E4M3 -> f16, exact), B columns
+                // 0 / 1 = the hi / lo terms of h.  The K order inside a 64-column group is permuted
+                // (A and B alike): step j's columns {2t, 2t+1, 2t+8, 2t+9} of lane t are the bytes
+                // 16t + 4j .. 16t + 4j + 3, so one 16-byte load of a row feeds four steps.  Each
+                // 128-column block's sum is scaled once.
+                const int g = lane >> 2, t = lane & 3;
+                for (int rt = 0; rt * 16 < drows; ++rt) {
+                    const int ra = rt * 16 + g, rb = ra + 8;
+                    const bool va = ra < drows, vb = rb < drows;
+                    const uint8_t* wa = wr + (size_t)(va ? ra : 0) * iu + 16 * t;
+                    const uint8_t* wb = wr + (size_t)(vb ? rb : 0) * iu + 16 * t;
+                    const float* sca = sc + (size_t)(((o_lo + (va ? ra : 0)) >> 7) - rb0) * nbpI;
+                    const float* scb = sc + (size_t)(((o_lo + (vb ? rb : 0)) >> 7) - rb0) * nbpI;
+                    const uint32_t* hbc = hb + (g == 1 ? nw2 : 0) + 8 * t;
+                    float acca = 0.0f, accb = 0.0f;
+                    for (int kb = 0; kb < (iu >> 7); ++kb) {
+                        float cc[4][4] = {};
+#pragma unroll
+                        for (int k64 = 0; k64 < 2; ++k64) {
+                            const int kbase = kb * 128 + k64 * 64;
+                            const uint4 xa = va ? *reinterpret_cast<const uint4*>(wa + kbase) : make_uint4(0u, 0u, 0u, 0u);
+                            const uint4 xb = vb ? *reinterpret_cast<const uint4*>(wb + kbase) : make_uint4(0u, 0u, 0u, 0u);
+                            const uint4 b01 = g < 2 ? *reinterpret_cast<const uint4*>(hbc + (kbase >> 1)) : make_uint4(0u, 0u, 0u, 0u);
+                            const uint4 b23 = g < 2 ? *reinterpret_cast<const uint4*>(hbc + (kbase >> 1) + 4) : make_uint4(0u, 0u, 0u, 0u);
+                            const uint32_t av[4] = {xa.x, xa.y, xa.z, xa.w}, bw[4] = {xb.x, xb.y, xb.z, xb.w};
+                            const uint32_t h0[4] = {b01.x, b01.z, b23.x, b23.z}, h1[4] = {b01.y, b01.w, b23.y, b23.w};
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                mma_f16(cc[j], e4m3x2_to_f16x2(av[j] & 0xffffu), e4m3x2_to_f16x2(bw[j] & 0xffffu),
+                                        e4m3x2_to_f16x2(av[j] >> 16), e4m3x2_to_f16x2(bw[j] >> 16), h0[j], h1[j]);
+                        }
+                        const float ra0 = (cc[0][0] + cc[1][0]) + (cc[2][0] + cc[3][0]);
+                        const float ra1 = (cc[0][1] + cc[1][1]) + (cc[2][1] + cc[3][1]);
+                        const float rb0 = (cc[0][2] + cc[1][2]) + (cc[2][2] + cc[3][2]);
+                        const float rb1 = (cc[0][3] + cc[1][3]) + (cc[2][3] + cc[3][3]);
+                        acca = __fmaf_rn(sca[kb], ra0 + ra1, acca);
+                        accb = __fmaf_rn(scb[kb], rb0 + rb1, accb);
+                    }
+                    if (t == 0) {
+                        if (va) dsum[(s.g_pair0[u] + q) * drows + ra] = acca * hsi;
+                        if (vb) dsum[(s.g_pair0[u] + q) * drows + rb] = accb * hsi;
+                    }
+                }
+                __syncwarp();
             }
-            part[it * NPART + pt] = sum;
         }
-        __syncthreads();
-        if (nitem > 0 && tid < nitem) {
-            const int tk = tid / nq4, o = o_lo + 4 * (tid - tk * nq4);
-            float4 sum = part[tid * NPART];
-            for (int k = 1; k < NPART; ++k) {
-                const float4 v = part[tid * NPART + k];
-                sum.x += v.x;
-                sum.y += v.y;
-                sum.z += v.z;
-                sum.w += v.w;
+        release_to(s.npk);
+        if (!ok && lane == 0 && !s.abort) set_error(err, s, CZ_DERR_FULL_WAIT);
+    }
+    __syncthreads();
+    if (!s.abort && drows > 0) {
+        // out[t][o] = (residual) + the token's pairs in group (ascending expert) order
+        for (int k = tid; k < T * drows; k += NTHREADS) {
+            const int tk = k / drows, r = k - tk * drows;
+            float sum = 0.0f;
+            bool any = false;
+            for (int rp = 0; rp < s.P; ++rp) {  // sorted pairs: groups in ascending expert order
+                if (s.rtok[rp] != tk) continue;
+                const float v = dsum[rp * drows + r];
+                sum = any ? sum + v : v;
+                any = true;
             }
-            if (p.residual) {
-                const float4 r = *reinterpret_cast<const float4*>(p.residual + (size_t)tk * H + o);
-                sum.x = __fadd_rn(r.x, sum.x);
-                sum.y = __fadd_rn(r.y, sum.y);
-                sum.z = __fadd_rn(r.z, sum.z);
-                sum.w = __fadd_rn(r.w, sum.w);
-            }
-            *reinterpret_cast<float4*>(p.out + (size_t)tk * H + o) = sum;
+            const size_t o = (size_t)tk * H + o_lo + r;
+            p.out[o] = p.residual ? __fadd_rn(p.residual[o], sum) : sum;
         }
     }
 
@@ -1149,22 +1119,17 @@ int decode_max_tokens(int H, int E, int K, int I, int SI, int x_bf16, int num_sm
     if (K < 1 || K > MAXK || E < K || E > MAXE || H % 16 || I % 16 || SI % 16 || H < 16 || I < 16) return 0;
     if (num_sms > kMaxGrid) return 0;
     const int IM = I > SI ? I : SI;
-    if (cz_nblk(H) > 64) return 0;  // per-(token, 128-row block) scale tables
-    // scales carried with a stage: gate/up row block + (first up slab) the expert's down table;
-    // a down stage: its 128-row blocks of the down table
-    if ((size_t)(cz_nbp(H) + cz_nblk(H) * cz_nbp(IM)) * 4 > (size_t)SC_BYTES) return 0;
-    if ((size_t)(OS / 128) * cz_nbp(IM) * 4 > (size_t)SC_BYTES) return 0;
+    // scales carried with a gate/up stage: its row block of the scale table
+    if ((size_t)cz_nbp(H) * 4 > (size_t)SC_BYTES) return 0;
+    // phase D: a CTA's output rows of one group (+ their <= 2 row blocks of scales) fit one ring stage
+    const int orows = (H + num_sms - 1) / num_sms;
+    if (orows > DMR || (size_t)orows * IM + (size_t)2 * cz_nbp(IM) * 4 > (size_t)SLOT_BYTES) return 0;
+    if (IM > DHW || IM % 128) return 0;  // phase D: a warp's h terms; whole 128-column blocks
     const int max_rows = (E + (SI ? 1 : 0) + num_sms - 1) / num_sms;  // router rows staged per CTA
-    const int IM16 = (I > SI ? I : SI) / CR;  // chunks of the largest group
     int t = MAXT;
     while (t > 0) {
         // gate/up MMA columns: a group holds at most t pairs, each as JX E4M3 term columns (<= 16)
         if (t * (x_bf16 ? 2 : 3) > 16) {
-            --t;
-            continue;
-        }
-        const int worst_chunks = (t * K + (SI ? t : 0)) * IM16;  // every pair its own group
-        if ((worst_chunks + num_sms - 1) / num_sms > MAXCH) {
             --t;
             continue;
         }
@@ -1196,32 +1161,6 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-bool make_down_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64_t cols, int H, int* grp) {
-    const EncodeTiledFn fn = encode_fn();
-    if (!fn || cols % 16 || rows == 0 || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
-    const cuuint32_t estr[3] = {1, 1, 1};
-    if (H % BOX_ROWS == 0 && rows % BOX_ROWS == 0) {
-        // [rows / 256][256][cols]: one box = 16 columns of up to 4 groups of 256 rows
-        const uint64_t ng = rows / BOX_ROWS;
-        const int g = (int)(ng < 4 ? ng : 4);
-        const cuuint64_t dims[3] = {cols, (cuuint64_t)BOX_ROWS, ng};
-        const cuuint64_t strides[2] = {cols, cols * BOX_ROWS};
-        const cuuint32_t box[3] = {16, (cuuint32_t)BOX_ROWS, (cuuint32_t)g};
-        if (fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
-            *grp = g;
-            return true;
-        }
-    }
-    const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols};
-    const cuuint32_t box[2] = {16, (cuuint32_t)BOX_ROWS};
-    *grp = 0;
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
 
 bool make_gu_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64_t H, int* kb) {
     const EncodeTiledFn fn = encode_fn();
