@@ -143,14 +143,18 @@ CZ_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait on an mbarrier phase.  Returns false if it gave up, either after
-// CZ_SPIN_LIMIT polls or because *abort became non-zero.
-static __device__ __noinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+// CZ_SPIN_LIMIT polls or because *abort became non-zero.  The first poll is
+// inline (the phase is often complete already); the loop is out of line.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, const volatile int* abort) {
     for (uint32_t it = 0; it < CZ_SPIN_LIMIT; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort) return false;
         if (it > 64) __nanosleep(it > 4096 ? 512 : 32);
     }
     return false;
+}
+CZ_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+    return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, abort);
 }
 
 // One bulk (TMA, non-tensor) global -> shared copy completing on `bar`.
