@@ -1109,24 +1109,25 @@ CZ_EXPORT int colizig_cuda_ep_shutdown(void) {
 
 // ---- colizig_cuda_moe_forward_noalloc -------------------------------------
 // The device-pointer forward with its scratch in one static device array
-// instead of cudaMalloc'd buffers: [sync words][router logits][per-CTA partial
-// sums].  Static device storage is zero when the module loads, which is all the
-// sync words need (every launch zeroes the region the next launch uses, and
-// the call clears the error word); logits and partial sums are written before
-// they are read.
+// instead of cudaMalloc'd buffers: [sync words][router logits][h rows of every
+// (token, expert) pair].  Static device storage is zero when the module loads,
+// which is all the sync words need (every launch zeroes the region the next
+// launch uses, and the call clears the error word); logits and h rows are
+// written before they are read.
 namespace {
 
 constexpr int kNoAllocMaxHidden = 4096;
 constexpr int kNoAllocMaxTokens = 4;  // tokens per launch through the static scratch
 constexpr size_t kNoAllocSyncBytes = 768;
 constexpr size_t kNoAllocLogitBytes = 8448;
-constexpr size_t kNoAllocPartialBytes =
-    (size_t)cz::kMaxGrid * kNoAllocMaxTokens * kNoAllocMaxHidden * sizeof(float);
-constexpr size_t kNoAllocBytes = kNoAllocSyncBytes + kNoAllocLogitBytes + kNoAllocPartialBytes;
+constexpr int kNoAllocMaxInter = 1024;  // moe_intermediate and shared_intermediate
+constexpr size_t kNoAllocHBytes =
+    (size_t)kNoAllocMaxTokens * (cz::kMaxTopk + 1) * kNoAllocMaxInter * sizeof(float);
+constexpr size_t kNoAllocBytes = kNoAllocSyncBytes + kNoAllocLogitBytes + kNoAllocHBytes;
 static_assert(cz::kSyncWords * sizeof(uint32_t) <= kNoAllocSyncBytes, "sync words");
 static_assert((size_t)kNoAllocMaxTokens * ((cz::kMaxExperts + 1 + 3) & ~3) * sizeof(float) <= kNoAllocLogitBytes,
               "logits");
-static_assert(kNoAllocBytes == 10494976, "the size stated in colizig_cuda.h");
+static_assert(kNoAllocBytes == 287744, "the size stated in colizig_cuda.h");
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 
@@ -1159,7 +1160,8 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
     const MoeLayer& L = it->second;
     if (L.ep) return CZ_EARGS;  // its all-reduce is not part of this entry point
     if (L.d.hidden > (uint32_t)kNoAllocMaxHidden || L.d.experts > (uint32_t)cz::kMaxExperts ||
-        L.d.topk > (uint32_t)cz::kMaxTopk || g.num_sms > cz::kMaxGrid)
+        L.d.topk > (uint32_t)cz::kMaxTopk || g.num_sms > cz::kMaxGrid ||
+        L.d.inter > (uint32_t)kNoAllocMaxInter || L.d.shared_inter > (uint32_t)kNoAllocMaxInter)
         return CZ_ESHAPE;
     if (!aligned16(x) || !aligned16(out)) return CZ_EARGS;
     if (T == 0) return CZ_OK;
@@ -1176,8 +1178,6 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
                                      (int)L.d.shared_inter, bf16, g.num_sms);
     if (tmax > kNoAllocMaxTokens) tmax = kNoAllocMaxTokens;
     if (tmax < 1) return CZ_ESHAPE;
-    const size_t im = L.d.inter > L.d.shared_inter ? L.d.inter : L.d.shared_inter;
-    if ((size_t)kNoAllocMaxTokens * (L.d.topk + 1) * im * sizeof(float) > kNoAllocPartialBytes) return CZ_ESHAPE;
     for (int t0 = 0; t0 < T; t0 += tmax) {
         const int n = T - t0 < tmax ? T - t0 : tmax;
         cz::DecodeParams p = make_params(L);

@@ -164,9 +164,9 @@ int colizig_cuda_moe_check(void* stream);
  * an engine that has already handed all of HBM to its own pool or to
  * colizig_cuda_set_vram_budget, or a decode loop where a cudaMalloc/cudaFree
  * (which synchronises the device) would stall every stream.  The scratch lives
- * in one static device array of 10,494,976 bytes inside the library, so no
- * call allocates.  Limits: hidden <= 4096, experts <= 512, topk <= 16, a
- * device of at most 160 SMs (launches of up to 4 tokens; larger T runs as
+ * in one static device array of 287,744 bytes inside the library, so no
+ * call allocates.  Limits: hidden <= 4096, experts <= 512, topk <= 16,
+ * moe_intermediate and shared_intermediate <= 1024, a device of at most 160 SMs (launches of up to 4 tokens; larger T runs as
  * several launches); a layer beyond
  * them returns -8 before anything is launched.  The FIRST call on a device does set-up (it looks up the
  * scratch address and configures the kernel), so make it before any stream
