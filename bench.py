@@ -423,7 +423,7 @@ def stack_main(args, world, rank, local, torch, dist, cz, _abi, moe, synth):
             "dtype": "e4m3 x e4m3 -> f32", "data": "synthetic",
             "config": stack_config(args, d, NL, T, world),
             "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
-            "gpu_launches": args.steps * NL * (10 if prefill else -(-args.tokens * world // 4)),
+            "gpu_launches": args.steps * NL * (12 if prefill else -(-args.tokens * world // 4)),  # prefill: rms + 11
         }
         print(json.dumps(line), flush=True)
     for lay in layers:
@@ -567,9 +567,9 @@ def sharded_main(args, world, rank, local, torch, dist, cz, _abi, moe, synth):
             "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32", "data": "synthetic",
             "config": cfg, "roofline": roof, "tflops": step_tf * world,
             "e2e": e2e, "cpu_baseline": None, "clocks": clocks,
-            # route (logits, top-k), plan (mask, slots), pack, unpack, xexp, count, scan, place,
+            # route (logits, top-k), plan (mask, slots), pack, unpack, xexp, xterms, count, scan, place,
             # tokpos, dispatch, 2 GEMMs, combine, ep_combine (NCCL's own kernels not counted)
-            "gpu_launches": args.steps * 16,
+            "gpu_launches": args.steps * 17,
         }
         print(json.dumps(line), flush=True)
     for lay in layers:
@@ -793,7 +793,7 @@ def main():
                "sample": f"{nsteps} layer forwards of {args.config} T={Tc} in {dt:.1f} s over {len(host_layers)} "
                          f"layers (C restatement of the reference AVX2 path, {cores} threads)"}
 
-    launches_per_step = 10 if prefill else -(-T // 4)  # prefill: logits, topk, count, scan, place, tokpos, dispatch, 2 GEMMs, combine
+    launches_per_step = 11 if prefill else -(-T // 4)  # prefill: logits, topk, xterms, count, scan, place, tokpos, dispatch, 2 GEMMs, combine
     if prefill:
         # tensor-bound.  Dominant kernel: the gate/up grouped GEMM.  Its algorithmic FLOPs
         # (2 x pairs x H x 2I routed + 2 x T x H x 2SI shared, pairs on this rank's

@@ -627,32 +627,54 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 for (int q = 0; q < s.g_npairs[u]; ++q)
                     s.rtok[s.g_pair0[u] + q] = here ? pair_token(s.order[s.g_pair0[u] + q], T, K) : -1;
             }
-            if (lane == 0) {
-                // phase D packs: this CTA's output rows of every group held here, groups in
-                // order, as many per ring stage as fit
-                const int o_lo = (int)((long long)c * H / G), o_hi = (int)((long long)(c + 1) * H / G);
-                const int drows = o_hi - o_lo;
-                const int nrb = drows > 0 ? ((o_hi - 1) >> 7) - (o_lo >> 7) + 1 : 0;
-                int nc = 0, npk = 0, fill = SLOT_BYTES;
-                for (int u = 0; u < base; ++u) {
-                    // groups of experts held elsewhere (expert parallelism) get no chunks
-                    const int eu = s.g_expert[u];
-                    const bool here = eu == E ? p.shared_here != 0 : (eu >= p.e_lo && eu < p.e_hi);
-                    const int iu = eu == E ? SI : Ir;
-                    s.g_chunk0[u] = nc;
+            // first chunk of every group (a warp scan) and phase D's packs: this CTA's output
+            // rows of every group held here, groups in order, as many per ring stage as fit.
+            // Routed groups all take rb bytes, so the greedy packing puts `per` of them in a
+            // pack; the shared expert (the last group) joins the last pack if it fits.
+            const int o_lo = (int)((long long)c * H / G), o_hi = (int)((long long)(c + 1) * H / G);
+            const int drows = o_hi - o_lo;
+            const int nrb = drows > 0 ? ((o_hi - 1) >> 7) - (o_lo >> 7) + 1 : 0;
+            const int rbytes = drows * Ir + nrb * cz_nbp(Ir) * 4;
+            const int per = drows > 0 ? SLOT_BYTES / rbytes : 1;
+            int nc = 0, nr = 0;  // chunks and held routed groups before this batch of 32 groups
+            for (int u0 = 0; u0 < base; u0 += 32) {
+                const int u = u0 + lane;
+                const int eu = u < base ? s.g_expert[u] : -1;
+                const bool here = u < base && (eu == E ? p.shared_here != 0 : (eu >= p.e_lo && eu < p.e_hi));
+                const bool routed = here && eu != E;
+                const int n = here ? (eu == E ? SI : Ir) / CR : 0;
+                int x = n;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, x, o);
+                    if (lane >= o) x += y;
+                }
+                const uint32_t rm = __ballot_sync(0xffffffffu, routed);
+                const int k = nr + __popc(rm & ((1u << lane) - 1u));  // index among held routed groups
+                if (u < base) {
+                    s.g_chunk0[u] = nc + x - n;
                     s.g_pack[u] = -1;
-                    if (here) {
-                        nc += iu / CR;
-                        if (drows > 0) {
-                            const int bytes = drows * iu + nrb * cz_nbp(iu) * 4;
-                            if (fill + bytes > SLOT_BYTES) {
-                                ++npk;
-                                fill = 0;
-                            }
-                            s.g_pack[u] = npk - 1;
-                            s.g_poff[u] = fill;
-                            fill += bytes;
-                        }
+                    if (routed && drows > 0) {
+                        s.g_pack[u] = k / per;
+                        s.g_poff[u] = (k % per) * rbytes;
+                    }
+                }
+                nc += __shfl_sync(0xffffffffu, x, 31);
+                nr += __popc(rm);
+            }
+            __syncwarp();
+            if (lane == 0) {
+                int npk = nr > 0 && drows > 0 ? (nr - 1) / per + 1 : 0;
+                if (base > 0 && s.g_expert[base - 1] == E && p.shared_here && drows > 0) {
+                    const int sbytes = drows * SI + nrb * cz_nbp(SI) * 4;
+                    const int fill = nr > 0 ? (nr - (npk - 1) * per) * rbytes : SLOT_BYTES;
+                    if (npk > 0 && fill + sbytes <= SLOT_BYTES) {
+                        s.g_pack[base - 1] = npk - 1;
+                        s.g_poff[base - 1] = fill;
+                    } else {
+                        s.g_pack[base - 1] = npk;
+                        s.g_poff[base - 1] = 0;
+                        ++npk;
                     }
                 }
                 s.g_chunk0[base] = nc;

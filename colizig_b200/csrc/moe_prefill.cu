@@ -71,7 +71,8 @@ struct Scratch {
     int* pos_of_pair;  // [P]
     int* pair_at_pos;  // [PP] (-1 = padding)
     int* tokpos;       // [T][K+1]
-    uint8_t* X;        // [3][PP][H] token terms
+    uint8_t* Xt;       // [3][T][H] token terms, per token
+    uint8_t* X;        // [3][PP][H] token terms, per position (grouped)
     uint8_t* Hp;       // [3][PP][IM] h terms
     int* hx;           // [PP][nb(IM)]
     float* y;          // [PP][H]
@@ -98,6 +99,7 @@ Scratch carve_scratch(uint8_t* base, int T, int H, int E, int K, int I, int SI) 
     s.gates = (float*)take((size_t)T * K * 4);
     s.xexp = (int*)take((size_t)T * 4);
     s.sg = (float*)take((size_t)T * 4);
+    s.Xt = (uint8_t*)take((size_t)3 * T * H);
     s.logits = (float*)take((size_t)T * logit_stride(E) * 4);
     s.cnt = (int*)take((size_t)s.Eg * 4);
     s.ccnt = (int*)take((size_t)((s.P + GCH - 1) / GCH) * s.Eg * 4);
@@ -352,6 +354,54 @@ __global__ void __launch_bounds__(256, 2) pf_logits_kernel(const RouteParams q) 
     }
 }
 
+// The token term planes: xt[j][t][H] with x_t * 2^xexp[t] = t0 + t1 (+ t2), E4M3, two
+// columns per conversion; one thread = 16 consecutive columns of one token.
+__global__ void __launch_bounds__(256) pf_xterms_kernel(const void* x, int x_bf16, int T, int H, const int* xexp, int JX,
+                                                        uint8_t* xt) {
+    const int per_row = H / 16;
+    const long long gi = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int t = (int)(gi / per_row), c16 = (int)(gi - (long long)t * per_row);
+    if (t >= T) return;
+    const float sc = pow2(xexp[t]);
+    float v[16];
+    const size_t base = (size_t)t * H + (size_t)c16 * 16;
+    if (x_bf16) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + base);
+        const uint4 raw2 = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + base + 8);
+        const uint32_t w[8] = {raw.x, raw.y, raw.z, raw.w, raw2.x, raw2.y, raw2.z, raw2.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            v[2 * k] = __uint_as_float(w[k] << 16);
+            v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+        }
+    } else {
+        const float4* xf = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + base);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float4 f = xf[k];
+            v[4 * k] = f.x;
+            v[4 * k + 1] = f.y;
+            v[4 * k + 2] = f.z;
+            v[4 * k + 3] = f.w;
+        }
+    }
+    uint32_t words[3][4] = {};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        float a = v[2 * k] * sc, b = v[2 * k + 1] * sc;
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            const uint16_t d = j < JX ? e4m3_term2(a, b) : (uint16_t)0;
+            words[j][k >> 1] |= (uint32_t)d << (16 * (k & 1));
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+        if (j < JX)
+            *reinterpret_cast<uint4*>(xt + ((size_t)j * T + t) * H + (size_t)c16 * 16) =
+                make_uint4(words[j][0], words[j][1], words[j][2], words[j][3]);
+}
+
 // top-k and the per-token term prescale: one warp per token
 __global__ void __launch_bounds__(256) pf_topk_kernel(const RouteParams q) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -564,7 +614,8 @@ struct DispatchParams {
     Scratch s;
 };
 
-// one thread = 16 consecutive elements of one position row, every term plane
+// one thread = 16 consecutive elements of one position row, every term plane:
+// the row's token's planes (padding positions get zeros)
 __global__ void pf_dispatch_kernel(const DispatchParams q) {
     const int per_row = q.H / 16;
     const long long gi = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -576,46 +627,9 @@ __global__ void pf_dispatch_kernel(const DispatchParams q) {
     uint4 out[3] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
     if (p >= 0) {
         const int t = pair_token(p, q.T, q.K);
-        const float sc = pow2(q.s.xexp[t]);
-        float v[16];
-        const size_t base = (size_t)t * q.H + (size_t)c16 * 16;
-        if (q.x_bf16) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(q.x) + base);
-            const uint4 raw2 = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(q.x) + base + 8);
-            const uint32_t w[8] = {raw.x, raw.y, raw.z, raw.w, raw2.x, raw2.y, raw2.z, raw2.w};
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                v[2 * k] = __uint_as_float(w[k] << 16);
-                v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
-            }
-        } else {
-            const float4* xf = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(q.x) + base);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float4 f = xf[k];
-                v[4 * k] = f.x;
-                v[4 * k + 1] = f.y;
-                v[4 * k + 2] = f.z;
-                v[4 * k + 3] = f.w;
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] *= sc;
-        uint32_t words[3][4];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            float a = v[2 * k], b = v[2 * k + 1];
-#pragma unroll
-            for (int j = 0; j < 3; ++j) {
-                const uint16_t d = j < q.JX ? e4m3_term2(a, b) : (uint16_t)0;
-                if (k & 1)
-                    words[j][k >> 1] |= (uint32_t)d << 16;
-                else
-                    words[j][k >> 1] = d;
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < 3; ++j) out[j] = make_uint4(words[j][0], words[j][1], words[j][2], words[j][3]);
+        for (int j = 0; j < 3; ++j)
+            if (j < q.JX) out[j] = *reinterpret_cast<const uint4*>(q.s.Xt + ((size_t)j * q.T + t) * q.H + (size_t)c16 * 16);
     }
 #pragma unroll
     for (int j = 0; j < 3; ++j)
@@ -1240,6 +1254,7 @@ int prefill_run(const PrefillLayer& L, const void* x, int x_bf16, int T, const f
     Scratch s = carve_scratch(base, T, H, E, K, I, SI);
     if (s.bytes + 1024 > scratch_bytes) return CZ_EALLOC;
     if (rms_w && x_bf16) return CZ_EARGS;
+    const int JX = x_bf16 ? 2 : 3;
     if (pre_idx) {
         if (rms_w) return CZ_EARGS;
         if (cudaMemcpyAsync(s.idx, pre_idx, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
@@ -1251,7 +1266,6 @@ int prefill_run(const PrefillLayer& L, const void* x, int x_bf16, int T, const f
         pf_rms_kernel<<<T, 256, 0, st>>>(reinterpret_cast<const float*>(x), rms_w, eps, T, H, s.xn);
         x = s.xn;
     }
-    const int JX = x_bf16 ? 2 : 3;
     // route
     if (!pre_idx) {
         RouteParams q{};
@@ -1283,6 +1297,11 @@ int prefill_run(const PrefillLayer& L, const void* x, int x_bf16, int T, const f
         }
         pf_logits_kernel<<<dim3((T + LG_T - 1) / LG_T, (Er + LG_R - 1) / LG_R), 256, smem, st>>>(q);
         pf_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(q);
+    }
+    // the token term planes (once per token; the dispatch below copies them per position)
+    {
+        const long long n = (long long)T * (H / 16);
+        pf_xterms_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, x_bf16, T, H, s.xexp, JX, s.Xt);
     }
     // grouping
     GroupParams gq{};
