@@ -496,18 +496,23 @@ __global__ void pf_scan_kernel(const GroupParams q) {
     // per group (one warp each): exclusive prefix of its counts over the chunks, in chunk order
     for (int gg = warp; gg < Eg; gg += 32) {
         int run = 0;
-        for (int b0 = 0; b0 < nch; b0 += 32) {
-            const int b = b0 + lane;
-            int* c = q.s.ccnt + (size_t)gg * nch + b;  // coalesced over the chunks
-            const int v = b < nch ? *c : 0;
-            int x = v;
+        int* const cg = q.s.ccnt + (size_t)gg * nch;  // coalesced over the chunks
+        for (int b0 = 0; b0 < nch; b0 += 128) {
+            int v[4];  // four loads in flight, then the scans in chunk order
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, x, o);
-                if (lane >= o) x += y;
+            for (int k = 0; k < 4; ++k) v[k] = b0 + 32 * k + lane < nch ? cg[b0 + 32 * k + lane] : 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int b = b0 + 32 * k + lane;
+                int x = v[k];
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, x, o);
+                    if (lane >= o) x += y;
+                }
+                if (b < nch) cg[b] = run + x - v[k];
+                run += __shfl_sync(0xffffffffu, x, 31);
             }
-            if (b < nch) *c = run + x - v;
-            run += __shfl_sync(0xffffffffu, x, 31);
         }
         if (lane == 0) gtot[gg] = run;
     }
