@@ -532,6 +532,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         }
     }
     __syncthreads();
+    // this CTA's logits are written: arrive at the router counter now, so that the
+    // token term split below runs while the other CTAs finish theirs
+    if (tid == 0) {
+        __threadfence();
+        red_release_add_gpu(&reg[0], 1u);
+    }
     if (tid < T) {
         const int e = prescale_exp(__uint_as_float(s.xmax[tid]));
         s.xexp[tid] = e;
@@ -555,8 +561,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     }
     __syncthreads();
     if (tid == 0) {
-        __threadfence();
-        red_release_add_gpu(&reg[0], 1u);
         if (!wait_geq_bounded(&reg[0], (uint32_t)G, err)) set_error(err, s, CZ_DERR_ROUTER_BARRIER);
         if (!s.abort) {
             // all logits -> shared memory (ring offset 0; the weight stream starts later)
