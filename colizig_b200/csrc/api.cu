@@ -113,7 +113,7 @@ struct Ctx {
     uint64_t hits = 0, misses = 0, uploaded = 0;
     // MoE
     std::map<uint32_t, MoeLayer> layers;
-    DevBuf logits, partial, io_x, io_out, io_idx, io_gates, ones, pf_scratch;
+    DevBuf logits, hrows, io_x, io_out, io_idx, io_gates, ones, pf_scratch;
     uint32_t* sync = nullptr;
     // expert parallelism (one process per GPU)
     bool ep_on = false;
@@ -220,7 +220,7 @@ void shutdown_locked() {
     g.lru.clear();
     for (auto& kv : g.layers) free_layer(kv.second);
     g.layers.clear();
-    for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.partial, &g.pf_scratch, &g.io_x, &g.io_out, &g.io_idx,
+    for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.hrows, &g.pf_scratch, &g.io_x, &g.io_out, &g.io_idx,
                       &g.io_gates, &g.ones, &g.sh_idx, &g.sh_gates, &g.sh_xn, &g.sh_slot, &g.sh_counts, &g.sh_allc,
                       &g.sh_tmp, &g.sh_send, &g.sh_recv, &g.sh_x, &g.sh_ridx, &g.sh_rgates, &g.sh_part, &g.sh_back})
         b->release();
@@ -292,7 +292,7 @@ int ensure_decode_scratch(const colizig_moe_dims& d) {
     const size_t T = cz::kDecodeMaxTokens;
     if (!g.logits.ensure(T * cz::logit_stride((int)d.experts) * sizeof(float))) return CZ_EALLOC;
     const size_t im = d.inter > d.shared_inter ? d.inter : d.shared_inter;
-    if (!g.partial.ensure(T * (d.topk + 1) * im * sizeof(float))) return CZ_EALLOC;
+    if (!g.hrows.ensure(T * (d.topk + 1) * im * sizeof(float))) return CZ_EALLOC;
     return ensure_sync();
 }
 
@@ -328,7 +328,7 @@ cz::DecodeParams make_params(const MoeLayer& L) {
     p.gu3d = L.gu_kb > 0;
     p.gu_kb = L.gu_kb;
     p.logits = g.logits.as<float>();
-    p.partial = g.partial.as<float>();
+    p.hrows = g.hrows.as<float>();
     p.sync = g.sync;
     return p;
 }
@@ -1170,7 +1170,7 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
     if (!base) return CZ_ELAUNCH;
     uint32_t* sync = reinterpret_cast<uint32_t*>(base);
     float* logits = reinterpret_cast<float*>(base + kNoAllocSyncBytes);
-    float* partial = reinterpret_cast<float*>(base + kNoAllocSyncBytes + kNoAllocLogitBytes);
+    float* hrows = reinterpret_cast<float*>(base + kNoAllocSyncBytes + kNoAllocLogitBytes);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int bf16 = x_dtype == COLIZIG_X_BF16;
     const size_t xelt = bf16 ? 2 : 4;
@@ -1182,7 +1182,7 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
         const int n = T - t0 < tmax ? T - t0 : tmax;
         cz::DecodeParams p = make_params(L);
         p.logits = logits;
-        p.partial = partial;
+        p.hrows = hrows;
         p.sync = sync;
         p.x = reinterpret_cast<const uint8_t*>(x) + (size_t)t0 * L.d.hidden * xelt;
         p.x_bf16 = bf16;

@@ -59,7 +59,7 @@ struct alignas(64) DecodeParams {
     int e_lo, e_hi;          // routed experts held (and computed) here: [e_lo, e_hi); stacked from e_lo
     int shared_here;         // the shared expert is computed here
     float* logits;           // scratch [T, logit_stride(E)]
-    float* partial;          // scratch [T*(K+1)][max(I, SI)] f32: the h row of every (token, expert) pair
+    float* hrows;          // scratch [T*(K+1)][max(I, SI)] f32: the h row of every (token, expert) pair
     uint32_t* sync;          // kSyncWords words, zeroed once at allocation
 };
 

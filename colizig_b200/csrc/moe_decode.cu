@@ -844,7 +844,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                                     us += uv[w][j];
                                 }
                         const float xsc = s.xscale[tk];
-                        p.partial[(size_t)pairs[q] * ldh + r0 + r] =
+                        p.hrows[(size_t)pairs[q] * ldh + r0 + r] =
                             s.pg[pairs[q]] * (silu_fast(gs * xsc) * (us * xsc));
                     }
                 }
@@ -1026,7 +1026,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 // terms (22 bits) in this warp's share of the idle reduction buffer: words [0, iu/2)
                 // hi, [iu/2, iu) lo
                 const int pr = s.order[s.g_pair0[u] + q];
-                const float2* hrow = reinterpret_cast<const float2*>(p.partial + (size_t)pr * ldh);
+                const float2* hrow = reinterpret_cast<const float2*>(p.hrows + (size_t)pr * ldh);
                 uint32_t* hb = reinterpret_cast<uint32_t*>(red) + warp * DHW;
                 const int nw2 = iu >> 1;
                 float2 hv[DHW / 64];
