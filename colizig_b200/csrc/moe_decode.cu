@@ -982,12 +982,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     }
 
     // ---------------- every h row of every CTA is written ----------------
-    // H_WRITTEN orders the h warp's global writes before thread 0's fence and release;
-    // the other CTAs acquire them through the counter.  The producer keeps issuing the
-    // phase D packs meanwhile (it joins the block again at the end).
+    // H_WRITTEN orders the h warp's global writes before thread 0's release add (a
+    // release is cumulative over what the barrier ordered before it); the other CTAs
+    // acquire them through the counter.  No separate fence: one here waits for this SM's
+    // outstanding writes and measured 1.1 us on the critical path.  The producer keeps
+    // issuing the phase D packs meanwhile (it joins the block again at the end).
     if (warp < NCW || warp == HW) bar_sync_n(BAR_H_WRITTEN);
     if (tid == 0) {
-        __threadfence();
         red_release_add_gpu(&reg[2], 1u);
         if (!wait_geq_bounded(&reg[2], (uint32_t)G, err)) set_error(err, s, CZ_DERR_READY_WAIT);
     }
