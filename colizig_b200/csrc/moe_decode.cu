@@ -404,6 +404,12 @@ __device__ __noinline__ void route_token(const float* __restrict__ lg, int E, in
     __syncwarp();
 }
 
+// Start of part c of n items split over G parts: floor(c * n / G).  32-bit: c <= G <= 160 and
+// n <= 5120 for every caller (hidden, router rows, chunks; decode_max_tokens bounds them).
+__device__ __forceinline__ int split_at(int c, int n, int G) {
+    return (int)(((uint32_t)c * (uint32_t)n) / (uint32_t)G);
+}
+
 __device__ __forceinline__ int pair_token(int pr, int T, int K) { return pr < T * K ? pr / K : pr - T * K; }
 
 // Bounded wait of all lanes on an mbarrier phase; warp-uniform result.
@@ -463,7 +469,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     __syncthreads();
 
     // ---------------- phase R: router logits ----------------
-    const int row_lo = (int)((long long)c * Er / G), row_hi = (int)((long long)(c + 1) * Er / G);
+    const int row_lo = split_at(c, Er, G), row_hi = split_at(c + 1, Er, G);
     const int nrows = row_hi - row_lo;
     const uint32_t xbytes = (uint32_t)T * H * (xbf ? 2u : 4u);
     const uint32_t rbytes = (uint32_t)nrows * H * 4u;
@@ -635,7 +641,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
             // rows of every group held here, groups in order, as many per ring stage as fit.
             // Routed groups all take rb bytes, so the greedy packing puts `per` of them in a
             // pack; the shared expert (the last group) joins the last pack if it fits.
-            const int o_lo = (int)((long long)c * H / G), o_hi = (int)((long long)(c + 1) * H / G);
+            const int o_lo = split_at(c, H, G), o_hi = split_at(c + 1, H, G);
             const int drows = o_hi - o_lo;
             const int nrb = drows > 0 ? ((o_hi - 1) >> 7) - (o_lo >> 7) + 1 : 0;
             const int rbytes = drows * Ir + nrb * cz_nbp(Ir) * 4;
@@ -696,14 +702,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     __syncthreads();
 
     // ---------------- phase C: this CTA's chunks; phase D: this CTA's output rows ----------------
-    const int o_lo = (int)((long long)c * H / G), o_hi = (int)((long long)(c + 1) * H / G);
+    const int o_lo = split_at(c, H, G), o_hi = split_at(c + 1, H, G);
     const int drows = o_hi - o_lo;
     const int ldh = Ir > SI ? Ir : SI;  // row stride of the h rows in global scratch
     float* const dsum = reinterpret_cast<float*>(sb + cv.dsum);  // phase D: [sorted pair][row] sums
     {
         const int NC = s.NC;
         const int NS = cv.ns;
-        const int ch_lo = (int)((long long)c * NC / G), ch_hi = (int)((long long)(c + 1) * NC / G);
+        const int ch_lo = split_at(c, NC, G), ch_hi = split_at(c + 1, NC, G);
         const int nks = (H + KS - 1) / KS;     // gate (and up) stages per chunk
         const int nbpH = cz_nbp(H);
         const int nkbH = cz_nblk(H);           // 128-column blocks of H
@@ -1001,7 +1007,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     if (warp < NCW && drows > 0) {
         const int NS = cv.ns;
         const int nch = s.NC;
-        const int si0 = 2 * ((H + KS - 1) / KS) * ((int)((long long)(c + 1) * nch / G) - (int)((long long)c * nch / G));
+        const int si0 = 2 * ((H + KS - 1) / KS) * (split_at(c + 1, nch, G) - split_at(c, nch, G));
         const int rb0 = o_lo >> 7;
         int pk_done = 0;   // packs waited for and released by this warp
         bool ok = !s.abort;
