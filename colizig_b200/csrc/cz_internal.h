@@ -32,6 +32,7 @@ struct alignas(64) DecodeParams {
     CUtensorMap sh_gate_map;  // shared expert [SI rows][H] (SI > 0)
     CUtensorMap sh_up_map;
     int gu3d, gu_kb;          // gate/up boxes span gu_kb 128-column blocks (3D map) or one (2D map)
+    int hslot;                // phase D's h terms in a free ring slot (set by decode_launch)
     const void* x;           // [T, H] f32 or bf16 (stack mode: h, f32)
     int x_bf16;
     int T;
@@ -68,7 +69,8 @@ struct alignas(64) DecodeParams {
 // (*kb = depth, else 0 = 2D).
 bool make_gu_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64_t H, int* kb);
 
-size_t decode_smem_bytes(int T, int H, int x_bf16);
+size_t decode_smem_bytes(int T, int H, int x_bf16, int hslot);
+int decode_hslot(int T, int H, int K, int I, int SI, int x_bf16, int num_sms);
 // Largest token count one decode launch takes for these dims (tokens and the
 // gate/up outputs must fit the kernel's shared staging area); 0 = unsupported.
 int decode_max_tokens(int H, int E, int K, int I, int SI, int x_bf16, int num_sms);

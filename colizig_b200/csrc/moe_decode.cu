@@ -72,8 +72,8 @@ constexpr int NTHREADS = NWARPS * 32;
 constexpr int CR = 16;                    // intermediate (h) rows per chunk
 constexpr int KS = 2048;                  // columns of a gate/up stage slab
 constexpr int GU_BYTES = CR * KS;         // a gate/up stage: [K block][16 rows][128 B], 128-byte swizzled
-constexpr int SC_BYTES = 2048;            // block scales carried with every stage
-constexpr int SLOT_BYTES = 34 * 1024;     // >= GU_BYTES + SC_BYTES; also one pack of down rows
+constexpr int SC_BYTES = 1024;            // block scales carried with every stage (hidden <= 32768)
+constexpr int SLOT_BYTES = 33 * 1024;     // >= GU_BYTES + SC_BYTES; also one pack of down rows
 constexpr int NSLOT = 4;                  // ring slots at least (more when shared memory allows)
 constexpr int MAXSLOT = 6;
 constexpr int RING_BYTES = NSLOT * SLOT_BYTES;  // the smallest ring (also stages phase R)
@@ -113,29 +113,39 @@ struct __align__(16) DecodeMisc {
     int rtok[MAXP];       // token of sorted pair r when its group is held here, else -1
 };
 
-// Shared-memory map of one launch: [ring][x terms][red][misc].
+// Shared-memory map of one launch: [ring][x terms][red][dsum][misc].
+// red holds the consumer warps' partial gate/up sums of two chunks in flight,
+// [chunk parity][warp][gate/up][16 rows][rc columns]; phase D then keeps each
+// warp's f16 h terms (DHW words a warp) in red, or, with hslot, in the ring slot
+// after the last pack (free: its last stage was a consumed gate/up slab), which
+// lets red shrink to 8 columns and one more ring slot fit.  The host picks hslot
+// when every group fits 8 MMA columns and every CTA's packs leave a slot free.
 struct Carve {
     int JX, CS;  // E4M3 terms per token; byte stride of one term column
     int ns;      // ring slots
+    int rc;      // columns of a warp's partial sums in red (16, or 8 with hslot)
     uint32_t xterm, red, dsum, misc, total;
 };
 
-__host__ __device__ inline Carve carve(int T, int H, int x_bf16) {
+__host__ __device__ inline Carve carve(int T, int H, int x_bf16, int hslot) {
     Carve c;
     c.JX = x_bf16 ? 2 : 3;
     c.CS = ((H + 127) & ~127) + 64;  // column stride = 64 mod 128: lanes of 2 columns hit disjoint banks
+    c.rc = hslot ? 8 : 16;
+    const uint32_t red_bytes = 2u * NCW * 2 * 16 * (uint32_t)c.rc * 4;  // 16 KB, or 32 KB = NCW * DHW words
+    const uint32_t dsum_bytes = (uint32_t)T * (MAXK + 1) * DMR * 4;     // [sorted pair][output row]
     // the rest of the map decides how many slots fit
-    const uint32_t rest = (((uint32_t)(T * c.JX * c.CS) + 127u) & ~127u) + 2 * NCW * 2 * 16 * 16 * 4 +
-                          MAXP * DMR * 4 + (((uint32_t)sizeof(DecodeMisc) + 127u) & ~127u);
+    const uint32_t rest = (((uint32_t)(T * c.JX * c.CS) + 127u) & ~127u) + red_bytes + dsum_bytes +
+                          (((uint32_t)sizeof(DecodeMisc) + 127u) & ~127u);
     const int fit = ((int)SMEM_LIMIT - 1024 - (int)rest) / SLOT_BYTES;
     c.ns = fit < NSLOT ? NSLOT : (fit > MAXSLOT ? MAXSLOT : fit);
     uint32_t off = (uint32_t)c.ns * SLOT_BYTES;
     c.xterm = off;
     off += ((uint32_t)(T * c.JX * c.CS) + 127u) & ~127u;
     c.red = off;
-    off += 2 * NCW * 2 * 16 * 16 * 4;  // two chunks in flight: [chunk parity][warp][gate/up][16 x 16]; then phase D h terms
+    off += red_bytes;
     c.dsum = off;
-    off += MAXP * DMR * 4;             // phase D: [sorted pair][output row] sums
+    off += dsum_bytes;
     c.misc = off;
     off += ((uint32_t)sizeof(DecodeMisc) + 127u) & ~127u;
     c.total = off;
@@ -445,7 +455,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     const int Er = E + (SI ? 1 : 0);
     const int LS = logit_stride(E);
     const bool xbf = p.x_bf16 != 0;
-    const Carve cv = carve(T, H, p.x_bf16);
+    const Carve cv = carve(T, H, p.x_bf16, p.hslot);
     DecodeMisc& s = *reinterpret_cast<DecodeMisc*>(sb + cv.misc);
     uint8_t* const ring = sb;
     uint8_t* const xterm = sb + cv.xterm;
@@ -687,6 +697,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                         ++npk;
                     }
                 }
+                // hslot: the slot after the last pack must be free (the host checked the worst case)
+                if (p.hslot && npk > cv.ns - 1) set_error(err, s, CZ_DERR_SHAPE);
                 s.g_chunk0[base] = nc;
                 s.U = base;
                 s.P = P;
@@ -823,7 +835,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 const int* pairs = s.order + s.g_pair0[u];
                 const int r0 = (ch - s.g_chunk0[u]) * CR;
                 bar_sync_n(BAR_RED_FULL + b);
-                const float* rb = red + b * (NCW * 2 * 256);
+                const int wst = 2 * 16 * cv.rc;  // floats of one warp's gate + up partial sums
+                const float* rb = red + b * (NCW * wst);
 #pragma unroll 1
                 for (int half = 0; half < (T + 1) / 2; ++half) {
                     const int tk = 2 * half + (lane >> 4), r = lane & 15;
@@ -832,14 +845,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                         if (pair_token(pairs[qq], T, K) == tk) q = qq;
                     if (q >= 0 && !s.abort) {
                         float gs = 0.0f, us = 0.0f;
-                        const float* rg = rb + r * 16 + q * cv.JX;
+                        const float* rg = rb + r * cv.rc + q * cv.JX;
                         float gv[NCW][3], uv[NCW][3];
 #pragma unroll
                         for (int w = 0; w < NCW; ++w)
 #pragma unroll
                             for (int j = 0; j < 3; ++j) {
-                                gv[w][j] = j < cv.JX ? rg[w * 512 + j] : 0.0f;
-                                uv[w][j] = j < cv.JX ? rg[w * 512 + 256 + j] : 0.0f;
+                                gv[w][j] = j < cv.JX ? rg[w * wst + j] : 0.0f;
+                                uv[w][j] = j < cv.JX ? rg[w * wst + 16 * cv.rc + j] : 0.0f;
                             }
 #pragma unroll
                         for (int w = 0; w < NCW; ++w)
@@ -966,19 +979,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
 
                 // ---- this warp's partial gate/up sums of the chunk -> red[b] (h warp) ----
                 {
-                    float* rg = red + (b * NCW * 2 + warp * 2 + 0) * 256;
-                    float* ru = rg + 256;
+                    const int rc = cv.rc;
+                    float* rg = red + (b * NCW * 2 + warp * 2 + 0) * (16 * rc);
+                    float* ru = rg + 16 * rc;
 #pragma unroll
                     for (int m = 0; m < 2; ++m) {
+                        if (8 * m >= rc) break;  // rc = 8: every group's columns fit MMA tile 0
                         const int col = 8 * m + 2 * t;
-                        rg[rho * 16 + col] = accg[m][0];
-                        rg[rho * 16 + col + 1] = accg[m][1];
-                        rg[(rho + 8) * 16 + col] = accg[m][2];
-                        rg[(rho + 8) * 16 + col + 1] = accg[m][3];
-                        ru[rho * 16 + col] = accu[m][0];
-                        ru[rho * 16 + col + 1] = accu[m][1];
-                        ru[(rho + 8) * 16 + col] = accu[m][2];
-                        ru[(rho + 8) * 16 + col + 1] = accu[m][3];
+                        rg[rho * rc + col] = accg[m][0];
+                        rg[rho * rc + col + 1] = accg[m][1];
+                        rg[(rho + 8) * rc + col] = accg[m][2];
+                        rg[(rho + 8) * rc + col + 1] = accg[m][3];
+                        ru[rho * rc + col] = accu[m][0];
+                        ru[rho * rc + col + 1] = accu[m][1];
+                        ru[(rho + 8) * rc + col] = accu[m][2];
+                        ru[(rho + 8) * rc + col + 1] = accu[m][3];
                     }
                 }
                 __threadfence_block();
@@ -1009,6 +1024,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         const int nch = s.NC;
         const int si0 = 2 * ((H + KS - 1) / KS) * (split_at(c + 1, nch, G) - split_at(c, nch, G));
         const int rb0 = o_lo >> 7;
+        // this warp's DHW words of f16 h terms: in red, or (hslot) in the ring slot after
+        // the last pack, whose last stage was a gate/up slab consumed in phase C
+        uint32_t* const hb = (p.hslot ? reinterpret_cast<uint32_t*>(ring + (size_t)((si0 + s.npk) % NS) * SLOT_BYTES)
+                                      : reinterpret_cast<uint32_t*>(red)) +
+                             warp * DHW;
         int pk_done = 0;   // packs waited for and released by this warp
         bool ok = !s.abort;
         auto release_to = [&](int j_end) {  // wait for and release packs [pk_done, j_end)
@@ -1034,7 +1054,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 // hi, [iu/2, iu) lo
                 const int pr = s.order[s.g_pair0[u] + q];
                 const float2* hrow = reinterpret_cast<const float2*>(p.hrows + (size_t)pr * ldh);
-                uint32_t* hb = reinterpret_cast<uint32_t*>(red) + warp * DHW;
                 const int nw2 = iu >> 1;
                 float2 hv[DHW / 64];
 #pragma unroll
@@ -1146,7 +1165,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
 
 static bool g_attr_set = false;
 
-size_t decode_smem_bytes(int T, int H, int x_bf16) { return carve(T, H, x_bf16).total + 1024; }
+size_t decode_smem_bytes(int T, int H, int x_bf16, int hslot) { return carve(T, H, x_bf16, hslot).total + 1024; }
+
+// Whether a launch can keep phase D's h terms in a ring slot (carve): every group's
+// term columns (at most T tokens x JX) fit one 8-column MMA tile, and on every CTA
+// the packs of down rows (routed groups <= T*K, at least `per` a pack with the most
+// output rows and two row blocks of scales, + one for the shared expert) leave one
+// of the ring's slots unused.
+int decode_hslot(int T, int H, int K, int I, int SI, int x_bf16, int num_sms) {
+    if (T * (x_bf16 ? 2 : 3) > 8) return 0;
+    const int ns = carve(T, H, x_bf16, 1).ns;
+    const int drows = (H + num_sms - 1) / num_sms;
+    const int rbytes = drows * I + 2 * cz_nbp(I) * 4;
+    const int per = SLOT_BYTES / rbytes;
+    if (per < 1) return 0;
+    const int npk = (T * K + per - 1) / per + (SI ? 1 : 0);
+    return npk <= ns - 1 ? 1 : 0;
+}
 
 int decode_max_tokens(int H, int E, int K, int I, int SI, int x_bf16, int num_sms) {
     if (K < 1 || K > MAXK || E < K || E > MAXE || H % 16 || I % 16 || SI % 16 || H < 16 || I < 16) return 0;
@@ -1168,7 +1203,7 @@ int decode_max_tokens(int H, int E, int K, int I, int SI, int x_bf16, int num_sm
         }
         const size_t stage_r = (size_t)max_rows * H * 4 + (size_t)t * H * (x_bf16 ? 2 : 4) + (size_t)H * 4;
         const size_t lg = (size_t)t * logit_stride(E) * 4;
-        if (stage_r <= (size_t)RING_BYTES && lg <= (size_t)RING_BYTES && decode_smem_bytes(t, H, x_bf16) <= SMEM_LIMIT)
+        if (stage_r <= (size_t)RING_BYTES && lg <= (size_t)RING_BYTES && decode_smem_bytes(t, H, x_bf16, 0) <= SMEM_LIMIT)
             break;
         --t;
     }
@@ -1239,14 +1274,16 @@ int decode_launch(const DecodeParams& prm, int num_sms, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);
     cfg.blockDim = dim3(NTHREADS);
-    cfg.dynamicSmemBytes = decode_smem_bytes(prm.T, prm.H, prm.x_bf16);
+    DecodeParams p = prm;
+    p.hslot = decode_hslot(p.T, p.H, p.K, p.I, p.SI, p.x_bf16, num_sms);
+    cfg.dynamicSmemBytes = decode_smem_bytes(p.T, p.H, p.x_bf16, p.hslot);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, kern[prm.T - 1], prm) != cudaSuccess) return CZ_ELAUNCH;
+    if (cudaLaunchKernelEx(&cfg, kern[p.T - 1], p) != cudaSuccess) return CZ_ELAUNCH;
     return CZ_OK;
 }
 
