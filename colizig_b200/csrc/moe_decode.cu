@@ -98,7 +98,6 @@ struct __align__(16) DecodeMisc {
     int abort;
     int U, P, NC;
     uint32_t xmax[MAXT];  // max |x_t| (f32 bits)
-    float lmax[MAXT];     // max logit of token t (phase K)
     int xexp[MAXT];       // s per token (terms hold x_t * 2^s)
     float xscale[MAXT];   // 2^-s per token
     int pe[MAXP];         // expert of pair p = t*K + z (shared: p = T*K + t -> E)
@@ -334,41 +333,36 @@ __device__ __noinline__ float router_dot(const float* __restrict__ wrow, const u
 }
 
 // Top-k of one token (moe.zig:435-463) by one warp; lg = the token's logits in
-// shared memory.  With PRE, exr holds the token's exp(logit - max) values,
-// computed beforehand by the whole CTA, one per thread (with 16 experts a lane,
-// the lane's 16 chains of dependent FP64 steps cost more than two extra block
-// barriers); else the warp computes them.  Lane l owns experts l, l+32, ...
-// (NKL of them, in registers).
+// shared memory.  Lane l owns experts l, l+32, ... (NKL of them, in registers).
 // Keys are the f32 bits of exp(v - max) + 1 (non-negative floats order like
 // their bits; 0 = not a candidate: chosen, NaN or beyond E).  Each round takes
 // the largest key and, among equal keys, the smallest id — the reference's
 // strict-greater scan from e = 0 with bv = -1.  A round without a candidate
 // yields id 0, as in the reference.  One round = two warp reductions: the
 // largest key, then the smallest id holding it.
-template <int NKL, bool PRE>
-__device__ __noinline__ void route_token(const float* __restrict__ exr, const float* __restrict__ lg, int E, int K,
-                                         int norm_topk, int has_shared,
+template <int NKL>
+__device__ __noinline__ void route_token(const float* __restrict__ lg, int E, int K, int norm_topk, int has_shared,
                                          int T, int t, int lane, DecodeMisc& s, uint32_t* topk_idx,
                                          float* topk_gates, bool write_out) {
     float mx = __int_as_float(0xffc00000);  // NaN: fmaxf ignores it
-    if (!PRE) {
-#pragma unroll
-        for (int j = 0; j < NKL; ++j) mx = fmaxf(mx, 32 * j + lane < E ? lg[32 * j + lane] : mx);
-        mx = warp_max(mx);
-    }
-    uint32_t kk[NKL];
-    double all = 0.0;
-    float ex0 = 0.0f;  // this lane's exp for j = 0 (lane 0: expert 0)
+    float lv[NKL];
 #pragma unroll
     for (int j = 0; j < NKL; ++j) {
-        const bool in = 32 * j + lane < E;
-        const float ex = !in ? 0.0f : PRE ? exr[32 * j + lane] : cz_expf_inline(__fsub_rn(lg[32 * j + lane], mx));
-        kk[j] = (in && ex > -1.0f) ? __float_as_uint(ex) + 1u : 0u;
-        if (!norm_topk && in) all += (double)ex;
-        if (j == 0) ex0 = ex;
+        lv[j] = 32 * j + lane < E ? lg[32 * j + lane] : __int_as_float(0xffc00000);
+        mx = fmaxf(mx, lv[j]);
+    }
+    mx = warp_max(mx);
+    uint32_t kk[NKL];
+    double all = 0.0;
+#pragma unroll
+    for (int j = 0; j < NKL; ++j) {
+        const float ex = 32 * j + lane < E ? cz_expf_inline(__fsub_rn(lv[j], mx)) : 0.0f;
+        kk[j] = (32 * j + lane < E && ex > -1.0f) ? __float_as_uint(ex) + 1u : 0u;
+        if (!norm_topk && 32 * j + lane < E) all += (double)ex;
+        lv[j] = ex;
     }
     if (!norm_topk) all = warp_sum_d(all);
-    const float ex_e0 = PRE ? exr[0] : __shfl_sync(0xffffffffu, ex0, 0);
+    const float ex_e0 = __shfl_sync(0xffffffffu, lv[0], 0);
     double top = 0.0;
     int my_e = 0;
     float my_v = 0.0f;
@@ -598,41 +592,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     // ---------------- phase K: top-k + grouping (every CTA) ----------------
     if (!s.abort && !mbar_wait_bounded(&s.lbar, 0, &s.abort) && lane == 0) set_error(err, s, CZ_DERR_FULL_WAIT);
     __syncthreads();
-    // more than 128 experts: exp(logit - max) of every (token, expert) into the ring
-    // after the logits (the weight stream starts after phase K): max per token by warp
-    // t, then one exp per thread, the same operations the top-k warp runs otherwise
-    const float* const lgs = reinterpret_cast<const float*>(ring);
-    float* const exs = reinterpret_cast<float*>(ring) + (size_t)T * LS;  // [T][E]
-    const bool pre = E > 128;
-    if (pre && !s.abort) {
-        for (int t = warp; t < T; t += NWARPS) {
-            float mx = __int_as_float(0xffc00000);  // NaN: fmaxf ignores it
-            for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lgs[(size_t)t * LS + e]);
-            mx = warp_max(mx);
-            if (lane == 0) s.lmax[t] = mx;
-        }
-    }
-    if (pre) __syncthreads();
-    if (pre && !s.abort) {
-        for (int i = tid; i < T * E; i += NTHREADS) {
-            const int t = i / E, e = i - t * E;
-            exs[i] = cz_expf_inline(__fsub_rn(lgs[(size_t)t * LS + e], s.lmax[t]));
-        }
-    }
-    if (pre) __syncthreads();
     if (!s.abort) {
         for (int t = warp; t < T; t += NWARPS) {
-            const float* lg = lgs + (size_t)t * LS;
-            const float* ex = exs + (size_t)t * E;
+            const float* lg = reinterpret_cast<const float*>(ring) + (size_t)t * LS;
             if (E <= 32)
-                route_token<1, false>(ex, lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates,
-                                      c == 0);
+                route_token<1>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates, c == 0);
             else if (E <= 128)
-                route_token<4, false>(ex, lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates,
-                                      c == 0);
+                route_token<4>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates, c == 0);
             else
-                route_token<MAXE / 32, true>(ex, lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx,
-                                             p.topk_gates, c == 0);
+                route_token<MAXE / 32>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates,
+                                       c == 0);
         }
     }
     __syncthreads();
