@@ -138,7 +138,8 @@ struct Ctx {
     // MoE
     std::map<uint32_t, MoeLayer> layers;
     DevBuf logits, hrows, io_x, io_out, io_res, ones, pf_scratch;
-    HostBuf io_host;  // pinned staging of io_res
+    HostBuf io_host;  // pinned staging of io_res (host-pointer forward, up to kHostStageCap bytes)
+    HostBuf io_xh;    // pinned staging of the tokens (host-pointer forward, up to kHostStageCap bytes)
     uint32_t* sync = nullptr;
     // expert parallelism (one process per GPU)
     bool ep_on = false;
@@ -194,11 +195,20 @@ NcclApi nccl;
 Ctx g;
 std::mutex g_mu;
 
+// Forgets the cached device addresses of the no-allocation scratch (defined with
+// colizig_cuda_moe_forward_noalloc below), so the first call after an init does
+// the look-up again: a context reset by the host application reloads the module.
+void noalloc_forget();
+
 size_t nb(size_t x) { return (x + 127) / 128; }
 
 // Token batches of at least this size take the prefill path (grouped GEMMs on
 // tcgen05); smaller ones the decode kernel.
 constexpr int kPrefillMinTokens = 32;
+
+// Largest host-pointer transfer staged through the library's page-locked
+// buffers (decode-sized calls); larger ones copy straight to/from the caller.
+constexpr size_t kHostStageCap = 4u << 20;
 
 int ensure_sync() {
     if (g.sync) return CZ_OK;
@@ -246,6 +256,7 @@ void shutdown_locked() {
     for (auto& kv : g.layers) free_layer(kv.second);
     g.layers.clear();
     g.io_host.release();
+    g.io_xh.release();
     for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.hrows, &g.pf_scratch, &g.io_x, &g.io_out, &g.io_res,
                       &g.ones, &g.sh_idx, &g.sh_gates, &g.sh_xn, &g.sh_slot, &g.sh_counts, &g.sh_allc,
                       &g.sh_tmp, &g.sh_send, &g.sh_recv, &g.sh_x, &g.sh_ridx, &g.sh_rgates, &g.sh_part, &g.sh_back})
@@ -254,6 +265,7 @@ void shutdown_locked() {
     for (cudaEvent_t e : g.tm_ev) cudaEventDestroy(e);
     if (g.stream) cudaStreamDestroy(g.stream);
     g = Ctx{};
+    noalloc_forget();
 }
 
 int init_locked(int device) {
@@ -946,25 +958,56 @@ CZ_EXPORT int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtyp
         return run(x, out, topk_idx, topk_gates, st);
     }
     // host pointers: synchronous on the library stream.  The results land in one
-    // device buffer [out][top-k ids][top-k gates] (256-byte aligned parts) and come
-    // back in one copy through pinned staging: a small copy costs mostly its fixed
-    // latency, so one copy instead of three shortens the call.
+    // device buffer [out][top-k ids][top-k gates][error word] (256-byte aligned
+    // parts) and come back in one copy through pinned staging, followed by one
+    // stream synchronisation: a small copy costs mostly its fixed latency.  The
+    // tokens go up through pinned staging too (a pageable source would make the
+    // driver stage them itself).  Past kHostStageCap bytes (prefill batches) the
+    // copies go straight between the caller's buffers and the device instead, so
+    // the page-locked staging stays small.
     const auto up256 = [](size_t n) { return (n + 255) & ~(size_t)255; };
     const size_t io = up256(ob), go = io + (topk_idx ? up256(kb) : 0);
-    const size_t rb = topk_gates ? go + kb : topk_idx ? io + kb : ob;
-    if (!g.io_x.ensure(xb) || !g.io_res.ensure(rb) || !g.io_host.ensure(rb)) return CZ_EALLOC;
+    const size_t eo = go + (topk_gates ? up256(kb) : 0);
+    const size_t rb = eo + sizeof(uint32_t);
+    const bool staged = rb <= kHostStageCap && xb <= kHostStageCap;
+    if (!g.io_x.ensure(xb) || !g.io_res.ensure(rb) || (staged && (!g.io_host.ensure(rb) || !g.io_xh.ensure(xb))) ||
+        ensure_sync())
+        return CZ_EALLOC;
     uint8_t* const res = g.io_res.as<uint8_t>();
-    if (xb && cudaMemcpyAsync(g.io_x.p, x, xb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess) return CZ_EH2D;
+    if (xb) {
+        const void* src = x;
+        if (staged) {
+            memcpy(g.io_xh.p, x, xb);
+            src = g.io_xh.p;
+        }
+        if (cudaMemcpyAsync(g.io_x.p, src, xb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess) return CZ_EH2D;
+    }
     int rc = run(g.io_x.p, reinterpret_cast<float*>(res), topk_idx ? reinterpret_cast<uint32_t*>(res + io) : nullptr,
                  topk_gates ? reinterpret_cast<float*>(res + go) : nullptr, g.stream);
     if (rc) {
         cudaStreamSynchronize(g.stream);
         return rc;
     }
-    if (ob && cudaMemcpyAsync(g.io_host.p, res, rb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess) return CZ_ED2H;
-    rc = check_device_error(g.stream);  // synchronises the stream
-    if (rc || !ob) return rc;
+    if (!ob) return check_device_error(g.stream);
+    if (!staged) {
+        if (cudaMemcpyAsync(out, res, ob, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess ||
+            (topk_idx && cudaMemcpyAsync(topk_idx, res + io, kb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess) ||
+            (topk_gates && cudaMemcpyAsync(topk_gates, res + go, kb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess))
+            return CZ_ED2H;
+        return check_device_error(g.stream);  // synchronises the stream
+    }
+    if (cudaMemcpyAsync(res + eo, g.sync + 1, sizeof(uint32_t), cudaMemcpyDeviceToDevice, g.stream) != cudaSuccess ||
+        cudaMemcpyAsync(g.io_host.p, res, rb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess)
+        return CZ_ED2H;
+    if (cudaStreamSynchronize(g.stream) != cudaSuccess) return CZ_ED2H;
     const uint8_t* const hs = static_cast<const uint8_t*>(g.io_host.p);
+    uint32_t err = 0;
+    memcpy(&err, hs + eo, sizeof err);
+    if (err) {
+        cudaMemsetAsync(g.sync + 1, 0, sizeof(uint32_t), g.stream);
+        cudaStreamSynchronize(g.stream);
+        return CZ_ETIMEOUT;
+    }
     memcpy(out, hs, ob);
     if (topk_idx) memcpy(topk_idx, hs + io, kb);
     if (topk_gates) memcpy(topk_gates, hs + go, kb);
@@ -1168,8 +1211,12 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 constexpr int kNoAllocMaxDevices = 64;
 uint8_t* g_noalloc_addr[kNoAllocMaxDevices] = {};
 
+void noalloc_forget() {
+    for (int i = 0; i < kNoAllocMaxDevices; ++i) g_noalloc_addr[i] = nullptr;
+}
+
 // Address of the static scratch on device `dev`: looked up on the first call
-// for that device (set-up), cached afterwards.
+// for that device after an init (set-up), cached until shutdown.
 uint8_t* noalloc_scratch(int dev) {
     if (dev < 0 || dev >= kNoAllocMaxDevices) return nullptr;
     if (!g_noalloc_addr[dev]) {
@@ -1227,8 +1274,12 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
         const int rc = cz::decode_launch(p, g.num_sms, st);
         if (rc) return rc;
     }
-    if (status && cudaMemcpyAsync(status, sync + 1, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-        return CZ_ELAUNCH;
-    if (cudaMemsetAsync(sync + 1, 0, sizeof(uint32_t), st) != cudaSuccess) return CZ_ELAUNCH;
+    // Without a status the error word is kept: a wait that gave up stays recorded
+    // until a later call passes a status (that call then reports it).
+    if (status) {
+        if (cudaMemcpyAsync(status, sync + 1, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+            return CZ_ELAUNCH;
+        if (cudaMemsetAsync(sync + 1, 0, sizeof(uint32_t), st) != cudaSuccess) return CZ_ELAUNCH;
+    }
     return CZ_OK;
 }

@@ -135,6 +135,53 @@ class Layer:
         return forward(self, x, out, topk_idx, topk_gates, stream)
 
 
+def _shape_of(a):
+    return tuple(int(s) for s in a.shape)
+
+
+def _dtype_name(a) -> str:
+    if torch is not None and isinstance(a, torch.Tensor):
+        return {torch.float32: "f32", torch.int32: "i32", torch.uint32: "u32", torch.bfloat16: "bf16",
+                torch.int16: "i16"}.get(a.dtype, str(a.dtype))
+    return {np.dtype(np.float32): "f32", np.dtype(np.int32): "i32", np.dtype(np.uint32): "u32",
+            np.dtype(np.int16): "i16", np.dtype(np.uint16): "u16"}.get(np.dtype(a.dtype), str(a.dtype))
+
+
+def check_io(dims: Dims, x, out=None, topk_idx=None, topk_gates=None, status=None, device=None) -> int:
+    """Validates the buffers of one forward call before anything reaches the
+    library, which only sees raw pointers and would read and write past a
+    mis-shaped buffer.  x must be [T, hidden] (f32 or bf16; bf16 host arrays as
+    16-bit integers); out f32 [T, hidden]; topk_idx 32-bit integers [T, topk];
+    topk_gates f32 [T, topk]; status (device calls only) a 32-bit integer tensor
+    of at least one element.  With `device` given, every tensor must live on
+    it.  Returns T; raises ValueError otherwise."""
+    if x is None or len(getattr(x, "shape", ())) != 2:
+        raise ValueError(f"x must be 2-D [T, {dims.hidden}], got shape {None if x is None else _shape_of(x)}")
+    T, H = _shape_of(x)
+    if H != dims.hidden:
+        raise ValueError(f"x has {H} columns, the layer's hidden size is {dims.hidden}")
+    if _dtype_name(x) not in ("f32", "bf16", "i16", "u16"):
+        raise ValueError(f"x must be f32 or bf16, got {_dtype_name(x)}")
+    want = (("out", out, ("f32",), (T, dims.hidden)), ("topk_idx", topk_idx, ("i32", "u32"), (T, dims.topk)),
+            ("topk_gates", topk_gates, ("f32",), (T, dims.topk)))
+    for name, a, dts, shape in want:
+        if a is None:
+            continue
+        if _dtype_name(a) not in dts:
+            raise ValueError(f"{name} must be {'/'.join(dts)}, got {_dtype_name(a)}")
+        if _shape_of(a) != shape:
+            raise ValueError(f"{name} must have shape {shape}, got {_shape_of(a)}")
+    if status is not None:
+        if _dtype_name(status) not in ("i32", "u32") or int(np.prod(_shape_of(status))) < 1:
+            raise ValueError("status must be a 32-bit integer tensor of at least one element")
+    if device is not None:
+        for name, a in (("x", x), ("out", out), ("topk_idx", topk_idx), ("topk_gates", topk_gates),
+                        ("status", status)):
+            if a is not None and (not isinstance(a, torch.Tensor) or a.device != device):
+                raise ValueError(f"{name} must be a tensor on {device}")
+    return T
+
+
 def forward(layer: Layer, x, out=None, topk_idx=None, topk_gates=None, stream=None, sharded: bool = False):
     """moe.zig:409-426: out[T, H] = MoE(x[T, H]).  Returns (out, topk_idx, topk_gates);
     the top-k arrays are allocated when not given.  sharded=True (a layer registered
@@ -144,13 +191,10 @@ def forward(layer: Layer, x, out=None, topk_idx=None, topk_gates=None, stream=No
     L = _abi.load()
     sh = _abi.COLIZIG_EP_SHARDED if sharded else 0
     if _is_cuda(x):
-        T = x.shape[0]
-        if x.dtype == torch.bfloat16:
-            dt = _abi.COLIZIG_X_BF16
-        elif x.dtype == torch.float32:
-            dt = _abi.COLIZIG_X_F32
-        else:
+        if x.dtype not in (torch.bfloat16, torch.float32):
             raise ValueError("x must be f32 or bf16")
+        T = check_io(d, x, out, topk_idx, topk_gates, device=x.device)
+        dt = _abi.COLIZIG_X_BF16 if x.dtype == torch.bfloat16 else _abi.COLIZIG_X_F32
         if out is None:
             out = torch.empty((T, d.hidden), dtype=torch.float32, device=x.device)
         if topk_idx is None:
@@ -173,14 +217,17 @@ def forward(layer: Layer, x, out=None, topk_idx=None, topk_gates=None, stream=No
         xa = np.ascontiguousarray(x, np.float32)
         dt = _abi.COLIZIG_X_F32
     if xa.ndim == 1:
-        xa = xa[None, :]
-    T = xa.shape[0]
+        xa = xa[None, :]  # one token
+    T = check_io(d, xa, out, topk_idx, topk_gates)
     if out is None:
         out = np.empty((T, d.hidden), np.float32)
     if topk_idx is None:
         topk_idx = np.empty((T, d.topk), np.uint32)
     if topk_gates is None:
         topk_gates = np.empty((T, d.topk), np.float32)
+    for name, a in (("out", out), ("topk_idx", topk_idx), ("topk_gates", topk_gates)):
+        if not isinstance(a, np.ndarray):
+            raise ValueError(f"{name} must be a numpy array for host tokens")
     rc = L.colizig_cuda_moe_forward(layer.id, _ptr(xa), dt, T, _ptr(out), _ptr(topk_idx), _ptr(topk_gates), sh,
                                     None)
     _abi.check("colizig_cuda_moe_forward", rc)
@@ -192,18 +239,18 @@ def forward_noalloc(layer: Layer, x, out, topk_idx=None, topk_gates=None, status
     the library allocates nothing during the call (its scratch is a static
     device array), and neither does this wrapper, so every output tensor is
     the caller's.  ``status`` (optional int32 CUDA tensor of one element)
-    receives the call's device error word (0 = ok).  The first call on a device
-    does set-up; calls that overlap in time race on the shared scratch."""
+    receives the call's device error word (0 = ok), which is then cleared;
+    without a status the word is kept for the next call that passes one.  The
+    first call on a device does set-up; calls that overlap in time race on the
+    shared scratch."""
     if not (_is_cuda(x) and _is_cuda(out)):
         raise ValueError("forward_noalloc takes CUDA tensors only")
-    if x.dtype == torch.bfloat16:
-        dt = _abi.COLIZIG_X_BF16
-    elif x.dtype == torch.float32:
-        dt = _abi.COLIZIG_X_F32
-    else:
+    if x.dtype not in (torch.bfloat16, torch.float32):
         raise ValueError("x must be f32 or bf16")
+    T = check_io(layer.dims, x, out, topk_idx, topk_gates, status, device=x.device)
+    dt = _abi.COLIZIG_X_BF16 if x.dtype == torch.bfloat16 else _abi.COLIZIG_X_F32
     rc = _abi.load().colizig_cuda_moe_forward_noalloc(
-        layer.id, _ptr(x), dt, x.shape[0], _ptr(out), None if topk_idx is None else _ptr(topk_idx),
+        layer.id, _ptr(x), dt, T, _ptr(out), None if topk_idx is None else _ptr(topk_idx),
         None if topk_gates is None else _ptr(topk_gates), None if status is None else _ptr(status),
         _stream_handle(stream))
     _abi.check("colizig_cuda_moe_forward_noalloc", rc)

@@ -123,7 +123,7 @@ def tokens_f32(x: torch.Tensor) -> np.ndarray:
     return x.detach().float().cpu().numpy()
 
 
-# Benchmark configurations.
+# Benchmark configurations 1, 2, 3 and 5 (config 4 is a 48-layer stack of config 2).
 CONFIGS = {
     "c1": Dims(hidden=256, experts=16, topk=4, inter=128, shared_inter=0, norm_topk=True),
     "c2": Dims(hidden=2048, experts=128, topk=8, inter=768, shared_inter=0, norm_topk=True),

@@ -176,7 +176,11 @@ int colizig_cuda_moe_check(void* stream);
  * when the library loads and every call leaves them ready for the next.
  * status (nullable, device u32): after the launches the call's device error
  * word is copied there (0 = ok; non-zero = a bounded wait in the kernel gave
- * up and the outputs are invalid), then cleared.  T == 0 launches nothing. */
+ * up and the outputs are invalid), then cleared.  With a NULL status the word
+ * is kept, so a wait that gave up is reported by the next call that passes a
+ * status.  T == 0 launches nothing.  colizig_cuda_shutdown forgets the
+ * scratch address, so the first call after a new init (for instance after the
+ * host application reset the device) is a set-up call again. */
 int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, int x_dtype, int T, float* out,
                                      uint32_t* topk_idx, float* topk_gates, uint32_t* status, void* stream);
 
