@@ -31,6 +31,7 @@ MOE_SYMBOLS = (
     "colizig_cuda_moe_stack_forward",
     "colizig_cuda_moe_check",
     "colizig_cuda_debug_expf",
+    "colizig_cuda_debug_hold_router",
     "colizig_cuda_moe_forward_noalloc",
     "colizig_cuda_ep_unique_id",
     "colizig_cuda_ep_init",
@@ -144,6 +145,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         L.colizig_cuda_kernel_timer_read.argtypes = [vp, vp, i32]
         L.colizig_cuda_debug_expf.restype = i32
         L.colizig_cuda_debug_expf.argtypes = [vp, vp, ctypes.c_size_t]
+        L.colizig_cuda_debug_hold_router.restype = i32
+        L.colizig_cuda_debug_hold_router.argtypes = [u32]
         _lib = L
         return L
 

@@ -148,6 +148,10 @@ struct Ctx {
     // sharded expert parallelism (prefill): routing of this rank's tokens, exchange buffers
     DevBuf sh_idx, sh_gates, sh_xn, sh_slot, sh_counts, sh_allc, sh_tmp, sh_send, sh_recv, sh_x, sh_ridx, sh_rgates,
         sh_part, sh_back;
+    // failure-path tests: the next decode launch holds back router row 0's logits
+    // and gives up its waits after dbg_spin_limit polls (one launch, then cleared)
+    int dbg_hold = 0;
+    uint32_t dbg_spin_limit = 0;
     // kernel timer (benchmarks): CUDA event pairs around the dominant launches
     std::vector<cudaEvent_t> tm_ev;
     std::vector<int> tm_kind;
@@ -326,11 +330,20 @@ int gather_copy_2d(uint8_t* dst, size_t dst_pitch, const colizig_moe_expert* ex,
     return CZ_OK;
 }
 
+// A device buffer of at least `need` bytes whose new contents are zero: the
+// decode kernel's tagged exchange words must not start with a stale tag.  Only
+// a (re)allocation clears, and waits for the clear, so the steady state costs
+// nothing.
+bool ensure_zeroed(DevBuf& b, size_t need) {
+    if (b.cap >= need && b.p) return true;
+    if (!b.ensure(need)) return false;
+    return cudaMemset(b.p, 0, b.cap) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+}
+
 int ensure_decode_scratch(const colizig_moe_dims& d) {
-    const size_t T = cz::kDecodeMaxTokens;
-    if (!g.logits.ensure(T * cz::logit_stride((int)d.experts) * sizeof(float))) return CZ_EALLOC;
-    const size_t im = d.inter > d.shared_inter ? d.inter : d.shared_inter;
-    if (!g.hrows.ensure(T * (d.topk + 1) * im * sizeof(float))) return CZ_EALLOC;
+    if (!ensure_zeroed(g.logits, cz::decode_logit_words((int)d.experts) * 8)) return CZ_EALLOC;
+    if (!ensure_zeroed(g.hrows, cz::decode_hrow_words((int)d.topk, (int)d.inter, (int)d.shared_inter) * 8))
+        return CZ_EALLOC;
     return ensure_sync();
 }
 
@@ -365,10 +378,20 @@ cz::DecodeParams make_params(const MoeLayer& L) {
     p.sh_up_map = L.shared_here ? L.sh_up_map : L.up_map;
     p.gu3d = L.gu_kb > 0;
     p.gu_kb = L.gu_kb;
-    p.logits = g.logits.as<float>();
-    p.hrows = g.hrows.as<float>();
+    p.logits = g.logits.as<unsigned long long>();
+    p.hrows = g.hrows.as<unsigned long long>();
+
     p.sync = g.sync;
     return p;
+}
+
+// Hands an armed failure-path hold (colizig_cuda_debug_hold_router) to this
+// launch and disarms it: it applies to exactly one decode launch.
+void take_debug_hold(cz::DecodeParams& p) {
+    p.dbg_hold = g.dbg_hold;
+    p.spin_limit = g.dbg_hold ? g.dbg_spin_limit : 0u;
+    g.dbg_hold = 0;
+    g.dbg_spin_limit = 0;
 }
 
 // Kernel timer.  Kinds of the recorded launch pairs.
@@ -400,7 +423,7 @@ void timer_free() {
 // Runs one layer over T tokens (device pointers, stream-ordered), in launches
 // of at most kDecodeMaxTokens tokens.
 int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uint32_t* idx, float* gates,
-            const float* rms_w, float eps, const float* residual, cudaStream_t st) {
+            const float* rms_w, float eps, const float* residual, cudaStream_t st, uint32_t* status_out = nullptr) {
     if (T >= kPrefillMinTokens && L.pf_ok) {
         const size_t need = cz::prefill_scratch_bytes(T, (int)L.d.hidden, (int)L.d.experts, (int)L.d.topk,
                                                       (int)L.d.inter, (int)L.d.shared_inter, g.num_sms);
@@ -438,8 +461,10 @@ int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uin
         p.out = out + (size_t)t0 * L.d.hidden;
         p.topk_idx = idx ? idx + (size_t)t0 * L.d.topk : nullptr;
         p.topk_gates = gates ? gates + (size_t)t0 * L.d.topk : nullptr;
+        p.status_out = t0 + n >= T ? status_out : nullptr;  // the last launch reports the error word
         cudaEvent_t* ev = timer_take(kTimerDecode, 1);
         if (ev && !cz::record_timer_event(ev[0], st)) return CZ_ELAUNCH;
+        take_debug_hold(p);
         rc = cz::decode_launch(p, g.num_sms, st);
         if (rc) return rc;
         if (ev && !cz::record_timer_event(ev[1], st)) return CZ_ELAUNCH;
@@ -948,9 +973,9 @@ CZ_EXPORT int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtyp
     const size_t H = L.d.hidden, K = L.d.topk;
     const int bf16 = x_dtype == COLIZIG_X_BF16;
     const size_t xb = (size_t)T * H * (bf16 ? 2 : 4), ob = (size_t)T * H * 4, kb = (size_t)T * K * 4;
-    auto run = [&](const void* xd, float* od, uint32_t* id, float* gd, cudaStream_t st) {
+    auto run = [&](const void* xd, float* od, uint32_t* id, float* gd, cudaStream_t st, uint32_t* status = nullptr) {
         return sharded ? moe_run_sharded(L, xd, bf16, T, od, id, gd, nullptr, 0.f, nullptr, st)
-                       : moe_run(L, xd, bf16, T, od, id, gd, nullptr, 0.f, nullptr, st);
+                       : moe_run(L, xd, bf16, T, od, id, gd, nullptr, 0.f, nullptr, st, status);
     };
     if (flags & COLIZIG_PTR_DEVICE) {
         if (T > 0 && (!aligned16(x) || !aligned16(out))) return CZ_EARGS;
@@ -982,8 +1007,12 @@ CZ_EXPORT int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtyp
         }
         if (cudaMemcpyAsync(g.io_x.p, src, xb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess) return CZ_EH2D;
     }
+    // decode launches copy the error word into the result buffer themselves (their
+    // last CTA); the other paths get one device-to-device copy of it below
+    const bool kernel_status = staged && !sharded && !(T >= kPrefillMinTokens && L.pf_ok);
     int rc = run(g.io_x.p, reinterpret_cast<float*>(res), topk_idx ? reinterpret_cast<uint32_t*>(res + io) : nullptr,
-                 topk_gates ? reinterpret_cast<float*>(res + go) : nullptr, g.stream);
+                 topk_gates ? reinterpret_cast<float*>(res + go) : nullptr, g.stream,
+                 kernel_status ? reinterpret_cast<uint32_t*>(res + eo) : nullptr);
     if (rc) {
         cudaStreamSynchronize(g.stream);
         return rc;
@@ -996,7 +1025,8 @@ CZ_EXPORT int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtyp
             return CZ_ED2H;
         return check_device_error(g.stream);  // synchronises the stream
     }
-    if (cudaMemcpyAsync(res + eo, g.sync + 1, sizeof(uint32_t), cudaMemcpyDeviceToDevice, g.stream) != cudaSuccess ||
+    if ((!kernel_status &&
+         cudaMemcpyAsync(res + eo, g.sync + 1, sizeof(uint32_t), cudaMemcpyDeviceToDevice, g.stream) != cudaSuccess) ||
         cudaMemcpyAsync(g.io_host.p, res, rb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess)
         return CZ_ED2H;
     if (cudaStreamSynchronize(g.stream) != cudaSuccess) return CZ_ED2H;
@@ -1076,7 +1106,9 @@ CZ_EXPORT int colizig_cuda_moe_check(void* stream) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g.inited) return CZ_EARGS;
     cudaSetDevice(g.dev);
-    return check_device_error(stream ? reinterpret_cast<cudaStream_t>(stream) : g.stream);
+    // NULL is the default stream, as for the device-pointer forward: the read is
+    // ordered after the calls issued there
+    return check_device_error(reinterpret_cast<cudaStream_t>(stream));
 }
 
 // Kernel timer for benchmarks (not in the reference surface).  capacity > 0
@@ -1123,6 +1155,19 @@ CZ_EXPORT int colizig_cuda_kernel_timer_read(int* kinds, float* ms, int max_n) {
         ms[i] = t;
     }
     return n;
+}
+
+// Failure-path test hook (no reference counterpart): the next decode launch
+// withholds router row 0's logits, so every CTA's bounded wait for them gives up
+// after `spin_limit` polls (about 0.2 us each) and the launch ends early with
+// the error word set.  Nothing faults and nothing hangs.
+CZ_EXPORT int colizig_cuda_debug_hold_router(uint32_t spin_limit) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited || spin_limit == 0) return CZ_EARGS;
+    g.dbg_hold = 1;
+    g.dbg_spin_limit = spin_limit;
+    return CZ_OK;
 }
 
 CZ_EXPORT int colizig_cuda_debug_expf(const float* x_dev, float* y_dev, size_t n) {
@@ -1188,23 +1233,22 @@ CZ_EXPORT int colizig_cuda_ep_shutdown(void) {
 // The device-pointer forward with its scratch in one static device array
 // instead of cudaMalloc'd buffers: [sync words][router logits][h rows of every
 // (token, expert) pair].  Static device storage is zero when the module loads,
-// which is all the sync words need (every launch zeroes the region the next
-// launch uses, and the call clears the error word); logits and h rows are
-// written before they are read.
+// which is what the sync words and the tagged exchange words need (every launch
+// zeroes the counter region the next launch uses, and tags the words it writes
+// with its own sequence number, which a zero word never carries).
 namespace {
 
 constexpr int kNoAllocMaxHidden = 4096;
 constexpr int kNoAllocMaxTokens = 4;  // tokens per launch through the static scratch
 constexpr size_t kNoAllocSyncBytes = 768;
-constexpr size_t kNoAllocLogitBytes = 8448;
 constexpr int kNoAllocMaxInter = 1024;  // moe_intermediate and shared_intermediate
-constexpr size_t kNoAllocHBytes =
-    (size_t)kNoAllocMaxTokens * (cz::kMaxTopk + 1) * kNoAllocMaxInter * sizeof(float);
+// tagged 8-byte exchange words (router logits, h rows), as the decode kernel reads them
+constexpr size_t kNoAllocLogitBytes = (size_t)cz::kDecodeMaxTokens * ((cz::kMaxExperts + 1 + 3) & ~3) * 8;
+constexpr size_t kNoAllocHBytes = (size_t)cz::kDecodeMaxTokens * (cz::kMaxTopk + 1) * kNoAllocMaxInter * 8;
 constexpr size_t kNoAllocBytes = kNoAllocSyncBytes + kNoAllocLogitBytes + kNoAllocHBytes;
+static_assert(kNoAllocMaxTokens == cz::kDecodeMaxTokens, "one launch's scratch");
 static_assert(cz::kSyncWords * sizeof(uint32_t) <= kNoAllocSyncBytes, "sync words");
-static_assert((size_t)kNoAllocMaxTokens * ((cz::kMaxExperts + 1 + 3) & ~3) * sizeof(float) <= kNoAllocLogitBytes,
-              "logits");
-static_assert(kNoAllocBytes == 287744, "the size stated in colizig_cuda.h");
+static_assert(kNoAllocBytes == 574336, "the size stated in colizig_cuda.h");
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 
@@ -1250,8 +1294,8 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
     uint8_t* base = noalloc_scratch(g.dev);
     if (!base) return CZ_ELAUNCH;
     uint32_t* sync = reinterpret_cast<uint32_t*>(base);
-    float* logits = reinterpret_cast<float*>(base + kNoAllocSyncBytes);
-    float* hrows = reinterpret_cast<float*>(base + kNoAllocSyncBytes + kNoAllocLogitBytes);
+    unsigned long long* logits = reinterpret_cast<unsigned long long*>(base + kNoAllocSyncBytes);
+    unsigned long long* hrows = reinterpret_cast<unsigned long long*>(base + kNoAllocSyncBytes + kNoAllocLogitBytes);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int bf16 = x_dtype == COLIZIG_X_BF16;
     const size_t xelt = bf16 ? 2 : 4;
@@ -1271,6 +1315,7 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
         p.out = out + (size_t)t0 * L.d.hidden;
         p.topk_idx = topk_idx ? topk_idx + (size_t)t0 * L.d.topk : nullptr;
         p.topk_gates = topk_gates ? topk_gates + (size_t)t0 * L.d.topk : nullptr;
+        take_debug_hold(p);
         const int rc = cz::decode_launch(p, g.num_sms, st);
         if (rc) return rc;
     }

@@ -180,6 +180,32 @@ CZ_DEV uint32_t ld_relaxed_gpu(const uint32_t* p) {
     return v;
 }
 
+// 8-byte exchange words: one single-copy-atomic access each.
+CZ_DEV unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Two consecutive 8-byte words (16-byte aligned); each word is its own
+// single-copy-atomic access.
+CZ_DEV void ld_relaxed_u64x2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+CZ_DEV void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+CZ_DEV unsigned long long tag_word(uint32_t tag, float v) {
+    return ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+}
+
+// L2 prefetch of `bytes` (a multiple of 16) from a 16-byte aligned global address.
+CZ_DEV void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 CZ_DEV void red_release_add_gpu(uint32_t* p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }

@@ -13,7 +13,7 @@ constexpr int kDecodeMaxTokens = 4;   // per decode launch (more tokens cost mor
 constexpr int kMaxTopk = 16;
 constexpr int kMaxExperts = 512;
 constexpr int kMaxGrid = 160;         // decode CTAs (one per SM) the no-allocation scratch is sized for
-constexpr int kSyncRegionWords = 8;   // router arrivals, CTAs done, h rows written, pad
+constexpr int kSyncRegionWords = 8;   // [1] = CTAs done (the other words are unused padding)
 constexpr int kSyncWords = 2 + 2 * kSyncRegionWords;  // seq, err, two regions
 
 __host__ __device__ inline int cz_nblk(int x) { return (x + 127) / 128; }
@@ -59,10 +59,22 @@ struct alignas(64) DecodeParams {
     int H, E, K, I, SI, norm_topk;
     int e_lo, e_hi;          // routed experts held (and computed) here: [e_lo, e_hi); stacked from e_lo
     int shared_here;         // the shared expert is computed here
-    float* logits;           // scratch [T, logit_stride(E)]
-    float* hrows;          // scratch [T*(K+1)][max(I, SI)] f32: the h row of every (token, expert) pair
+    // Tagged exchange words: (tag << 32) | f32 bits, tag = launch sequence + 1.  A
+    // reader polls a word until it carries the current tag, so the data itself is
+    // the flag (no grid counter, no fence); both buffers are zeroed at allocation.
+    unsigned long long* logits;  // scratch [kDecodeMaxTokens, logit_stride(E)]: router logits
+    unsigned long long* hrows;   // scratch [T*(K+1)][max(I, SI)]: the h row of every (token, expert) pair
     uint32_t* sync;          // kSyncWords words, zeroed once at allocation
+    uint32_t* status_out;    // nullable: the last CTA copies the device error word here
+    uint32_t spin_limit;     // polls before a wait gives up (0 = CZ_SPIN_LIMIT)
+    int dbg_hold;            // failure-path tests: router row 0's logits are never published
 };
+
+// Bytes of the decode kernel's tagged scratch for these dims (logits, h rows).
+inline size_t decode_logit_words(int E) { return (size_t)kDecodeMaxTokens * logit_stride(E); }
+inline size_t decode_hrow_words(int K, int I, int SI) {
+    return (size_t)kDecodeMaxTokens * (K + 1) * (size_t)(I > SI ? I : SI);
+}
 
 // Decode-kernel tensor map of gate/up weights: u8 [rows][H] in 128-byte-swizzled
 // boxes of 16 rows x 128 columns, up to 16 column blocks deep when H % 128 == 0

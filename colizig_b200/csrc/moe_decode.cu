@@ -87,6 +87,12 @@ constexpr int MAXG = MAXP;                // groups <= pairs
 constexpr int SMEM_LIMIT = 227 * 1024;
 
 static_assert(GU_BYTES + SC_BYTES <= SLOT_BYTES, "slot");
+// routing scratch in the ring: logits + exps [T][LS] f32, two candidate buffers
+// [T][ceil(E/32)][K] and the winners [T][MAXK] (8-byte entries)
+static_assert(2 * ((kDecodeMaxTokens * ((kMaxExperts + 4) & ~3) * 4 + 15) & ~15) +
+                      2 * kDecodeMaxTokens * ((kMaxExperts + 31) / 32) * kMaxTopk * 8 + kDecodeMaxTokens * kMaxTopk * 8 <=
+                  NSLOT * SLOT_BYTES,
+              "routing scratch");
 static_assert(SLOT_BYTES % 1024 == 0, "TMA destinations stay 1024-aligned");
 
 // Small shared state (after the large regions).
@@ -94,12 +100,12 @@ struct __align__(16) DecodeMisc {
     uint64_t full[MAXSLOT];
     uint64_t empty[MAXSLOT];
     uint64_t rbar;
-    uint64_t lbar;
     int abort;
     int U, P, NC;
     uint32_t xmax[MAXT];  // max |x_t| (f32 bits)
     int xexp[MAXT];       // s per token (terms hold x_t * 2^s)
     float xscale[MAXT];   // 2^-s per token
+    float mxs[MAXT];      // max logit per token (routing)
     int pe[MAXP];         // expert of pair p = t*K + z (shared: p = T*K + t -> E)
     float pg[MAXP];       // gate of pair p
     int order[MAXP];      // pairs sorted by (expert, pair)
@@ -332,88 +338,6 @@ __device__ __noinline__ float router_dot(const float* __restrict__ wrow, const u
     return sum;
 }
 
-// Top-k of one token (moe.zig:435-463) by one warp; lg = the token's logits in
-// shared memory.  Lane l owns experts l, l+32, ... (NKL of them, in registers).
-// Keys are the f32 bits of exp(v - max) + 1 (non-negative floats order like
-// their bits; 0 = not a candidate: chosen, NaN or beyond E).  Each round takes
-// the largest key and, among equal keys, the smallest id — the reference's
-// strict-greater scan from e = 0 with bv = -1.  A round without a candidate
-// yields id 0, as in the reference.  One round = two warp reductions: the
-// largest key, then the smallest id holding it.
-template <int NKL>
-__device__ __noinline__ void route_token(const float* __restrict__ lg, int E, int K, int norm_topk, int has_shared,
-                                         int T, int t, int lane, DecodeMisc& s, uint32_t* topk_idx,
-                                         float* topk_gates, bool write_out) {
-    float mx = __int_as_float(0xffc00000);  // NaN: fmaxf ignores it
-    float lv[NKL];
-#pragma unroll
-    for (int j = 0; j < NKL; ++j) {
-        lv[j] = 32 * j + lane < E ? lg[32 * j + lane] : __int_as_float(0xffc00000);
-        mx = fmaxf(mx, lv[j]);
-    }
-    mx = warp_max(mx);
-    uint32_t kk[NKL];
-    double all = 0.0;
-#pragma unroll
-    for (int j = 0; j < NKL; ++j) {
-        const float ex = 32 * j + lane < E ? cz_expf_inline(__fsub_rn(lv[j], mx)) : 0.0f;
-        kk[j] = (32 * j + lane < E && ex > -1.0f) ? __float_as_uint(ex) + 1u : 0u;
-        if (!norm_topk && 32 * j + lane < E) all += (double)ex;
-        lv[j] = ex;
-    }
-    if (!norm_topk) all = warp_sum_d(all);
-    const float ex_e0 = __shfl_sync(0xffffffffu, lv[0], 0);
-    double top = 0.0;
-    int my_e = 0;
-    float my_v = 0.0f;
-#pragma unroll 1
-    for (int z = 0; z < K; ++z) {
-        uint32_t lb = 0u;
-        int lj = 0;
-#pragma unroll
-        for (int j = 0; j < NKL; ++j)
-            if (kk[j] > lb) {
-                lb = kk[j];
-                lj = j;
-            }
-        const uint32_t kmax = redux_max_u32(lb);
-        int best;
-        float bv;
-        if (kmax == 0u) {
-            best = 0;
-            bv = ex_e0;
-        } else {
-            best = (int)redux_min_u32(lb == kmax ? (uint32_t)(32 * lj + lane) : 0xffffffffu);
-            bv = __uint_as_float(kmax - 1u);
-            if ((best & 31) == lane) {
-#pragma unroll
-                for (int j = 0; j < NKL; ++j)
-                    if (j == (best >> 5)) kk[j] = 0u;
-            }
-        }
-        if (lane == z) {
-            my_e = best;
-            my_v = bv;
-        }
-        top = __dadd_rn(top, (double)bv);
-    }
-    const double den = norm_topk ? top : all;
-    if (lane < K) {
-        const float g = __double2float_rn(__ddiv_rn((double)my_v, den));
-        s.pe[t * K + lane] = my_e;
-        s.pg[t * K + lane] = g;
-        if (write_out) {
-            if (topk_idx) topk_idx[(size_t)t * K + lane] = (uint32_t)my_e;
-            if (topk_gates) topk_gates[(size_t)t * K + lane] = g;
-        }
-    }
-    if (lane == 0 && has_shared) {
-        s.pe[T * K + t] = E;
-        s.pg[T * K + t] = cz_sigmoid(lg[E]);
-    }
-    __syncwarp();
-}
-
 // Start of part c of n items split over G parts: floor(c * n / G).  32-bit: c <= G <= 160 and
 // n <= 5120 for every caller (hidden, router rows, chunks; decode_max_tokens bounds them).
 __device__ __forceinline__ int split_at(int c, int n, int G) {
@@ -427,16 +351,198 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, Decode
     return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, &s.abort));
 }
 
+// ---- routing (moe.zig:435-463) ----------------------------------------------
+// The reference picks, K times, the unchosen expert with the largest
+// exp(logit - max) by a strict-greater scan from expert 0 (ties to the lowest
+// id).  That order is a total order on (key, id): a larger key first, among
+// equal keys the smaller id, where key = f32 bits of exp(logit - max) + 1
+// (non-negative floats order like their bits; 0 = not a candidate: NaN, or past
+// the last expert).  The top K of a set under a total order are the union of
+// the top K of its parts, so each warp ranks a part of 32 entries by counting
+// the entries that beat each one, keeps its top K, and the survivors are ranked
+// again until one part is left.  A selection round without a candidate (every
+// remaining key 0) yields id 0 with expert 0's value, as the reference's scan
+// does.
+
+// Empty entries (key 0, ids from 0x80000000 up) rank after every expert.  Every
+// entry of a part must differ from the others, so that the counted ranks are
+// 0, 1, 2, ... and the top K slots are all written: past-the-end experts carry
+// 0x80000000 + their index, merge padding 0xc0000000 + its position.
+__device__ __forceinline__ unsigned long long empty_entry(uint32_t unique) {
+    return (unsigned long long)unique;
+}
+
+__device__ __forceinline__ unsigned long long route_entry(uint32_t key, uint32_t id) {
+    return ((unsigned long long)key << 32) | id;
+}
+
+// How many of the warp's 32 entries beat this lane's entry.
+__device__ __forceinline__ int rank_in_warp(unsigned long long v) {
+    const uint32_t key = (uint32_t)(v >> 32), id = (uint32_t)v;
+    int r = 0;
+#pragma unroll 8
+    for (int m = 0; m < 32; ++m) {
+        const unsigned long long w = __shfl_sync(0xffffffffu, v, m);
+        const uint32_t km = (uint32_t)(w >> 32), im = (uint32_t)w;
+        r += (km > key) || (km == key && im < id);
+    }
+    return r;
+}
+
+// Shared-memory scratch of the routing step (carved from the ring, which is
+// free between the token term split and the first weight copy).
+struct RouteScratch {
+    float* lg;                // [T][LS] logits (+ the shared gate logit at column E)
+    float* ex;                // [T][LS] exp(logit - max), kept for the all-expert sum
+    unsigned long long* ca;   // [T][nch * K] candidates (two buffers for the merge rounds)
+    unsigned long long* cb;
+    unsigned long long* fin;  // [T][MAXK] the winners in selection order
+};
+
+// Top-k of every token by the whole CTA (all threads call it).  Writes s.pe /
+// s.pg (pair p = t*K + z, shared-expert pairs p = T*K + t) and, from CTA 0, the
+// caller's top-k outputs.
+__device__ __noinline__ void route_all(const RouteScratch& rs, int T, int E, int K, int LS, int norm_topk,
+                                       int has_shared, DecodeMisc& s, uint32_t* topk_idx, float* topk_gates,
+                                       bool write_out) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nch = (E + 31) >> 5;
+    // stage 1: (token, 32 experts) per warp; exps computed in parallel over the CTA
+    for (int it = warp; it < T * nch; it += NWARPS) {
+        const int t = it / nch, j = it - t * nch;
+        const float* l = rs.lg + (size_t)t * LS;
+        float mx = __int_as_float(0xffc00000);  // NaN: fmaxf ignores it (@max over the row)
+        for (int e = lane; e < E; e += 32) mx = fmaxf(mx, l[e]);
+        mx = warp_max(mx);
+        if (j == 0 && lane == 0) s.mxs[t] = mx;
+        const int e = 32 * j + lane;
+        uint32_t key = 0u;
+        if (e < E) {
+            const float ex = cz_expf_inline(__fsub_rn(l[e], mx));
+            key = ex > -1.0f ? __float_as_uint(ex) + 1u : 0u;
+            rs.ex[(size_t)t * LS + e] = ex;
+        }
+        const unsigned long long v = route_entry(key, e < E ? (uint32_t)e : 0x80000000u + (uint32_t)e);
+        const int r = rank_in_warp(v);
+        if (r < K) rs.ca[((size_t)t * nch + j) * K + r] = v;
+    }
+    __syncthreads();
+    // merge rounds: parts of 32 survivors -> their top K, until one part is left
+    unsigned long long* cur = rs.ca;
+    unsigned long long* nxt = rs.cb;
+    int n = nch * K;  // entries per token in cur
+    const int stride = nch * K;
+    while (n > 32) {
+        const int ng = (n + 31) >> 5;
+        for (int it = warp; it < T * ng; it += NWARPS) {
+            const int t = it / ng, gi = it - t * ng, k = 32 * gi + lane;
+            const unsigned long long v = k < n ? cur[(size_t)t * stride + k] : empty_entry(0xc0000000u + (uint32_t)k);
+            const int r = rank_in_warp(v);
+            if (r < K) nxt[(size_t)t * stride + gi * K + r] = v;
+        }
+        __syncthreads();
+        unsigned long long* tmp = cur;
+        cur = nxt;
+        nxt = tmp;
+        n = ng * K;
+    }
+    // final part: warp t ranks token t's last <= 32 entries
+    for (int t = warp; t < T; t += NWARPS) {
+        const unsigned long long v = lane < n ? cur[(size_t)t * stride + lane] : empty_entry(0xc0000000u + lane);
+        const int r = rank_in_warp(v);
+        unsigned long long* fin = rs.fin + (size_t)t * MAXK;
+        if (r < K) fin[r] = v;
+        __syncwarp();
+        const unsigned long long w = lane < K ? fin[lane] : empty_entry(0xc0000000u + lane);
+        const uint32_t key = (uint32_t)(w >> 32);
+        const float* lt = rs.lg + (size_t)t * LS;
+        // a round without a candidate: id 0 and expert 0's value
+        float ex0 = 0.0f;
+        if (__any_sync(0xffffffffu, lane < K && key == 0u)) ex0 = rs.ex[(size_t)t * LS];
+        const float val = key ? __uint_as_float(key - 1u) : ex0;
+        const int id = key ? (int)(uint32_t)w : 0;
+        // top = sum of the winners' values in selection order, all = sum over every
+        // expert in id order (both f64, moe.zig:443-458)
+        double den;
+        if (norm_topk) {
+            double top = 0.0;
+            for (int z = 0; z < K; ++z) top = __dadd_rn(top, (double)__shfl_sync(0xffffffffu, val, z));
+            den = top;
+        } else {
+            double all = 0.0;
+            if (lane == 0)
+                for (int e = 0; e < E; ++e) all = __dadd_rn(all, (double)rs.ex[(size_t)t * LS + e]);
+            den = __shfl_sync(0xffffffffu, all, 0);
+        }
+        if (lane < K) {
+            const float g = __double2float_rn(__ddiv_rn((double)val, den));
+            s.pe[t * K + lane] = id;
+            s.pg[t * K + lane] = g;
+            if (write_out) {
+                if (topk_idx) topk_idx[(size_t)t * K + lane] = (uint32_t)id;
+                if (topk_gates) topk_gates[(size_t)t * K + lane] = g;
+            }
+        }
+        if (lane == 0 && has_shared) {
+            s.pe[T * K + t] = E;
+            s.pg[T * K + t] = cz_sigmoid(lt[E]);
+        }
+    }
+    __syncthreads();
+}
+
 // Named barriers between the consumer warps and the h warp (288 threads each):
 // RED_FULL(b): the consumers' partial gate/up sums of a chunk of parity b are in
-// red[b]; RED_FREE(b): the h warp has read them; H_WRITTEN: every h row of this
-// CTA is in global scratch.  D_GO (consumers only): the grid-wide h barrier has
-// passed.  The producer warp takes part in none of them: it may still be waiting
-// for ring slots that only phase D frees.
-constexpr int BAR_RED_FULL = 2, BAR_RED_FREE = 4, BAR_H_WRITTEN = 6, BAR_D_GO = 7;
+// red[b]; RED_FREE(b): the h warp has read them; H_DONE: the h warp has read
+// every chunk of this CTA (red is free for phase D).  The producer warp takes
+// part in none of them: it may still be waiting for ring slots that only phase D
+// frees.
+constexpr int BAR_RED_FULL = 2, BAR_RED_FREE = 4, BAR_H_DONE = 6;
 __device__ __forceinline__ void bar_sync_n(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "n"((NCW + 1) * 32) : "memory"); }
 __device__ __forceinline__ void bar_arrive_n(int id) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "n"((NCW + 1) * 32) : "memory"); }
-__device__ __forceinline__ void bar_sync_c(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "n"(NCW * 32) : "memory"); }
+
+// Bounded poll of tagged exchange words into f32 values.  Every thread polls its
+// words p[k] (k = tid, tid + NTHREADS, ... < n) until each carries `tag`, issuing
+// all of its loads before checking any.  Returns false if it gave up (spin limit,
+// or another warp of the CTA already gave up).
+template <int NPW>
+__device__ __noinline__ bool poll_words(const unsigned long long* __restrict__ src, int n, int row_words,
+                                        int src_stride, float* __restrict__ dst, int dst_stride, uint32_t tag,
+                                        uint32_t limit, DecodeMisc& s) {
+    const int tid = threadIdx.x;
+    uint32_t pend = 0;
+    const unsigned long long* a[NPW];
+    float* d[NPW];
+#pragma unroll
+    for (int i = 0; i < NPW; ++i) {
+        const int k = tid + i * NTHREADS;
+        a[i] = src;
+        d[i] = dst;
+        if (k < n) {
+            const int r = k / row_words, cix = k - r * row_words;
+            a[i] = src + (size_t)r * src_stride + cix;
+            d[i] = dst + (size_t)r * dst_stride + cix;
+            pend |= 1u << i;
+        }
+    }
+    for (uint32_t it = 0; pend && it < limit; ++it) {
+        unsigned long long w[NPW];
+#pragma unroll
+        for (int i = 0; i < NPW; ++i)
+            if (pend & (1u << i)) w[i] = ld_relaxed_u64(a[i]);
+#pragma unroll
+        for (int i = 0; i < NPW; ++i)
+            if ((pend & (1u << i)) && (uint32_t)(w[i] >> 32) == tag) {
+                *d[i] = __uint_as_float((uint32_t)w[i]);
+                pend &= ~(1u << i);
+            }
+        if (pend) {
+            if (*(volatile int*)&s.abort) break;
+            __nanosleep(it < 64 ? 20 : 200);
+        }
+    }
+    return pend == 0;
+}
 
 // One instance per token count: loop trip counts, fragment shapes and slab sizes
 // become constants, so each launch runs a short, branch-free path.
@@ -461,8 +567,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     uint8_t* const xterm = sb + cv.xterm;
     float* const red = reinterpret_cast<float*>(sb + cv.red);
     uint32_t* const err = p.sync + 1;
+    const uint32_t limit = p.spin_limit ? p.spin_limit : CZ_SPIN_LIMIT;
 
     const uint32_t seq = ld_relaxed_gpu(p.sync);
+    const uint32_t tag = seq + 1u;  // this launch's exchange tag (zeroed scratch never matches)
     uint32_t* reg = region(p.sync, seq & 1);
     if (c == 0 && tid < kSyncRegionWords) region(p.sync, (seq & 1) ^ 1)[tid] = 0u;
     if (tid == 0) {
@@ -471,7 +579,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
             mbar_init(&s.empty[i], NCW);
         }
         mbar_init(&s.rbar, 1);
-        mbar_init(&s.lbar, 1);
         s.abort = 0;
         fence_mbarrier_init();
     }
@@ -490,12 +597,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     if (tid == 0) {
         const uint32_t wbytes = p.rms_w ? (uint32_t)H * 4u : 0u;
         mbar_arrive_expect_tx(&s.rbar, xbytes + rbytes + wbytes);
-        bulk_g2s(xs, p.x, xbytes, &s.rbar);
-        if (wbytes) bulk_g2s(wnorm, p.rms_w, wbytes, &s.rbar);
         for (int r = 0; r < nrows; ++r) {
             const int e = row_lo + r;
             bulk_g2s(rows + (size_t)r * H, (e < E) ? p.router + (size_t)e * H : p.sh_gate, (uint32_t)H * 4u, &s.rbar);
         }
+        bulk_g2s(xs, p.x, xbytes, &s.rbar);
+        if (wbytes) bulk_g2s(wnorm, p.rms_w, wbytes, &s.rbar);
     }
     if (!mbar_wait_bounded(&s.rbar, 0, &s.abort) && lane == 0) set_error(err, s, CZ_DERR_FULL_WAIT);
     __syncthreads();
@@ -529,12 +636,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                    : reinterpret_cast<const float*>(xs)[k];
     };
     if (!s.abort) {
+        // each logit goes out as one tagged word the moment it is formed
         for (int it = warp; it < nrows * T; it += NWARPS) {
             const int r = it / T, t = it - r * T;
             const float* wr = rows + (size_t)r * H;
             const float v = xbf ? router_dot<true>(wr, xs + (size_t)t * H * 2, H, lane)
                                 : router_dot<false>(wr, xs + (size_t)t * H * 4, H, lane);
-            if (lane == 0) p.logits[(size_t)t * LS + row_lo + r] = v;
+            if (lane == 0 && !(p.dbg_hold && row_lo + r == 0))
+                st_relaxed_u64(p.logits + (size_t)t * LS + row_lo + r, tag_word(tag, v));
         }
         // max |x_t| for the per-token power-of-two prescale (one atomic per warp)
         for (int t = 0; t < T; ++t) {
@@ -548,12 +657,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         }
     }
     __syncthreads();
-    // this CTA's logits are written: arrive at the router counter now, so that the
-    // token term split below runs while the other CTAs finish theirs
-    if (tid == 0) {
-        __threadfence();
-        red_release_add_gpu(&reg[0], 1u);
-    }
     if (tid < T) {
         const int e = prescale_exp(__uint_as_float(s.xmax[tid]));
         s.xexp[tid] = e;
@@ -562,6 +665,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     __syncthreads();
     // Tokens as MMA columns: x_t * 2^s_t = term 0 + term 1 (+ term 2), E4M3.
     // Column (t, j) holds term j of token t, H bytes at xterm + (t*JX + j)*CS.
+    // This runs while the other CTAs still form their logits.
     if (!s.abort) {
         for (int t = 0; t < T; ++t) {
             const int sx = s.xexp[t];
@@ -575,36 +679,32 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
             }
         }
     }
-    __syncthreads();
-    if (tid == 0) {
-        if (!wait_geq_bounded(&reg[0], (uint32_t)G, err)) set_error(err, s, CZ_DERR_ROUTER_BARRIER);
-        if (!s.abort) {
-            // all logits -> shared memory (ring offset 0; the weight stream starts later)
-            fence_proxy_async_smem();
-            asm volatile("fence.proxy.async.global;" ::: "memory");
-            const uint32_t lbytes = (uint32_t)T * LS * 4u;
-            mbar_arrive_expect_tx(&s.lbar, lbytes);
-            bulk_g2s(ring, p.logits, lbytes, &s.lbar);
-        }
-    }
-    __syncthreads();
+    __syncthreads();  // the ring's tokens are dead from here on: it holds the routing scratch
 
-    // ---------------- phase K: top-k + grouping (every CTA) ----------------
-    if (!s.abort && !mbar_wait_bounded(&s.lbar, 0, &s.abort) && lane == 0) set_error(err, s, CZ_DERR_FULL_WAIT);
-    __syncthreads();
+    // ---------------- phase K: every logit of the grid, top-k, grouping (every CTA) ----------------
+    RouteScratch rs;
+    {
+        const int nch = (E + 31) >> 5;
+        const uint32_t lgb = ((uint32_t)T * LS * 4u + 15u) & ~15u;
+        const uint32_t cab = (uint32_t)T * nch * K * 8u;
+        rs.lg = reinterpret_cast<float*>(ring);
+        rs.ex = reinterpret_cast<float*>(ring + lgb);
+        rs.ca = reinterpret_cast<unsigned long long*>(ring + 2 * lgb);
+        rs.cb = reinterpret_cast<unsigned long long*>(ring + 2 * lgb + cab);
+        rs.fin = reinterpret_cast<unsigned long long*>(ring + 2 * lgb + 2 * cab);
+    }
     if (!s.abort) {
-        for (int t = warp; t < T; t += NWARPS) {
-            const float* lg = reinterpret_cast<const float*>(ring) + (size_t)t * LS;
-            if (E <= 32)
-                route_token<1>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates, c == 0);
-            else if (E <= 128)
-                route_token<4>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates, c == 0);
-            else
-                route_token<MAXE / 32>(lg, E, K, p.norm_topk, SI != 0, T, t, lane, s, p.topk_idx, p.topk_gates,
-                                       c == 0);
-        }
+        constexpr int NPW = (MAXT * (MAXE + 1) + NTHREADS - 1) / NTHREADS;
+        const bool ok = poll_words<(T * (MAXE + 1) + NTHREADS - 1) / NTHREADS <= NPW
+                                       ? (T * (MAXE + 1) + NTHREADS - 1) / NTHREADS
+                                       : NPW>(p.logits, T * Er, Er, LS, rs.lg, LS, tag, limit, s);
+        if (!ok) set_error(err, s, CZ_DERR_ROUTER_BARRIER);
     }
     __syncthreads();
+    if (!s.abort) route_all(rs, T, E, K, LS, p.norm_topk, SI != 0, s, p.topk_idx, p.topk_gates, c == 0);
+    // the ring held generic-proxy data (the routing scratch) and is next written by
+    // bulk copies: order every thread's accesses before them
+    fence_proxy_async_smem();
     if (!s.abort) {
         const int P = T * K + (SI ? T : 0);
         // sort pairs by (expert, pair) with ranks: P <= 68
@@ -622,11 +722,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     if (warp == 0) {
         if (!s.abort) {
             const int P = T * K + (SI ? T : 0);
-            // group starts: positions where the expert changes
+            // group starts: positions where the expert changes.  A token picks an
+            // expert at most once, except in selection rounds without a candidate
+            // (every remaining logit NaN), which all pick expert 0; a run longer than
+            // the gate/up MMA columns hold (cv.rc / JX pairs) is split into groups
+            // of that many pairs (each reads the expert's weights again).
+            const int maxq = cv.rc / cv.JX;
             int base = 0;
             for (int r0 = 0; r0 < P; r0 += 32) {
                 const int r = r0 + lane;
-                const bool start = r < P && (r == 0 || s.pe[s.order[r]] != s.pe[s.order[r - 1]]);
+                bool start = false;
+                if (r < P) {
+                    const int e = s.pe[s.order[r]];
+                    int rs0 = r;
+                    while (rs0 > 0 && s.pe[s.order[rs0 - 1]] == e) --rs0;
+                    start = (r - rs0) % maxq == 0;
+                }
                 const uint32_t m = __ballot_sync(0xffffffffu, start);
                 if (start) {
                     const int u = base + __popc(m & ((1u << lane) - 1u));
@@ -743,6 +854,37 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                     if (!ok && !s.abort) set_error(err, s, CZ_DERR_EMPTY_WAIT);
                     return ok;
                 };
+                // Once the ring is full (stage NS is next), everything this CTA streams
+                // later is prefetched into L2: the HBM reads of the whole layer call are
+                // then in flight from the start, and a stage issued when its slot frees
+                // up finds its bytes in L2.
+                const int nst = 2 * nks * (ch_hi - ch_lo);  // gate/up stages; the packs follow
+                auto prefetch_rest = [&]() {
+                    int u = 0;
+                    for (int ch = ch_lo; ch < ch_hi; ++ch) {
+                        while (s.g_chunk0[u + 1] <= ch) ++u;
+                        if (2 * nks * (ch - ch_lo + 1) <= NS) continue;  // inside the first ring fill
+                        const GroupW gw = group_w(p, s.g_expert[u]);
+                        const size_t r0 = (size_t)(ch - s.g_chunk0[u]) * CR;
+                        prefetch_l2(gw.gw + r0 * H, (uint32_t)(CR * H));  // 16 whole rows, contiguous
+                        prefetch_l2(gw.uw + r0 * H, (uint32_t)(CR * H));
+                    }
+                    if (drows > 0) {
+                        const int rb0 = o_lo >> 7, nrb = ((o_hi - 1) >> 7) - rb0 + 1;
+                        for (int v = 0; v < s.U; ++v) {
+                            if (s.g_pack[v] < 0 || nst + s.g_pack[v] < NS) continue;
+                            const int ev = s.g_expert[v];
+                            const bool sh = ev == E;
+                            const int iu = sh ? SI : Ir;
+                            prefetch_l2(sh ? p.sh_down_w + (size_t)o_lo * SI
+                                           : p.down_w + ((size_t)(ev - p.e_lo) * H + o_lo) * Ir,
+                                        (uint32_t)drows * (uint32_t)iu);
+                            prefetch_l2(sh ? p.sh_down_s + (size_t)rb0 * cz_nbp(SI)
+                                           : p.down_s + ((size_t)(ev - p.e_lo) * nkbH + rb0) * cz_nbp(Ir),
+                                        (uint32_t)(nrb * cz_nbp(iu) * 4));
+                        }
+                    }
+                };
                 // phase C: gate/up slabs of every chunk
                 {
                     int u = 0;
@@ -752,6 +894,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                         const int r0 = (ch - s.g_chunk0[u]) * CR;
                         for (int st = 0; st < 2 * nks && !s.abort; ++st, ++si) {
                             const int slot = si % NS;
+                            if (si == NS) prefetch_rest();
                             if (!acquire_slot(slot, si / NS)) break;
                             uint8_t* dst = ring + (size_t)slot * SLOT_BYTES;
                             float* sdst = reinterpret_cast<float*>(dst + GU_BYTES);
@@ -789,6 +932,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                             bytes += (uint32_t)(drows * iu + nrb * cz_nbp(iu) * 4);
                         }
                         const int slot = si % NS;
+                        if (si == NS) prefetch_rest();
                         if (!acquire_slot(slot, si / NS)) break;
                         uint8_t* dst = ring + (size_t)slot * SLOT_BYTES;
                         mbar_arrive_expect_tx(&s.full[slot], bytes);
@@ -838,12 +982,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 const int wst = 2 * 16 * cv.rc;  // floats of one warp's gate + up partial sums
                 const float* rb = red + b * (NCW * wst);
 #pragma unroll 1
-                for (int half = 0; half < (T + 1) / 2; ++half) {
-                    const int tk = 2 * half + (lane >> 4), r = lane & 15;
-                    int q = -1;
-                    for (int qq = 0; qq < np; ++qq)
-                        if (pair_token(pairs[qq], T, K) == tk) q = qq;
-                    if (q >= 0 && !s.abort) {
+                for (int q0 = 0; q0 < np; q0 += 2) {  // lanes: two pairs x 16 rows
+                    const int q = q0 + (lane >> 4), r = lane & 15;
+                    const int tk = q < np ? pair_token(pairs[q], T, K) : 0;
+                    if (q < np && !s.abort) {
                         float gs = 0.0f, us = 0.0f;
                         const float* rg = rb + r * cv.rc + q * cv.JX;
                         float gv[NCW][3], uv[NCW][3];
@@ -863,8 +1005,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                                     us += uv[w][j];
                                 }
                         const float xsc = s.xscale[tk];
-                        p.hrows[(size_t)pairs[q] * ldh + r0 + r] =
-                            s.pg[pairs[q]] * (silu_fast(gs * xsc) * (us * xsc));
+                        st_relaxed_u64(p.hrows + (size_t)pairs[q] * ldh + r0 + r,
+                                       tag_word(tag, s.pg[pairs[q]] * (silu_fast(gs * xsc) * (us * xsc))));
                     }
                 }
                 __threadfence_block();
@@ -1002,18 +1144,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         }
     }
 
-    // ---------------- every h row of every CTA is written ----------------
-    // H_WRITTEN orders the h warp's global writes before thread 0's release add (a
-    // release is cumulative over what the barrier ordered before it); the other CTAs
-    // acquire them through the counter.  No separate fence: one here waits for this SM's
-    // outstanding writes and measured 1.1 us on the critical path.  The producer keeps
-    // issuing the phase D packs meanwhile (it joins the block again at the end).
-    if (warp < NCW || warp == HW) bar_sync_n(BAR_H_WRITTEN);
-    if (tid == 0) {
-        red_release_add_gpu(&reg[2], 1u);
-        if (!wait_geq_bounded(&reg[2], (uint32_t)G, err)) set_error(err, s, CZ_DERR_READY_WAIT);
-    }
-    if (warp < NCW) bar_sync_c(BAR_D_GO);
+    // No grid-wide barrier: phase D reads every h row as tagged words and polls
+    // until each carries this launch's tag.  Only the h warp must be done reading
+    // red, which phase D reuses for the h terms.  The producer keeps issuing the
+    // phase D packs meanwhile (it joins the block again at the end).
+    if (warp < NCW || warp == HW) bar_sync_n(BAR_H_DONE);
 
     // ---------------- phase D: output rows [o_lo, o_hi) over every pair held here ----------------
     // Pair j (in group order) goes to consumer warp j % NCW.  For one pair and one row:
@@ -1053,17 +1188,43 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 // terms (22 bits) in this warp's share of the idle reduction buffer: words [0, iu/2)
                 // hi, [iu/2, iu) lo
                 const int pr = s.order[s.g_pair0[u] + q];
-                const float2* hrow = reinterpret_cast<const float2*>(p.hrows + (size_t)pr * ldh);
+                // The row is tagged words written by other CTAs' h warps: poll until every
+                // word carries this launch's tag (the first loads go out before the pack wait).
+                const unsigned long long* hrow = p.hrows + (size_t)pr * ldh;
                 const int nw2 = iu >> 1;
                 float2 hv[DHW / 64];
+                unsigned long long wa[DHW / 64], wb[DHW / 64];
+                uint32_t pend = 0;
 #pragma unroll
-                for (int j = 0; j < DHW / 64; ++j)
-                    hv[j] = lane + 32 * j < nw2 ? __ldcg(hrow + lane + 32 * j) : make_float2(0.f, 0.f);
+                for (int j = 0; j < DHW / 64; ++j) {
+                    hv[j] = make_float2(0.f, 0.f);
+                    if (lane + 32 * j < nw2) {
+                        pend |= 1u << j;
+                        ld_relaxed_u64x2(hrow + 2 * (lane + 32 * j), wa[j], wb[j]);
+                    }
+                }
                 release_to(pk);  // every earlier pack is done for this warp
                 const int sidx = si0 + pk;
                 if (ok) ok = warp_wait(&s.full[sidx % NS], (sidx / NS) & 1, s);
+                for (uint32_t it = 0; ok; ++it) {
+#pragma unroll
+                    for (int j = 0; j < DHW / 64; ++j)
+                        if ((pend & (1u << j)) && (uint32_t)(wa[j] >> 32) == tag && (uint32_t)(wb[j] >> 32) == tag) {
+                            hv[j] = make_float2(__uint_as_float((uint32_t)wa[j]), __uint_as_float((uint32_t)wb[j]));
+                            pend &= ~(1u << j);
+                        }
+                    if (__all_sync(0xffffffffu, pend == 0)) break;
+                    if (it >= limit || *(volatile int*)&s.abort) {
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(it < 64 ? 20 : 200);
+#pragma unroll
+                    for (int j = 0; j < DHW / 64; ++j)
+                        if (pend & (1u << j)) ld_relaxed_u64x2(hrow + 2 * (lane + 32 * j), wa[j], wb[j]);
+                }
                 if (!ok) {
-                    if (lane == 0 && !s.abort) set_error(err, s, CZ_DERR_FULL_WAIT);
+                    if (lane == 0 && !s.abort) set_error(err, s, CZ_DERR_READY_WAIT);
                     continue;
                 }
                 const uint8_t* wr = ring + (size_t)(sidx % NS) * SLOT_BYTES + s.g_poff[u];
@@ -1157,7 +1318,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     if (tid == 0) {
         __threadfence();
         const uint32_t old = atomicAdd(&reg[1], 1u);
-        if (old == (uint32_t)G - 1u) atomicExch(p.sync, seq + 1u);
+        if (old == (uint32_t)G - 1u) {
+            // every CTA has arrived, so every error bit is in the word
+            __threadfence();
+            if (p.status_out) *p.status_out = ld_relaxed_gpu(err);
+            atomicExch(p.sync, seq + 1u);
+        }
     }
 }
 

@@ -280,8 +280,10 @@ def stack_forward(first_layer: int, n_layers: int, h, norm_w=None, eps: float = 
 
 
 def check(stream=None) -> None:
-    """Raise if a device-side wait of an earlier asynchronous call gave up."""
-    h = None if stream is None else _stream_handle(stream)
+    """Raise if a device-side wait of an earlier asynchronous call gave up.  The
+    error word is read in order on `stream` (default: torch's current stream, the
+    one forward() launches on), so it sees every call issued there before."""
+    h = _stream_handle(stream) if torch is not None else None
     _abi.check("colizig_cuda_moe_check", _abi.load().colizig_cuda_moe_check(h))
 
 

@@ -155,7 +155,9 @@ int colizig_cuda_ep_init(int rank, int world, const void* id);
 int colizig_cuda_ep_shutdown(void);
 
 /* Device-side error word of the last asynchronous call(s) on the library's
- * MoE scratch (0 = none); reading it synchronises `stream` and clears it. */
+ * MoE scratch (0 = none); reading it synchronises `stream` (NULL = the default
+ * stream, as in the device-pointer forward) and clears it.  Returns 0, or -7
+ * when a bounded wait in a kernel gave up since the last read. */
 int colizig_cuda_moe_check(void* stream);
 
 /* No counterpart in the reference.  The same computation as
@@ -164,7 +166,7 @@ int colizig_cuda_moe_check(void* stream);
  * an engine that has already handed all of HBM to its own pool or to
  * colizig_cuda_set_vram_budget, or a decode loop where a cudaMalloc/cudaFree
  * (which synchronises the device) would stall every stream.  The scratch lives
- * in one static device array of 287,744 bytes inside the library, so no
+ * in one static device array of 574,336 bytes inside the library, so no
  * call allocates.  Limits: hidden <= 4096, experts <= 512, topk <= 16,
  * moe_intermediate and shared_intermediate <= 1024, a device of at most 160 SMs (launches of up to 4 tokens; larger T runs as
  * several launches); a layer beyond
@@ -201,6 +203,14 @@ int colizig_cuda_kernel_timer_read(int* kinds, float* ms, int max_n);
 /* Diagnostics used by the parity tests: the router's exp (the reference's
  * @exp(f32) restated in double precision) over n device floats. */
 int colizig_cuda_debug_expf(const float* x_dev, float* y_dev, size_t n);
+
+/* Failure-path test hook, no reference counterpart.  Arms a one-shot hold for
+ * the next decode launch: router row 0's logits are never published, so every
+ * CTA's bounded wait for them gives up after spin_limit polls (about 0.2 us
+ * each) and the call reports -7 (or the no-allocation call's status is
+ * non-zero).  Nothing faults or hangs; the next call starts clean.  0 ok, -1
+ * not initialised or spin_limit == 0. */
+int colizig_cuda_debug_hold_router(uint32_t spin_limit);
 
 #ifdef __cplusplus
 }

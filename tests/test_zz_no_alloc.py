@@ -68,6 +68,26 @@ def test_noalloc_matches_forward_two_calls_in_a_row(c2_layer, T, dtype):
         assert_close(out.cpu().numpy(), w_out.cpu().numpy(), OUT_TOL, f"call {i}")
 
 
+def test_noalloc_recovers_after_a_wait_gave_up(c2_layer):
+    """A launch whose bounded waits give up (router row 0 withheld by the
+    failure-path hook) reports it in status; the shared static scratch is left
+    ready, so the next call is clean and matches colizig_cuda_moe_forward."""
+    d, layer = c2_layer
+    x = synth.make_tokens(2, d.hidden, seed=4242, device="cuda", dtype=torch.bfloat16)
+    w_out, w_idx, w_g = moe.forward(layer, x)
+    out, idx, g = _outputs(2, d)
+    status = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    _abi.check("colizig_cuda_debug_hold_router", _abi.load().colizig_cuda_debug_hold_router(4000))
+    moe.forward_noalloc(layer, x, out, idx, g, status=status)
+    torch.cuda.synchronize()
+    assert status.item() != 0
+    moe.forward_noalloc(layer, x, out, idx, g, status=status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    assert torch.equal(idx, w_idx) and torch.equal(g, w_g)
+    assert_close(out.cpu().numpy(), w_out.cpu().numpy(), OUT_TOL, "after recovery")
+
+
 def test_noalloc_rejects_layer_beyond_static_scratch():
     torch.cuda.init()
     cz.gpu.init()
