@@ -201,6 +201,12 @@ CZ_DEV unsigned long long tag_word(uint32_t tag, float v) {
     return ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
 }
 
+// Prefetch of a tensor map (a __grid_constant__ kernel parameter) into the TMA
+// unit's descriptor cache.
+CZ_DEV void prefetch_tensormap(const void* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
 // L2 prefetch of `bytes` (a multiple of 16) from a 16-byte aligned global address.
 CZ_DEV void prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");

@@ -105,7 +105,8 @@ struct __align__(16) DecodeMisc {
     uint32_t xmax[MAXT];  // max |x_t| (f32 bits)
     int xexp[MAXT];       // s per token (terms hold x_t * 2^s)
     float xscale[MAXT];   // 2^-s per token
-    float mxs[MAXT];      // max logit per token (routing)
+    int fastgroup;        // the groups were formed by the top-k warp (one token, distinct experts)
+    int geo_drows, geo_nrb, geo_rbytes, geo_per;  // phase D geometry of this CTA (output rows, packs)
     int pe[MAXP];         // expert of pair p = t*K + z (shared: p = T*K + t -> E)
     float pg[MAXP];       // gate of pair p
     int order[MAXP];      // pairs sorted by (expert, pair)
@@ -297,10 +298,9 @@ __device__ __forceinline__ uint16_t e4m3_term2(float& a, float& b) {
 
 // Router dot of one row with one token, in dotF32's exact order (lane l holds
 // chain l: elements l, l+32, ...; then the lane-ordered combine and the FMA
-// tail).  wrow / xs are shared memory.  Returns the logit in every lane.  Kept
-// rolled and out of line: it runs once per launch, fetched cold.
+// tail).  wrow / xs are shared memory.  Returns the logit in every lane.
 template <bool BF16>
-__device__ __noinline__ float router_dot(const float* __restrict__ wrow, const uint8_t* __restrict__ xs, int H,
+__device__ __forceinline__ float router_dot(const float* __restrict__ wrow, const uint8_t* __restrict__ xs, int H,
                                          int lane) {
     auto xv = [&](int i) -> float {
         return BF16 ? __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(xs)[i] << 16)
@@ -330,9 +330,12 @@ __device__ __noinline__ float router_dot(const float* __restrict__ wrow, const u
     const float a16 = __shfl_down_sync(0xffffffffu, acc, 16);
     const float a24 = __shfl_down_sync(0xffffffffu, acc, 24);
     const float tl = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, acc), a8), a16), a24);
-    float sum = __shfl_sync(0xffffffffu, tl, 0);
-#pragma unroll 1
-    for (int l = 1; l < 8; ++l) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, tl, l));
+    float tv[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) tv[l] = __shfl_sync(0xffffffffu, tl, l);  // independent: issued together
+    float sum = tv[0];
+#pragma unroll
+    for (int l = 1; l < 8; ++l) sum = __fadd_rn(sum, tv[l]);
 #pragma unroll 1
     for (; i < H; ++i) sum = __fmaf_rn(xv(i), wrow[i], sum);
     return sum;
@@ -399,22 +402,33 @@ struct RouteScratch {
     unsigned long long* fin;  // [T][MAXK] the winners in selection order
 };
 
+// Largest non-NaN value of the warp (NaN when every lane holds NaN): the
+// reference's @max fold over the logits (moe.zig:441), one instruction.
+__device__ __forceinline__ float warp_max_f32(float v) {
+    float r;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+    return r;
+}
+
 // Top-k of every token by the whole CTA (all threads call it).  Writes s.pe /
 // s.pg (pair p = t*K + z, shared-expert pairs p = T*K + t) and, from CTA 0, the
-// caller's top-k outputs.
-__device__ __noinline__ void route_all(const RouteScratch& rs, int T, int E, int K, int LS, int norm_topk,
+// caller's top-k outputs.  Token t's results are written by warp t % NWARPS; the
+// caller synchronises before other warps read them.
+__device__ __forceinline__ void route_all(const RouteScratch& rs, int T, int E, int K, int LS, int norm_topk,
                                        int has_shared, DecodeMisc& s, uint32_t* topk_idx, float* topk_gates,
                                        bool write_out) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nch = (E + 31) >> 5;
-    // stage 1: (token, 32 experts) per warp; exps computed in parallel over the CTA
+    const int stride = nch * K;  // entries per token in the candidate buffers
+    // stage 1: (token, 32 experts) per warp.  The exps of a token are computed by
+    // several warps side by side; inside a part the ids follow the lanes, so one
+    // 32-bit shuffle per lane ranks it.
     for (int it = warp; it < T * nch; it += NWARPS) {
         const int t = it / nch, j = it - t * nch;
         const float* l = rs.lg + (size_t)t * LS;
-        float mx = __int_as_float(0xffc00000);  // NaN: fmaxf ignores it (@max over the row)
+        float mx = __int_as_float(0xffc00000);  // NaN: fmaxf and the reduction ignore it
         for (int e = lane; e < E; e += 32) mx = fmaxf(mx, l[e]);
-        mx = warp_max(mx);
-        if (j == 0 && lane == 0) s.mxs[t] = mx;
+        mx = warp_max_f32(mx);
         const int e = 32 * j + lane;
         uint32_t key = 0u;
         if (e < E) {
@@ -422,16 +436,19 @@ __device__ __noinline__ void route_all(const RouteScratch& rs, int T, int E, int
             key = ex > -1.0f ? __float_as_uint(ex) + 1u : 0u;
             rs.ex[(size_t)t * LS + e] = ex;
         }
-        const unsigned long long v = route_entry(key, e < E ? (uint32_t)e : 0x80000000u + (uint32_t)e);
-        const int r = rank_in_warp(v);
-        if (r < K) rs.ca[((size_t)t * nch + j) * K + r] = v;
+        int r = 0;
+#pragma unroll
+        for (int m = 0; m < 32; ++m) {
+            const uint32_t km = __shfl_sync(0xffffffffu, key, m);
+            r += (km > key) | ((km == key) & (m < lane));
+        }
+        if (r < K) rs.ca[((size_t)t * nch + j) * K + r] = route_entry(key, e < E ? (uint32_t)e : 0x80000000u + (uint32_t)e);
     }
     __syncthreads();
     // merge rounds: parts of 32 survivors -> their top K, until one part is left
     unsigned long long* cur = rs.ca;
     unsigned long long* nxt = rs.cb;
-    int n = nch * K;  // entries per token in cur
-    const int stride = nch * K;
+    int n = stride;
     while (n > 32) {
         const int ng = (n + 31) >> 5;
         for (int it = warp; it < T * ng; it += NWARPS) {
@@ -455,24 +472,22 @@ __device__ __noinline__ void route_all(const RouteScratch& rs, int T, int E, int
         __syncwarp();
         const unsigned long long w = lane < K ? fin[lane] : empty_entry(0xc0000000u + lane);
         const uint32_t key = (uint32_t)(w >> 32);
-        const float* lt = rs.lg + (size_t)t * LS;
         // a round without a candidate: id 0 and expert 0's value
-        float ex0 = 0.0f;
-        if (__any_sync(0xffffffffu, lane < K && key == 0u)) ex0 = rs.ex[(size_t)t * LS];
-        const float val = key ? __uint_as_float(key - 1u) : ex0;
+        const float val = key ? __uint_as_float(key - 1u) : rs.ex[(size_t)t * LS];
         const int id = key ? (int)(uint32_t)w : 0;
         // top = sum of the winners' values in selection order, all = sum over every
         // expert in id order (both f64, moe.zig:443-458)
-        double den;
+        double den = 0.0;
         if (norm_topk) {
-            double top = 0.0;
-            for (int z = 0; z < K; ++z) top = __dadd_rn(top, (double)__shfl_sync(0xffffffffu, val, z));
-            den = top;
+#pragma unroll
+            for (int z = 0; z < MAXK; ++z) {
+                const float vz = __shfl_sync(0xffffffffu, val, z);
+                if (z < K) den = __dadd_rn(den, (double)vz);
+            }
         } else {
-            double all = 0.0;
             if (lane == 0)
-                for (int e = 0; e < E; ++e) all = __dadd_rn(all, (double)rs.ex[(size_t)t * LS + e]);
-            den = __shfl_sync(0xffffffffu, all, 0);
+                for (int e = 0; e < E; ++e) den = __dadd_rn(den, (double)rs.ex[(size_t)t * LS + e]);
+            den = __shfl_sync(0xffffffffu, den, 0);
         }
         if (lane < K) {
             const float g = __double2float_rn(__ddiv_rn((double)val, den));
@@ -485,10 +500,9 @@ __device__ __noinline__ void route_all(const RouteScratch& rs, int T, int E, int
         }
         if (lane == 0 && has_shared) {
             s.pe[T * K + t] = E;
-            s.pg[T * K + t] = cz_sigmoid(lt[E]);
+            s.pg[T * K + t] = cz_sigmoid(rs.lg[(size_t)t * LS + E]);
         }
     }
-    __syncthreads();
 }
 
 // Named barriers between the consumer warps and the h warp (288 threads each):
@@ -506,7 +520,7 @@ __device__ __forceinline__ void bar_arrive_n(int id) { asm volatile("bar.arrive 
 // all of its loads before checking any.  Returns false if it gave up (spin limit,
 // or another warp of the CTA already gave up).
 template <int NPW>
-__device__ __noinline__ bool poll_words(const unsigned long long* __restrict__ src, int n, int row_words,
+__device__ __forceinline__ bool poll_words(const unsigned long long* __restrict__ src, int n, int row_words,
                                         int src_stride, float* __restrict__ dst, int dst_stride, uint32_t tag,
                                         uint32_t limit, DecodeMisc& s) {
     const int tid = threadIdx.x;
@@ -603,6 +617,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         }
         bulk_g2s(xs, p.x, xbytes, &s.rbar);
         if (wbytes) bulk_g2s(wnorm, p.rms_w, wbytes, &s.rbar);
+    } else if (tid == 64) {
+        // phase D geometry of this CTA: output rows [o_lo, o_hi), their row blocks, the
+        // bytes one routed group's rows take in a pack, and the groups a pack holds
+        const int o_lo = split_at(c, H, G), o_hi = split_at(c + 1, H, G);
+        const int drows = o_hi - o_lo;
+        const int nrb = drows > 0 ? ((o_hi - 1) >> 7) - (o_lo >> 7) + 1 : 0;
+        const int rbytes = drows * Ir + nrb * cz_nbp(Ir) * 4;
+        s.geo_drows = drows;
+        s.geo_nrb = nrb;
+        s.geo_rbytes = rbytes;
+        s.geo_per = drows > 0 ? SLOT_BYTES / rbytes : 1;
+    } else if (tid == 32) {
+        // the weight stream's tensor maps: fetched now, not at the first weight copy
+        prefetch_tensormap(&p.gate_map);
+        prefetch_tensormap(&p.up_map);
+        if (SI) {
+            prefetch_tensormap(&p.sh_gate_map);
+            prefetch_tensormap(&p.sh_up_map);
+        }
     }
     if (!mbar_wait_bounded(&s.rbar, 0, &s.abort) && lane == 0) set_error(err, s, CZ_DERR_FULL_WAIT);
     __syncthreads();
@@ -635,49 +668,57 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         return xbf ? __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(xs)[k] << 16)
                    : reinterpret_cast<const float*>(xs)[k];
     };
+    // max |x_t| for the per-token power-of-two prescale (one atomic per warp)
     if (!s.abort) {
-        // each logit goes out as one tagged word the moment it is formed
-        for (int it = warp; it < nrows * T; it += NWARPS) {
-            const int r = it / T, t = it - r * T;
-            const float* wr = rows + (size_t)r * H;
-            const float v = xbf ? router_dot<true>(wr, xs + (size_t)t * H * 2, H, lane)
-                                : router_dot<false>(wr, xs + (size_t)t * H * 4, H, lane);
-            if (lane == 0 && !(p.dbg_hold && row_lo + r == 0))
-                st_relaxed_u64(p.logits + (size_t)t * LS + row_lo + r, tag_word(tag, v));
-        }
-        // max |x_t| for the per-token power-of-two prescale (one atomic per warp)
         for (int t = 0; t < T; ++t) {
             float m = 0.0f;
             for (int i = tid; i < H; i += NTHREADS) {
                 const float a = fabsf(xval(t * H + i));
                 if (a < 3.0e38f) m = fmaxf(m, a);
             }
-            m = warp_max(m);
+            m = warp_max_f32(m);
             if (lane == 0 && m > 0.0f) atomicMax(&s.xmax[t], __float_as_uint(m));
         }
     }
     __syncthreads();
+    // The first nd warps form the router logits (one (row, token) item each, in
+    // turn); each logit goes out as one tagged word the moment it is formed.  The
+    // other warps split the tokens into E4M3 terms meanwhile:
+    //   x_t * 2^s_t = term 0 + term 1 (+ term 2), column (t, j) holding term j of
+    //   token t, H bytes at xterm + (t*JX + j)*CS.
+    const int nitems = nrows * T;
+    const int nd = nitems < NWARPS ? nitems : NWARPS;
+    if (!s.abort) {
+        if (warp < nd) {
+            for (int it = warp; it < nitems; it += NWARPS) {
+                const int r = it / T, t = it - r * T;
+                const float* wr = rows + (size_t)r * H;
+                const float v = xbf ? router_dot<true>(wr, xs + (size_t)t * H * 2, H, lane)
+                                    : router_dot<false>(wr, xs + (size_t)t * H * 4, H, lane);
+                if (lane == 0 && !(p.dbg_hold && row_lo + r == 0))
+                    st_relaxed_u64(p.logits + (size_t)t * LS + row_lo + r, tag_word(tag, v));
+            }
+        }
+        if (warp >= nd || nd == NWARPS) {
+            const int nsw = nd == NWARPS ? NWARPS : NWARPS - nd;  // warps on the split
+            const int st0 = (nd == NWARPS ? warp : warp - nd) * 32 + lane;
+            for (int t = 0; t < T; ++t) {
+                const int sx = prescale_exp(__uint_as_float(s.xmax[t]));
+                uint8_t* col = xterm + (size_t)(t * cv.JX) * cv.CS;
+                for (int i = 2 * st0; i < H; i += 2 * 32 * nsw) {
+                    float a = scale2(xval(t * H + i), sx), b = scale2(xval(t * H + i + 1), sx);
+                    for (int j = 0; j < cv.JX; ++j) {
+                        const uint16_t d = e4m3_term2(a, b);
+                        *reinterpret_cast<uint16_t*>(col + (size_t)j * cv.CS + i) = d;
+                    }
+                }
+            }
+        }
+    }
     if (tid < T) {
         const int e = prescale_exp(__uint_as_float(s.xmax[tid]));
         s.xexp[tid] = e;
         s.xscale[tid] = scale2(1.0f, -e);
-    }
-    __syncthreads();
-    // Tokens as MMA columns: x_t * 2^s_t = term 0 + term 1 (+ term 2), E4M3.
-    // Column (t, j) holds term j of token t, H bytes at xterm + (t*JX + j)*CS.
-    // This runs while the other CTAs still form their logits.
-    if (!s.abort) {
-        for (int t = 0; t < T; ++t) {
-            const int sx = s.xexp[t];
-            uint8_t* col = xterm + (size_t)(t * cv.JX) * cv.CS;
-            for (int i = 2 * tid; i < H; i += 2 * NTHREADS) {
-                float a = scale2(xval(t * H + i), sx), b = scale2(xval(t * H + i + 1), sx);
-                for (int j = 0; j < cv.JX; ++j) {
-                    const uint16_t d = e4m3_term2(a, b);
-                    *reinterpret_cast<uint16_t*>(col + (size_t)j * cv.CS + i) = d;
-                }
-            }
-        }
     }
     __syncthreads();  // the ring's tokens are dead from here on: it holds the routing scratch
 
@@ -694,118 +735,191 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         rs.fin = reinterpret_cast<unsigned long long*>(ring + 2 * lgb + 2 * cab);
     }
     if (!s.abort) {
-        constexpr int NPW = (MAXT * (MAXE + 1) + NTHREADS - 1) / NTHREADS;
-        const bool ok = poll_words<(T * (MAXE + 1) + NTHREADS - 1) / NTHREADS <= NPW
-                                       ? (T * (MAXE + 1) + NTHREADS - 1) / NTHREADS
-                                       : NPW>(p.logits, T * Er, Er, LS, rs.lg, LS, tag, limit, s);
-        if (!ok) set_error(err, s, CZ_DERR_ROUTER_BARRIER);
+        constexpr int NPW = (T * (MAXE + 1) + NTHREADS - 1) / NTHREADS;
+        if (!poll_words<NPW>(p.logits, T * Er, Er, LS, rs.lg, LS, tag, limit, s))
+            set_error(err, s, CZ_DERR_ROUTER_BARRIER);
     }
     __syncthreads();
-    if (!s.abort) route_all(rs, T, E, K, LS, p.norm_topk, SI != 0, s, p.topk_idx, p.topk_gates, c == 0);
+    const int P = T * K + (SI ? T : 0);
+    if (tid == 0) s.fastgroup = 0;
+    if (!s.abort) {
+        route_all(rs, T, E, K, LS, p.norm_topk, SI != 0, s, p.topk_idx, p.topk_gates, c == 0);
+        if (T == 1 && warp == 0) {
+            // One token: its K experts are distinct unless a selection round found no
+            // candidate (NaN logits), so each pair is a group of its own, in ascending
+            // expert order.  The warp that ranked the token forms the groups in a few
+            // shuffles; duplicates fall through to the general path below.
+            __syncwarp();
+            const bool act = lane < K;
+            const int myid = act ? s.pe[lane] : 0x7fffffff;
+            int rho = 0;
+            bool dup = false;
+#pragma unroll
+            for (int m = 0; m < MAXK; ++m) {
+                const int im = __shfl_sync(0xffffffffu, myid, m);
+                rho += (m < K) & (im < myid);
+                dup |= act & (m < K) & (m != lane) & (im == myid);
+            }
+            if (!__any_sync(0xffffffffu, dup)) {
+                const int drows = s.geo_drows, per = s.geo_per, rbytes = s.geo_rbytes;
+                const bool held = act && myid >= p.e_lo && myid < p.e_hi;
+                const uint32_t hm = __reduce_or_sync(0xffffffffu, held ? (1u << rho) : 0u);
+                const int k = __popc(hm & ((1u << rho) - 1u));  // index among held routed groups
+                const int nr = __popc(hm);
+                if (act) {
+                    s.g_expert[rho] = myid;
+                    s.g_pair0[rho] = rho;
+                    s.g_npairs[rho] = 1;
+                    s.order[rho] = lane;
+                    s.rtok[rho] = held ? 0 : -1;
+                    s.g_chunk0[rho] = k * (Ir / CR);
+                    s.g_pack[rho] = held && drows > 0 ? k / per : -1;
+                    s.g_poff[rho] = held && drows > 0 ? (k % per) * rbytes : 0;
+                }
+                if (lane == 0) {
+                    int U = K, nc = nr * (Ir / CR);
+                    int npk = nr > 0 && drows > 0 ? (nr - 1) / per + 1 : 0;
+                    if (SI) {  // the shared expert: pair T*K = K, the last group
+                        s.g_expert[K] = E;
+                        s.g_pair0[K] = K;
+                        s.g_npairs[K] = 1;
+                        s.order[K] = K;
+                        s.rtok[K] = p.shared_here ? 0 : -1;
+                        s.g_chunk0[K] = nc;
+                        s.g_pack[K] = -1;
+                        s.g_poff[K] = 0;
+                        if (p.shared_here) {
+                            nc += SI / CR;
+                            if (drows > 0) {
+                                const int sbytes = drows * SI + s.geo_nrb * cz_nbp(SI) * 4;
+                                const int fill = nr > 0 ? (nr - (npk - 1) * per) * rbytes : SLOT_BYTES;
+                                if (npk > 0 && fill + sbytes <= SLOT_BYTES) {
+                                    s.g_pack[K] = npk - 1;
+                                    s.g_poff[K] = fill;
+                                } else {
+                                    s.g_pack[K] = npk;
+                                    ++npk;
+                                }
+                            }
+                        }
+                        U = K + 1;
+                    }
+                    if (p.hslot && npk > cv.ns - 1) set_error(err, s, CZ_DERR_SHAPE);
+                    s.g_chunk0[U] = nc;
+                    s.U = U;
+                    s.P = P;
+                    s.NC = nc;
+                    s.npk = npk;
+                    s.fastgroup = 1;
+                }
+            }
+        }
+    }
     // the ring held generic-proxy data (the routing scratch) and is next written by
     // bulk copies: order every thread's accesses before them
     fence_proxy_async_smem();
-    if (!s.abort) {
-        const int P = T * K + (SI ? T : 0);
-        // sort pairs by (expert, pair) with ranks: P <= 68
+    __syncthreads();
+    if (!s.abort && !s.fastgroup) {
+        // pairs sorted by (expert, pair) with ranks: P <= 68
         for (int i = tid; i < P; i += NTHREADS) {
             const int e = s.pe[i];
             int r = 0;
             for (int j = 0; j < P; ++j) {
                 const int ej = s.pe[j];
-                r += (ej < e) || (ej == e && j < i);
+                r += (ej < e) | ((ej == e) & (j < i));
             }
             s.order[r] = i;
         }
     }
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 0 && !s.fastgroup) {
         if (!s.abort) {
-            const int P = T * K + (SI ? T : 0);
-            // group starts: positions where the expert changes.  A token picks an
-            // expert at most once, except in selection rounds without a candidate
-            // (every remaining logit NaN), which all pick expert 0; a run longer than
-            // the gate/up MMA columns hold (cv.rc / JX pairs) is split into groups
-            // of that many pairs (each reads the expert's weights again).
+            // Groups: runs of one expert in sorted order.  A token picks an expert at
+            // most once, except in selection rounds without a candidate (every
+            // remaining logit NaN), which all pick expert 0; a run longer than the
+            // gate/up MMA columns hold (maxq pairs) is split into groups of maxq pairs
+            // (each reads the expert's weights again).  Up to 3 sorted positions per
+            // lane: r = 32 w + lane.
             const int maxq = cv.rc / cv.JX;
+            int pe_r[3];
+            uint32_t chg[3];
+#pragma unroll
+            for (int w = 0; w < 3; ++w) {
+                const int r = 32 * w + lane;
+                pe_r[w] = r < P ? s.pe[s.order[r]] : -1;
+                const int prev = __shfl_up_sync(0xffffffffu, pe_r[w], 1);
+                const int prev_w = w > 0 ? __shfl_sync(0xffffffffu, pe_r[w > 0 ? w - 1 : 0], 31) : -1;
+                const int pv = lane == 0 ? prev_w : prev;
+                chg[w] = __ballot_sync(0xffffffffu, r < P && (r == 0 || pe_r[w] != pv));
+            }
+            // a position starts a group when its distance to its run's first position
+            // is a multiple of maxq
+            uint32_t stw[3];
+            int u_base[3];
             int base = 0;
-            for (int r0 = 0; r0 < P; r0 += 32) {
-                const int r = r0 + lane;
-                bool start = false;
-                if (r < P) {
-                    const int e = s.pe[s.order[r]];
-                    int rs0 = r;
-                    while (rs0 > 0 && s.pe[s.order[rs0 - 1]] == e) --rs0;
-                    start = (r - rs0) % maxq == 0;
+#pragma unroll
+            for (int w = 0; w < 3; ++w) {
+                const int r = 32 * w + lane;
+                int rs0 = -1;  // the run's first position: the last change at or before r
+                const uint32_t below = lane == 31 ? 0xffffffffu : ((2u << lane) - 1u);
+#pragma unroll
+                for (int v = w; v >= 0; --v) {
+                    const uint32_t m = v == w ? (chg[v] & below) : chg[v];
+                    if (rs0 < 0 && m) rs0 = 32 * v + 31 - __clz(m);
                 }
-                const uint32_t m = __ballot_sync(0xffffffffu, start);
+                const bool start = r < P && (r - rs0) % maxq == 0;
+                stw[w] = __ballot_sync(0xffffffffu, start);
+                u_base[w] = base;
                 if (start) {
-                    const int u = base + __popc(m & ((1u << lane) - 1u));
-                    s.g_expert[u] = s.pe[s.order[r]];
+                    const int u = base + __popc(stw[w] & ((1u << lane) - 1u));
+                    s.g_expert[u] = pe_r[w];
                     s.g_pair0[u] = r;
                 }
-                base += __popc(m);
+                base += __popc(stw[w]);
             }
             __syncwarp();
-            for (int u = lane; u < base; u += 32) {
-                const int end = (u + 1 < base) ? s.g_pair0[u + 1] : P;
-                s.g_npairs[u] = end - s.g_pair0[u];
-            }
-            __syncwarp();
-            for (int u = lane; u < base; u += 32) {  // token of every sorted pair of a group held here
-                const int eu = s.g_expert[u];
-                const bool here = eu == E ? p.shared_here != 0 : (eu >= p.e_lo && eu < p.e_hi);
-                for (int q = 0; q < s.g_npairs[u]; ++q)
-                    s.rtok[s.g_pair0[u] + q] = here ? pair_token(s.order[s.g_pair0[u] + q], T, K) : -1;
-            }
-            // first chunk of every group (a warp scan) and phase D's packs: this CTA's output
-            // rows of every group held here, groups in order, as many per ring stage as fit.
-            // Routed groups all take rb bytes, so the greedy packing puts `per` of them in a
-            // pack; the shared expert (the last group) joins the last pack if it fits.
-            const int o_lo = split_at(c, H, G), o_hi = split_at(c + 1, H, G);
-            const int drows = o_hi - o_lo;
-            const int nrb = drows > 0 ? ((o_hi - 1) >> 7) - (o_lo >> 7) + 1 : 0;
-            const int rbytes = drows * Ir + nrb * cz_nbp(Ir) * 4;
-            const int per = drows > 0 ? SLOT_BYTES / rbytes : 1;
-            int nc = 0, nr = 0;  // chunks and held routed groups before this batch of 32 groups
-            for (int u0 = 0; u0 < base; u0 += 32) {
-                const int u = u0 + lane;
-                const int eu = u < base ? s.g_expert[u] : -1;
-                const bool here = u < base && (eu == E ? p.shared_here != 0 : (eu >= p.e_lo && eu < p.e_hi));
-                const bool routed = here && eu != E;
-                const int n = here ? (eu == E ? SI : Ir) / CR : 0;
-                int x = n;
+            // per group (up to 3 per lane, u = 32 v + lane): size, held here, first
+            // chunk, phase D pack.  Routed groups all have Ir/CR chunks and rb bytes
+            // of down rows per pack; the shared expert (expert E) is the last group.
+            const int drows = s.geo_drows, nrb = s.geo_nrb, rbytes = s.geo_rbytes, per = s.geo_per;
+            int nr = 0;  // held routed groups before this batch
 #pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int y = __shfl_up_sync(0xffffffffu, x, o);
-                    if (lane >= o) x += y;
-                }
+            for (int v = 0; v < 3; ++v) {
+                const int u = 32 * v + lane;
+                const bool in = u < base;
+                const int eu = in ? s.g_expert[u] : -1;
+                const int p0 = in ? s.g_pair0[u] : 0;
+                const int p1 = u + 1 < base ? s.g_pair0[u + 1] : P;
+                const bool here = in && (eu == E ? p.shared_here != 0 : (eu >= p.e_lo && eu < p.e_hi));
+                const bool routed = here && eu != E;
                 const uint32_t rm = __ballot_sync(0xffffffffu, routed);
                 const int k = nr + __popc(rm & ((1u << lane) - 1u));  // index among held routed groups
-                if (u < base) {
-                    s.g_chunk0[u] = nc + x - n;
-                    s.g_pack[u] = -1;
-                    if (routed && drows > 0) {
-                        s.g_pack[u] = k / per;
-                        s.g_poff[u] = (k % per) * rbytes;
-                    }
+                if (in) {
+                    s.g_npairs[u] = p1 - p0;
+                    s.g_chunk0[u] = k * (Ir / CR);
+                    s.g_pack[u] = routed && drows > 0 ? k / per : -1;
+                    s.g_poff[u] = routed && drows > 0 ? (k % per) * rbytes : 0;
+                    for (int q = p0; q < p1; ++q) s.rtok[q] = here ? pair_token(s.order[q], T, K) : -1;
                 }
-                nc += __shfl_sync(0xffffffffu, x, 31);
                 nr += __popc(rm);
             }
             __syncwarp();
             if (lane == 0) {
+                int nc = nr * (Ir / CR);
                 int npk = nr > 0 && drows > 0 ? (nr - 1) / per + 1 : 0;
-                if (base > 0 && s.g_expert[base - 1] == E && p.shared_here && drows > 0) {
-                    const int sbytes = drows * SI + nrb * cz_nbp(SI) * 4;
-                    const int fill = nr > 0 ? (nr - (npk - 1) * per) * rbytes : SLOT_BYTES;
-                    if (npk > 0 && fill + sbytes <= SLOT_BYTES) {
-                        s.g_pack[base - 1] = npk - 1;
-                        s.g_poff[base - 1] = fill;
-                    } else {
-                        s.g_pack[base - 1] = npk;
-                        s.g_poff[base - 1] = 0;
-                        ++npk;
+                if (base > 0 && s.g_expert[base - 1] == E && p.shared_here) {
+                    nc += SI / CR;
+                    if (drows > 0) {
+                        const int sbytes = drows * SI + nrb * cz_nbp(SI) * 4;
+                        const int fill = nr > 0 ? (nr - (npk - 1) * per) * rbytes : SLOT_BYTES;
+                        if (npk > 0 && fill + sbytes <= SLOT_BYTES) {
+                            s.g_pack[base - 1] = npk - 1;
+                            s.g_poff[base - 1] = fill;
+                        } else {
+                            s.g_pack[base - 1] = npk;
+                            s.g_poff[base - 1] = 0;
+                            ++npk;
+                        }
                     }
                 }
                 // hslot: the slot after the last pack must be free (the host checked the worst case)
