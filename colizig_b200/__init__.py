@@ -12,12 +12,14 @@ the reference's host-side interfaces:
                               (src/qwen3moe/model.zig:227-232)
   ep    expert parallelism over the GPUs of one node (partition of moe.zig's
         experts; NCCL all-reduce inside the library)
+  checkpoint  src/model/weights.zig + moe.zig Layer.load / loadExpert: one MoE
+        layer from safetensors shards straight into resident device memory
 
 There is no CPU fallback: if the library is missing or a call fails, an
 exception is raised.
 """
 
-from . import _abi, ep, fp8, gpu, moe  # noqa: F401
+from . import _abi, checkpoint, ep, fp8, gpu, moe  # noqa: F401
 from ._abi import ColizigError  # noqa: F401
 
-__all__ = ["gpu", "fp8", "moe", "ep", "ColizigError"]
+__all__ = ["gpu", "fp8", "moe", "ep", "checkpoint", "ColizigError"]

@@ -27,6 +27,7 @@ MOE_SYMBOLS = (
     "colizig_cuda_init_device",
     "colizig_cuda_moe_register_layer",
     "colizig_cuda_moe_unregister_layer",
+    "colizig_cuda_moe_load_safetensors",
     "colizig_cuda_moe_forward",
     "colizig_cuda_moe_stack_forward",
     "colizig_cuda_moe_check",
@@ -56,6 +57,7 @@ ERRORS = {
     -7: "device-side wait timed out",
     -8: "shape not supported",
     -9: "NCCL / expert-parallel error",
+    -10: "checkpoint file missing, unreadable or malformed, or a tensor missing",
 }
 
 
@@ -125,6 +127,9 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
                                                       ctypes.POINTER(MoeExpert), vp, u32]
         L.colizig_cuda_moe_unregister_layer.restype = i32
         L.colizig_cuda_moe_unregister_layer.argtypes = [u32]
+        L.colizig_cuda_moe_load_safetensors.restype = i32
+        L.colizig_cuda_moe_load_safetensors.argtypes = [u32, ctypes.POINTER(ctypes.c_char_p), i32, ctypes.c_char_p, u32,
+                                                        ctypes.POINTER(MoeDims), u32]
         L.colizig_cuda_moe_forward.restype = i32
         L.colizig_cuda_moe_forward.argtypes = [u32, vp, i32, i32, vp, vp, vp, u32, vp]
         L.colizig_cuda_moe_stack_forward.restype = i32

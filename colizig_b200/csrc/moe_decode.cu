@@ -106,6 +106,9 @@ struct __align__(16) DecodeMisc {
     int xexp[MAXT];       // s per token (terms hold x_t * 2^s)
     float xscale[MAXT];   // 2^-s per token
     int fastgroup;        // the groups were formed by the top-k warp (one token, distinct experts)
+    int exact[MAXT];      // token t was routed by the exact exp-keyed selection (its gates are set)
+    float pd[MAXP];       // logit - max of the winner of pair p (the gates are formed from it later)
+    float shlog[MAXT];    // the shared expert's gate logit per token
     int geo_drows, geo_nrb, geo_rbytes, geo_per;  // phase D geometry of this CTA (output rows, packs)
     int pe[MAXP];         // expert of pair p = t*K + z (shared: p = T*K + t -> E)
     float pg[MAXP];       // gate of pair p
@@ -410,32 +413,104 @@ __device__ __forceinline__ float warp_max_f32(float v) {
     return r;
 }
 
-// Top-k of every token by the whole CTA (all threads call it).  Writes s.pe /
-// s.pg (pair p = t*K + z, shared-expert pairs p = T*K + t) and, from CTA 0, the
-// caller's top-k outputs.  Token t's results are written by warp t % NWARPS; the
-// caller synchronises before other warps read them.
+// Order-preserving key of an f32 logit: a larger logit gives a larger key, -0
+// and +0 the same key, NaN 0 (never ahead of a number).
+__device__ __forceinline__ uint32_t logit_key(float v) {
+    const uint32_t u = __float_as_uint(__fadd_rn(v, 0.0f));  // -0 -> +0
+    if (v != v) return 0u;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_logit(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Exact selection for one token (moe.zig:435-463, the reference's own rules), by
+// one warp: every exp(logit - max) is formed; K rounds take the largest value,
+// among equal values the smallest id (a strict-greater scan from expert 0 with
+// bv = -1); a round without a candidate (every remaining value NaN) yields id 0
+// with expert 0's value.  Writes the token's ids and gates.  The fast path below
+// falls back to it when the logit order might not be the exp order.
+__device__ __noinline__ void route_exact(const float* __restrict__ lg, float* __restrict__ ex, int E, int K,
+                                         int norm_topk, int t, DecodeMisc& s, uint32_t* topk_idx,
+                                         float* topk_gates, bool write_out) {
+    const int lane = threadIdx.x & 31;
+    float mx = __int_as_float(0xffc00000);
+    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+    mx = warp_max_f32(mx);
+    for (int e = lane; e < E; e += 32) ex[e] = cz_expf(__fsub_rn(lg[e], mx));
+    __syncwarp();
+    double top = 0.0;
+    int my_e = 0;
+    float my_v = 0.0f;
+    unsigned long long chosen[(MAXE + 63) / 64] = {};
+    for (int z = 0; z < K; ++z) {
+        // largest value (then smallest id) among the unchosen, NaN never taken
+        uint32_t bk = 0u;
+        int bi = 0x7fffffff;
+        for (int e = lane; e < E; e += 32) {
+            const float v = ex[e];
+            const uint32_t k = (!(chosen[e >> 6] >> (e & 63) & 1ull) && v > -1.0f) ? __float_as_uint(v) + 1u : 0u;
+            if (k > bk) {
+                bk = k;
+                bi = e;
+            }
+        }
+        const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
+        const int best = kmax == 0u ? 0 : (int)__reduce_min_sync(0xffffffffu, bk == kmax ? (uint32_t)bi : 0x7fffffffu);
+        const float bv = kmax == 0u ? ex[0] : __uint_as_float(kmax - 1u);
+        if (kmax) chosen[best >> 6] |= 1ull << (best & 63);
+        if (lane == z) {
+            my_e = best;
+            my_v = bv;
+        }
+        top = __dadd_rn(top, (double)bv);
+    }
+    double den = top;
+    if (!norm_topk) {
+        double all = 0.0;
+        if (lane == 0)
+            for (int e = 0; e < E; ++e) all = __dadd_rn(all, (double)ex[e]);
+        den = __shfl_sync(0xffffffffu, all, 0);
+    }
+    if (lane < K) {
+        const float g = __double2float_rn(__ddiv_rn((double)my_v, den));
+        s.pe[t * K + lane] = my_e;
+        s.pg[t * K + lane] = g;
+        if (write_out) {
+            if (topk_idx) topk_idx[(size_t)t * K + lane] = (uint32_t)my_e;
+            if (topk_gates) topk_gates[(size_t)t * K + lane] = g;
+        }
+    }
+    if (lane == 0) s.exact[t] = 1;
+    __syncwarp();
+}
+
+// Top-k ids of every token by the whole CTA (all threads call it).  The experts
+// are ranked by their f32 logits, which is the reference's exp order (exp is
+// monotone) except where two different logits give the same f32 exp; ties of
+// equal logits go to the smaller id as in the reference.  Each warp ranks a part
+// of 32 experts by counting the entries that beat each one and keeps its top K;
+// the survivors are ranked again until one part is left (the top K of a set
+// under a total order are the union of its parts' top K).  The winners are then
+// checked: finite, their exps clear of underflow, and every two consecutive
+// winners with different logits, and the last winner and the largest logit
+// below it, at least 2^-22 apart after the subtraction of the max, so that
+// their f32 exps differ.  A token that fails the check (or with norm_topk off)
+// is routed again by route_exact.  Writes s.pe, s.pd (logit - max of each
+// winner, for route_gates) and, from CTA 0, the top-k ids.  Token t's results
+// are written by warp t % NWARPS; the caller synchronises before other warps
+// read them.
 __device__ __forceinline__ void route_all(const RouteScratch& rs, int T, int E, int K, int LS, int norm_topk,
-                                       int has_shared, DecodeMisc& s, uint32_t* topk_idx, float* topk_gates,
-                                       bool write_out) {
+                                          int has_shared, DecodeMisc& s, uint32_t* topk_idx, float* topk_gates,
+                                          bool write_out) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nch = (E + 31) >> 5;
     const int stride = nch * K;  // entries per token in the candidate buffers
-    // stage 1: (token, 32 experts) per warp.  The exps of a token are computed by
-    // several warps side by side; inside a part the ids follow the lanes, so one
-    // 32-bit shuffle per lane ranks it.
+    // stage 1: (token, 32 experts) per warp, ids following the lanes
     for (int it = warp; it < T * nch; it += NWARPS) {
         const int t = it / nch, j = it - t * nch;
-        const float* l = rs.lg + (size_t)t * LS;
-        float mx = __int_as_float(0xffc00000);  // NaN: fmaxf and the reduction ignore it
-        for (int e = lane; e < E; e += 32) mx = fmaxf(mx, l[e]);
-        mx = warp_max_f32(mx);
         const int e = 32 * j + lane;
-        uint32_t key = 0u;
-        if (e < E) {
-            const float ex = cz_expf_inline(__fsub_rn(l[e], mx));
-            key = ex > -1.0f ? __float_as_uint(ex) + 1u : 0u;
-            rs.ex[(size_t)t * LS + e] = ex;
-        }
+        const uint32_t key = e < E ? logit_key(rs.lg[(size_t)t * LS + e]) : 0u;
         int r = 0;
 #pragma unroll
         for (int m = 0; m < 32; ++m) {
@@ -463,46 +538,82 @@ __device__ __forceinline__ void route_all(const RouteScratch& rs, int T, int E, 
         nxt = tmp;
         n = ng * K;
     }
-    // final part: warp t ranks token t's last <= 32 entries
+    // final part: warp t ranks token t's last <= 32 entries, checks the winners
     for (int t = warp; t < T; t += NWARPS) {
+        const float* lt = rs.lg + (size_t)t * LS;
         const unsigned long long v = lane < n ? cur[(size_t)t * stride + lane] : empty_entry(0xc0000000u + lane);
         const int r = rank_in_warp(v);
         unsigned long long* fin = rs.fin + (size_t)t * MAXK;
         if (r < K) fin[r] = v;
         __syncwarp();
-        const unsigned long long w = lane < K ? fin[lane] : empty_entry(0xc0000000u + lane);
+        const unsigned long long w = lane < K ? fin[lane] : 0ull;
         const uint32_t key = (uint32_t)(w >> 32);
-        // a round without a candidate: id 0 and expert 0's value
-        const float val = key ? __uint_as_float(key - 1u) : rs.ex[(size_t)t * LS];
-        const int id = key ? (int)(uint32_t)w : 0;
-        // top = sum of the winners' values in selection order, all = sum over every
-        // expert in id order (both f64, moe.zig:443-458)
-        double den = 0.0;
-        if (norm_topk) {
-#pragma unroll
-            for (int z = 0; z < MAXK; ++z) {
-                const float vz = __shfl_sync(0xffffffffu, val, z);
-                if (z < K) den = __dadd_rn(den, (double)vz);
-            }
-        } else {
-            if (lane == 0)
-                for (int e = 0; e < E; ++e) den = __dadd_rn(den, (double)rs.ex[(size_t)t * LS + e]);
-            den = __shfl_sync(0xffffffffu, den, 0);
+        const int id = (int)(uint32_t)w;
+        const float val = lane < K ? key_logit(key) : 0.0f;
+        const float mx = __shfl_sync(0xffffffffu, val, 0);
+        const float d = __fsub_rn(val, mx);
+        const float vn = __shfl_down_sync(0xffffffffu, val, 1), dn = __shfl_down_sync(0xffffffffu, d, 1);
+        const uint32_t klast = __shfl_sync(0xffffffffu, key, K - 1);
+        // the largest key strictly below the last winner's (0: none, or NaN only)
+        uint32_t wk = 0u;
+        for (int e = lane; e < E; e += 32) {
+            const uint32_t ke = logit_key(lt[e]);
+            if (ke < klast && ke > wk) wk = ke;
         }
+        wk = __reduce_max_sync(0xffffffffu, wk);
+        bool ok = true;
         if (lane < K) {
-            const float g = __double2float_rn(__ddiv_rn((double)val, den));
-            s.pe[t * K + lane] = id;
-            s.pg[t * K + lane] = g;
-            if (write_out) {
-                if (topk_idx) topk_idx[(size_t)t * K + lane] = (uint32_t)id;
-                if (topk_gates) topk_gates[(size_t)t * K + lane] = g;
+            ok = key != 0u && fabsf(val) <= 3.0e38f;
+            if (lane + 1 < K) ok = ok && (vn == val || __fsub_rn(d, dn) >= 0x1p-22f);
+            if (lane + 1 == K) {
+                ok = ok && d >= -80.0f;
+                if (wk) ok = ok && __fsub_rn(d, __fsub_rn(key_logit(wk), mx)) >= 0x1p-22f;
             }
+        }
+        const bool fast = __all_sync(0xffffffffu, ok) && norm_topk;
+        if (fast) {
+            if (lane < K) {
+                s.pe[t * K + lane] = id;
+                s.pd[t * K + lane] = d;
+                if (write_out && topk_idx) topk_idx[(size_t)t * K + lane] = (uint32_t)id;
+            }
+            if (lane == 0) s.exact[t] = 0;
+        } else {
+            route_exact(lt, rs.ex + (size_t)t * LS, E, K, norm_topk, t, s, topk_idx, topk_gates, write_out);
         }
         if (lane == 0 && has_shared) {
             s.pe[T * K + t] = E;
-            s.pg[T * K + t] = cz_sigmoid(rs.lg[(size_t)t * LS + E]);
+            s.shlog[t] = lt[E];
         }
     }
+}
+
+// The gates of the tokens routed by the fast path (route_all), by one warp:
+// g_z = f32(f64(exp(d_z)) / top) with top the f64 sum of the winners' exps in
+// selection order (moe.zig:447-462; the same exp as the reference's @exp,
+// cz_expf), and the shared expert's sigmoid gate.  Off the critical path: only
+// the h warp reads the gates, and it runs this itself before its first chunk.
+__device__ __noinline__ void route_gates(int T, int K, int has_shared, DecodeMisc& s, float* topk_gates,
+                                         bool write_out) {
+    const int lane = threadIdx.x & 31;
+    for (int t = 0; t < T; ++t) {
+        if (!s.exact[t]) {
+            const float ex = lane < K ? cz_expf(s.pd[t * K + lane]) : 0.0f;
+            double top = 0.0;
+#pragma unroll
+            for (int z = 0; z < MAXK; ++z) {
+                const float vz = __shfl_sync(0xffffffffu, ex, z);
+                if (z < K) top = __dadd_rn(top, (double)vz);
+            }
+            if (lane < K) {
+                const float g = __double2float_rn(__ddiv_rn((double)ex, top));
+                s.pg[t * K + lane] = g;
+                if (write_out && topk_gates) topk_gates[(size_t)t * K + lane] = g;
+            }
+        }
+        if (lane == 0 && has_shared) s.pg[T * K + t] = cz_sigmoid(s.shlog[t]);
+    }
+    __syncwarp();
 }
 
 // Named barriers between the consumer warps and the h warp (288 threads each):
@@ -1081,9 +1192,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
             __syncwarp();
         } else if (warp == HW) {
             // ---------------- h warp ----------------
-            // Per chunk, once the consumers' partial gate/up sums are in red[b]:
-            // hw = gate * silu(g) * u per (row r, routed token) into the pair's h row in
-            // global scratch.  Runs beside the next chunk's MMAs.
+            // First the gates of the tokens the fast path routed (while the first
+            // stages land), then per chunk, once the consumers' partial gate/up sums
+            // are in red[b]: hw = gate * silu(g) * u per (row r, routed token) into the
+            // pair's h row in global scratch.  Runs beside the next chunk's MMAs.
+            if (!s.abort) route_gates(T, K, SI != 0, s, p.topk_gates, c == 0);
             const int nch = ch_hi - ch_lo;
             int u = 0;
             for (int ch = ch_lo; ch < ch_hi; ++ch) {

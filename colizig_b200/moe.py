@@ -120,6 +120,16 @@ class Layer:
         del keep
         _abi.check("colizig_cuda_moe_register_layer", rc)
 
+    @classmethod
+    def registered(cls, layer_id: int, dims: Dims, ep: bool = False) -> "Layer":
+        """A handle to a layer the library already holds (registered by another
+        entry point, e.g. the checkpoint loader)."""
+        self = cls.__new__(cls)
+        self.id = int(layer_id)
+        self.dims = dims
+        self.ep = bool(ep)
+        return self
+
     @staticmethod
     def from_weights(layer_id: int, dims: Dims, w: dict, ep: bool = False) -> "Layer":
         shared = None

@@ -21,6 +21,7 @@
  *   -7 a device-side wait timed out (the kernel stopped early; the context is
  *      still usable and the next call starts clean)
  *   -8 shape not supported by this build     -9 NCCL / expert-parallel error
+ *  -10 checkpoint file missing, unreadable or malformed, or a tensor missing
  *
  * Threading: one process-wide context, internally serialised by a mutex.
  * Ownership: callers own every buffer they pass; no pointer is retained after
@@ -127,6 +128,27 @@ int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_dims* dims
                                     const float* shared_gate, uint32_t flags);
 
 int colizig_cuda_moe_unregister_layer(uint32_t layer);
+
+/* Registers MoE layer `layer` straight from a safetensors checkpoint: the
+ * reference's host indexes the shards (src/model/manifest.zig,
+ * src/model/weights.zig:198-235) and loads each routed expert from the mmap on
+ * demand (src/qwen38/moe.zig:251-292 loadExpert, 306-329 Layer.load); here the
+ * shards are parsed and mapped once and checkpoint layer `layer_index`'s router,
+ * experts and shared expert go into resident device memory in this one call.
+ * Tensor names are tried as "<prefix>.<suffix>", then as the bare suffix, with
+ * suffixes layers.L.mlp.gate.weight (router [E, H], F32 or BF16),
+ * layers.L.mlp.experts.e.{gate,up,down}_proj.weight (F8_E4M3) and
+ * .weight_scale_inv (F32, BF16 or F16 [nblk, nblk]), and for dims->shared_inter
+ * > 0 layers.L.mlp.shared_expert.{gate,up,down}_proj.weight(_scale_inv)
+ * (F8_E4M3) and layers.L.mlp.shared_expert_gate.weight ([H] or [1, H]).  BF16 /
+ * F16 values are widened exactly to f32 (a BF16 router then gives the logits of
+ * the reference's dotBf16, matmul.zig:84-110).  prefix may be NULL; flags: 0 or
+ * COLIZIG_EP.  Returns 0, -10 when a shard cannot be read or parsed or a
+ * tensor is missing (checked before anything else, so also without a device),
+ * -8 on a dtype or shape that does not match dims, or register_layer's codes. */
+int colizig_cuda_moe_load_safetensors(uint32_t layer, const char* const* shard_paths, int n_shards,
+                                      const char* prefix, uint32_t layer_index, const colizig_moe_dims* dims,
+                                      uint32_t flags);
 
 /* moe.zig:409-426 forward for T tokens: out[T, hidden] f32 =
  * sum_k gate_k * down_k(silu(gate_k(x)) * up_k(x)) (+ shared expert).
