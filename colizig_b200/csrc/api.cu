@@ -22,6 +22,7 @@
 #include <map>
 #include <mutex>
 #include <unordered_map>
+#include <tuple>
 #include <vector>
 
 #if defined(__x86_64__) || defined(_M_X64)
@@ -45,17 +46,24 @@ struct CsrGuard {
 #endif
 };
 
-// Pinned host staging (grown on demand, freed at shutdown).
+// Pinned host staging (grown on demand, freed at shutdown), mapped into the
+// device's address space: `dev` is the address kernels write it through.
 struct HostBuf {
     void* p = nullptr;
+    void* dev = nullptr;
     size_t cap = 0;
     bool ensure(size_t need) {
         if (cap >= need && p) return true;
         if (p) cudaFreeHost(p);
-        p = nullptr;
+        p = dev = nullptr;
         cap = 0;
         if (need == 0) need = 16;
-        if (cudaHostAlloc(&p, need, cudaHostAllocDefault) != cudaSuccess) {
+        if (cudaHostAlloc(&p, need, cudaHostAllocMapped) != cudaSuccess) {
+            p = nullptr;
+            return false;
+        }
+        if (cudaHostGetDevicePointer(&dev, p, 0) != cudaSuccess) {
+            cudaFreeHost(p);
             p = nullptr;
             return false;
         }
@@ -64,7 +72,7 @@ struct HostBuf {
     }
     void release() {
         if (p) cudaFreeHost(p);
-        p = nullptr;
+        p = dev = nullptr;
         cap = 0;
     }
 };
@@ -120,6 +128,22 @@ struct MoeLayer {
     bool pf_ok = false;
     CUtensorMap gate_map{}, up_map{}, sh_gate_map{}, sh_up_map{};  // decode views of the gate/up weights
     int gu_kb = 0;              // depth of those boxes (0 = 2D maps)
+    uint64_t serial = 0;        // distinct for every registration (keys the captured host-call graphs)
+};
+
+// A host-pointer decode call captured as a CUDA graph (token upload, decode
+// launches, one copy of the results back): the key holds everything the
+// captured nodes point at or depend on.
+struct HostGraphKey {
+    uint32_t layer;
+    uint64_t serial;
+    int T, bf16, has_idx, has_gates;
+    const void *io_x, *io_res, *io_host, *io_xh, *logits, *hrows, *sync;
+    bool operator<(const HostGraphKey& o) const {
+        return std::tie(layer, serial, T, bf16, has_idx, has_gates, io_x, io_res, io_host, io_xh, logits, hrows, sync) <
+               std::tie(o.layer, o.serial, o.T, o.bf16, o.has_idx, o.has_gates, o.io_x, o.io_res, o.io_host, o.io_xh,
+                        o.logits, o.hrows, o.sync);
+    }
 };
 
 struct Ctx {
@@ -152,6 +176,11 @@ struct Ctx {
     // and gives up its waits after dbg_spin_limit polls (one launch, then cleared)
     int dbg_hold = 0;
     uint32_t dbg_spin_limit = 0;
+    // host-pointer decode calls: captured graphs, and the keys seen once (a key's
+    // first call runs directly, which also makes every allocation it needs)
+    std::map<HostGraphKey, cudaGraphExec_t> host_graphs;
+    std::map<HostGraphKey, int> host_seen;
+    uint64_t next_serial = 1;
     // kernel timer (benchmarks): CUDA event pairs around the dominant launches
     std::vector<cudaEvent_t> tm_ev;
     std::vector<int> tm_kind;
@@ -224,6 +253,19 @@ int ensure_sync() {
     return CZ_OK;
 }
 
+void drop_host_graphs(bool all, uint32_t layer) {
+    for (auto it = g.host_graphs.begin(); it != g.host_graphs.end();) {
+        if (all || it->first.layer == layer) {
+            cudaGraphExecDestroy(it->second);
+            it = g.host_graphs.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    for (auto it = g.host_seen.begin(); it != g.host_seen.end();)
+        it = (all || it->first.layer == layer) ? g.host_seen.erase(it) : std::next(it);
+}
+
 void free_layer(MoeLayer& L) {
     if (L.mem) cudaFree(L.mem);
     L = MoeLayer{};
@@ -259,6 +301,7 @@ void shutdown_locked() {
     g.lru.clear();
     for (auto& kv : g.layers) free_layer(kv.second);
     g.layers.clear();
+    drop_host_graphs(true, 0);
     g.io_host.release();
     g.io_xh.release();
     for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.hrows, &g.pf_scratch, &g.io_x, &g.io_out, &g.io_res,
@@ -941,6 +984,8 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
     }
     auto it = g.layers.find(layer);
     if (it != g.layers.end()) free_layer(it->second);
+    drop_host_graphs(false, layer);
+    L.serial = g.next_serial++;
     g.layers[layer] = L;
     return CZ_OK;
 }
@@ -952,6 +997,7 @@ CZ_EXPORT int colizig_cuda_moe_unregister_layer(uint32_t layer) {
     if (it == g.layers.end()) return CZ_ENOLAYER;
     cudaSetDevice(g.dev);
     cudaDeviceSynchronize();
+    drop_host_graphs(false, layer);
     free_layer(it->second);
     g.layers.erase(it);
     return CZ_OK;
@@ -999,6 +1045,63 @@ CZ_EXPORT int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtyp
         ensure_sync())
         return CZ_EALLOC;
     uint8_t* const res = g.io_res.as<uint8_t>();
+    // decode launches copy the error word into the result buffer themselves (their
+    // last CTA); the other paths get one device-to-device copy of it below
+    const bool kernel_status = staged && !sharded && !(T >= kPrefillMinTokens && L.pf_ok);
+    // Decode-sized calls on a single GPU are replayed from a captured CUDA graph
+    // (the token upload and the decode launches), one launch call per forward;
+    // the kernel writes outputs, top-k and the error word straight into the mapped
+    // pinned staging, so no copy back is needed.  A key's first call runs directly
+    // (it allocates the decode scratch and sets the kernel attributes); the second
+    // captures.
+    const bool graphable = kernel_status && !L.ep && xb && ob && !g.dbg_hold && g.tm_ev.empty();
+    if (graphable && ensure_decode_scratch(L.d) == CZ_OK) {
+        const HostGraphKey key{layer, L.serial, T, bf16, topk_idx != nullptr, topk_gates != nullptr, g.io_x.p,
+                               g.io_res.p, g.io_host.p, g.io_xh.p, g.logits.p, g.hrows.p, g.sync};
+        auto gi = g.host_graphs.find(key);
+        if (gi == g.host_graphs.end() && g.host_seen.count(key)) {
+            if (g.host_graphs.size() >= 4096) drop_host_graphs(true, 0);
+            cudaGraph_t graph = nullptr;
+            cudaGraphExec_t exec = nullptr;
+            bool ok = cudaStreamBeginCapture(g.stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+            if (ok) {
+                ok = cudaMemcpyAsync(g.io_x.p, g.io_xh.p, xb, cudaMemcpyHostToDevice, g.stream) == cudaSuccess;
+                uint8_t* const hd = static_cast<uint8_t*>(g.io_host.dev);
+                ok = ok && moe_run(L, g.io_x.p, bf16, T, reinterpret_cast<float*>(hd),
+                                   topk_idx ? reinterpret_cast<uint32_t*>(hd + io) : nullptr,
+                                   topk_gates ? reinterpret_cast<float*>(hd + go) : nullptr, nullptr, 0.f, nullptr,
+                                   g.stream, reinterpret_cast<uint32_t*>(hd + eo)) == CZ_OK;
+                const bool ended = cudaStreamEndCapture(g.stream, &graph) == cudaSuccess;
+                ok = ok && ended && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+                if (graph) cudaGraphDestroy(graph);
+            }
+            if (ok) {
+                gi = g.host_graphs.emplace(key, exec).first;
+            } else {
+                if (exec) cudaGraphExecDestroy(exec);
+                cudaGetLastError();  // a failed capture leaves nothing behind: run directly
+            }
+        }
+        if (gi != g.host_graphs.end()) {
+            memcpy(g.io_xh.p, x, xb);
+            if (cudaGraphLaunch(gi->second, g.stream) != cudaSuccess) return CZ_ELAUNCH;
+            if (cudaStreamSynchronize(g.stream) != cudaSuccess) return CZ_ED2H;
+            const uint8_t* const hs = static_cast<const uint8_t*>(g.io_host.p);
+            uint32_t err = 0;
+            memcpy(&err, hs + eo, sizeof err);
+            if (err) {
+                cudaMemsetAsync(g.sync + 1, 0, sizeof(uint32_t), g.stream);
+                cudaStreamSynchronize(g.stream);
+                return CZ_ETIMEOUT;
+            }
+            memcpy(out, hs, ob);
+            if (topk_idx) memcpy(topk_idx, hs + io, kb);
+            if (topk_gates) memcpy(topk_gates, hs + go, kb);
+            return CZ_OK;
+        }
+        if (g.host_seen.size() >= 8192) g.host_seen.clear();
+        g.host_seen[key] = 1;
+    }
     if (xb) {
         const void* src = x;
         if (staged) {
@@ -1007,9 +1110,6 @@ CZ_EXPORT int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtyp
         }
         if (cudaMemcpyAsync(g.io_x.p, src, xb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess) return CZ_EH2D;
     }
-    // decode launches copy the error word into the result buffer themselves (their
-    // last CTA); the other paths get one device-to-device copy of it below
-    const bool kernel_status = staged && !sharded && !(T >= kPrefillMinTokens && L.pf_ok);
     int rc = run(g.io_x.p, reinterpret_cast<float*>(res), topk_idx ? reinterpret_cast<uint32_t*>(res + io) : nullptr,
                  topk_gates ? reinterpret_cast<float*>(res + go) : nullptr, g.stream,
                  kernel_status ? reinterpret_cast<uint32_t*>(res + eo) : nullptr);

@@ -263,3 +263,30 @@ def test_error_codes():
     exp = (_abi.MoeExpert * 16)()
     r = np.zeros((16, 250), np.float32)
     assert L.colizig_cuda_moe_register_layer(1, ctypes.byref(d), r.ctypes.data, exp, None, None, 0) == -8
+
+
+def test_host_pointer_calls_replayed_from_graph_match_device_calls():
+    """Host-pointer decode calls are run directly the first time and replayed from
+    a captured CUDA graph afterwards; every call must equal the device-pointer
+    forward on its own tokens, and a re-registered layer must not reuse a graph
+    captured for the old weights."""
+    d, w, L = _device_layer("c2", 4, 205)
+    try:
+        for T in (1, 3):
+            for i in range(5):
+                x = synth.make_tokens(T, d.hidden, 7000 + 10 * T + i, device="cuda", dtype=torch.bfloat16)
+                od, idd, gd = moe.forward(L, x)
+                oh, ih, gh = moe.forward(L, x.cpu())
+                torch.cuda.synchronize()
+                assert np.array_equal(od.cpu().numpy(), oh), (T, i)
+                assert np.array_equal(idd.cpu().numpy().view(np.uint32), ih) and np.array_equal(gd.cpu().numpy(), gh)
+        x = synth.make_tokens(1, d.hidden, 7100, device="cpu", dtype=torch.bfloat16)
+        before, _, _ = moe.forward(L, x)
+        w2 = synth.make_layer(d, seed=5, device="cuda")
+        L2 = moe.Layer.from_weights(205, d, w2)  # same id, new weights
+        after, _, _ = moe.forward(L2, x)
+        want, _, _ = moe.forward(L2, x.cuda())
+        torch.cuda.synchronize()
+        assert np.array_equal(after, want.cpu().numpy()) and not np.array_equal(after, before)
+    finally:
+        L.unregister()
