@@ -143,6 +143,32 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def native_host_forwards(L, layer_ids, xh, T, oh, ih, gh, steps):
+    """Seconds for `steps` synchronous host-pointer forwards (bf16 tokens), called
+    from the native loop in libcz_hostbench.so, after one warm-up pass over every
+    layer twice; None when the helper is not built."""
+    import ctypes
+
+    path = os.path.join(ROOT, "colizig_b200", "libcz_hostbench.so")
+    if not os.path.exists(path):
+        return None
+    hb = ctypes.CDLL(path)
+    hb.cz_hostbench_forwards.restype = ctypes.c_double
+    hb.cz_hostbench_forwards.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                         ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
+    fn = ctypes.cast(L.colizig_cuda_moe_forward, ctypes.c_void_p).value
+    lids = (ctypes.c_uint32 * len(layer_ids))(*layer_ids)
+    xs = (ctypes.c_void_p * len(xh))(*[x.data_ptr() for x in xh])
+    rc = ctypes.c_int(0)
+    args = (lids, len(layer_ids), xs, len(xh), 1, T, oh.data_ptr(), ih.data_ptr(), gh.data_ptr(), ctypes.byref(rc))
+    hb.cz_hostbench_forwards(fn, 2 * len(layer_ids), *args)  # warm-up: direct, then captured, per layer
+    dt = hb.cz_hostbench_forwards(fn, steps, *args)
+    if dt < 0:
+        raise RuntimeError(f"colizig_cuda_moe_forward returned {rc.value} in the native loop")
+    return dt
+
+
 def timed_replays(torch, graph, stream, dev, reps):
     """Device time (ms) of `reps` replays of a captured graph, each between its own
     CUDA event pair on the launching stream, with L2 flushed (a 256 MB write, more
@@ -803,9 +829,22 @@ def main():
         tt = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_s = float(tt.item())
+    py_e2e_s = e2e_s
+    # The same calls from a native caller loop (the reference's host is a compiled
+    # program calling the C ABI, src/backend/gpu.zig): no interpreter between calls.
+    native_s = native_host_forwards(L, [lay.id for lay in layers], xh, T, oh, ih, gh, args.steps)
+    if native_s is not None:
+        if world > 1:
+            tt = torch.tensor([native_s], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            native_s = float(tt.item())
+        e2e_s = native_s
     e2e = {"value": args.steps * T / e2e_s, "unit": "tokens/s",
            "h2d_bytes_per_step": T * d.hidden * 2, "d2h_bytes_per_step": T * d.hidden * 4 + T * d.topk * 8,
-           "ms_per_step": e2e_s / args.steps * 1e3}
+           "ms_per_step": e2e_s / args.steps * 1e3,
+           "caller": ("native C loop through colizig_cuda_moe_forward (libcz_hostbench.so)" if native_s is not None
+                      else "python ctypes"),
+           "python_ctypes_ms_per_step": py_e2e_s / args.steps * 1e3}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

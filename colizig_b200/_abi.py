@@ -12,7 +12,8 @@ import os
 import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libcolizig_cuda.so")
+# COLIZIG_LIBRARY overrides the in-tree library (to compare builds); unset in normal use.
+LIB_PATH = os.environ.get("COLIZIG_LIBRARY") or os.path.join(HERE, "libcolizig_cuda.so")
 
 # the six symbols of the reference surface (gpu.zig:84-89) + the MoE-level ones
 REFERENCE_SYMBOLS = (

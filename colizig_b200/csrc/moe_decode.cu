@@ -512,7 +512,7 @@ __device__ __forceinline__ void route_all(const RouteScratch& rs, int T, int E, 
         const int e = 32 * j + lane;
         const uint32_t key = e < E ? logit_key(rs.lg[(size_t)t * LS + e]) : 0u;
         int r = 0;
-#pragma unroll
+#pragma unroll 4
         for (int m = 0; m < 32; ++m) {
             const uint32_t km = __shfl_sync(0xffffffffu, key, m);
             r += (km > key) | ((km == key) & (m < lane));
@@ -600,7 +600,7 @@ __device__ __noinline__ void route_gates(int T, int K, int has_shared, DecodeMis
         if (!s.exact[t]) {
             const float ex = lane < K ? cz_expf(s.pd[t * K + lane]) : 0.0f;
             double top = 0.0;
-#pragma unroll
+#pragma unroll 1
             for (int z = 0; z < MAXK; ++z) {
                 const float vz = __shfl_sync(0xffffffffu, ex, z);
                 if (z < K) top = __dadd_rn(top, (double)vz);
@@ -865,7 +865,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
             const int myid = act ? s.pe[lane] : 0x7fffffff;
             int rho = 0;
             bool dup = false;
-#pragma unroll
+#pragma unroll 4
             for (int m = 0; m < MAXK; ++m) {
                 const int im = __shfl_sync(0xffffffffu, myid, m);
                 rho += (m < K) & (im < myid);
@@ -954,7 +954,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
             const int maxq = cv.rc / cv.JX;
             int pe_r[3];
             uint32_t chg[3];
-#pragma unroll
+#pragma unroll 1
             for (int w = 0; w < 3; ++w) {
                 const int r = 32 * w + lane;
                 pe_r[w] = r < P ? s.pe[s.order[r]] : -1;
@@ -968,7 +968,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
             uint32_t stw[3];
             int u_base[3];
             int base = 0;
-#pragma unroll
+#pragma unroll 1
             for (int w = 0; w < 3; ++w) {
                 const int r = 32 * w + lane;
                 int rs0 = -1;  // the run's first position: the last change at or before r
@@ -994,7 +994,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
             // of down rows per pack; the shared expert (expert E) is the last group.
             const int drows = s.geo_drows, nrb = s.geo_nrb, rbytes = s.geo_rbytes, per = s.geo_per;
             int nr = 0;  // held routed groups before this batch
-#pragma unroll
+#pragma unroll 1
             for (int v = 0; v < 3; ++v) {
                 const int u = 32 * v + lane;
                 const bool in = u < base;
