@@ -206,7 +206,8 @@ int open_shard(const char* path, Shard& s) {
     s.map = static_cast<const uint8_t*>(m);
     uint64_t n = 0;
     for (int i = 0; i < 8; ++i) n |= (uint64_t)s.map[i] << (8 * i);
-    if (n == 0 || n > s.size - 8 || n > (100ull << 20)) return CZ_EIO;
+    // header cap as the reference's (safetensors.zig:23 max_header_bytes, checked at :139)
+    if (n == 0 || n > s.size - 8 || n > (256ull << 20)) return CZ_EIO;
     s.data0 = 8 + (size_t)n;
     Json j{reinterpret_cast<const char*>(s.map) + 8, reinterpret_cast<const char*>(s.map) + 8 + n};
     if (!j.header(s.index)) return CZ_EIO;
