@@ -30,6 +30,7 @@ enum : uint32_t {
     CZ_DERR_READY_WAIT = 1u << 3,
     CZ_DERR_DRAIN_WAIT = 1u << 4,
     CZ_DERR_SHAPE = 1u << 5,
+    CZ_DERR_SEQ_WAIT = 1u << 6,
 };
 
 // Spin limits: every wait in these kernels is bounded.  With the nanosleep
@@ -191,6 +192,14 @@ CZ_DEV unsigned long long ld_relaxed_u64(const unsigned long long* p) {
 // single-copy-atomic access.
 CZ_DEV void ld_relaxed_u64x2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
     asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+CZ_DEV void st_relaxed_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+CZ_DEV void red_relaxed_add_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 CZ_DEV void st_relaxed_u64(unsigned long long* p, unsigned long long v) {

@@ -106,6 +106,7 @@ struct __align__(16) DecodeMisc {
     int xexp[MAXT];       // s per token (terms hold x_t * 2^s)
     float xscale[MAXT];   // 2^-s per token
     int fastgroup;        // the groups were formed by the top-k warp (one token, distinct experts)
+    int dots_done;        // one token: warps of this CTA that have published their router logits
     int exact[MAXT];      // token t was routed by the exact exp-keyed selection (its gates are set)
     float pd[MAXP];       // logit - max of the winner of pair p (the gates are formed from it later)
     float shlog[MAXT];    // the shared expert's gate logit per token
@@ -616,6 +617,183 @@ __device__ __noinline__ void route_gates(int T, int K, int has_shared, DecodeMis
     __syncwarp();
 }
 
+// One token (T = 1), by one warp and with no CTA barrier: route_all's selection,
+// check and the one-token grouping in a compact form.  The warp polls the tagged
+// router logits straight into registers (expert 32j + lane in key[j]), then takes
+// K + 1 selection rounds: the largest key left, among equal keys the smallest id
+// (the reference's strict-greater scan from expert 0); the round after the K-th
+// only reads the largest key left, which the check compares with the last winner.
+// The winners are distinct, so each is a group of its own; its place in ascending
+// expert order comes from ballots of the taken flags.  Returns false when the
+// check fails (the caller then routes through route_all / route_exact), when
+// norm_topk is off, or when a logit never arrives (error word set).  Writes what
+// route_all and the one-token grouping write: pe, pd, exact, shlog, the groups,
+// U, P, NC, npk, fastgroup, and from CTA 0 the top-k ids.
+template <int NJ>
+__device__ __forceinline__ bool route_one(const DecodeParams& p, DecodeMisc& s, int ns, int E, int K, int SI,
+                                          int Ir, uint32_t tag, uint32_t limit, uint32_t* err, bool write_out) {
+    const int lane = threadIdx.x & 31;
+    const int Er = E + (SI ? 1 : 0);
+    uint32_t key[NJ];  // logit bits while polling, then the order-preserving keys
+    uint32_t pend = 0u;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+        key[j] = 0u;
+        if (32 * j + lane < Er) pend |= 1u << j;
+    }
+    for (uint32_t it = 0; it < limit; ++it) {
+        // every pending word's load first, then the tag checks: the loads overlap
+        unsigned long long w[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) w[j] = (pend & (1u << j)) ? ld_relaxed_u64(p.logits + 32 * j + lane) : 0ull;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j)
+            if ((pend & (1u << j)) && (uint32_t)(w[j] >> 32) == tag) {
+                key[j] = (uint32_t)w[j];
+                pend &= ~(1u << j);
+            }
+        if (!__any_sync(0xffffffffu, pend)) break;
+        if (*(volatile int*)&s.abort) break;
+        __nanosleep(it < 256 ? 50 : 200);
+    }
+    if (__any_sync(0xffffffffu, pend)) {
+        if (lane == 0) set_error(err, s, CZ_DERR_ROUTER_BARRIER);
+        return false;
+    }
+    float shl = 0.0f;  // the shared expert's gate logit (word E)
+    if (SI) {
+        uint32_t b = 0u;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j)
+            if (j == (E >> 5)) b = key[j];
+        shl = __uint_as_float(__shfl_sync(0xffffffffu, b, E & 31));
+    }
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) key[j] = 32 * j + lane < E ? logit_key(__uint_as_float(key[j])) : 0u;
+    if (!p.norm_topk) return false;
+
+    uint32_t taken = 0u, mykey = 0u, wk = 0u;
+    int myid = 0;
+#pragma unroll 1
+    for (int z = 0; z <= K; ++z) {
+        uint32_t bk = 0u;
+        int bj = 0;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j)
+            if (key[j] > bk) {
+                bk = key[j];
+                bj = j;
+            }
+        const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
+        if (z == K) {
+            wk = kmax;
+            break;
+        }
+        const uint32_t win = __reduce_min_sync(0xffffffffu, bk == kmax ? (uint32_t)(32 * bj + lane) : 0xffffffffu);
+        if (lane == (int)(win & 31u)) {
+#pragma unroll
+            for (int j = 0; j < NJ; ++j)
+                if (j == (int)(win >> 5)) {
+                    key[j] = 0u;
+                    taken |= 1u << j;
+                }
+        }
+        if (lane == z) {
+            myid = (int)win;
+            mykey = kmax;
+        }
+    }
+    // the check of route_all: finite winners, exps clear of underflow, f32 exps that
+    // differ between consecutive winners of different logits and between the last
+    // winner and the largest logit left
+    const float val = lane < K ? key_logit(mykey) : 0.0f;
+    const float mx = __shfl_sync(0xffffffffu, val, 0);
+    const float d = __fsub_rn(val, mx);
+    const float vn = __shfl_down_sync(0xffffffffu, val, 1), dn = __shfl_down_sync(0xffffffffu, d, 1);
+    bool ok = true;
+    if (lane < K) {
+        ok = mykey != 0u && fabsf(val) <= 3.0e38f;
+        if (lane + 1 < K) ok = ok && (vn == val || __fsub_rn(d, dn) >= 0x1p-22f);
+        if (lane + 1 == K) {
+            ok = ok && d >= -80.0f;
+            if (wk) ok = ok && __fsub_rn(d, __fsub_rn(key_logit(wk), mx)) >= 0x1p-22f;
+        }
+    }
+    if (!__all_sync(0xffffffffu, ok)) return false;
+
+    const bool act = lane < K;
+    if (act) {
+        s.pe[lane] = myid;
+        s.pd[lane] = d;
+        if (write_out && p.topk_idx) p.topk_idx[lane] = (uint32_t)myid;
+    }
+    // rank of this lane's winner among the winners, by expert id
+    int rho = 0;
+    {
+        const int jj = myid >> 5, ll = myid & 31;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            const uint32_t m = __ballot_sync(0xffffffffu, (taken >> j) & 1u);
+            if (j < jj) rho += __popc(m);
+            if (j == jj) rho += __popc(m & ((1u << ll) - 1u));
+        }
+    }
+    const int drows = s.geo_drows, per = s.geo_per, rbytes = s.geo_rbytes;
+    const bool held = act && myid >= p.e_lo && myid < p.e_hi;
+    const uint32_t hm = __reduce_or_sync(0xffffffffu, held ? (1u << rho) : 0u);
+    const int k = __popc(hm & ((1u << rho) - 1u));  // index among held routed groups
+    const int nr = __popc(hm);
+    if (act) {
+        s.g_expert[rho] = myid;
+        s.g_pair0[rho] = rho;
+        s.g_npairs[rho] = 1;
+        s.order[rho] = lane;
+        s.rtok[rho] = held ? 0 : -1;
+        s.g_chunk0[rho] = k * (Ir / CR);
+        s.g_pack[rho] = held && drows > 0 ? k / per : -1;
+        s.g_poff[rho] = held && drows > 0 ? (k % per) * rbytes : 0;
+    }
+    if (lane == 0) {
+        s.exact[0] = 0;
+        int U = K, nc = nr * (Ir / CR);
+        int npk = nr > 0 && drows > 0 ? (nr - 1) / per + 1 : 0;
+        if (SI) {  // the shared expert: pair K, the last group
+            s.pe[K] = E;
+            s.shlog[0] = shl;
+            s.g_expert[K] = E;
+            s.g_pair0[K] = K;
+            s.g_npairs[K] = 1;
+            s.order[K] = K;
+            s.rtok[K] = p.shared_here ? 0 : -1;
+            s.g_chunk0[K] = nc;
+            s.g_pack[K] = -1;
+            s.g_poff[K] = 0;
+            if (p.shared_here) {
+                nc += SI / CR;
+                if (drows > 0) {
+                    const int sbytes = drows * SI + s.geo_nrb * cz_nbp(SI) * 4;
+                    const int fill = nr > 0 ? (nr - (npk - 1) * per) * rbytes : SLOT_BYTES;
+                    if (npk > 0 && fill + sbytes <= SLOT_BYTES) {
+                        s.g_pack[K] = npk - 1;
+                        s.g_poff[K] = fill;
+                    } else {
+                        s.g_pack[K] = npk;
+                        ++npk;
+                    }
+                }
+            }
+            U = K + 1;
+        }
+        if (p.hslot && npk > ns - 1) set_error(err, s, CZ_DERR_SHAPE);
+        s.g_chunk0[U] = nc;
+        s.U = U;
+        s.P = K + (SI ? 1 : 0);
+        s.NC = nc;
+        s.npk = npk;
+    }
+    return true;
+}
+
 // Named barriers between the consumer warps and the h warp (288 threads each):
 // RED_FULL(b): the consumers' partial gate/up sums of a chunk of parity b are in
 // red[b]; RED_FREE(b): the h warp has read them; H_DONE: the h warp has read
@@ -623,7 +801,13 @@ __device__ __noinline__ void route_gates(int T, int K, int has_shared, DecodeMis
 // part in none of them: it may still be waiting for ring slots that only phase D
 // frees.
 constexpr int BAR_RED_FULL = 2, BAR_RED_FREE = 4, BAR_H_DONE = 6;
+// One-token prologue (every warp but the producer, or all threads): XMAX: max |x|
+// is complete (288 threads); SPLIT: the token's terms are written and the ring's
+// copy of the token is dead; ROUTED: the producer warp has routed and grouped.
+constexpr int BAR_XMAX = 7, BAR_ROUTED = 8, BAR_SPLIT = 9;
 __device__ __forceinline__ void bar_sync_n(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "n"((NCW + 1) * 32) : "memory"); }
+__device__ __forceinline__ void bar_sync_all(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "n"(NTHREADS) : "memory"); }
+__device__ __forceinline__ void bar_arrive_all(int id) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "n"(NTHREADS) : "memory"); }
 __device__ __forceinline__ void bar_arrive_n(int id) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "n"((NCW + 1) * 32) : "memory"); }
 
 // Bounded poll of tagged exchange words into f32 values.  Every thread polls its
@@ -694,22 +878,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     uint32_t* const err = p.sync + 1;
     const uint32_t limit = p.spin_limit ? p.spin_limit : CZ_SPIN_LIMIT;
 
-    const uint32_t seq = ld_relaxed_gpu(p.sync);
-    const uint32_t tag = seq + 1u;  // this launch's exchange tag (zeroed scratch never matches)
-    uint32_t* reg = region(p.sync, seq & 1);
-    if (c == 0 && tid < kSyncRegionWords) region(p.sync, (seq & 1) ^ 1)[tid] = 0u;
-    if (tid == 0) {
-        for (int i = 0; i < cv.ns; ++i) {
-            mbar_init(&s.full[i], 1);
-            mbar_init(&s.empty[i], NCW);
-        }
-        mbar_init(&s.rbar, 1);
-        s.abort = 0;
-        fence_mbarrier_init();
-    }
-    if (tid < MAXT) s.xmax[tid] = 0u;
-    __syncthreads();
-
     // ---------------- phase R: router logits ----------------
     const int row_lo = split_at(c, Er, G), row_hi = split_at(c + 1, Er, G);
     const int nrows = row_hi - row_lo;
@@ -719,13 +887,27 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     float* rows = reinterpret_cast<float*>(ring);
     uint8_t* xs = ring + rbytes;
     float* wnorm = reinterpret_cast<float*>(ring + rbytes + xbytes);
+    // The next launch in the stream may start its CTAs as this launch's CTAs end.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (tid == 0) {
+        // the barriers, then the router rows at once: weights, which no kernel writes,
+        // so the copy goes out before the wait for the previous kernel
+        for (int i = 0; i < cv.ns; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.empty[i], NCW);
+        }
+        mbar_init(&s.rbar, 1);
+        s.abort = 0;
+        s.dots_done = 0;
+        fence_mbarrier_init();
         const uint32_t wbytes = p.rms_w ? (uint32_t)H * 4u : 0u;
         mbar_arrive_expect_tx(&s.rbar, xbytes + rbytes + wbytes);
         for (int r = 0; r < nrows; ++r) {
             const int e = row_lo + r;
             bulk_g2s(rows + (size_t)r * H, (e < E) ? p.router + (size_t)e * H : p.sh_gate, (uint32_t)H * 4u, &s.rbar);
         }
+        // the tokens (and the sequence word) may come from the previous kernel
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         bulk_g2s(xs, p.x, xbytes, &s.rbar);
         if (wbytes) bulk_g2s(wnorm, p.rms_w, wbytes, &s.rbar);
     } else if (tid == 64) {
@@ -748,6 +930,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
             prefetch_tensormap(&p.sh_up_map);
         }
     }
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the previous kernel's writes are visible
+    const uint32_t seq = ld_relaxed_gpu(p.sync);
+    const uint32_t tag = seq + 1u;  // this launch's exchange tag (zeroed scratch never matches)
+    uint32_t* reg = region(p.sync, seq & 1);
+    if (c == 0 && tid < kSyncRegionWords) region(p.sync, (seq & 1) ^ 1)[tid] = 0u;
+    if (tid == 0) red_relaxed_add_gpu(&reg[0], 1u);  // this CTA has read the sequence
+    if (tid < MAXT) s.xmax[tid] = 0u;
+    __syncthreads();
     if (!mbar_wait_bounded(&s.rbar, 0, &s.abort) && lane == 0) set_error(err, s, CZ_DERR_FULL_WAIT);
     __syncthreads();
 
@@ -779,275 +969,350 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         return xbf ? __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(xs)[k] << 16)
                    : reinterpret_cast<const float*>(xs)[k];
     };
-    // max |x_t| for the per-token power-of-two prescale (one atomic per warp)
-    if (!s.abort) {
-        for (int t = 0; t < T; ++t) {
-            float m = 0.0f;
-            for (int i = tid; i < H; i += NTHREADS) {
-                const float a = fabsf(xval(t * H + i));
-                if (a < 3.0e38f) m = fmaxf(m, a);
-            }
-            m = warp_max_f32(m);
-            if (lane == 0 && m > 0.0f) atomicMax(&s.xmax[t], __float_as_uint(m));
-        }
-    }
-    __syncthreads();
-    // The first nd warps form the router logits (one (row, token) item each, in
-    // turn); each logit goes out as one tagged word the moment it is formed.  The
-    // other warps split the tokens into E4M3 terms meanwhile:
-    //   x_t * 2^s_t = term 0 + term 1 (+ term 2), column (t, j) holding term j of
-    //   token t, H bytes at xterm + (t*JX + j)*CS.
     const int nitems = nrows * T;
-    const int nd = nitems < NWARPS ? nitems : NWARPS;
-    if (!s.abort) {
-        if (warp < nd) {
-            for (int it = warp; it < nitems; it += NWARPS) {
-                const int r = it / T, t = it - r * T;
-                const float* wr = rows + (size_t)r * H;
-                const float v = xbf ? router_dot<true>(wr, xs + (size_t)t * H * 2, H, lane)
-                                    : router_dot<false>(wr, xs + (size_t)t * H * 4, H, lane);
-                if (lane == 0 && !(p.dbg_hold && row_lo + r == 0))
-                    st_relaxed_u64(p.logits + (size_t)t * LS + row_lo + r, tag_word(tag, v));
+    if constexpr (T == 1) {
+        // One token: the producer warp routes and groups it alone (route_one) while
+        // the other warps form this CTA's router logits, max |x| and the token's
+        // E4M3 terms (x * 2^s = term 0 + term 1 (+ term 2), term j at xterm + j*CS);
+        // the producer then waits only for the terms (SPLIT: the ring's copy of the
+        // token is dead) before it streams.
+        if (warp == PW) {
+            // Polls from every CTA while the logits are still being formed slow their
+            // publication down (the words share a few L2 lines): the first poll waits
+            // until this CTA has published its own logits, the grid's others being
+            // due about then, or about a microsecond in a CTA without router rows.
+            {
+                const int nd = nitems < NCW ? nitems : NCW;
+                if (nd == 0) __nanosleep(1000);
+                for (uint32_t it = 0; it < limit && *(volatile int*)&s.dots_done < nd && !*(volatile int*)&s.abort; ++it)
+                    __nanosleep(32);
             }
-        }
-        if (warp >= nd || nd == NWARPS) {
-            const int nsw = nd == NWARPS ? NWARPS : NWARPS - nd;  // warps on the split
-            const int st0 = (nd == NWARPS ? warp : warp - nd) * 32 + lane;
-            for (int t = 0; t < T; ++t) {
-                const int sx = prescale_exp(__uint_as_float(s.xmax[t]));
-                uint8_t* col = xterm + (size_t)(t * cv.JX) * cv.CS;
+            bool ok = false;
+            if (!s.abort)
+                ok = Er <= 128 ? route_one<4>(p, s, cv.ns, E, K, SI, Ir, tag, limit, err, c == 0)
+                               : route_one<17>(p, s, cv.ns, E, K, SI, Ir, tag, limit, err, c == 0);
+            if (lane == 0) s.fastgroup = ok ? 1 : 0;
+            __syncwarp();
+            bar_arrive_all(BAR_ROUTED);
+            bar_sync_all(BAR_SPLIT);
+        } else {
+            const int nd = nitems < NCW ? nitems : NCW;     // warps on the router dot
+            const int wt = tid < PW * 32 ? tid : tid - 32;  // thread index among the 288
+            if (!s.abort && warp < nd) {
+                for (int r = warp; r < nrows; r += nd) {
+                    const float* wr = rows + (size_t)r * H;
+                    const float v = xbf ? router_dot<true>(wr, xs, H, lane) : router_dot<false>(wr, xs, H, lane);
+                    if (lane == 0 && !(p.dbg_hold && row_lo + r == 0))
+                        st_relaxed_u64(p.logits + row_lo + r, tag_word(tag, v));
+                }
+                if (lane == 0) atomicAdd(&s.dots_done, 1);
+            }
+            if (!s.abort) {
+                float m = 0.0f;
+                for (int i = wt; i < H; i += NTHREADS - 32) {
+                    const float a = fabsf(xval(i));
+                    if (a < 3.0e38f) m = fmaxf(m, a);
+                }
+                m = warp_max_f32(m);
+                if (lane == 0 && m > 0.0f) atomicMax(&s.xmax[0], __float_as_uint(m));
+            }
+            bar_sync_n(BAR_XMAX);
+            if (!s.abort && warp >= nd) {
+                const int nsw = NWARPS - 1 - nd;  // warps on the split
+                const int st0 = (warp - nd - (warp > PW ? 1 : 0)) * 32 + lane;
+                const int sx = prescale_exp(__uint_as_float(s.xmax[0]));
                 for (int i = 2 * st0; i < H; i += 2 * 32 * nsw) {
-                    float a = scale2(xval(t * H + i), sx), b = scale2(xval(t * H + i + 1), sx);
+                    float a = scale2(xval(i), sx), b = scale2(xval(i + 1), sx);
                     for (int j = 0; j < cv.JX; ++j) {
                         const uint16_t d = e4m3_term2(a, b);
-                        *reinterpret_cast<uint16_t*>(col + (size_t)j * cv.CS + i) = d;
+                        *reinterpret_cast<uint16_t*>(xterm + (size_t)j * cv.CS + i) = d;
+                    }
+                }
+            }
+            if (tid == 0) {
+                const int e = prescale_exp(__uint_as_float(s.xmax[0]));
+                s.xexp[0] = e;
+                s.xscale[0] = scale2(1.0f, -e);
+            }
+            fence_proxy_async_smem();  // the token's generic reads precede the producer's copies
+            bar_arrive_all(BAR_SPLIT);
+            bar_sync_all(BAR_ROUTED);
+        }
+    } else {
+        // max |x_t| for the per-token power-of-two prescale (one atomic per warp)
+        if (!s.abort) {
+            for (int t = 0; t < T; ++t) {
+                float m = 0.0f;
+                for (int i = tid; i < H; i += NTHREADS) {
+                    const float a = fabsf(xval(t * H + i));
+                    if (a < 3.0e38f) m = fmaxf(m, a);
+                }
+                m = warp_max_f32(m);
+                if (lane == 0 && m > 0.0f) atomicMax(&s.xmax[t], __float_as_uint(m));
+            }
+        }
+        __syncthreads();
+        // The first nd warps form the router logits (one (row, token) item each, in
+        // turn); each logit goes out as one tagged word the moment it is formed.  The
+        // other warps split the tokens into E4M3 terms meanwhile:
+        //   x_t * 2^s_t = term 0 + term 1 (+ term 2), column (t, j) holding term j of
+        //   token t, H bytes at xterm + (t*JX + j)*CS.
+        const int nd = nitems < NWARPS ? nitems : NWARPS;
+        if (!s.abort) {
+            if (warp < nd) {
+                for (int it = warp; it < nitems; it += NWARPS) {
+                    const int r = it / T, t = it - r * T;
+                    const float* wr = rows + (size_t)r * H;
+                    const float v = xbf ? router_dot<true>(wr, xs + (size_t)t * H * 2, H, lane)
+                                        : router_dot<false>(wr, xs + (size_t)t * H * 4, H, lane);
+                    if (lane == 0 && !(p.dbg_hold && row_lo + r == 0))
+                        st_relaxed_u64(p.logits + (size_t)t * LS + row_lo + r, tag_word(tag, v));
+                }
+            }
+            if (warp >= nd || nd == NWARPS) {
+                const int nsw = nd == NWARPS ? NWARPS : NWARPS - nd;  // warps on the split
+                const int st0 = (nd == NWARPS ? warp : warp - nd) * 32 + lane;
+                for (int t = 0; t < T; ++t) {
+                    const int sx = prescale_exp(__uint_as_float(s.xmax[t]));
+                    uint8_t* col = xterm + (size_t)(t * cv.JX) * cv.CS;
+                    for (int i = 2 * st0; i < H; i += 2 * 32 * nsw) {
+                        float a = scale2(xval(t * H + i), sx), b = scale2(xval(t * H + i + 1), sx);
+                        for (int j = 0; j < cv.JX; ++j) {
+                            const uint16_t d = e4m3_term2(a, b);
+                            *reinterpret_cast<uint16_t*>(col + (size_t)j * cv.CS + i) = d;
+                        }
                     }
                 }
             }
         }
+        if (tid < T) {
+            const int e = prescale_exp(__uint_as_float(s.xmax[tid]));
+            s.xexp[tid] = e;
+            s.xscale[tid] = scale2(1.0f, -e);
+        }
     }
-    if (tid < T) {
-        const int e = prescale_exp(__uint_as_float(s.xmax[tid]));
-        s.xexp[tid] = e;
-        s.xscale[tid] = scale2(1.0f, -e);
-    }
-    __syncthreads();  // the ring's tokens are dead from here on: it holds the routing scratch
-
     // ---------------- phase K: every logit of the grid, top-k, grouping (every CTA) ----------------
-    RouteScratch rs;
-    {
-        const int nch = (E + 31) >> 5;
-        const uint32_t lgb = ((uint32_t)T * LS * 4u + 15u) & ~15u;
-        const uint32_t cab = (uint32_t)T * nch * K * 8u;
-        rs.lg = reinterpret_cast<float*>(ring);
-        rs.ex = reinterpret_cast<float*>(ring + lgb);
-        rs.ca = reinterpret_cast<unsigned long long*>(ring + 2 * lgb);
-        rs.cb = reinterpret_cast<unsigned long long*>(ring + 2 * lgb + cab);
-        rs.fin = reinterpret_cast<unsigned long long*>(ring + 2 * lgb + 2 * cab);
-    }
-    if (!s.abort) {
-        constexpr int NPW = (T * (MAXE + 1) + NTHREADS - 1) / NTHREADS;
-        if (!poll_words<NPW>(p.logits, T * Er, Er, LS, rs.lg, LS, tag, limit, s))
-            set_error(err, s, CZ_DERR_ROUTER_BARRIER);
-    }
-    __syncthreads();
+    // (one token: only when route_one gave up)
     const int P = T * K + (SI ? T : 0);
-    if (tid == 0) s.fastgroup = 0;
-    if (!s.abort) {
-        route_all(rs, T, E, K, LS, p.norm_topk, SI != 0, s, p.topk_idx, p.topk_gates, c == 0);
-        if (T == 1 && warp == 0) {
-            // One token: its K experts are distinct unless a selection round found no
-            // candidate (NaN logits), so each pair is a group of its own, in ascending
-            // expert order.  The warp that ranked the token forms the groups in a few
-            // shuffles; duplicates fall through to the general path below.
-            __syncwarp();
-            const bool act = lane < K;
-            const int myid = act ? s.pe[lane] : 0x7fffffff;
-            int rho = 0;
-            bool dup = false;
-#pragma unroll 4
-            for (int m = 0; m < MAXK; ++m) {
-                const int im = __shfl_sync(0xffffffffu, myid, m);
-                rho += (m < K) & (im < myid);
-                dup |= act & (m < K) & (m != lane) & (im == myid);
-            }
-            if (!__any_sync(0xffffffffu, dup)) {
-                const int drows = s.geo_drows, per = s.geo_per, rbytes = s.geo_rbytes;
-                const bool held = act && myid >= p.e_lo && myid < p.e_hi;
-                const uint32_t hm = __reduce_or_sync(0xffffffffu, held ? (1u << rho) : 0u);
-                const int k = __popc(hm & ((1u << rho) - 1u));  // index among held routed groups
-                const int nr = __popc(hm);
-                if (act) {
-                    s.g_expert[rho] = myid;
-                    s.g_pair0[rho] = rho;
-                    s.g_npairs[rho] = 1;
-                    s.order[rho] = lane;
-                    s.rtok[rho] = held ? 0 : -1;
-                    s.g_chunk0[rho] = k * (Ir / CR);
-                    s.g_pack[rho] = held && drows > 0 ? k / per : -1;
-                    s.g_poff[rho] = held && drows > 0 ? (k % per) * rbytes : 0;
+    bool general = true;
+    if constexpr (T == 1) general = s.fastgroup == 0;
+    if (general) {
+        __syncthreads();  // the ring's tokens are dead from here on: it holds the routing scratch
+
+        RouteScratch rs;
+        {
+            const int nch = (E + 31) >> 5;
+            const uint32_t lgb = ((uint32_t)T * LS * 4u + 15u) & ~15u;
+            const uint32_t cab = (uint32_t)T * nch * K * 8u;
+            rs.lg = reinterpret_cast<float*>(ring);
+            rs.ex = reinterpret_cast<float*>(ring + lgb);
+            rs.ca = reinterpret_cast<unsigned long long*>(ring + 2 * lgb);
+            rs.cb = reinterpret_cast<unsigned long long*>(ring + 2 * lgb + cab);
+            rs.fin = reinterpret_cast<unsigned long long*>(ring + 2 * lgb + 2 * cab);
+        }
+        if (!s.abort) {
+            constexpr int NPW = (T * (MAXE + 1) + NTHREADS - 1) / NTHREADS;
+            if (!poll_words<NPW>(p.logits, T * Er, Er, LS, rs.lg, LS, tag, limit, s))
+                set_error(err, s, CZ_DERR_ROUTER_BARRIER);
+        }
+        __syncthreads();
+        if (tid == 0) s.fastgroup = 0;
+        if (!s.abort) {
+            route_all(rs, T, E, K, LS, p.norm_topk, SI != 0, s, p.topk_idx, p.topk_gates, c == 0);
+            if (T == 1 && warp == 0) {
+                // One token: its K experts are distinct unless a selection round found no
+                // candidate (NaN logits), so each pair is a group of its own, in ascending
+                // expert order.  The warp that ranked the token forms the groups in a few
+                // shuffles; duplicates fall through to the general path below.
+                __syncwarp();
+                const bool act = lane < K;
+                const int myid = act ? s.pe[lane] : 0x7fffffff;
+                int rho = 0;
+                bool dup = false;
+    #pragma unroll 4
+                for (int m = 0; m < MAXK; ++m) {
+                    const int im = __shfl_sync(0xffffffffu, myid, m);
+                    rho += (m < K) & (im < myid);
+                    dup |= act & (m < K) & (m != lane) & (im == myid);
                 }
-                if (lane == 0) {
-                    int U = K, nc = nr * (Ir / CR);
-                    int npk = nr > 0 && drows > 0 ? (nr - 1) / per + 1 : 0;
-                    if (SI) {  // the shared expert: pair T*K = K, the last group
-                        s.g_expert[K] = E;
-                        s.g_pair0[K] = K;
-                        s.g_npairs[K] = 1;
-                        s.order[K] = K;
-                        s.rtok[K] = p.shared_here ? 0 : -1;
-                        s.g_chunk0[K] = nc;
-                        s.g_pack[K] = -1;
-                        s.g_poff[K] = 0;
-                        if (p.shared_here) {
-                            nc += SI / CR;
-                            if (drows > 0) {
-                                const int sbytes = drows * SI + s.geo_nrb * cz_nbp(SI) * 4;
-                                const int fill = nr > 0 ? (nr - (npk - 1) * per) * rbytes : SLOT_BYTES;
-                                if (npk > 0 && fill + sbytes <= SLOT_BYTES) {
-                                    s.g_pack[K] = npk - 1;
-                                    s.g_poff[K] = fill;
-                                } else {
-                                    s.g_pack[K] = npk;
-                                    ++npk;
+                if (!__any_sync(0xffffffffu, dup)) {
+                    const int drows = s.geo_drows, per = s.geo_per, rbytes = s.geo_rbytes;
+                    const bool held = act && myid >= p.e_lo && myid < p.e_hi;
+                    const uint32_t hm = __reduce_or_sync(0xffffffffu, held ? (1u << rho) : 0u);
+                    const int k = __popc(hm & ((1u << rho) - 1u));  // index among held routed groups
+                    const int nr = __popc(hm);
+                    if (act) {
+                        s.g_expert[rho] = myid;
+                        s.g_pair0[rho] = rho;
+                        s.g_npairs[rho] = 1;
+                        s.order[rho] = lane;
+                        s.rtok[rho] = held ? 0 : -1;
+                        s.g_chunk0[rho] = k * (Ir / CR);
+                        s.g_pack[rho] = held && drows > 0 ? k / per : -1;
+                        s.g_poff[rho] = held && drows > 0 ? (k % per) * rbytes : 0;
+                    }
+                    if (lane == 0) {
+                        int U = K, nc = nr * (Ir / CR);
+                        int npk = nr > 0 && drows > 0 ? (nr - 1) / per + 1 : 0;
+                        if (SI) {  // the shared expert: pair T*K = K, the last group
+                            s.g_expert[K] = E;
+                            s.g_pair0[K] = K;
+                            s.g_npairs[K] = 1;
+                            s.order[K] = K;
+                            s.rtok[K] = p.shared_here ? 0 : -1;
+                            s.g_chunk0[K] = nc;
+                            s.g_pack[K] = -1;
+                            s.g_poff[K] = 0;
+                            if (p.shared_here) {
+                                nc += SI / CR;
+                                if (drows > 0) {
+                                    const int sbytes = drows * SI + s.geo_nrb * cz_nbp(SI) * 4;
+                                    const int fill = nr > 0 ? (nr - (npk - 1) * per) * rbytes : SLOT_BYTES;
+                                    if (npk > 0 && fill + sbytes <= SLOT_BYTES) {
+                                        s.g_pack[K] = npk - 1;
+                                        s.g_poff[K] = fill;
+                                    } else {
+                                        s.g_pack[K] = npk;
+                                        ++npk;
+                                    }
                                 }
                             }
+                            U = K + 1;
                         }
-                        U = K + 1;
+                        if (p.hslot && npk > cv.ns - 1) set_error(err, s, CZ_DERR_SHAPE);
+                        s.g_chunk0[U] = nc;
+                        s.U = U;
+                        s.P = P;
+                        s.NC = nc;
+                        s.npk = npk;
+                        s.fastgroup = 1;
                     }
+                }
+            }
+        }
+        // the ring held generic-proxy data (the routing scratch) and is next written by
+        // bulk copies: order every thread's accesses before them
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (!s.abort && !s.fastgroup) {
+            // pairs sorted by (expert, pair) with ranks: P <= 68
+            for (int i = tid; i < P; i += NTHREADS) {
+                const int e = s.pe[i];
+                int r = 0;
+                for (int j = 0; j < P; ++j) {
+                    const int ej = s.pe[j];
+                    r += (ej < e) | ((ej == e) & (j < i));
+                }
+                s.order[r] = i;
+            }
+        }
+        __syncthreads();
+        if (warp == 0 && !s.fastgroup) {
+            if (!s.abort) {
+                // Groups: runs of one expert in sorted order.  A token picks an expert at
+                // most once, except in selection rounds without a candidate (every
+                // remaining logit NaN), which all pick expert 0; a run longer than the
+                // gate/up MMA columns hold (maxq pairs) is split into groups of maxq pairs
+                // (each reads the expert's weights again).  Up to 3 sorted positions per
+                // lane: r = 32 w + lane.
+                const int maxq = cv.rc / cv.JX;
+                int pe_r[3];
+                uint32_t chg[3];
+    #pragma unroll 1
+                for (int w = 0; w < 3; ++w) {
+                    const int r = 32 * w + lane;
+                    pe_r[w] = r < P ? s.pe[s.order[r]] : -1;
+                    const int prev = __shfl_up_sync(0xffffffffu, pe_r[w], 1);
+                    const int prev_w = w > 0 ? __shfl_sync(0xffffffffu, pe_r[w > 0 ? w - 1 : 0], 31) : -1;
+                    const int pv = lane == 0 ? prev_w : prev;
+                    chg[w] = __ballot_sync(0xffffffffu, r < P && (r == 0 || pe_r[w] != pv));
+                }
+                // a position starts a group when its distance to its run's first position
+                // is a multiple of maxq
+                uint32_t stw[3];
+                int u_base[3];
+                int base = 0;
+    #pragma unroll 1
+                for (int w = 0; w < 3; ++w) {
+                    const int r = 32 * w + lane;
+                    int rs0 = -1;  // the run's first position: the last change at or before r
+                    const uint32_t below = lane == 31 ? 0xffffffffu : ((2u << lane) - 1u);
+    #pragma unroll
+                    for (int v = w; v >= 0; --v) {
+                        const uint32_t m = v == w ? (chg[v] & below) : chg[v];
+                        if (rs0 < 0 && m) rs0 = 32 * v + 31 - __clz(m);
+                    }
+                    const bool start = r < P && (r - rs0) % maxq == 0;
+                    stw[w] = __ballot_sync(0xffffffffu, start);
+                    u_base[w] = base;
+                    if (start) {
+                        const int u = base + __popc(stw[w] & ((1u << lane) - 1u));
+                        s.g_expert[u] = pe_r[w];
+                        s.g_pair0[u] = r;
+                    }
+                    base += __popc(stw[w]);
+                }
+                __syncwarp();
+                // per group (up to 3 per lane, u = 32 v + lane): size, held here, first
+                // chunk, phase D pack.  Routed groups all have Ir/CR chunks and rb bytes
+                // of down rows per pack; the shared expert (expert E) is the last group.
+                const int drows = s.geo_drows, nrb = s.geo_nrb, rbytes = s.geo_rbytes, per = s.geo_per;
+                int nr = 0;  // held routed groups before this batch
+    #pragma unroll 1
+                for (int v = 0; v < 3; ++v) {
+                    const int u = 32 * v + lane;
+                    const bool in = u < base;
+                    const int eu = in ? s.g_expert[u] : -1;
+                    const int p0 = in ? s.g_pair0[u] : 0;
+                    const int p1 = u + 1 < base ? s.g_pair0[u + 1] : P;
+                    const bool here = in && (eu == E ? p.shared_here != 0 : (eu >= p.e_lo && eu < p.e_hi));
+                    const bool routed = here && eu != E;
+                    const uint32_t rm = __ballot_sync(0xffffffffu, routed);
+                    const int k = nr + __popc(rm & ((1u << lane) - 1u));  // index among held routed groups
+                    if (in) {
+                        s.g_npairs[u] = p1 - p0;
+                        s.g_chunk0[u] = k * (Ir / CR);
+                        s.g_pack[u] = routed && drows > 0 ? k / per : -1;
+                        s.g_poff[u] = routed && drows > 0 ? (k % per) * rbytes : 0;
+                        for (int q = p0; q < p1; ++q) s.rtok[q] = here ? pair_token(s.order[q], T, K) : -1;
+                    }
+                    nr += __popc(rm);
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    int nc = nr * (Ir / CR);
+                    int npk = nr > 0 && drows > 0 ? (nr - 1) / per + 1 : 0;
+                    if (base > 0 && s.g_expert[base - 1] == E && p.shared_here) {
+                        nc += SI / CR;
+                        if (drows > 0) {
+                            const int sbytes = drows * SI + nrb * cz_nbp(SI) * 4;
+                            const int fill = nr > 0 ? (nr - (npk - 1) * per) * rbytes : SLOT_BYTES;
+                            if (npk > 0 && fill + sbytes <= SLOT_BYTES) {
+                                s.g_pack[base - 1] = npk - 1;
+                                s.g_poff[base - 1] = fill;
+                            } else {
+                                s.g_pack[base - 1] = npk;
+                                s.g_poff[base - 1] = 0;
+                                ++npk;
+                            }
+                        }
+                    }
+                    // hslot: the slot after the last pack must be free (the host checked the worst case)
                     if (p.hslot && npk > cv.ns - 1) set_error(err, s, CZ_DERR_SHAPE);
-                    s.g_chunk0[U] = nc;
-                    s.U = U;
+                    s.g_chunk0[base] = nc;
+                    s.U = base;
                     s.P = P;
                     s.NC = nc;
                     s.npk = npk;
-                    s.fastgroup = 1;
                 }
+            } else if (lane == 0) {
+                s.U = 0;
+                s.NC = 0;
+                s.npk = 0;
             }
         }
+        __syncthreads();
     }
-    // the ring held generic-proxy data (the routing scratch) and is next written by
-    // bulk copies: order every thread's accesses before them
-    fence_proxy_async_smem();
-    __syncthreads();
-    if (!s.abort && !s.fastgroup) {
-        // pairs sorted by (expert, pair) with ranks: P <= 68
-        for (int i = tid; i < P; i += NTHREADS) {
-            const int e = s.pe[i];
-            int r = 0;
-            for (int j = 0; j < P; ++j) {
-                const int ej = s.pe[j];
-                r += (ej < e) | ((ej == e) & (j < i));
-            }
-            s.order[r] = i;
-        }
-    }
-    __syncthreads();
-    if (warp == 0 && !s.fastgroup) {
-        if (!s.abort) {
-            // Groups: runs of one expert in sorted order.  A token picks an expert at
-            // most once, except in selection rounds without a candidate (every
-            // remaining logit NaN), which all pick expert 0; a run longer than the
-            // gate/up MMA columns hold (maxq pairs) is split into groups of maxq pairs
-            // (each reads the expert's weights again).  Up to 3 sorted positions per
-            // lane: r = 32 w + lane.
-            const int maxq = cv.rc / cv.JX;
-            int pe_r[3];
-            uint32_t chg[3];
-#pragma unroll 1
-            for (int w = 0; w < 3; ++w) {
-                const int r = 32 * w + lane;
-                pe_r[w] = r < P ? s.pe[s.order[r]] : -1;
-                const int prev = __shfl_up_sync(0xffffffffu, pe_r[w], 1);
-                const int prev_w = w > 0 ? __shfl_sync(0xffffffffu, pe_r[w > 0 ? w - 1 : 0], 31) : -1;
-                const int pv = lane == 0 ? prev_w : prev;
-                chg[w] = __ballot_sync(0xffffffffu, r < P && (r == 0 || pe_r[w] != pv));
-            }
-            // a position starts a group when its distance to its run's first position
-            // is a multiple of maxq
-            uint32_t stw[3];
-            int u_base[3];
-            int base = 0;
-#pragma unroll 1
-            for (int w = 0; w < 3; ++w) {
-                const int r = 32 * w + lane;
-                int rs0 = -1;  // the run's first position: the last change at or before r
-                const uint32_t below = lane == 31 ? 0xffffffffu : ((2u << lane) - 1u);
-#pragma unroll
-                for (int v = w; v >= 0; --v) {
-                    const uint32_t m = v == w ? (chg[v] & below) : chg[v];
-                    if (rs0 < 0 && m) rs0 = 32 * v + 31 - __clz(m);
-                }
-                const bool start = r < P && (r - rs0) % maxq == 0;
-                stw[w] = __ballot_sync(0xffffffffu, start);
-                u_base[w] = base;
-                if (start) {
-                    const int u = base + __popc(stw[w] & ((1u << lane) - 1u));
-                    s.g_expert[u] = pe_r[w];
-                    s.g_pair0[u] = r;
-                }
-                base += __popc(stw[w]);
-            }
-            __syncwarp();
-            // per group (up to 3 per lane, u = 32 v + lane): size, held here, first
-            // chunk, phase D pack.  Routed groups all have Ir/CR chunks and rb bytes
-            // of down rows per pack; the shared expert (expert E) is the last group.
-            const int drows = s.geo_drows, nrb = s.geo_nrb, rbytes = s.geo_rbytes, per = s.geo_per;
-            int nr = 0;  // held routed groups before this batch
-#pragma unroll 1
-            for (int v = 0; v < 3; ++v) {
-                const int u = 32 * v + lane;
-                const bool in = u < base;
-                const int eu = in ? s.g_expert[u] : -1;
-                const int p0 = in ? s.g_pair0[u] : 0;
-                const int p1 = u + 1 < base ? s.g_pair0[u + 1] : P;
-                const bool here = in && (eu == E ? p.shared_here != 0 : (eu >= p.e_lo && eu < p.e_hi));
-                const bool routed = here && eu != E;
-                const uint32_t rm = __ballot_sync(0xffffffffu, routed);
-                const int k = nr + __popc(rm & ((1u << lane) - 1u));  // index among held routed groups
-                if (in) {
-                    s.g_npairs[u] = p1 - p0;
-                    s.g_chunk0[u] = k * (Ir / CR);
-                    s.g_pack[u] = routed && drows > 0 ? k / per : -1;
-                    s.g_poff[u] = routed && drows > 0 ? (k % per) * rbytes : 0;
-                    for (int q = p0; q < p1; ++q) s.rtok[q] = here ? pair_token(s.order[q], T, K) : -1;
-                }
-                nr += __popc(rm);
-            }
-            __syncwarp();
-            if (lane == 0) {
-                int nc = nr * (Ir / CR);
-                int npk = nr > 0 && drows > 0 ? (nr - 1) / per + 1 : 0;
-                if (base > 0 && s.g_expert[base - 1] == E && p.shared_here) {
-                    nc += SI / CR;
-                    if (drows > 0) {
-                        const int sbytes = drows * SI + nrb * cz_nbp(SI) * 4;
-                        const int fill = nr > 0 ? (nr - (npk - 1) * per) * rbytes : SLOT_BYTES;
-                        if (npk > 0 && fill + sbytes <= SLOT_BYTES) {
-                            s.g_pack[base - 1] = npk - 1;
-                            s.g_poff[base - 1] = fill;
-                        } else {
-                            s.g_pack[base - 1] = npk;
-                            s.g_poff[base - 1] = 0;
-                            ++npk;
-                        }
-                    }
-                }
-                // hslot: the slot after the last pack must be free (the host checked the worst case)
-                if (p.hslot && npk > cv.ns - 1) set_error(err, s, CZ_DERR_SHAPE);
-                s.g_chunk0[base] = nc;
-                s.U = base;
-                s.P = P;
-                s.NC = nc;
-                s.npk = npk;
-            }
-        } else if (lane == 0) {
-            s.U = 0;
-            s.NC = 0;
-            s.npk = 0;
-        }
-    }
-    __syncthreads();
 
     // ---------------- phase C: this CTA's chunks; phase D: this CTA's output rows ----------------
     const int o_lo = split_at(c, H, G), o_hi = split_at(c + 1, H, G);
@@ -1177,6 +1442,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                         }
                         u = u1;
                     }
+                }
+                // CTA 0 advances the launch sequence (the next launch's tag) once every
+                // CTA has counted itself in (reg[0], right after it read the sequence):
+                // no CTA of this launch reads it later, and the next launch starts only
+                // after this one has ended.  A count that never completes leaves the
+                // sequence as it is and sets an error bit.
+                if (c == 0) {
+                    bool in = false;
+                    for (uint32_t it = 0; it < limit && !in; ++it) {
+                        in = ld_relaxed_gpu(&reg[0]) >= (uint32_t)G;
+                        if (!in) __nanosleep(100);
+                    }
+                    if (in)
+                        st_relaxed_u32(p.sync, seq + 1u);
+                    else
+                        atomicOr(err, CZ_DERR_SEQ_WAIT);
                 }
                 // drain: no copy may land after this CTA exits (waiting on a phase
                 // that already completed returns at once)
@@ -1541,15 +1822,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     }
 
     // ---------------- completion: advance the launch sequence ----------------
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        const uint32_t old = atomicAdd(&reg[1], 1u);
-        if (old == (uint32_t)G - 1u) {
-            // every CTA has arrived, so every error bit is in the word
+    // With a status slot the last CTA to finish copies the error word there (every
+    // CTA's bits are in it by then).  The sequence was advanced by CTA 0's producer.
+    if (p.status_out) {
+        __syncthreads();
+        if (tid == 0) {
             __threadfence();
-            if (p.status_out) *p.status_out = ld_relaxed_gpu(err);
-            atomicExch(p.sync, seq + 1u);
+            const uint32_t old = atomicAdd(&reg[1], 1u);
+            if (old == (uint32_t)G - 1u) {
+                __threadfence();
+                *p.status_out = ld_relaxed_gpu(err);
+            }
         }
     }
 }
@@ -1671,11 +1954,17 @@ int decode_launch(const DecodeParams& prm, int num_sms, cudaStream_t stream) {
     p.hslot = decode_hslot(p.T, p.H, p.K, p.I, p.SI, p.x_bf16, num_sms);
     cfg.dynamicSmemBytes = decode_smem_bytes(p.T, p.H, p.x_bf16, p.hslot);
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    // Cooperative (every CTA resident: they exchange words), and programmatic
+    // dependent launch: the launch may begin while the previous kernel of the stream
+    // ends (its CTAs take the SMs that kernel's CTAs leave); it reads nothing that
+    // kernel writes before its griddepcontrol.wait.
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     if (cudaLaunchKernelEx(&cfg, kern[p.T - 1], p) != cudaSuccess) return CZ_ELAUNCH;
     return CZ_OK;
 }
