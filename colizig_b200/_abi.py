@@ -34,13 +34,20 @@ MOE_SYMBOLS = (
     "colizig_cuda_moe_check",
     "colizig_cuda_debug_expf",
     "colizig_cuda_debug_hold_router",
+    "colizig_cuda_debug_watch_wait",
     "colizig_cuda_moe_forward_noalloc",
     "colizig_cuda_ep_unique_id",
     "colizig_cuda_ep_init",
     "colizig_cuda_ep_shutdown",
+    "colizig_cuda_ep_set_timeout",
+    "colizig_cuda_ep_abort",
     "colizig_cuda_kernel_timer",
     "colizig_cuda_kernel_timer_read",
 )
+
+# callback types of colizig_cuda_debug_watch_wait (query / async error, abort)
+WATCH_QUERY = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
+WATCH_ABORT = ctypes.CFUNCTYPE(None, ctypes.c_void_p)
 
 COLIZIG_PTR_DEVICE = 1
 COLIZIG_EP = 2
@@ -145,6 +152,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         L.colizig_cuda_ep_init.argtypes = [i32, i32, vp]
         L.colizig_cuda_ep_shutdown.restype = i32
         L.colizig_cuda_ep_shutdown.argtypes = []
+        L.colizig_cuda_ep_set_timeout.restype = i32
+        L.colizig_cuda_ep_set_timeout.argtypes = [i32]
+        L.colizig_cuda_ep_abort.restype = i32
+        L.colizig_cuda_ep_abort.argtypes = []
         L.colizig_cuda_kernel_timer.restype = i32
         L.colizig_cuda_kernel_timer.argtypes = [i32]
         L.colizig_cuda_kernel_timer_read.restype = i32
@@ -153,6 +164,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         L.colizig_cuda_debug_expf.argtypes = [vp, vp, ctypes.c_size_t]
         L.colizig_cuda_debug_hold_router.restype = i32
         L.colizig_cuda_debug_hold_router.argtypes = [u32]
+        L.colizig_cuda_debug_watch_wait.restype = i32
+        L.colizig_cuda_debug_watch_wait.argtypes = [WATCH_QUERY, WATCH_QUERY, WATCH_ABORT, ctypes.c_void_p, i32]
         _lib = L
         return L
 

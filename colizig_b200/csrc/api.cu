@@ -17,10 +17,12 @@
 #include <string.h>
 
 #include <algorithm>
+#include <chrono>
 #include <climits>
 #include <list>
 #include <map>
 #include <mutex>
+#include <thread>
 #include <unordered_map>
 #include <tuple>
 #include <vector>
@@ -169,6 +171,8 @@ struct Ctx {
     bool ep_on = false;
     int ep_rank = 0, ep_world = 1;
     ncclComm_t ep_comm = nullptr;
+    int ep_timeout_ms = 60000;  // watched host waits while a communicator is active (<= 0: unwatched)
+    bool ep_aborted = false;    // the communicator was aborted; EP calls return -9 until re-initialised
     // sharded expert parallelism (prefill): routing of this rank's tokens, exchange buffers
     DevBuf sh_idx, sh_gates, sh_xn, sh_slot, sh_counts, sh_allc, sh_tmp, sh_send, sh_recv, sh_x, sh_ridx, sh_rgates,
         sh_part, sh_back;
@@ -202,6 +206,9 @@ struct NcclApi {
     ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*groupStart)() = nullptr;
     ncclResult_t (*groupEnd)() = nullptr;
+    // optional (the watchdog uses them when present)
+    ncclResult_t (*commAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*commGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
     bool load() {
         if (h) return true;
         void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
@@ -216,6 +223,8 @@ struct NcclApi {
         recv = reinterpret_cast<decltype(recv)>(dlsym(lib, "ncclRecv"));
         groupStart = reinterpret_cast<decltype(groupStart)>(dlsym(lib, "ncclGroupStart"));
         groupEnd = reinterpret_cast<decltype(groupEnd)>(dlsym(lib, "ncclGroupEnd"));
+        commAbort = reinterpret_cast<decltype(commAbort)>(dlsym(lib, "ncclCommAbort"));
+        commGetAsyncError = reinterpret_cast<decltype(commGetAsyncError)>(dlsym(lib, "ncclCommGetAsyncError"));
         if (!getUniqueId || !commInitRank || !allReduce || !commDestroy || !allGather || !send || !recv ||
             !groupStart || !groupEnd)
             return false;
@@ -227,6 +236,57 @@ NcclApi nccl;
 
 Ctx g;
 std::mutex g_mu;
+
+// A host wait with a deadline.  query(): 0 done, 1 pending, < 0 failed;
+// async_error(): true when the communicator reports an error of its own;
+// abort_comm(): called once when the wait gives up.  A peer that never joins a
+// collective would otherwise keep the caller waiting for good: after timeout_ms
+// (or on an asynchronous communicator error) the communicator is aborted, which
+// makes its kernels return, and -9 comes back.
+template <class Q, class AE, class AB>
+int watch_wait(Q query, AE async_error, AB abort_comm, int timeout_ms) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (uint64_t it = 0;; ++it) {
+        const int q = query();
+        if (q == 0) return CZ_OK;
+        if (q < 0) return CZ_ED2H;
+        const bool late = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0)
+                              .count() >= timeout_ms;
+        if (async_error() || late) {
+            abort_comm();
+            return CZ_ENCCL;
+        }
+        if (it >= 64) std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+// Abort the EP communicator (caller holds g_mu): its kernels return, later EP
+// calls return -9 until colizig_cuda_ep_shutdown + colizig_cuda_ep_init.
+void ep_abort_locked() {
+    if (g.ep_comm) {
+        if (nccl.commAbort) nccl.commAbort(g.ep_comm);
+        g.ep_comm = nullptr;
+    }
+    if (g.ep_on && g.ep_world > 1) g.ep_aborted = true;
+}
+
+// Synchronise `st`; watched (watch_wait) while an EP communicator is active.
+int stream_sync(cudaStream_t st) {
+    if (!g.ep_comm || g.ep_timeout_ms <= 0) return cudaStreamSynchronize(st) == cudaSuccess ? CZ_OK : CZ_ED2H;
+    return watch_wait(
+        [&]() -> int {
+            const cudaError_t e = cudaStreamQuery(st);
+            if (e == cudaSuccess) return 0;
+            if (e == cudaErrorNotReady) return 1;
+            return -1;
+        },
+        [&]() -> bool {
+            ncclResult_t r = ncclSuccess;
+            if (!nccl.commGetAsyncError || nccl.commGetAsyncError(g.ep_comm, &r) != ncclSuccess) return false;
+            return r != ncclSuccess && r != ncclInProgress;
+        },
+        [&]() { ep_abort_locked(); }, g.ep_timeout_ms);
+}
 
 // Forgets the cached device addresses of the no-allocation scratch (defined with
 // colizig_cuda_moe_forward_noalloc below), so the first call after an init does
@@ -531,7 +591,8 @@ int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uin
 // the counts, so this path synchronises the stream once per call).
 int moe_run_sharded(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uint32_t* idx_out,
                     float* gates_out, const float* rms_w, float eps, const float* residual, cudaStream_t st) {
-    if (!L.ep || g.ep_world < 2 || !g.ep_comm) return CZ_EARGS;
+    if (!L.ep || g.ep_world < 2) return CZ_EARGS;
+    if (!g.ep_comm) return CZ_ENCCL;  // aborted
     if (L.d.shared_inter || !L.pf_ok) return CZ_ESHAPE;  // the same verdict on every rank (same layer)
     const int W = g.ep_world, me = g.ep_rank;
     const int K = (int)L.d.topk, E = (int)L.d.experts, H = (int)L.d.hidden;
@@ -589,9 +650,9 @@ int moe_run_sharded(const MoeLayer& L, const void* x, int x_bf16, int T, float* 
     const int CW = W + 5;
     if (nccl.allGather(g.sh_counts.p, g.sh_allc.p, (size_t)CW, ncclInt32, g.ep_comm, st) != ncclSuccess) return CZ_ENCCL;
     std::vector<int> allc((size_t)W * CW);
-    if (cudaMemcpyAsync(allc.data(), g.sh_allc.p, allc.size() * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-        cudaStreamSynchronize(st) != cudaSuccess)
+    if (cudaMemcpyAsync(allc.data(), g.sh_allc.p, allc.size() * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
         return CZ_ED2H;
+    if (const int src = stream_sync(st)) return src;
     for (int r = 0; r < W; ++r)  // the same verdict on every rank: no exchange of mismatched sizes
         if (allc[(size_t)r * CW + W] != (int)rs || allc[(size_t)r * CW + W + 1] != H)
             return local_rc ? local_rc : CZ_EARGS;
@@ -630,9 +691,8 @@ int moe_run_sharded(const MoeLayer& L, const void* x, int x_bf16, int T, float* 
         int* dv = g.sh_tmp.as<int>();
         if (cudaMemcpyAsync(dv, &v, 4, cudaMemcpyHostToDevice, st) != cudaSuccess) return CZ_EH2D;
         if (nccl.allReduce(dv, dv, 1, ncclInt32, ncclMin, g.ep_comm, st) != ncclSuccess) return CZ_ENCCL;
-        if (cudaMemcpyAsync(&all, dv, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-            cudaStreamSynchronize(st) != cudaSuccess)
-            return CZ_ED2H;
+        if (cudaMemcpyAsync(&all, dv, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) return CZ_ED2H;
+        if (const int src = stream_sync(st)) return src;
         if (!all) return CZ_EALLOC;
     }
     // 4. pack; 5. exchange the rows
@@ -689,7 +749,7 @@ int check_device_error(cudaStream_t st) {
     if (!g.sync) return CZ_OK;
     uint32_t err = 0;
     if (cudaMemcpyAsync(&err, g.sync + 1, sizeof err, cudaMemcpyDeviceToHost, st) != cudaSuccess) return CZ_ED2H;
-    if (cudaStreamSynchronize(st) != cudaSuccess) return CZ_ED2H;
+    if (const int src = stream_sync(st)) return src;
     if (err) {
         cudaMemsetAsync(g.sync + 1, 0, sizeof(uint32_t), st);
         cudaStreamSynchronize(st);
@@ -1085,7 +1145,7 @@ CZ_EXPORT int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtyp
         if (gi != g.host_graphs.end()) {
             memcpy(g.io_xh.p, x, xb);
             if (cudaGraphLaunch(gi->second, g.stream) != cudaSuccess) return CZ_ELAUNCH;
-            if (cudaStreamSynchronize(g.stream) != cudaSuccess) return CZ_ED2H;
+            if (const int src = stream_sync(g.stream)) return src;
             const uint8_t* const hs = static_cast<const uint8_t*>(g.io_host.p);
             uint32_t err = 0;
             memcpy(&err, hs + eo, sizeof err);
@@ -1114,7 +1174,7 @@ CZ_EXPORT int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtyp
                  topk_gates ? reinterpret_cast<float*>(res + go) : nullptr, g.stream,
                  kernel_status ? reinterpret_cast<uint32_t*>(res + eo) : nullptr);
     if (rc) {
-        cudaStreamSynchronize(g.stream);
+        stream_sync(g.stream);
         return rc;
     }
     if (!ob) return check_device_error(g.stream);
@@ -1129,7 +1189,7 @@ CZ_EXPORT int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtyp
          cudaMemcpyAsync(res + eo, g.sync + 1, sizeof(uint32_t), cudaMemcpyDeviceToDevice, g.stream) != cudaSuccess) ||
         cudaMemcpyAsync(g.io_host.p, res, rb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess)
         return CZ_ED2H;
-    if (cudaStreamSynchronize(g.stream) != cudaSuccess) return CZ_ED2H;
+    if (const int src = stream_sync(g.stream)) return src;
     const uint8_t* const hs = static_cast<const uint8_t*>(g.io_host.p);
     uint32_t err = 0;
     memcpy(&err, hs + eo, sizeof err);
@@ -1324,9 +1384,36 @@ CZ_EXPORT int colizig_cuda_ep_shutdown(void) {
     if (g.ep_comm) nccl.commDestroy(g.ep_comm);
     g.ep_comm = nullptr;
     g.ep_on = false;
+    g.ep_aborted = false;
     g.ep_rank = 0;
     g.ep_world = 1;
     return CZ_OK;
+}
+
+// Deadline of the library's host waits while an EP communicator is active
+// (<= 0: unwatched); see watch_wait.
+CZ_EXPORT int colizig_cuda_ep_set_timeout(int ms) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    g.ep_timeout_ms = ms;
+    return CZ_OK;
+}
+
+// Abort the EP communicator now (a host watchdog that learned a peer has left
+// calls it between steps): its kernels return, and EP calls return -9 until
+// colizig_cuda_ep_shutdown + colizig_cuda_ep_init.  Needs no device work.
+CZ_EXPORT int colizig_cuda_ep_abort(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    ep_abort_locked();
+    return CZ_OK;
+}
+
+// Test hook for the watched wait: watch_wait over caller-provided fakes of the
+// stream query, the communicator's error report and the abort.
+CZ_EXPORT int colizig_cuda_debug_watch_wait(int (*query)(void*), int (*async_error)(void*), void (*abort_comm)(void*),
+                                            void* ctx, int timeout_ms) {
+    if (!query || !async_error || !abort_comm) return CZ_EARGS;
+    return watch_wait([&]() { return query(ctx); }, [&]() { return async_error(ctx) != 0; },
+                      [&]() { abort_comm(ctx); }, timeout_ms);
 }
 
 // ---- colizig_cuda_moe_forward_noalloc -------------------------------------

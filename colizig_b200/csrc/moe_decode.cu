@@ -617,6 +617,75 @@ __device__ __noinline__ void route_gates(int T, int K, int has_shared, DecodeMis
     __syncwarp();
 }
 
+// One gate/up stage into ring slot `slot` (one thread): slab st/2 of chunk rows
+// [r0, r0+16) of group weights gw, gate (st even) or up (st odd), column blocks
+// [kb0, kb0 + nkbs) as [block][row][128 B] (128-byte swizzle), plus the row block's
+// scales after the slab.
+__device__ __forceinline__ void issue_gu_stage(const DecodeParams& p, DecodeMisc& s, uint8_t* ring, const GroupW& gw,
+                                               int r0, int st, int slot, int nkbH, int nbpH, uint64_t pol) {
+    uint8_t* dst = ring + (size_t)slot * SLOT_BYTES;
+    float* sdst = reinterpret_cast<float*>(dst + GU_BYTES);
+    const bool up = st & 1;
+    const int kb0 = (st >> 1) * (KS / 128), nkbs = min(KS / 128, nkbH - kb0);
+    const CUtensorMap* map = up ? gw.umap : gw.gmap;
+    const float* ssrc = (up ? gw.us : gw.gs) + (size_t)(r0 >> 7) * nbpH;
+    const uint32_t wb = (uint32_t)(CR * 128) * (uint32_t)(p.gu3d ? p.gu_kb : nkbs);
+    mbar_arrive_expect_tx(&s.full[slot], wb + (uint32_t)(nbpH * 4));
+    if (p.gu3d) {
+        tma_box3_g2s(dst, map, 0, gw.gu_row0 + r0, kb0, &s.full[slot], pol);
+    } else {
+        for (int kb = 0; kb < nkbs; ++kb)
+            tma_box_g2s(dst + (size_t)kb * CR * 128, map, (kb0 + kb) * 128, gw.gu_row0 + r0, &s.full[slot], pol);
+    }
+    bulk_g2s(sdst, ssrc, (uint32_t)nbpH * 4u, &s.full[slot]);
+}
+
+// Producer: wait until ring slot `slot` is free for its use number `round`
+// (bounded); false = stop.
+__device__ __forceinline__ bool slot_acquire(DecodeMisc& s, uint32_t* err, int slot, int round) {
+    if (round == 0) return true;
+    bool ok = false;
+    for (uint32_t it = 0; it < CZ_SPIN_LIMIT && !ok && !s.abort; ++it) {
+        ok = mbar_try_wait(&s.empty[slot], (round - 1) & 1);
+        if (!ok && it > 64) __nanosleep(64);
+    }
+    if (!ok && !s.abort) set_error(err, s, CZ_DERR_EMPTY_WAIT);
+    return ok;
+}
+
+// Producer, once the ring is full (stage NS is next): everything this CTA streams
+// later is prefetched into L2, so that the HBM reads of the whole layer call are
+// in flight from the start and a stage issued when its slot frees up finds its
+// bytes in L2.  nst = this CTA's gate/up stages; the packs of down rows follow.
+__device__ __forceinline__ void prefetch_rest(const DecodeParams& p, const DecodeMisc& s, int ch_lo, int ch_hi, int nks,
+                                              int NS, int nst, int drows, int o_lo, int o_hi, bool packs) {
+    const int H = p.H, E = p.E, SI = p.SI, Ir = p.I;
+    int u = 0;
+    for (int ch = ch_lo; ch < ch_hi; ++ch) {
+        while (s.g_chunk0[u + 1] <= ch) ++u;
+        if (2 * nks * (ch - ch_lo + 1) <= NS) continue;  // inside the first ring fill
+        const GroupW gw = group_w(p, s.g_expert[u]);
+        const size_t r0 = (size_t)(ch - s.g_chunk0[u]) * CR;
+        prefetch_l2(gw.gw + r0 * H, (uint32_t)(CR * H));  // 16 whole rows, contiguous
+        prefetch_l2(gw.uw + r0 * H, (uint32_t)(CR * H));
+    }
+    if (packs && drows > 0) {
+        const int rb0 = o_lo >> 7, nrb = ((o_hi - 1) >> 7) - rb0 + 1;
+        const int nkbH = cz_nblk(H);
+        for (int v = 0; v < s.U; ++v) {
+            if (s.g_pack[v] < 0 || nst + s.g_pack[v] < NS) continue;
+            const int ev = s.g_expert[v];
+            const bool sh = ev == E;
+            const int iu = sh ? SI : Ir;
+            prefetch_l2(sh ? p.sh_down_w + (size_t)o_lo * SI : p.down_w + ((size_t)(ev - p.e_lo) * H + o_lo) * Ir,
+                        (uint32_t)drows * (uint32_t)iu);
+            prefetch_l2(sh ? p.sh_down_s + (size_t)rb0 * cz_nbp(SI)
+                           : p.down_s + ((size_t)(ev - p.e_lo) * nkbH + rb0) * cz_nbp(Ir),
+                        (uint32_t)(nrb * cz_nbp(iu) * 4));
+        }
+    }
+}
+
 // One token (T = 1), by one warp and with no CTA barrier: route_all's selection,
 // check and the one-token grouping in a compact form.  The warp polls the tagged
 // router logits straight into registers (expert 32j + lane in key[j]), then takes
@@ -633,41 +702,42 @@ template <int NJ>
 __device__ __forceinline__ bool route_one(const DecodeParams& p, DecodeMisc& s, int ns, int E, int K, int SI,
                                           int Ir, uint32_t tag, uint32_t limit, uint32_t* err, bool write_out) {
     const int lane = threadIdx.x & 31;
-    const int Er = E + (SI ? 1 : 0);
     uint32_t key[NJ];  // logit bits while polling, then the order-preserving keys
     uint32_t pend = 0u;
 #pragma unroll
     for (int j = 0; j < NJ; ++j) {
         key[j] = 0u;
-        if (32 * j + lane < Er) pend |= 1u << j;
+        if (32 * j + lane < E) pend |= 1u << j;
     }
+    // the shared expert's gate logit (word E), by lane 0 (kept out of key[], which
+    // is only ever indexed by constants and so stays in registers)
+    bool psh = SI && lane == 0;
+    uint32_t shb = 0u;
     for (uint32_t it = 0; it < limit; ++it) {
         // every pending word's load first, then the tag checks: the loads overlap
         unsigned long long w[NJ];
 #pragma unroll
         for (int j = 0; j < NJ; ++j) w[j] = (pend & (1u << j)) ? ld_relaxed_u64(p.logits + 32 * j + lane) : 0ull;
+        const unsigned long long ws = psh ? ld_relaxed_u64(p.logits + E) : 0ull;
 #pragma unroll
         for (int j = 0; j < NJ; ++j)
             if ((pend & (1u << j)) && (uint32_t)(w[j] >> 32) == tag) {
                 key[j] = (uint32_t)w[j];
                 pend &= ~(1u << j);
             }
-        if (!__any_sync(0xffffffffu, pend)) break;
+        if (psh && (uint32_t)(ws >> 32) == tag) {
+            shb = (uint32_t)ws;
+            psh = false;
+        }
+        if (!__any_sync(0xffffffffu, pend != 0u || psh)) break;
         if (*(volatile int*)&s.abort) break;
         __nanosleep(it < 256 ? 50 : 200);
     }
-    if (__any_sync(0xffffffffu, pend)) {
+    if (__any_sync(0xffffffffu, pend != 0u || psh)) {
         if (lane == 0) set_error(err, s, CZ_DERR_ROUTER_BARRIER);
         return false;
     }
-    float shl = 0.0f;  // the shared expert's gate logit (word E)
-    if (SI) {
-        uint32_t b = 0u;
-#pragma unroll
-        for (int j = 0; j < NJ; ++j)
-            if (j == (E >> 5)) b = key[j];
-        shl = __uint_as_float(__shfl_sync(0xffffffffu, b, E & 31));
-    }
+    const float shl = __uint_as_float(shb);  // lane 0's
 #pragma unroll
     for (int j = 0; j < NJ; ++j) key[j] = 32 * j + lane < E ? logit_key(__uint_as_float(key[j])) : 0u;
     if (!p.norm_topk) return false;
@@ -690,14 +760,12 @@ __device__ __forceinline__ bool route_one(const DecodeParams& p, DecodeMisc& s, 
             break;
         }
         const uint32_t win = __reduce_min_sync(0xffffffffu, bk == kmax ? (uint32_t)(32 * bj + lane) : 0xffffffffu);
-        if (lane == (int)(win & 31u)) {
+        // the winner's key is cleared by arithmetic on every j (a store to key[win >> 5]
+        // would put key[] in local memory)
+        const uint32_t hit = lane == (int)(win & 31u) ? 1u << (win >> 5) : 0u;
 #pragma unroll
-            for (int j = 0; j < NJ; ++j)
-                if (j == (int)(win >> 5)) {
-                    key[j] = 0u;
-                    taken |= 1u << j;
-                }
-        }
+        for (int j = 0; j < NJ; ++j) key[j] &= ((hit >> j) & 1u) - 1u;
+        taken |= hit;
         if (lane == z) {
             myid = (int)win;
             mykey = kmax;
@@ -792,6 +860,17 @@ __device__ __forceinline__ bool route_one(const DecodeParams& p, DecodeMisc& s, 
         s.npk = npk;
     }
     return true;
+}
+
+// Phase D, one consumer warp: wait for and release packs [pk_done, j_end) (stages
+// si0 + j of the ring); ok turns false when a wait gives up.
+__device__ __forceinline__ void release_packs(DecodeMisc& s, int si0, int NS, int j_end, int& pk_done, bool& ok) {
+    for (; pk_done < j_end; ++pk_done) {
+        const int sidx = si0 + pk_done;
+        if (ok) ok = warp_wait(&s.full[sidx % NS], (sidx / NS) & 1, s);
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&s.empty[sidx % NS]);
+    }
 }
 
 // Named barriers between the consumer warps and the h warp (288 threads each):
@@ -970,6 +1049,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                    : reinterpret_cast<const float*>(xs)[k];
     };
     const int nitems = nrows * T;
+    int si_early = 0;  // gate/up stages the producer issued right after routing (one token)
     if constexpr (T == 1) {
         // One token: the producer warp routes and groups it alone (route_one) while
         // the other warps form this CTA's router logits, max |x| and the token's
@@ -989,12 +1069,53 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
             }
             bool ok = false;
             if (!s.abort)
-                ok = Er <= 128 ? route_one<4>(p, s, cv.ns, E, K, SI, Ir, tag, limit, err, c == 0)
-                               : route_one<17>(p, s, cv.ns, E, K, SI, Ir, tag, limit, err, c == 0);
+                ok = E <= 128 ? route_one<4>(p, s, cv.ns, E, K, SI, Ir, tag, limit, err, c == 0)
+                              : route_one<16>(p, s, cv.ns, E, K, SI, Ir, tag, limit, err, c == 0);
             if (lane == 0) s.fastgroup = ok ? 1 : 0;
             __syncwarp();
             bar_arrive_all(BAR_ROUTED);
             bar_sync_all(BAR_SPLIT);
+            // The down rows of this CTA's output rows (phase D's packs) are prefetched
+            // into L2 now, line by line from the producer warp's other lanes: their HBM
+            // reads then overlap the gate/up stream instead of following it (bulk
+            // prefetches would queue behind the tensor copies of the ring fill).
+            if (ok && lane > 0 && !s.abort) {
+                const int o_lo = split_at(c, H, G), drows = s.geo_drows;
+                const int rb0 = o_lo >> 7, nkbH = cz_nblk(H);
+                for (int v = 0; v < s.U; ++v) {
+                    if (s.g_pack[v] < 0) continue;
+                    const int ev = s.g_expert[v];
+                    const bool sh = ev == E;
+                    const int iu = sh ? SI : Ir;
+                    const uint8_t* w = sh ? p.sh_down_w + (size_t)o_lo * SI
+                                          : p.down_w + ((size_t)(ev - p.e_lo) * H + o_lo) * Ir;
+                    const float* sc = sh ? p.sh_down_s + (size_t)rb0 * cz_nbp(SI)
+                                         : p.down_s + ((size_t)(ev - p.e_lo) * nkbH + rb0) * cz_nbp(Ir);
+                    const int nl = (drows * iu + 127) >> 7;
+                    for (int l = lane - 1; l < nl; l += 31) prefetch_line_l2(w + (size_t)l * 128);
+                    if (lane == 1) {  // the <= 2 row blocks of scales: first and last byte's lines
+                        prefetch_line_l2(sc);
+                        prefetch_line_l2(reinterpret_cast<const uint8_t*>(sc) + s.geo_nrb * cz_nbp(iu) * 4 - 1);
+                    }
+                }
+            }
+            // The first ring fill goes out here, in the code right after routing (the
+            // phase C loop below, cold in the instruction cache when it is first
+            // reached, skips these stages).
+            if (ok && lane == 0 && !s.abort) {
+                fence_proxy_async_smem();  // the ring's generic accesses precede the copies
+                const uint64_t pol = l2_evict_first_policy();
+                const int NC = s.NC, ch_lo = split_at(c, NC, G), ch_hi = split_at(c + 1, NC, G);
+                const int nks = (H + KS - 1) / KS, nkbH = cz_nblk(H), nbpH = cz_nbp(H);
+                int u = 0;
+                for (int ch = ch_lo; ch < ch_hi && si_early < cv.ns; ++ch) {
+                    while (s.g_chunk0[u + 1] <= ch) ++u;
+                    const GroupW gw = group_w(p, s.g_expert[u]);
+                    const int r0 = (ch - s.g_chunk0[u]) * CR;
+                    for (int st = 0; st < 2 * nks && si_early < cv.ns; ++st, ++si_early)
+                        issue_gu_stage(p, s, ring, gw, r0, st, si_early, nkbH, nbpH, pol);
+                }
+            }
         } else {
             const int nd = nitems < NCW ? nitems : NCW;     // warps on the router dot
             const int wt = tid < PW * 32 ? tid : tid - 32;  // thread index among the 288
@@ -1218,7 +1339,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 const int maxq = cv.rc / cv.JX;
                 int pe_r[3];
                 uint32_t chg[3];
-    #pragma unroll 1
+    #pragma unroll
                 for (int w = 0; w < 3; ++w) {
                     const int r = 32 * w + lane;
                     pe_r[w] = r < P ? s.pe[s.order[r]] : -1;
@@ -1232,7 +1353,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 uint32_t stw[3];
                 int u_base[3];
                 int base = 0;
-    #pragma unroll 1
+    #pragma unroll
                 for (int w = 0; w < 3; ++w) {
                     const int r = 32 * w + lane;
                     int rs0 = -1;  // the run's first position: the last change at or before r
@@ -1258,7 +1379,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 // of down rows per pack; the shared expert (expert E) is the last group.
                 const int drows = s.geo_drows, nrb = s.geo_nrb, rbytes = s.geo_rbytes, per = s.geo_per;
                 int nr = 0;  // held routed groups before this batch
-    #pragma unroll 1
+    #pragma unroll
                 for (int v = 0; v < 3; ++v) {
                     const int u = 32 * v + lane;
                     const bool in = u < base;
@@ -1333,48 +1454,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 fence_proxy_async_smem();  // generic reads of the ring (logits) precede the async writes
                 const uint64_t pol = l2_evict_first_policy();
                 int si = 0;
-                // wait until slot si % NS is free again (bounded); false = stop
-                auto acquire_slot = [&](int slot, int round) -> bool {
-                    if (round == 0) return true;
-                    bool ok = false;
-                    for (uint32_t it = 0; it < CZ_SPIN_LIMIT && !ok && !s.abort; ++it) {
-                        ok = mbar_try_wait(&s.empty[slot], (round - 1) & 1);
-                        if (!ok && it > 64) __nanosleep(64);
-                    }
-                    if (!ok && !s.abort) set_error(err, s, CZ_DERR_EMPTY_WAIT);
-                    return ok;
-                };
-                // Once the ring is full (stage NS is next), everything this CTA streams
-                // later is prefetched into L2: the HBM reads of the whole layer call are
-                // then in flight from the start, and a stage issued when its slot frees
-                // up finds its bytes in L2.
                 const int nst = 2 * nks * (ch_hi - ch_lo);  // gate/up stages; the packs follow
-                auto prefetch_rest = [&]() {
-                    int u = 0;
-                    for (int ch = ch_lo; ch < ch_hi; ++ch) {
-                        while (s.g_chunk0[u + 1] <= ch) ++u;
-                        if (2 * nks * (ch - ch_lo + 1) <= NS) continue;  // inside the first ring fill
-                        const GroupW gw = group_w(p, s.g_expert[u]);
-                        const size_t r0 = (size_t)(ch - s.g_chunk0[u]) * CR;
-                        prefetch_l2(gw.gw + r0 * H, (uint32_t)(CR * H));  // 16 whole rows, contiguous
-                        prefetch_l2(gw.uw + r0 * H, (uint32_t)(CR * H));
-                    }
-                    if (drows > 0) {
-                        const int rb0 = o_lo >> 7, nrb = ((o_hi - 1) >> 7) - rb0 + 1;
-                        for (int v = 0; v < s.U; ++v) {
-                            if (s.g_pack[v] < 0 || nst + s.g_pack[v] < NS) continue;
-                            const int ev = s.g_expert[v];
-                            const bool sh = ev == E;
-                            const int iu = sh ? SI : Ir;
-                            prefetch_l2(sh ? p.sh_down_w + (size_t)o_lo * SI
-                                           : p.down_w + ((size_t)(ev - p.e_lo) * H + o_lo) * Ir,
-                                        (uint32_t)drows * (uint32_t)iu);
-                            prefetch_l2(sh ? p.sh_down_s + (size_t)rb0 * cz_nbp(SI)
-                                           : p.down_s + ((size_t)(ev - p.e_lo) * nkbH + rb0) * cz_nbp(Ir),
-                                        (uint32_t)(nrb * cz_nbp(iu) * 4));
-                        }
-                    }
-                };
                 // phase C: gate/up slabs of every chunk
                 {
                     int u = 0;
@@ -1383,27 +1463,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                         const GroupW gw = group_w(p, s.g_expert[u]);
                         const int r0 = (ch - s.g_chunk0[u]) * CR;
                         for (int st = 0; st < 2 * nks && !s.abort; ++st, ++si) {
+                            if (si < si_early) continue;  // issued right after routing
                             const int slot = si % NS;
-                            if (si == NS) prefetch_rest();
-                            if (!acquire_slot(slot, si / NS)) break;
-                            uint8_t* dst = ring + (size_t)slot * SLOT_BYTES;
-                            float* sdst = reinterpret_cast<float*>(dst + GU_BYTES);
-                            // slab st/2: gate (st even) or up (st odd) rows [r0, r0+16), column
-                            // blocks [kb0, kb0 + nkbs) as [block][row][128 B] (128-byte swizzle)
-                            const bool up = st & 1;
-                            const int kb0 = (st >> 1) * (KS / 128), nkbs = min(KS / 128, nkbH - kb0);
-                            const CUtensorMap* map = up ? gw.umap : gw.gmap;
-                            const float* ssrc = (up ? gw.us : gw.gs) + (size_t)(r0 >> 7) * nbpH;
-                            const uint32_t wb = (uint32_t)(CR * 128) * (uint32_t)(p.gu3d ? p.gu_kb : nkbs);
-                            mbar_arrive_expect_tx(&s.full[slot], wb + (uint32_t)(nbpH * 4));
-                            if (p.gu3d) {
-                                tma_box3_g2s(dst, map, 0, gw.gu_row0 + r0, kb0, &s.full[slot], pol);
-                            } else {
-                                for (int kb = 0; kb < nkbs; ++kb)
-                                    tma_box_g2s(dst + (size_t)kb * CR * 128, map, (kb0 + kb) * 128, gw.gu_row0 + r0,
-                                                &s.full[slot], pol);
-                            }
-                            bulk_g2s(sdst, ssrc, (uint32_t)nbpH * 4u, &s.full[slot]);
+                            if (si == NS) prefetch_rest(p, s, ch_lo, ch_hi, nks, NS, nst, drows, o_lo, o_hi, T != 1);
+                            if (!slot_acquire(s, err, slot, si / NS)) break;
+                            issue_gu_stage(p, s, ring, gw, r0, st, slot, nkbH, nbpH, pol);
                         }
                     }
                 }
@@ -1422,8 +1486,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                             bytes += (uint32_t)(drows * iu + nrb * cz_nbp(iu) * 4);
                         }
                         const int slot = si % NS;
-                        if (si == NS) prefetch_rest();
-                        if (!acquire_slot(slot, si / NS)) break;
+                        if (si == NS) prefetch_rest(p, s, ch_lo, ch_hi, nks, NS, nst, drows, o_lo, o_hi, T != 1);
+                        if (!slot_acquire(s, err, slot, si / NS)) break;
                         uint8_t* dst = ring + (size_t)slot * SLOT_BYTES;
                         mbar_arrive_expect_tx(&s.full[slot], bytes);
                         for (int v = u; v < u1; ++v) {
@@ -1674,14 +1738,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                              warp * DHW;
         int pk_done = 0;   // packs waited for and released by this warp
         bool ok = !s.abort;
-        auto release_to = [&](int j_end) {  // wait for and release packs [pk_done, j_end)
-            for (; pk_done < j_end; ++pk_done) {
-                const int sidx = si0 + pk_done;
-                if (ok) ok = warp_wait(&s.full[sidx % NS], (sidx / NS) & 1, s);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s.empty[sidx % NS]);
-            }
-        };
         int jp = 0;  // running index of held pairs
         for (int u = 0; u < s.U; ++u) {
             const int pk = s.g_pack[u];
@@ -1711,7 +1767,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                         ld_relaxed_u64x2(hrow + 2 * (lane + 32 * j), wa[j], wb[j]);
                     }
                 }
-                release_to(pk);  // every earlier pack is done for this warp
+                release_packs(s, si0, NS, pk, pk_done, ok);  // every earlier pack is done for this warp
                 const int sidx = si0 + pk;
                 if (ok) ok = warp_wait(&s.full[sidx % NS], (sidx / NS) & 1, s);
                 for (uint32_t it = 0; ok; ++it) {
@@ -1800,7 +1856,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 __syncwarp();
             }
         }
-        release_to(s.npk);
+        release_packs(s, si0, NS, s.npk, pk_done, ok);
         if (!ok && lane == 0 && !s.abort) set_error(err, s, CZ_DERR_FULL_WAIT);
     }
     __syncthreads();

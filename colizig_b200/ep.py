@@ -6,11 +6,21 @@ src/qwen38/moe.zig:637-664), so the experts partition: rank r holds experts
 replicated on every rank (identical, bit-exact); each rank adds the outputs of
 the experts it holds, and one all-reduce (sum) over the ranks completes every
 forward.  The all-reduce runs inside the library (NCCL) on the call's stream.
+
+Failure detection (no reference counterpart: the reference runs on one
+process).  The library's host waits are watched while its communicator is
+active (set_timeout): one that runs out aborts the communicator and the call
+raises ColizigError(-9) instead of waiting for a peer that never comes.  A host
+that steps in lockstep can learn earlier, before it launches anything:
+Heartbeat.step() checks through the torch.distributed store that every peer
+has reached the same step, and aborts (abort()) and raises -9 when one has not
+within its timeout.
 """
 
 from __future__ import annotations
 
 import ctypes
+import datetime
 from typing import Optional, Tuple
 
 from . import _abi
@@ -59,3 +69,46 @@ def init(rank: Optional[int] = None, world: Optional[int] = None, uid: Optional[
 
 def shutdown() -> None:
     _abi.check("colizig_cuda_ep_shutdown", _abi.load().colizig_cuda_ep_shutdown())
+
+
+def set_timeout(ms: int) -> None:
+    """Deadline of the library's host waits while the EP communicator is active
+    (colizig_cuda_ep_set_timeout; <= 0 waits without one)."""
+    _abi.check("colizig_cuda_ep_set_timeout", _abi.load().colizig_cuda_ep_set_timeout(int(ms)))
+
+
+def abort() -> None:
+    """Abort the EP communicator now (colizig_cuda_ep_abort): EP calls raise -9
+    until shutdown() and init()."""
+    _abi.check("colizig_cuda_ep_abort", _abi.load().colizig_cuda_ep_abort())
+
+
+class Heartbeat:
+    """Lockstep liveness check between EP steps over a torch.distributed store.
+
+    step() marks this rank as having reached step n, then waits (at most
+    `timeout_s`) until every other rank has marked step n too.  A peer that has
+    exited or stopped stepping makes step() call `on_lost` (default: abort the
+    library's communicator) and raise ColizigError(-9); nothing has been
+    launched for that step on this rank.  Ranks leave only between steps."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 5.0, prefix: str = "cz_hb",
+                 on_lost=None):
+        self.store, self.rank, self.world = store, int(rank), int(world)
+        self.timeout = datetime.timedelta(seconds=float(timeout_s))
+        self.prefix = prefix
+        self.on_lost = abort if on_lost is None else on_lost
+        self.n = 0
+
+    def step(self) -> int:
+        self.n += 1
+        self.store.set(f"{self.prefix}/{self.n}/{self.rank}", b"1")
+        peers = [f"{self.prefix}/{self.n}/{r}" for r in range(self.world) if r != self.rank]
+        try:
+            if peers:
+                self.store.wait(peers, self.timeout)
+        except Exception as e:  # the store's timeout (or a lost store connection)
+            self.on_lost()
+            raise _abi.ColizigError(f"heartbeat step {self.n}: a peer did not arrive ({type(e).__name__})",
+                                    -9) from e
+        return self.n

@@ -176,6 +176,18 @@ int colizig_cuda_ep_unique_id(void* id_out);
 int colizig_cuda_ep_init(int rank, int world, const void* id);
 int colizig_cuda_ep_shutdown(void);
 
+/* No reference counterpart.  Deadline (ms) of the library's host waits while an
+ * EP communicator is active (default 60000; <= 0 waits without one).  A wait
+ * that runs out, or an asynchronous NCCL error, aborts the communicator
+ * (ncclCommAbort: its kernels return) and the call returns -9; every EP call
+ * then returns -9 until colizig_cuda_ep_shutdown and colizig_cuda_ep_init. */
+int colizig_cuda_ep_set_timeout(int ms);
+
+/* No reference counterpart.  Abort the EP communicator now, as the deadline
+ * does (for a host watchdog that learned between steps that a peer has left).
+ * No device work; returns 0. */
+int colizig_cuda_ep_abort(void);
+
 /* Device-side error word of the last asynchronous call(s) on the library's
  * MoE scratch (0 = none); reading it synchronises `stream` (NULL = the default
  * stream, as in the device-pointer forward) and clears it.  Returns 0, or -7
@@ -233,6 +245,14 @@ int colizig_cuda_debug_expf(const float* x_dev, float* y_dev, size_t n);
  * non-zero).  Nothing faults or hangs; the next call starts clean.  0 ok, -1
  * not initialised or spin_limit == 0. */
 int colizig_cuda_debug_hold_router(uint32_t spin_limit);
+
+/* Test hook for the watched host wait (colizig_cuda_ep_set_timeout), over
+ * caller-provided fakes: query(ctx) 0 done, 1 pending, < 0 failed;
+ * async_error(ctx) non-zero = the communicator reports an error; abort_comm(ctx)
+ * is called once when the wait gives up.  Returns 0, -5 (query failed) or -9
+ * (aborted: deadline or error); -1 for a null callback. */
+int colizig_cuda_debug_watch_wait(int (*query)(void*), int (*async_error)(void*), void (*abort_comm)(void*),
+                                  void* ctx, int timeout_ms);
 
 #ifdef __cplusplus
 }
