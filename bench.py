@@ -18,9 +18,10 @@ stream, max over ranks), inputs resident in HBM.  e2e = the same metric through
 the C ABI with host buffers (pinned H2D of the tokens and D2H of the outputs
 inside the timed region).  --gpus N > 1 runs one process per GPU (torchrun) as
 expert parallelism: every layer's experts are partitioned over the GPUs, the
-router runs replicated, and the library sums the GPUs' outputs with one NCCL
-all-reduce per layer call; each GPU contributes --tokens tokens to the step's
-batch (N x --tokens tokens per step, weak scaling).
+router runs replicated, and the GPUs' outputs are summed inside the decode
+kernel (peer stores over NVLink; prefill-sized batches: one NCCL all-reduce per
+layer call); each GPU contributes --tokens tokens to the step's batch (N x
+--tokens tokens per step, weak scaling).
 
 --impl reference times the reference path's CPU implementation (the oracle's C
 restatement of the Zig AVX2 path, all host threads) on the same config.
@@ -278,8 +279,7 @@ def stack_config(args, d, NL, T, world):
             "layers": NL, "tokens_per_step": T, "tokens_per_gpu": args.tokens, "global_batch": T,
             "expert_weight_bytes": NL * d.experts * expert_bytes(d),
             "l2": "inputs larger than L2: each step streams every layer's routed experts",
-            "parallelism": (f"ep{world}: experts partitioned over the GPUs, router replicated, NCCL "
-                            "all-reduce per layer") if world > 1 else "single GPU"}
+            "parallelism": ep_label(world, T)}
 
 
 def reference_stack(args):
@@ -635,6 +635,15 @@ def metric_name(args, T):
     return f"MoE-layer {mode} tokens/s ({args.config}, T={T})"
 
 
+def ep_label(world, T):
+    if world < 2:
+        return "single GPU"
+    if T >= PREFILL_MIN_TOKENS:
+        return f"ep{world}: experts partitioned over the GPUs, router replicated, NCCL all-reduce of each layer's output"
+    return (f"ep{world}: experts partitioned over the GPUs, router replicated, ranks summed inside the decode "
+            "kernel (partial rows stored into every rank's peer-mapped buffer over NVLink)")
+
+
 def config_block(args, d):
     g = args.tokens * args.gpus
     if g >= PREFILL_MIN_TOKENS:
@@ -647,8 +656,7 @@ def config_block(args, d):
             "shared_intermediate": d.shared_inter, "tokens_per_step": g, "tokens_per_gpu": args.tokens,
             "global_batch": g, "layers_cycled": args.layers,
             "l2": "inputs larger than L2: steps cycle through distinct layers; L2 flushed once before the timed replay",
-            "parallelism": (f"ep{args.gpus}: experts partitioned over the GPUs, router replicated, NCCL all-reduce "
-                            "of the layer output") if args.gpus > 1 else "single GPU"}
+            "parallelism": ep_label(args.gpus, g)}
 
 
 def main():
@@ -697,7 +705,7 @@ def main():
     cz.gpu.init(local)
     if world > 1:
         # expert parallelism: rank r holds experts [r*E/W, (r+1)*E/W) of every layer; the
-        # library sums the ranks' outputs with one NCCL all-reduce per layer call
+        # ranks' outputs are summed inside the decode kernel (or by NCCL for prefill batches)
         from colizig_b200 import ep
 
         ep.init()
@@ -913,6 +921,9 @@ def main():
             "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "timing": timing,
             "gpu_launches": args.steps * launches_per_step,
         }
+        if world > 1:
+            line["ep_combine"] = ("in the decode kernel (peer stores)" if ep.combine_mode() == 1 and not prefill
+                                  else "NCCL all-reduce")
         print(json.dumps(line), flush=True)
     for lay in layers:
         lay.unregister()

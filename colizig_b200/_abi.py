@@ -34,6 +34,7 @@ MOE_SYMBOLS = (
     "colizig_cuda_moe_check",
     "colizig_cuda_debug_expf",
     "colizig_cuda_debug_hold_router",
+    "colizig_cuda_debug_error_bits",
     "colizig_cuda_debug_watch_wait",
     "colizig_cuda_moe_forward_noalloc",
     "colizig_cuda_ep_unique_id",
@@ -41,6 +42,8 @@ MOE_SYMBOLS = (
     "colizig_cuda_ep_shutdown",
     "colizig_cuda_ep_set_timeout",
     "colizig_cuda_ep_abort",
+    "colizig_cuda_ep_combine_mode",
+    "colizig_cuda_ep_set_combine",
     "colizig_cuda_kernel_timer",
     "colizig_cuda_kernel_timer_read",
 )
@@ -156,6 +159,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         L.colizig_cuda_ep_set_timeout.argtypes = [i32]
         L.colizig_cuda_ep_abort.restype = i32
         L.colizig_cuda_ep_abort.argtypes = []
+        L.colizig_cuda_ep_combine_mode.restype = i32
+        L.colizig_cuda_ep_combine_mode.argtypes = []
+        L.colizig_cuda_ep_set_combine.restype = i32
+        L.colizig_cuda_ep_set_combine.argtypes = [i32]
         L.colizig_cuda_kernel_timer.restype = i32
         L.colizig_cuda_kernel_timer.argtypes = [i32]
         L.colizig_cuda_kernel_timer_read.restype = i32
@@ -164,6 +171,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         L.colizig_cuda_debug_expf.argtypes = [vp, vp, ctypes.c_size_t]
         L.colizig_cuda_debug_hold_router.restype = i32
         L.colizig_cuda_debug_hold_router.argtypes = [u32]
+        L.colizig_cuda_debug_error_bits.restype = i32
+        L.colizig_cuda_debug_error_bits.argtypes = [ctypes.c_void_p]
         L.colizig_cuda_debug_watch_wait.restype = i32
         L.colizig_cuda_debug_watch_wait.argtypes = [WATCH_QUERY, WATCH_QUERY, WATCH_ABORT, ctypes.c_void_p, i32]
         _lib = L

@@ -173,6 +173,13 @@ struct Ctx {
     ncclComm_t ep_comm = nullptr;
     int ep_timeout_ms = 60000;  // watched host waits while a communicator is active (<= 0: unwatched)
     bool ep_aborted = false;    // the communicator was aborted; EP calls return -9 until re-initialised
+    // decode combine inside the kernel: this rank's receive buffer (kEpRecvBytes,
+    // zeroed), every rank's slot area as mapped here, the peers' IPC mappings
+    void* ep_recv = nullptr;
+    void* ep_peer_map[cz::kEpMaxRanks] = {};
+    unsigned long long* ep_slots[cz::kEpMaxRanks] = {};
+    bool ep_p2p = false;       // set up on every rank
+    bool ep_p2p_use = true;    // colizig_cuda_ep_set_combine (the same on every rank)
     // sharded expert parallelism (prefill): routing of this rank's tokens, exchange buffers
     DevBuf sh_idx, sh_gates, sh_xn, sh_slot, sh_counts, sh_allc, sh_tmp, sh_send, sh_recv, sh_x, sh_ridx, sh_rgates,
         sh_part, sh_back;
@@ -288,6 +295,92 @@ int stream_sync(cudaStream_t st) {
         [&]() { ep_abort_locked(); }, g.ep_timeout_ms);
 }
 
+// Releases the in-kernel combine's buffers.  With `barrier`, first waits until
+// every rank has reached this point with its kernels done (one NCCL all-reduce),
+// so no peer still stores into the buffer freed here.
+void ep_p2p_teardown_locked(bool barrier) {
+    if (!g.ep_recv) return;
+    cudaDeviceSynchronize();
+    if (barrier && g.ep_comm) {
+        DevBuf one;
+        if (one.ensure(4) && cudaMemsetAsync(one.p, 0, 4, g.stream) == cudaSuccess &&
+            nccl.allReduce(one.p, one.p, 1, ncclInt32, ncclSum, g.ep_comm, g.stream) == ncclSuccess)
+            stream_sync(g.stream);
+        cudaStreamSynchronize(g.stream);
+        one.release();
+    }
+    for (int q = 0; q < cz::kEpMaxRanks; ++q) {
+        if (g.ep_peer_map[q]) cudaIpcCloseMemHandle(g.ep_peer_map[q]);
+        g.ep_peer_map[q] = nullptr;
+        g.ep_slots[q] = nullptr;
+    }
+    cudaFree(g.ep_recv);
+    g.ep_recv = nullptr;
+    g.ep_p2p = false;
+}
+
+// Sets up the decode kernel's in-kernel combine (expert parallelism with
+// replicated tokens): every rank allocates a zeroed receive buffer, the CUDA IPC
+// handles go round with one NCCL all-gather, every rank maps its peers' buffers,
+// and one NCCL all-reduce (min) of the outcomes decides for all ranks together.
+// Any failure leaves the NCCL all-reduce combine in place.  Every rank takes
+// part in both collectives whatever happened before them.
+void ep_p2p_setup_locked() {
+    const int W = g.ep_world, me = g.ep_rank;
+    if (W < 2 || W > cz::kEpMaxRanks || !g.ep_comm) return;
+    struct alignas(16) Rec {
+        int ok;
+        int pad;
+        cudaIpcMemHandle_t h;
+        char tail[128 - 8 - sizeof(cudaIpcMemHandle_t)];
+    };
+    static_assert(sizeof(Rec) == 128, "record size");
+    Rec mine{};
+    bool ok = cudaMalloc(&g.ep_recv, cz::kEpRecvBytes) == cudaSuccess;
+    if (!ok) g.ep_recv = nullptr;
+    ok = ok && cudaMemset(g.ep_recv, 0, cz::kEpRecvBytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+    ok = ok && cudaIpcGetMemHandle(&mine.h, g.ep_recv) == cudaSuccess;
+    mine.ok = ok ? 1 : 0;
+    std::vector<Rec> all(W);
+    DevBuf rec, flag;
+    bool coll = rec.ensure(sizeof(Rec) * W) && flag.ensure(4) &&
+                cudaMemcpy(rec.as<uint8_t>() + sizeof(Rec) * me, &mine, sizeof(Rec), cudaMemcpyHostToDevice) ==
+                    cudaSuccess;
+    // the all-gather runs even after a local failure (the record says ok = 0)
+    if (!coll || nccl.allGather(rec.as<uint8_t>() + sizeof(Rec) * me, rec.p, sizeof(Rec), ncclUint8, g.ep_comm,
+                                g.stream) != ncclSuccess || stream_sync(g.stream) != CZ_OK ||
+        cudaMemcpy(all.data(), rec.p, sizeof(Rec) * W, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        ok = false;
+    }
+    for (int q = 0; q < W && ok; ++q) ok = all[q].ok == 1;
+    for (int q = 0; q < W && ok; ++q) {
+        if (q == me) {
+            g.ep_slots[q] = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(g.ep_recv) + cz::kEpRecvHeader);
+            continue;
+        }
+        void* m = nullptr;
+        if (cudaIpcOpenMemHandle(&m, all[q].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+            break;
+        }
+        g.ep_peer_map[q] = m;
+        g.ep_slots[q] = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(m) + cz::kEpRecvHeader);
+    }
+    int v = ok ? 1 : 0;
+    bool agreed = flag.p && cudaMemcpy(flag.p, &v, 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+                  nccl.allReduce(flag.p, flag.p, 1, ncclInt32, ncclMin, g.ep_comm, g.stream) == ncclSuccess &&
+                  stream_sync(g.stream) == CZ_OK && cudaMemcpy(&v, flag.p, 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+    rec.release();
+    flag.release();
+    if (agreed && v == 1) {
+        g.ep_p2p = true;
+        return;
+    }
+    ep_p2p_teardown_locked(false);
+    cudaGetLastError();
+}
+
 // Forgets the cached device addresses of the no-allocation scratch (defined with
 // colizig_cuda_moe_forward_noalloc below), so the first call after an init does
 // the look-up again: a context reset by the host application reloads the module.
@@ -348,6 +441,7 @@ void shutdown_locked() {
     if (!g.inited) return;
     cudaSetDevice(g.dev);
     cudaDeviceSynchronize();
+    ep_p2p_teardown_locked(false);
     if (g.ep_comm) nccl.commDestroy(g.ep_comm);
     g.ep_comm = nullptr;
     g.ep_on = false;
@@ -551,9 +645,24 @@ int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uin
     const int tmax = cz::decode_max_tokens((int)L.d.hidden, (int)L.d.experts, (int)L.d.topk, (int)L.d.inter,
                                            (int)L.d.shared_inter, x_bf16, g.num_sms);
     if (tmax < 1) return CZ_ESHAPE;
+    // expert parallelism: the ranks' outputs are summed inside the decode kernel
+    // (peer stores) when every rank mapped its peers' receive buffers, else by one
+    // NCCL all-reduce after the launches; the choice is the same on every rank
+    const bool ep_multi = L.ep && g.ep_world > 1;
+    if (ep_multi && !g.ep_comm) return CZ_ENCCL;
+    const bool p2p = ep_multi && g.ep_p2p && g.ep_p2p_use && L.d.hidden <= (uint32_t)cz::kEpMaxHidden &&
+                     tmax <= cz::kDecodeMaxTokens;
     for (int t0 = 0; t0 < T; t0 += tmax) {
         const int n = T - t0 < tmax ? T - t0 : tmax;
         cz::DecodeParams p = make_params(L);
+        if (p2p) {
+            p.ep_world = g.ep_world;
+            p.ep_rank = g.ep_rank;
+            for (int q = 0; q < g.ep_world; ++q) p.ep_recv[q] = g.ep_slots[q];
+            p.ep_seq = static_cast<uint32_t*>(g.ep_recv);
+            // the peers' rows are waited for as long as the host waits for a collective
+            p.ep_wait_ns = (uint64_t)(g.ep_timeout_ms > 0 ? g.ep_timeout_ms : 60000) * 1000000ull;
+        }
         p.x = reinterpret_cast<const uint8_t*>(x) + (size_t)t0 * L.d.hidden * xelt;
         p.x_bf16 = x_bf16;
         p.T = n;
@@ -572,11 +681,9 @@ int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uin
         if (rc) return rc;
         if (ev && !cz::record_timer_event(ev[1], st)) return CZ_ELAUNCH;
     }
-    if (L.ep && g.ep_world > 1) {
-        if (!g.ep_comm) return CZ_ENCCL;
-        if (nccl.allReduce(out, out, (size_t)T * L.d.hidden, ncclFloat, ncclSum, g.ep_comm, st) != ncclSuccess)
-            return CZ_ENCCL;
-    }
+    if (ep_multi && !p2p &&
+        nccl.allReduce(out, out, (size_t)T * L.d.hidden, ncclFloat, ncclSum, g.ep_comm, st) != ncclSuccess)
+        return CZ_ENCCL;
     return CZ_OK;
 }
 
@@ -1330,6 +1437,19 @@ CZ_EXPORT int colizig_cuda_debug_hold_router(uint32_t spin_limit) {
     return CZ_OK;
 }
 
+// Diagnostics: the device error word's bits as they stand (after all device
+// work so far has finished), without clearing them; 0 before any MoE call.
+CZ_EXPORT int colizig_cuda_debug_error_bits(uint32_t* bits) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited || !bits) return CZ_EARGS;
+    cudaSetDevice(g.dev);
+    *bits = 0;
+    if (!g.sync) return CZ_OK;
+    if (cudaDeviceSynchronize() != cudaSuccess) return CZ_ED2H;
+    return cudaMemcpy(bits, g.sync + 1, sizeof(uint32_t), cudaMemcpyDeviceToHost) == cudaSuccess ? CZ_OK : CZ_ED2H;
+}
+
 CZ_EXPORT int colizig_cuda_debug_expf(const float* x_dev, float* y_dev, size_t n) {
     CsrGuard _csr;
     std::lock_guard<std::mutex> lk(g_mu);
@@ -1370,6 +1490,7 @@ CZ_EXPORT int colizig_cuda_ep_init(int rank, int world, const void* id) {
     g.ep_rank = rank;
     g.ep_world = world;
     g.ep_on = true;
+    ep_p2p_setup_locked();  // collective: every rank of the communicator is here too
     return CZ_OK;
 }
 
@@ -1381,6 +1502,7 @@ CZ_EXPORT int colizig_cuda_ep_shutdown(void) {
     cudaDeviceSynchronize();
     for (auto& kv : g.layers)
         if (kv.second.ep) return CZ_EARGS;  // unregister the expert-parallel layers first
+    ep_p2p_teardown_locked(true);
     if (g.ep_comm) nccl.commDestroy(g.ep_comm);
     g.ep_comm = nullptr;
     g.ep_on = false;
@@ -1404,6 +1526,23 @@ CZ_EXPORT int colizig_cuda_ep_set_timeout(int ms) {
 CZ_EXPORT int colizig_cuda_ep_abort(void) {
     std::lock_guard<std::mutex> lk(g_mu);
     ep_abort_locked();
+    return CZ_OK;
+}
+
+// How expert-parallel decode calls sum the ranks: 1 = inside the decode kernel
+// (peer stores into every rank's receive buffer), 0 = one NCCL all-reduce per call.
+CZ_EXPORT int colizig_cuda_ep_combine_mode(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return g.ep_p2p && g.ep_p2p_use ? 1 : 0;
+}
+
+// Chooses the decode combine: 1 = inside the kernel when it was set up at
+// colizig_cuda_ep_init (the default), 0 = NCCL all-reduce.  Every rank must make
+// the same choice before its next EP call.
+CZ_EXPORT int colizig_cuda_ep_set_combine(int in_kernel) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (in_kernel != 0 && in_kernel != 1) return CZ_EARGS;
+    g.ep_p2p_use = in_kernel == 1;
     return CZ_OK;
 }
 

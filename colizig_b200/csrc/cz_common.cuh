@@ -31,6 +31,7 @@ enum : uint32_t {
     CZ_DERR_DRAIN_WAIT = 1u << 4,
     CZ_DERR_SHAPE = 1u << 5,
     CZ_DERR_SEQ_WAIT = 1u << 6,
+    CZ_DERR_EP_WAIT = 1u << 7,  // a peer rank's partial sums never arrived
 };
 
 // Spin limits: every wait in these kernels is bounded.  With the nanosleep
@@ -204,6 +205,31 @@ CZ_DEV void red_relaxed_add_gpu(uint32_t* p, uint32_t v) {
 
 CZ_DEV void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Exchange words between GPUs (a peer's memory mapped into this process): system
+// scope, one single-copy-atomic 8-byte access each.
+CZ_DEV void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+CZ_DEV unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Nanoseconds of the GPU's global timer (deadlines of waits on other GPUs).
+CZ_DEV uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+CZ_DEV uint32_t ld_acquire_gpu_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 CZ_DEV unsigned long long tag_word(uint32_t tag, float v) {

@@ -15,6 +15,16 @@ constexpr int kMaxExperts = 512;
 constexpr int kMaxGrid = 160;         // decode CTAs (one per SM) the no-allocation scratch is sized for
 constexpr int kSyncRegionWords = 8;   // [1] = CTAs done (the other words are unused padding)
 constexpr int kSyncWords = 2 + 2 * kSyncRegionWords;  // seq, err, two regions
+// Expert-parallel decode with the ranks' partial outputs summed inside the decode
+// kernel (peer stores over NVLink): at most this many ranks and this hidden size.
+constexpr int kEpMaxRanks = 8;
+constexpr int kEpMaxHidden = 8192;
+// Receive buffer of that combine, per rank: a 256-byte header (word 0 = the EP
+// launch counter) and [2 parities][kEpMaxRanks senders][kDecodeMaxTokens][kEpMaxHidden]
+// tagged words.
+constexpr size_t kEpRecvHeader = 256;
+constexpr size_t kEpRecvWords = (size_t)2 * kEpMaxRanks * kDecodeMaxTokens * kEpMaxHidden;
+constexpr size_t kEpRecvBytes = kEpRecvHeader + kEpRecvWords * 8;
 
 __host__ __device__ inline int cz_nblk(int x) { return (x + 127) / 128; }
 // Row stride (floats) of the router-logit scratch: E experts + the shared
@@ -68,6 +78,16 @@ struct alignas(64) DecodeParams {
     uint32_t* status_out;    // nullable: the last CTA copies the device error word here
     uint32_t spin_limit;     // polls before a wait gives up (0 = CZ_SPIN_LIMIT)
     int dbg_hold;            // failure-path tests: router row 0's logits are never published
+    // Expert parallelism with replicated tokens, ranks summed in the kernel
+    // (ep_world > 1; else 0 and out is this rank's own sum).  Each CTA stores its
+    // output rows' partial sums as tagged words (tag = EP launch counter + 1) into
+    // slot [par][ep_rank] of every rank's receive buffer (peer-mapped), then polls
+    // slots [par][0..ep_world) of its own and adds them in ascending rank order;
+    // par = counter & 1.  The counter advances once per such launch on every rank.
+    unsigned long long* ep_recv[kEpMaxRanks];  // word 0 of each rank's slot area (header skipped)
+    uint32_t* ep_seq;        // this rank's EP launch counter (receive buffer header)
+    int ep_world, ep_rank;
+    uint64_t ep_wait_ns;     // how long a CTA waits for the peers' rows before it gives up
 };
 
 // Bytes of the decode kernel's tagged scratch for these dims (logits, h rows).

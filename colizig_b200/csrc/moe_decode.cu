@@ -1012,11 +1012,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the previous kernel's writes are visible
     const uint32_t seq = ld_relaxed_gpu(p.sync);
     const uint32_t tag = seq + 1u;  // this launch's exchange tag (zeroed scratch never matches)
+    // expert parallelism: this launch's counter, the same on every rank
+    const uint32_t eseq = p.ep_world > 1 ? ld_relaxed_gpu(p.ep_seq) : 0u;
     uint32_t* reg = region(p.sync, seq & 1);
     if (c == 0 && tid < kSyncRegionWords) region(p.sync, (seq & 1) ^ 1)[tid] = 0u;
-    if (tid == 0) red_relaxed_add_gpu(&reg[0], 1u);  // this CTA has read the sequence
     if (tid < MAXT) s.xmax[tid] = 0u;
     __syncthreads();
+    // this CTA has read the sequence words: every thread's loads are ordered before
+    // the count-in by the barrier above
+    if (tid == 0) red_relaxed_add_gpu(&reg[0], 1u);
     if (!mbar_wait_bounded(&s.rbar, 0, &s.abort) && lane == 0) set_error(err, s, CZ_DERR_FULL_WAIT);
     __syncthreads();
 
@@ -1518,10 +1522,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                         in = ld_relaxed_gpu(&reg[0]) >= (uint32_t)G;
                         if (!in) __nanosleep(100);
                     }
-                    if (in)
+                    if (in) {
                         st_relaxed_u32(p.sync, seq + 1u);
-                    else
+                        if (p.ep_world > 1) st_relaxed_u32(p.ep_seq, eseq + 1u);
+                    } else {
                         atomicOr(err, CZ_DERR_SEQ_WAIT);
+                    }
                 }
                 // drain: no copy may land after this CTA exits (waiting on a phase
                 // that already completed returns at once)
@@ -1873,7 +1879,53 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                 any = true;
             }
             const size_t o = (size_t)tk * H + o_lo + r;
-            p.out[o] = p.residual ? __fadd_rn(p.residual[o], sum) : sum;
+            const float v = p.residual ? __fadd_rn(p.residual[o], sum) : sum;
+            if (p.ep_world > 1) {
+                // this rank's partial sum goes to slot [par][ep_rank] of every rank
+                const size_t w = ((size_t)((eseq & 1u) * kEpMaxRanks + p.ep_rank) * kDecodeMaxTokens + tk) *
+                                     kEpMaxHidden + o_lo + r;
+                const unsigned long long tw = tag_word(eseq + 1u, v);
+                for (int q = 0; q < p.ep_world; ++q) st_relaxed_sys_u64(p.ep_recv[q] + w, tw);
+            } else {
+                p.out[o] = v;
+            }
+        }
+        if (p.ep_world > 1) {
+            // out = the ranks' partial sums added in ascending rank order (ascending
+            // expert ranges), polled from this rank's own receive slots
+            const uint32_t etag = eseq + 1u;
+            const int W = p.ep_world;
+            // a deadline, not a poll count: peers may reach this launch seconds apart
+            const uint64_t t_end = global_ns() + p.ep_wait_ns;
+            for (int k = tid; k < T * drows; k += NTHREADS) {
+                const int tk = k / drows, r = k - tk * drows;
+                const unsigned long long* src = p.ep_recv[p.ep_rank] +
+                                                ((size_t)(eseq & 1u) * kEpMaxRanks * kDecodeMaxTokens + tk) *
+                                                    kEpMaxHidden + o_lo + r;
+                constexpr size_t RS = (size_t)kDecodeMaxTokens * kEpMaxHidden;  // between senders
+                unsigned long long wv[kEpMaxRanks] = {};
+                uint32_t pend = (1u << W) - 1u;
+                for (uint32_t it = 0; pend; ++it) {
+#pragma unroll
+                    for (int q = 0; q < kEpMaxRanks; ++q)
+                        if (pend & (1u << q)) wv[q] = ld_relaxed_sys_u64(src + q * RS);
+#pragma unroll
+                    for (int q = 0; q < kEpMaxRanks; ++q)
+                        if ((pend & (1u << q)) && (uint32_t)(wv[q] >> 32) == etag) pend &= ~(1u << q);
+                    if (!pend) break;
+                    if ((it & 63u) == 63u && global_ns() > t_end) break;
+                    __nanosleep(it < 64 ? 32 : 1024);
+                }
+                if (pend) {
+                    atomicOr(err, CZ_DERR_EP_WAIT);
+                    continue;
+                }
+                float sum = __uint_as_float((uint32_t)wv[0]);
+#pragma unroll
+                for (int q = 1; q < kEpMaxRanks; ++q)
+                    if (q < W) sum = __fadd_rn(sum, __uint_as_float((uint32_t)wv[q]));
+                p.out[(size_t)tk * H + o_lo + r] = sum;
+            }
         }
     }
 

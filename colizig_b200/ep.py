@@ -4,8 +4,10 @@ The reference evaluates every expert independently (forwardGrouped,
 src/qwen38/moe.zig:637-664), so the experts partition: rank r holds experts
 [r*E/W, (r+1)*E/W) and rank 0 also the shared expert.  Router and top-k run
 replicated on every rank (identical, bit-exact); each rank adds the outputs of
-the experts it holds, and one all-reduce (sum) over the ranks completes every
-forward.  The all-reduce runs inside the library (NCCL) on the call's stream.
+the experts it holds, and the ranks' outputs are summed: for decode batches
+inside the decode kernel (each rank stores its partial rows into every rank's
+peer-mapped receive buffer and adds the ranks' rows in rank order), otherwise
+by one NCCL all-reduce inside the library on the call's stream.
 
 Failure detection (no reference counterpart: the reference runs on one
 process).  The library's host waits are watched while its communicator is
@@ -75,6 +77,18 @@ def set_timeout(ms: int) -> None:
     """Deadline of the library's host waits while the EP communicator is active
     (colizig_cuda_ep_set_timeout; <= 0 waits without one)."""
     _abi.check("colizig_cuda_ep_set_timeout", _abi.load().colizig_cuda_ep_set_timeout(int(ms)))
+
+
+def combine_mode() -> int:
+    """1 when expert-parallel decode calls sum the ranks inside the decode kernel
+    (peer stores into every rank's receive buffer), 0 when by an NCCL all-reduce."""
+    return int(_abi.load().colizig_cuda_ep_combine_mode())
+
+
+def set_combine(in_kernel: bool) -> None:
+    """Choose the decode combine (colizig_cuda_ep_set_combine); every rank must
+    make the same choice before its next EP call."""
+    _abi.check("colizig_cuda_ep_set_combine", _abi.load().colizig_cuda_ep_set_combine(1 if in_kernel else 0))
 
 
 def abort() -> None:

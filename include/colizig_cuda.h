@@ -188,6 +188,21 @@ int colizig_cuda_ep_set_timeout(int ms);
  * No device work; returns 0. */
 int colizig_cuda_ep_abort(void);
 
+/* No reference counterpart (the reference runs on one process).  How
+ * expert-parallel decode calls (replicated tokens, fewer than 32 per call) sum
+ * the ranks' outputs.  colizig_cuda_ep_init maps every rank's receive buffer
+ * into every other rank (CUDA IPC, up to 8 ranks); when all ranks succeed, the
+ * decode kernel itself stores its partial output rows into every rank's buffer
+ * and adds the ranks' rows in ascending rank order, with no NCCL call.
+ * Otherwise, and for prefill-sized batches, one NCCL all-reduce sums them.
+ * colizig_cuda_ep_combine_mode returns 1 (in the kernel) or 0 (NCCL);
+ * colizig_cuda_ep_set_combine(0 or 1) chooses; every rank must choose the same
+ * before its next EP call.  The kernel waits for a peer's rows as long as the
+ * host waits for a collective (colizig_cuda_ep_set_timeout, 60 s by default);
+ * rows that never arrive make the call (or colizig_cuda_moe_check) return -7. */
+int colizig_cuda_ep_combine_mode(void);
+int colizig_cuda_ep_set_combine(int in_kernel);
+
 /* Device-side error word of the last asynchronous call(s) on the library's
  * MoE scratch (0 = none); reading it synchronises `stream` (NULL = the default
  * stream, as in the device-pointer forward) and clears it.  Returns 0, or -7
@@ -245,6 +260,12 @@ int colizig_cuda_debug_expf(const float* x_dev, float* y_dev, size_t n);
  * non-zero).  Nothing faults or hangs; the next call starts clean.  0 ok, -1
  * not initialised or spin_limit == 0. */
 int colizig_cuda_debug_hold_router(uint32_t spin_limit);
+
+/* Diagnostics (no reference counterpart): the device error word's bits as they
+ * stand once all device work so far has finished, not cleared (1 router wait,
+ * 2/4 ring waits, 8 h-row wait, 16 drain, 32 shape, 64 sequence, 128 a peer
+ * rank's partial sums).  0 before any MoE call. */
+int colizig_cuda_debug_error_bits(uint32_t* bits);
 
 /* Test hook for the watched host wait (colizig_cuda_ep_set_timeout), over
  * caller-provided fakes: query(ctx) 0 done, 1 pending, < 0 failed;

@@ -1,7 +1,7 @@
 """One rank of the 2-GPU expert-parallel check (launched by tests/test_gpu_ep.py
 through torch.distributed.run).  Rank r holds experts [r*E/2, (r+1)*E/2) of
-every layer; the layer outputs (summed over ranks by the library's NCCL
-all-reduce) are compared with the CPU oracle (top-k bit-exact, outputs within
+every layer; the layer outputs (summed over ranks inside the decode kernel,
+and again by the library's NCCL all-reduce: both must agree) are compared with the CPU oracle (top-k bit-exact, outputs within
 the layer tolerance) and with the same layer run whole on one GPU.  Then the
 sharded-token path (each rank its own batch, rows exchanged with NCCL
 send/recv), the batches together against the oracle and the one-GPU layer,
@@ -32,6 +32,10 @@ def main() -> int:
     oracle.set_threads(os.cpu_count() or 1)
     ok = True
     lid = 700
+    # decode calls sum the ranks inside the kernel (peer stores) on an NVLink box
+    mode = ep.combine_mode()
+    print(f"rank {rank}: decode combine mode {mode}", flush=True)
+    ok &= mode == 1
     for cfg, Ts in (("c2", (1, 4, 16)), ("c5", (1, 5))):
         d = synth.CONFIGS[cfg]
         w = synth.make_layer(d, seed=11, device="cuda")
@@ -43,8 +47,17 @@ def main() -> int:
             x = synth.make_tokens(T, d.hidden, 300 + T, device="cuda", dtype=torch.bfloat16)
             out, idx, gates = moe.forward(Lep, x)
             ref, ridx, rg = moe.forward(Lfull, x)
+            # the same call with the NCCL all-reduce combine: a two-rank sum commutes,
+            # so both combines give the same bits
+            ep.set_combine(False)
+            out_nccl, _, _ = moe.forward(Lep, x)
+            ep.set_combine(True)
             torch.cuda.synchronize()
             moe.check()
+            if not torch.equal(out, out_nccl):
+                print(f"rank {rank} {cfg} T={T}: in-kernel and NCCL combines differ by "
+                      f"{(out - out_nccl).abs().max().item():.3e}", flush=True)
+                ok = False
             if rank == 0:
                 ol = oracle.layer_from_dict(wn)
                 od = oracle.Dims(d.hidden, d.experts, d.topk, d.inter, d.shared_inter, d.norm_topk)
@@ -54,6 +67,19 @@ def main() -> int:
                 same = np.array_equal(idx.cpu().numpy().view(np.uint32), oi)
                 print(f"{cfg} T={T}: top-k exact {same}, vs oracle {e_or:.2e}, vs one GPU {e_one:.2e}", flush=True)
                 ok &= same and e_or <= OUT_TOL and e_one <= OUT_TOL and torch.equal(idx, ridx) and torch.equal(gates, rg)
+        if cfg == "c2":
+            # many calls back to back (receive slots reused every second call, the
+            # 4-token launches of a 9-token call each exchanging): each equals its first result
+            xs = [synth.make_tokens(T, d.hidden, 500 + T, device="cuda", dtype=torch.bfloat16) for T in (1, 9, 3)]
+            firsts = [moe.forward(Lep, x)[0] for x in xs]
+            same = True
+            for k in range(60):
+                o = moe.forward(Lep, xs[k % 3])[0]
+                same &= bool(torch.equal(o, firsts[k % 3]))
+            torch.cuda.synchronize()
+            moe.check()
+            print(f"rank {rank}: 60 back-to-back EP decode calls repeat their results: {same}", flush=True)
+            ok &= same
         Lep.unregister()
         Lfull.unregister()
     # sharded tokens (prefill): each rank its own batch (one rank may have none); the
