@@ -55,6 +55,7 @@ WATCH_ABORT = ctypes.CFUNCTYPE(None, ctypes.c_void_p)
 COLIZIG_PTR_DEVICE = 1
 COLIZIG_EP = 2
 COLIZIG_EP_SHARDED = 4
+COLIZIG_SHARED_BF16 = 8
 COLIZIG_X_F32 = 0
 COLIZIG_X_BF16 = 1
 

@@ -131,6 +131,13 @@ struct MoeLayer {
     CUtensorMap gate_map{}, up_map{}, sh_gate_map{}, sh_up_map{};  // decode views of the gate/up weights
     int gu_kb = 0;              // depth of those boxes (0 = 2D maps)
     uint64_t serial = 0;        // distinct for every registration (keys the captured host-call graphs)
+    // BF16 shared expert (the reference's NativeMatrix, moe.zig:297-338): its own
+    // allocation, held and computed on every rank; the routed kernels see d with
+    // shared_inter = 0 and it runs beside them (moe_shared_bf16.cu)
+    uint32_t shb_si = 0;
+    void* shb_mem = nullptr;
+    uint16_t *shb_g = nullptr, *shb_u = nullptr, *shb_d = nullptr;  // [SI][H], [SI][H], [H][SI]
+    float* shb_gate = nullptr;                                      // [H]
 };
 
 // A host-pointer decode call captured as a CUDA graph (token upload, decode
@@ -164,6 +171,7 @@ struct Ctx {
     // MoE
     std::map<uint32_t, MoeLayer> layers;
     DevBuf logits, hrows, io_x, io_out, io_res, ones, pf_scratch;
+    DevBuf shb_scratch;  // BF16 shared expert: gate/up rows and sigmoid gates of the call's tokens
     HostBuf io_host;  // pinned staging of io_res (host-pointer forward, up to kHostStageCap bytes)
     HostBuf io_xh;    // pinned staging of the tokens (host-pointer forward, up to kHostStageCap bytes)
     uint32_t* sync = nullptr;
@@ -257,13 +265,14 @@ int watch_wait(Q query, AE async_error, AB abort_comm, int timeout_ms) {
         const int q = query();
         if (q == 0) return CZ_OK;
         if (q < 0) return CZ_ED2H;
-        const bool late = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0)
-                              .count() >= timeout_ms;
-        if (async_error() || late) {
+        const auto us =
+            std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0).count();
+        if (async_error() || us >= (int64_t)timeout_ms * 1000) {
             abort_comm();
             return CZ_ENCCL;
         }
-        if (it >= 64) std::this_thread::sleep_for(std::chrono::microseconds(20));
+        // spin through the first 2 ms (decode calls end within it), then back off
+        if (it >= 64 && us >= 2000) std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
 }
 
@@ -421,6 +430,7 @@ void drop_host_graphs(bool all, uint32_t layer) {
 
 void free_layer(MoeLayer& L) {
     if (L.mem) cudaFree(L.mem);
+    if (L.shb_mem) cudaFree(L.shb_mem);
     L = MoeLayer{};
 }
 
@@ -458,7 +468,7 @@ void shutdown_locked() {
     drop_host_graphs(true, 0);
     g.io_host.release();
     g.io_xh.release();
-    for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.hrows, &g.pf_scratch, &g.io_x, &g.io_out, &g.io_res,
+    for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.hrows, &g.pf_scratch, &g.shb_scratch, &g.io_x, &g.io_out, &g.io_res,
                       &g.ones, &g.sh_idx, &g.sh_gates, &g.sh_xn, &g.sh_slot, &g.sh_counts, &g.sh_allc,
                       &g.sh_tmp, &g.sh_send, &g.sh_recv, &g.sh_x, &g.sh_ridx, &g.sh_rgates, &g.sh_part, &g.sh_back})
         b->release();
@@ -619,8 +629,8 @@ void timer_free() {
 
 // Runs one layer over T tokens (device pointers, stream-ordered), in launches
 // of at most kDecodeMaxTokens tokens.
-int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uint32_t* idx, float* gates,
-            const float* rms_w, float eps, const float* residual, cudaStream_t st, uint32_t* status_out = nullptr) {
+int moe_run_routed(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uint32_t* idx, float* gates,
+                   const float* rms_w, float eps, const float* residual, cudaStream_t st, uint32_t* status_out) {
     if (T >= kPrefillMinTokens && L.pf_ok) {
         const size_t need = cz::prefill_scratch_bytes(T, (int)L.d.hidden, (int)L.d.experts, (int)L.d.topk,
                                                       (int)L.d.inter, (int)L.d.shared_inter, g.num_sms);
@@ -687,6 +697,37 @@ int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uin
     return CZ_OK;
 }
 
+// One layer over T tokens: the routed experts (moe_run_routed) and, for a layer
+// with a BF16 shared expert, its gate/up rows and sigmoid gate before them (from
+// the layer input, which stack mode overwrites in place) and its down rows added
+// into out after them (after the ranks' combine, so every rank's out has it).
+int moe_run(const MoeLayer& L, const void* x, int x_bf16, int T, float* out, uint32_t* idx, float* gates,
+            const float* rms_w, float eps, const float* residual, cudaStream_t st, uint32_t* status_out = nullptr) {
+    if (!L.shb_si || T <= 0) return moe_run_routed(L, x, x_bf16, T, out, idx, gates, rms_w, eps, residual, st, status_out);
+    const void* before = g.shb_scratch.p;
+    if (!g.shb_scratch.ensure(cz::shb_scratch_bytes(T, (int)L.shb_si))) return CZ_EALLOC;
+    if (before && before != g.shb_scratch.p) drop_host_graphs(true, 0);  // captured calls used the old scratch
+    cz::ShbParams sp{};
+    sp.x = x;
+    sp.x_bf16 = x_bf16;
+    sp.T = T;
+    sp.H = (int)L.d.hidden;
+    sp.SI = (int)L.shb_si;
+    sp.rms_w = rms_w;
+    sp.eps = eps;
+    sp.wg = L.shb_g;
+    sp.wu = L.shb_u;
+    sp.wd = L.shb_d;
+    sp.sh_gate = L.shb_gate;
+    sp.hsh = g.shb_scratch.as<float>();
+    sp.sg = reinterpret_cast<float*>(g.shb_scratch.as<uint8_t>() + ((size_t)T * L.shb_si * 4 + 255) / 256 * 256);
+    sp.out = out;
+    int rc = cz::shb_launch(sp, true, st);
+    if (!rc) rc = moe_run_routed(L, x, x_bf16, T, out, idx, gates, rms_w, eps, residual, st, status_out);
+    if (!rc) rc = cz::shb_launch(sp, false, st);
+    return rc;
+}
+
 // Expert parallelism with sharded tokens (prefill): every rank passes its own
 // T tokens (T may differ between ranks, 0 included) and gets their outputs.
 // Each rank routes its tokens, sends every token row once to each rank holding
@@ -700,7 +741,7 @@ int moe_run_sharded(const MoeLayer& L, const void* x, int x_bf16, int T, float* 
                     float* gates_out, const float* rms_w, float eps, const float* residual, cudaStream_t st) {
     if (!L.ep || g.ep_world < 2) return CZ_EARGS;
     if (!g.ep_comm) return CZ_ENCCL;  // aborted
-    if (L.d.shared_inter || !L.pf_ok) return CZ_ESHAPE;  // the same verdict on every rank (same layer)
+    if (L.d.shared_inter || L.shb_si || !L.pf_ok) return CZ_ESHAPE;  // the same verdict on every rank (same layer)
     const int W = g.ep_world, me = g.ep_rank;
     const int K = (int)L.d.topk, E = (int)L.d.experts, H = (int)L.d.hidden;
     // Until the first collective, a failure here is only recorded: the rank still takes
@@ -999,13 +1040,20 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
     CsrGuard _csr;
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g.inited || !dims || !router || !experts) return CZ_EARGS;
-    const colizig_moe_dims d = *dims;
+    colizig_moe_dims d = *dims;
     if (d.hidden == 0 || d.experts == 0 || d.topk == 0 || d.inter == 0 || d.topk > d.experts) return CZ_EARGS;
     if (d.topk > (uint32_t)cz::kMaxTopk || d.experts > (uint32_t)cz::kMaxExperts) return CZ_ESHAPE;
     if (d.hidden % 16 || d.inter % 16 || d.shared_inter % 16 || d.hidden > 16384 || d.inter > 32768 ||
         d.shared_inter > 32768)
         return CZ_ESHAPE;
     if (d.shared_inter && (!shared || !shared_gate)) return CZ_EARGS;
+    // a BF16 shared expert is registered beside the routed experts, which then see none
+    const uint32_t shb_si = (flags & COLIZIG_SHARED_BF16) ? d.shared_inter : 0u;
+    if (shb_si) {
+        if (!shared->gate_w || !shared->up_w || !shared->down_w) return CZ_EARGS;
+        if (!cz::shb_supported((int)d.hidden, (int)shb_si)) return CZ_ESHAPE;
+        d.shared_inter = 0;
+    }
     const bool ep = (flags & COLIZIG_EP) != 0;
     if (ep && (!g.ep_on || (uint32_t)g.ep_world > d.experts)) return CZ_EARGS;
     cudaSetDevice(g.dev);
@@ -1143,6 +1191,27 @@ CZ_EXPORT int colizig_cuda_moe_register_layer(uint32_t layer, const colizig_moe_
         P.shared_here = shared_here;
         L.pf_ok = ok;
     }
+    if (!rc && shb_si) {
+        // BF16 shared expert: gate, up [SI][H] and down [H][SI] bf16 bits, gate vector [H] f32
+        const size_t wb = (size_t)shb_si * H * 2;
+        const size_t o_g = 0, o_u = (wb + 255) & ~size_t(255), o_d = 2 * o_u, o_v = 3 * o_u;
+        if (cudaMalloc(&L.shb_mem, o_v + H * 4) != cudaSuccess) {
+            L.shb_mem = nullptr;
+            rc = CZ_EALLOC;
+        } else {
+            uint8_t* b = static_cast<uint8_t*>(L.shb_mem);
+            L.shb_si = shb_si;
+            L.shb_g = reinterpret_cast<uint16_t*>(b + o_g);
+            L.shb_u = reinterpret_cast<uint16_t*>(b + o_u);
+            L.shb_d = reinterpret_cast<uint16_t*>(b + o_d);
+            L.shb_gate = reinterpret_cast<float*>(b + o_v);
+            if (cudaMemcpyAsync(L.shb_g, shared->gate_w, wb, kind, g.stream) != cudaSuccess ||
+                cudaMemcpyAsync(L.shb_u, shared->up_w, wb, kind, g.stream) != cudaSuccess ||
+                cudaMemcpyAsync(L.shb_d, shared->down_w, wb, kind, g.stream) != cudaSuccess ||
+                cudaMemcpyAsync(L.shb_gate, shared_gate, H * 4, kind, g.stream) != cudaSuccess)
+                rc = CZ_EH2D;
+        }
+    }
     if (!rc && cudaStreamSynchronize(g.stream) != cudaSuccess) rc = CZ_EH2D;
     if (rc) {
         cudaStreamSynchronize(g.stream);
@@ -1221,7 +1290,12 @@ CZ_EXPORT int colizig_cuda_moe_forward(uint32_t layer, const void* x, int x_dtyp
     // pinned staging, so no copy back is needed.  A key's first call runs directly
     // (it allocates the decode scratch and sets the kernel attributes); the second
     // captures.
-    const bool graphable = kernel_status && !L.ep && xb && ob && !g.dbg_hold && g.tm_ev.empty();
+    // (expert-parallel layers too when the decode kernel sums the ranks itself: no
+    // NCCL call is captured, and every rank replays the same launches)
+    const bool ep_kernel_combine = L.ep && g.ep_world > 1 && g.ep_p2p && g.ep_p2p_use && g.ep_comm &&
+                                   L.d.hidden <= (uint32_t)cz::kEpMaxHidden;
+    const bool graphable = kernel_status && (!L.ep || ep_kernel_combine) && xb && ob && !g.dbg_hold &&
+                           g.tm_ev.empty();
     if (graphable && ensure_decode_scratch(L.d) == CZ_OK) {
         const HostGraphKey key{layer, L.serial, T, bf16, topk_idx != nullptr, topk_gates != nullptr, g.io_x.p,
                                g.io_res.p, g.io_host.p, g.io_xh.p, g.logits.p, g.hrows.p, g.sync};
@@ -1517,6 +1591,7 @@ CZ_EXPORT int colizig_cuda_ep_shutdown(void) {
 CZ_EXPORT int colizig_cuda_ep_set_timeout(int ms) {
     std::lock_guard<std::mutex> lk(g_mu);
     g.ep_timeout_ms = ms;
+    drop_host_graphs(true, 0);  // captured decode launches carry the kernel's wait deadline
     return CZ_OK;
 }
 
@@ -1542,6 +1617,7 @@ CZ_EXPORT int colizig_cuda_ep_combine_mode(void) {
 CZ_EXPORT int colizig_cuda_ep_set_combine(int in_kernel) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (in_kernel != 0 && in_kernel != 1) return CZ_EARGS;
+    if (g.ep_p2p_use != (in_kernel == 1)) drop_host_graphs(true, 0);
     g.ep_p2p_use = in_kernel == 1;
     return CZ_OK;
 }
@@ -1610,6 +1686,7 @@ CZ_EXPORT int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, in
     if (it == g.layers.end()) return CZ_ENOLAYER;
     const MoeLayer& L = it->second;
     if (L.ep) return CZ_EARGS;  // its all-reduce is not part of this entry point
+    if (L.shb_si) return CZ_ESHAPE;  // the BF16 shared expert's scratch is allocated
     if (L.d.hidden > (uint32_t)kNoAllocMaxHidden || L.d.experts > (uint32_t)cz::kMaxExperts ||
         L.d.topk > (uint32_t)cz::kMaxTopk || g.num_sms > cz::kMaxGrid ||
         L.d.inter > (uint32_t)kNoAllocMaxInter || L.d.shared_inter > (uint32_t)kNoAllocMaxInter)

@@ -14,6 +14,7 @@
 //   layers.L.mlp.experts.e.{gate,up,down}_proj.weight      E4M3 [I, H] / [H, I]
 //   layers.L.mlp.experts.e.{gate,up,down}_proj.weight_scale_inv   [nblk, nblk] F32 | BF16 | F16
 //   layers.L.mlp.shared_expert.{gate,up,down}_proj.weight(_scale_inv), shared_expert_gate.weight
+//   (a BF16 shared expert, as real Qwen4-Exp checkpoints hold it, has no _scale_inv)
 // BF16 / F16 values are widened exactly to f32 (bf16: the top 16 bits of an
 // f32, as matmul.zig:105-107 bf16ToF32), which is what the reference's dotBf16
 // multiplies by, so a BF16 router gives the same logits as its f32 widening.
@@ -330,17 +331,33 @@ CZ_EXPORT int colizig_cuda_moe_load_safetensors(uint32_t layer, const char* cons
     }
     colizig_moe_expert sh{};
     const float* sh_gate = nullptr;
+    uint32_t sh_flag = 0;
     if (SI) {
         const std::string stem = L + "shared_expert.";
-        int rc = fp8(stem + "gate_proj", SI, H, &sh.gate_w, &sh.gate_s);
-        if (!rc) rc = fp8(stem + "up_proj", SI, H, &sh.up_w, &sh.up_s);
-        if (!rc) rc = fp8(stem + "down_proj", H, SI, &sh.down_w, &sh.down_s);
-        if (rc) return rc;
+        const View g0 = ix.find(stem + "gate_proj.weight");
+        if (g0.t && g0.t->dtype == "BF16") {
+            // the reference's BF16 NativeMatrix shared expert (moe.zig:319-325,
+            // tensors.zig:74-95): bf16 [SI, H] gate/up, [H, SI] down, no scales
+            const View u0 = ix.find(stem + "up_proj.weight"), dn = ix.find(stem + "down_proj.weight");
+            if (!u0.t || !dn.t) return CZ_EIO;
+            if (u0.t->dtype != "BF16" || dn.t->dtype != "BF16" || !shape_is(*g0.t, {SI, H}) ||
+                !shape_is(*u0.t, {SI, H}) || !shape_is(*dn.t, {H, SI}))
+                return CZ_ESHAPE;
+            sh.gate_w = g0.bytes;
+            sh.up_w = u0.bytes;
+            sh.down_w = dn.bytes;
+            sh_flag = COLIZIG_SHARED_BF16;
+        } else {
+            int rc = fp8(stem + "gate_proj", SI, H, &sh.gate_w, &sh.gate_s);
+            if (!rc) rc = fp8(stem + "up_proj", SI, H, &sh.up_w, &sh.up_s);
+            if (!rc) rc = fp8(stem + "down_proj", H, SI, &sh.down_w, &sh.down_s);
+            if (rc) return rc;
+        }
         const View g = ix.find(L + "shared_expert_gate.weight");
         if (!g.t) return CZ_EIO;
         if (!is_float(*g.t) || !(shape_is(*g.t, {H}) || shape_is(*g.t, {1, H}))) return CZ_ESHAPE;
         sh_gate = as_f32(g, keep);
     }
     return colizig_cuda_moe_register_layer(layer, &d, router_f, ex.data(), SI ? &sh : nullptr, sh_gate,
-                                           flags & COLIZIG_EP);
+                                           (flags & COLIZIG_EP) | sh_flag);
 }

@@ -165,6 +165,26 @@ int ep_unpack(const uint8_t* recv, size_t rs, int R, size_t xrow_bytes, int K, v
 int ep_combine(const float* back, const int* slot, int T, int W, int H, const float* residual, float* out,
                cudaStream_t st);
 
+// BF16 shared expert (moe_shared_bf16.cu), for layers whose shared expert is the
+// reference's BF16 NativeMatrix (moe.zig:297-338).  gate_up: hsh[T][SI] =
+// silu(x.Wg)*(x.Wu) and sg[T] = sigmoid(x.sh_gate), x rms-normalised when rms_w;
+// else out[T][H] += sg * (hsh . Wd).  Stream-ordered.
+struct ShbParams {
+    const void* x;            // [T][H] f32 or bf16
+    int x_bf16, T, H, SI;
+    const float* rms_w;       // stack mode: rmsnorm weight [H] (else null)
+    float eps;
+    const uint16_t *wg, *wu;  // bf16 [SI][H]
+    const uint16_t* wd;       // bf16 [H][SI]
+    const float* sh_gate;     // [H]
+    float* hsh;               // scratch [T][SI]
+    float* sg;                // scratch [T]
+    float* out;               // [T][H]
+};
+bool shb_supported(int H, int SI);
+size_t shb_scratch_bytes(int T, int SI);  // hsh, then sg at a 256-byte boundary
+int shb_launch(const ShbParams& p, bool gate_up, cudaStream_t st);
+
 // Legacy per-matrix block-FP8 matmul (device pointers, stream-ordered).
 int fp8_matmul_launch(float* y, const float* x, const uint8_t* w, const float* scales, int S, int I, int O,
                       cudaStream_t stream);

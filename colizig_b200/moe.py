@@ -102,16 +102,32 @@ class Layer:
                                         ds + e * nbs)
         sh_ptr = None
         sg_ptr = None
+        sh_bf16 = False
         if dims.has_shared():
             if shared is None or shared_gate is None:
                 raise ValueError("dims.shared_inter > 0 needs shared weights and shared_gate")
-            sh = _abi.MoeExpert(_ptr(shared["sh_gate_w"]), _ptr(shared["sh_gate_s"]), _ptr(shared["sh_up_w"]),
-                                _ptr(shared["sh_up_s"]), _ptr(shared["sh_down_w"]), _ptr(shared["sh_down_s"]))
+            SI = dims.shared_inter
+            if "sh_gate_bf16" in shared:
+                # the reference's BF16 NativeMatrix shared expert (moe.zig:297-338): raw bf16
+                # [SI, H] gate / up and [H, SI] down, no block scales
+                sh_bf16 = True
+                for k, shp in (("sh_gate_bf16", (SI, H)), ("sh_up_bf16", (SI, H)), ("sh_down_bf16", (H, SI))):
+                    a = shared[k]
+                    if tuple(a.shape) != shp or _dtype_name(a) not in ("bf16", "u16", "i16"):
+                        raise ValueError(f"{k} must be bf16 {shp}, got {_dtype_name(a)} {tuple(a.shape)}")
+                    if _is_cuda(a) != device:
+                        raise ValueError("mix of host and device arrays")
+                sh = _abi.MoeExpert(_ptr(shared["sh_gate_bf16"]), 0, _ptr(shared["sh_up_bf16"]), 0,
+                                    _ptr(shared["sh_down_bf16"]), 0)
+            else:
+                sh = _abi.MoeExpert(_ptr(shared["sh_gate_w"]), _ptr(shared["sh_gate_s"]), _ptr(shared["sh_up_w"]),
+                                    _ptr(shared["sh_up_s"]), _ptr(shared["sh_down_w"]), _ptr(shared["sh_down_s"]))
             keep += list(shared.values()) + [shared_gate]
             sh_ptr = ctypes.byref(sh)
             sg_ptr = _ptr(shared_gate)
         cd = dims.c()
-        flags = (_abi.COLIZIG_PTR_DEVICE if device else 0) | (_abi.COLIZIG_EP if ep else 0)
+        flags = ((_abi.COLIZIG_PTR_DEVICE if device else 0) | (_abi.COLIZIG_EP if ep else 0) |
+                 (_abi.COLIZIG_SHARED_BF16 if sh_bf16 else 0))
         self.ep = bool(ep)
         if device:
             torch.cuda.synchronize()
@@ -134,7 +150,9 @@ class Layer:
     def from_weights(layer_id: int, dims: Dims, w: dict, ep: bool = False) -> "Layer":
         shared = None
         if dims.has_shared():
-            shared = {k: w[k] for k in ("sh_gate_w", "sh_gate_s", "sh_up_w", "sh_up_s", "sh_down_w", "sh_down_s")}
+            keys = (("sh_gate_bf16", "sh_up_bf16", "sh_down_bf16") if "sh_gate_bf16" in w else
+                    ("sh_gate_w", "sh_gate_s", "sh_up_w", "sh_up_s", "sh_down_w", "sh_down_s"))
+            shared = {k: w[k] for k in keys}
         return Layer(layer_id, dims, w["router"], w["gate_w"], w["gate_s"], w["up_w"], w["up_s"], w["down_w"],
                      w["down_s"], shared, w.get("sh_gate"), ep=ep)
 

@@ -113,9 +113,30 @@ def make_tokens(T: int, H: int, seed: int, device="cpu", dtype=torch.bfloat16) -
     return torch.randn((T, H), generator=gen, device=device, dtype=torch.float32).to(dtype)
 
 
+def bf16_shared(w: dict, d: Dims, seed: int = 0) -> dict:
+    """Replace a layer's shared expert (in place) by a BF16 one as real Qwen4-Exp
+    checkpoints hold it (the reference's NativeMatrix, moe.zig:297-338): gate/up
+    [SI, H] and down [H, SI] bf16 from N(0, 0.02), no block scales."""
+    SI, H = d.shared_inter, d.hidden
+    dev = w["router"].device
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(int(seed) + 777)
+    for k in ("sh_gate_w", "sh_gate_s", "sh_up_w", "sh_up_s", "sh_down_w", "sh_down_s"):
+        w.pop(k, None)
+    for k, shp in (("sh_gate_bf16", (SI, H)), ("sh_up_bf16", (SI, H)), ("sh_down_bf16", (H, SI))):
+        w[k] = torch.randn(shp, generator=gen, device=dev, dtype=torch.float32).mul_(0.02).to(torch.bfloat16)
+    if "sh_gate" not in w:
+        w["sh_gate"] = torch.randn((H,), generator=gen, device=dev, dtype=torch.float32).mul_(0.02)
+    return w
+
+
 def to_numpy_layer(w: dict) -> dict:
-    """Host numpy copies (for the CPU oracle)."""
-    return {k: v.detach().cpu().numpy() for k, v in w.items()}
+    """Host numpy copies (for the CPU oracle); bf16 tensors as their raw bits (uint16)."""
+    out = {}
+    for k, v in w.items():
+        v = v.detach().cpu()
+        out[k] = v.view(torch.int16).numpy().view(np.uint16) if v.dtype == torch.bfloat16 else v.numpy()
+    return out
 
 
 def tokens_f32(x: torch.Tensor) -> np.ndarray:

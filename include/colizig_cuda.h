@@ -112,6 +112,15 @@ typedef struct colizig_moe_expert {
     NCCL send/recv (expert-parallel prefill).  Every rank of the group makes the
     call.  Layers with a shared expert are not supported here (-8). */
 
+#define COLIZIG_SHARED_BF16 8u /* register_layer: the shared expert is the reference's BF16
+    NativeMatrix (src/qwen38/moe.zig:297-338, tensors.zig:65-120), as real Qwen4-Exp
+    checkpoints hold it: shared->gate_w / up_w point at bf16 [shared_inter, hidden]
+    and shared->down_w at bf16 [hidden, shared_inter] (raw bf16 bits, cast the
+    pointers), the scale pointers are ignored.  Computed from the layer input
+    (after rms in stack mode) beside the routed experts and added to out with its
+    sigmoid gate; under COLIZIG_EP it is held and computed on every rank.  Not
+    with COLIZIG_EP_SHARDED nor colizig_cuda_moe_forward_noalloc (-8). */
+
 /* x dtypes */
 #define COLIZIG_X_F32 0
 #define COLIZIG_X_BF16 1
@@ -140,7 +149,8 @@ int colizig_cuda_moe_unregister_layer(uint32_t layer);
  * layers.L.mlp.experts.e.{gate,up,down}_proj.weight (F8_E4M3) and
  * .weight_scale_inv (F32, BF16 or F16 [nblk, nblk]), and for dims->shared_inter
  * > 0 layers.L.mlp.shared_expert.{gate,up,down}_proj.weight(_scale_inv)
- * (F8_E4M3) and layers.L.mlp.shared_expert_gate.weight ([H] or [1, H]).  BF16 /
+ * (F8_E4M3; or BF16 [SI, H] / [H, SI] without scales, registered as
+ * COLIZIG_SHARED_BF16) and layers.L.mlp.shared_expert_gate.weight ([H] or [1, H]).  BF16 /
  * F16 values are widened exactly to f32 (a BF16 router then gives the logits of
  * the reference's dotBf16, matmul.zig:84-110).  prefix may be NULL; flags: 0 or
  * COLIZIG_EP.  Returns 0, -10 when a shard cannot be read or parsed or a

@@ -63,6 +63,9 @@ class CLayer(ctypes.Structure):
         ("sh_down_w", _PU8),
         ("sh_down_s", _PF32),
         ("sh_gate", _PF32),
+        ("sh_gate_bf16", ctypes.POINTER(ctypes.c_uint16)),
+        ("sh_up_bf16", ctypes.POINTER(ctypes.c_uint16)),
+        ("sh_down_bf16", ctypes.POINTER(ctypes.c_uint16)),
     ]
 
 
@@ -98,6 +101,7 @@ def lib():
     L.czref_dot_f32.restype = ctypes.c_float
     L.czref_matmul_f32.argtypes = [vp, vp, vp, sz, sz, sz]
     L.czref_matmul_fp8.argtypes = [vp, vp, vp, vp, sz, sz, sz]
+    L.czref_matmul_bf16.argtypes = [vp, vp, vp, sz, sz, sz]
     L.czref_rms.argtypes = [vp, vp, vp, sz, ctypes.c_float]
     L.czref_set_threads.argtypes = [ctypes.c_int]
     L.czref_get_threads.restype = ctypes.c_int
@@ -168,6 +172,17 @@ def matmul_f32(x: np.ndarray, w: np.ndarray) -> np.ndarray:
     return y
 
 
+def matmul_bf16(x: np.ndarray, w_bits: np.ndarray) -> np.ndarray:
+    """matmulBf16 (matmul.zig:36-48): y[S,O] = x[S,I] @ bf16(w)[O,I]^T, w as raw bf16 bits."""
+    x = np.ascontiguousarray(x, np.float32)
+    w_bits = np.ascontiguousarray(w_bits, np.uint16)
+    S, I = x.shape
+    O = w_bits.shape[0]
+    y = np.empty((S, O), np.float32)
+    lib().czref_matmul_bf16(_p(y), _p(x), _p(w_bits), S, I, O)
+    return y
+
+
 def matmul_fp8(x: np.ndarray, w: np.ndarray, scales: np.ndarray) -> np.ndarray:
     """y[S,O] = x[S,I] @ dequant(w[O,I])^T with [nblk(O), nblk(I)] block scales."""
     x = np.ascontiguousarray(x, np.float32)
@@ -227,7 +242,9 @@ class LayerWeights:
     router [E,H] f32; gate_w/up_w [E,I,H] u8 (E4M3); gate_s/up_s [E,nb(I),nb(H)] f32;
     down_w [E,H,I] u8; down_s [E,nb(H),nb(I)] f32.  Optional shared expert
     (always-on FP8 expert): sh_gate_w/sh_up_w [SI,H], sh_down_w [H,SI] + scales,
-    sh_gate [H] f32 (the sigmoid gate vector).
+    sh_gate [H] f32 (the sigmoid gate vector).  Or the reference's BF16 shared
+    expert (NativeMatrix, moe.zig:297-338): sh_gate_bf16/sh_up_bf16 [SI,H] and
+    sh_down_bf16 [H,SI] as raw bf16 bits (uint16), with sh_gate.
     """
 
     router: np.ndarray
@@ -244,10 +261,14 @@ class LayerWeights:
     sh_down_w: Optional[np.ndarray] = None
     sh_down_s: Optional[np.ndarray] = None
     sh_gate: Optional[np.ndarray] = None
+    sh_gate_bf16: Optional[np.ndarray] = None
+    sh_up_bf16: Optional[np.ndarray] = None
+    sh_down_bf16: Optional[np.ndarray] = None
 
 
 LAYER_KEYS = ("router", "gate_w", "gate_s", "up_w", "up_s", "down_w", "down_s")
 SHARED_KEYS = ("sh_gate_w", "sh_gate_s", "sh_up_w", "sh_up_s", "sh_down_w", "sh_down_s", "sh_gate")
+SHARED_BF16_KEYS = ("sh_gate_bf16", "sh_up_bf16", "sh_down_bf16", "sh_gate")
 
 
 def layer_from_dict(w: dict) -> LayerWeights:
@@ -255,6 +276,8 @@ def layer_from_dict(w: dict) -> LayerWeights:
     kw = {k: np.ascontiguousarray(w[k]) for k in LAYER_KEYS}
     if "sh_gate_w" in w:
         kw.update({k: np.ascontiguousarray(w[k]) for k in SHARED_KEYS})
+    elif "sh_gate_bf16" in w:
+        kw.update({k: np.ascontiguousarray(w[k]) for k in SHARED_BF16_KEYS})
     return LayerWeights(**kw)
 
 
@@ -290,6 +313,13 @@ class _CLayerHolder:
                              ("sh_down_w", ctypes.c_uint8), ("sh_down_s", ctypes.c_float),
                              ("sh_gate", ctypes.c_float)):
                 arr = np.ascontiguousarray(getattr(lw, name))
+                self.arrays.append(arr)
+                setattr(c, name, ctypes.cast(arr.ctypes.data, ctypes.POINTER(ct)))
+        elif lw.sh_gate_bf16 is not None:
+            for name, ct in (("sh_gate_bf16", ctypes.c_uint16), ("sh_up_bf16", ctypes.c_uint16),
+                             ("sh_down_bf16", ctypes.c_uint16), ("sh_gate", ctypes.c_float)):
+                arr = np.ascontiguousarray(getattr(lw, name))
+                assert arr.dtype == (np.uint16 if ct is ctypes.c_uint16 else np.float32), name
                 self.arrays.append(arr)
                 setattr(c, name, ctypes.cast(arr.ctypes.data, ctypes.POINTER(ct)))
         self.c = c

@@ -385,6 +385,70 @@ void czref_matmul_f32(float* y, const float* x, const float* w, size_t S, size_t
     chunks(O, O * I * S, &c, mm_body);
 }
 
+/* bf16ToF32 (matmul.zig:108-110): bf16 is the top half of an f32. */
+static inline float bf16_f32(uint16_t b) {
+    const uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* dotBf16 (matmul.zig:84-106): dotF32's 4 FMA chains x 8 lanes, each weight lane
+ * widened exactly (bits << 16), then the same ordered reduction and FMA tail. */
+float czref_dot_bf16(const float* a, const uint16_t* b, size_t n) {
+    size_t i = 0;
+#if CZ_AVX2
+    __m256 acc[UNROLL];
+    for (int k = 0; k < UNROLL; ++k) acc[k] = _mm256_setzero_ps();
+#define CZ_WIDEN(p) _mm256_castsi256_ps(_mm256_slli_epi32(_mm256_cvtepu16_epi32(_mm_loadu_si128((const __m128i*)(p))), 16))
+    for (; i + UNROLL * LANES <= n; i += UNROLL * LANES)
+        for (int k = 0; k < UNROLL; ++k)
+            acc[k] = _mm256_fmadd_ps(_mm256_loadu_ps(a + i + k * LANES), CZ_WIDEN(b + i + k * LANES), acc[k]);
+    for (; i + LANES <= n; i += LANES) acc[0] = _mm256_fmadd_ps(_mm256_loadu_ps(a + i), CZ_WIDEN(b + i), acc[0]);
+#undef CZ_WIDEN
+    __m256 total = _mm256_setzero_ps();
+    for (int k = 0; k < UNROLL; ++k) total = _mm256_add_ps(total, acc[k]);
+    float sum = reduce_ordered(total);
+#else
+    float acc[UNROLL][LANES];
+    memset(acc, 0, sizeof acc);
+    for (; i + UNROLL * LANES <= n; i += UNROLL * LANES)
+        for (int k = 0; k < UNROLL; ++k)
+            for (int l = 0; l < LANES; ++l)
+                acc[k][l] = fmaf(a[i + k * LANES + l], bf16_f32(b[i + k * LANES + l]), acc[k][l]);
+    for (; i + LANES <= n; i += LANES)
+        for (int l = 0; l < LANES; ++l) acc[0][l] = fmaf(a[i + l], bf16_f32(b[i + l]), acc[0][l]);
+    float total[LANES] = {0};
+    for (int k = 0; k < UNROLL; ++k)
+        for (int l = 0; l < LANES; ++l) total[l] += acc[k][l];
+    float sum = total[0];
+    for (int l = 1; l < LANES; ++l) sum += total[l];
+#endif
+    for (; i < n; ++i) sum = fmaf(a[i], bf16_f32(b[i]), sum);
+    return sum;
+}
+
+typedef struct {
+    float* y;
+    const float* x;
+    const uint16_t* w;
+    size_t S, I, O;
+} mmb_ctx;
+
+static void mmb_body(void* p, size_t o0, size_t o1) {
+    const mmb_ctx* c = (const mmb_ctx*)p;
+    for (size_t o = o0; o < o1; ++o) {
+        const uint16_t* wr = c->w + o * c->I;
+        for (size_t s = 0; s < c->S; ++s) c->y[s * c->O + o] = czref_dot_bf16(c->x + s * c->I, wr, c->I);
+    }
+}
+
+/* matmulBf16 (matmul.zig:36-48): y[S,O] = x[S,I] @ w[O,I]^T, fan-out over O rows. */
+void czref_matmul_bf16(float* y, const float* x, const uint16_t* w, size_t S, size_t I, size_t O) {
+    mmb_ctx c = {y, x, w, S, I, O};
+    chunks(O, O * I * S, &c, mmb_body);
+}
+
 typedef struct {
     float* y;
     const float* x;
@@ -479,14 +543,23 @@ typedef struct {
 
 static int has_shared(const czref_dims* d) { return d->shared_inter != 0; }
 
-/* addSharedExpert (moe.zig:467-479) with block-FP8 shared projections. */
+/* addSharedExpert (moe.zig:467-479): block-FP8 shared projections, or the
+ * reference's own BF16 NativeMatrix projections (matmulBf16) when given. */
 static void add_shared(const czref_layer* L, const czref_dims* d, const float* xs, float* ys, scratch* sc) {
     if (!has_shared(d)) return;
     const size_t H = d->hidden, SI = d->shared_inter;
-    czref_matmul_fp8(sc->sg, xs, L->sh_gate_w, L->sh_gate_s, 1, H, SI);
-    czref_matmul_fp8(sc->su, xs, L->sh_up_w, L->sh_up_s, 1, H, SI);
+    if (L->sh_gate_bf16) {
+        czref_matmul_bf16(sc->sg, xs, L->sh_gate_bf16, 1, H, SI);
+        czref_matmul_bf16(sc->su, xs, L->sh_up_bf16, 1, H, SI);
+    } else {
+        czref_matmul_fp8(sc->sg, xs, L->sh_gate_w, L->sh_gate_s, 1, H, SI);
+        czref_matmul_fp8(sc->su, xs, L->sh_up_w, L->sh_up_s, 1, H, SI);
+    }
     for (size_t j = 0; j < SI; ++j) sc->sh[j] = czref_silu(sc->sg[j]) * sc->su[j];
-    czref_matmul_fp8(sc->shared, sc->sh, L->sh_down_w, L->sh_down_s, 1, SI, H);
+    if (L->sh_gate_bf16)
+        czref_matmul_bf16(sc->shared, sc->sh, L->sh_down_bf16, 1, SI, H);
+    else
+        czref_matmul_fp8(sc->shared, sc->sh, L->sh_down_w, L->sh_down_s, 1, SI, H);
     float sgate = 0;
     for (size_t dd = 0; dd < H; ++dd) sgate += xs[dd] * L->sh_gate[dd];
     sgate = czref_sigmoid(sgate);

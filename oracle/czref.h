@@ -57,7 +57,10 @@ typedef struct {
  * [nblk(inter), nblk(hidden)]; up likewise; down_w[e] u8 [hidden, inter],
  * down_s[e] f32 [nblk(hidden), nblk(inter)].
  * The shared expert (optional) is an always-on block-FP8 expert with the
- * reference's sigmoid gate vector sh_gate [hidden]. */
+ * reference's sigmoid gate vector sh_gate [hidden]; when sh_gate_bf16 is set it
+ * is instead the reference's BF16 NativeMatrix shared expert (moe.zig:297-338,
+ * tensors.zig:65-120): sh_{gate,up}_bf16 [shared_inter, hidden] and
+ * sh_down_bf16 [hidden, shared_inter] raw bf16 bits, run through dotBf16. */
 typedef struct {
     const float* router; /* [experts, hidden] f32 */
     const uint8_t* const* gate_w;
@@ -73,6 +76,9 @@ typedef struct {
     const uint8_t* sh_down_w;
     const float* sh_down_s;
     const float* sh_gate; /* [hidden] */
+    const uint16_t* sh_gate_bf16;
+    const uint16_t* sh_up_bf16;
+    const uint16_t* sh_down_bf16;
 } czref_layer;
 
 size_t czref_nblk(size_t x);
@@ -85,6 +91,8 @@ void czref_dequant_row(float* out, const uint8_t* w, const float* scale_row, siz
 float czref_dot_fp8_row(const float* x, const uint8_t* w, const float* scale_row, size_t n);
 float czref_dot_f32(const float* a, const float* b, size_t n);
 void czref_matmul_f32(float* y, const float* x, const float* w, size_t S, size_t I, size_t O);
+float czref_dot_bf16(const float* a, const uint16_t* b, size_t n);
+void czref_matmul_bf16(float* y, const float* x, const uint16_t* w, size_t S, size_t I, size_t O);
 void czref_matmul_fp8(float* y, const float* x, const uint8_t* w, const float* scales,
                       size_t S, size_t I, size_t O);
 

@@ -7,7 +7,7 @@ Runs the reference's independent NumPy implementation of the path
 synthetic inputs and stores inputs + outputs as ``.npz`` files.  The reference
 tree is only needed to regenerate; the committed fixtures are what the tests read.
 
-Usage:  python tests/golden/make_golden.py <reference source root>
+Usage:  python tests/golden/make_golden.py <reference source root> [shared_bf16]
 """
 
 import os
@@ -139,10 +139,61 @@ def main(refroot):
         idxs.append(np.asarray(idx, np.uint32))
     np.savez_compressed(os.path.join(HERE, "moe_shared_tiny.npz"), x=x, out=np.stack(outs),
                         idx=np.stack(idxs), H=H, E=E, I=I, K=K, SI=SI, **L)
+    shared_bf16(r38)
     print("golden fixtures written to", HERE)
 
 
+def bf16_bits(f32: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even to bf16, as raw 16-bit patterns."""
+    t = torch.from_numpy(np.ascontiguousarray(f32, np.float32)).to(torch.bfloat16)
+    return t.view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def shared_bf16(r38):
+    """5. tiny layer whose shared expert is BF16, as the reference loads real
+    Qwen4-Exp checkpoints (NativeMatrix, moe.zig:297-338): the numpy model gets
+    the bf16 weights widened to f32 exactly, as its load_safetensors does."""
+    H, E, I, K, SI = 256, 16, 128, 4, 256
+    rng = np.random.default_rng(5)
+    L = layer_tensors(rng, H, E, I)
+    sh = {"sh_gate_bf16": bf16_bits(rng.standard_normal((SI, H)) * 0.05),
+          "sh_up_bf16": bf16_bits(rng.standard_normal((SI, H)) * 0.05),
+          "sh_down_bf16": bf16_bits(rng.standard_normal((H, SI)) * 0.05),
+          "sh_gate": (rng.standard_normal(H) * 0.02).astype(np.float32)}
+    widen = lambda b: (b.astype(np.uint32) << 16).view(np.float32)  # noqa: E731
+    x = rng.standard_normal((3, H)).astype(np.float32)
+    m = object.__new__(r38.Model)
+    m.H, m.E, m.topk, m.norm_topk, m.prefix = H, E, K, True, "model"
+    T = {
+        "layers.0.mlp.gate.weight": L["router"],
+        "layers.0.mlp.shared_expert.gate_proj.weight": widen(sh["sh_gate_bf16"]),
+        "layers.0.mlp.shared_expert.up_proj.weight": widen(sh["sh_up_bf16"]),
+        "layers.0.mlp.shared_expert.down_proj.weight": widen(sh["sh_down_bf16"]),
+        "layers.0.mlp.shared_expert_gate.weight": sh["sh_gate"],
+    }
+    for e in range(E):
+        for proj, wn, sn in (("gate_proj", "gate_w", "gate_s"), ("up_proj", "up_w", "up_s"),
+                             ("down_proj", "down_w", "down_s")):
+            T[f"layers.0.mlp.experts.{e}.{proj}.weight"] = r38.e4m3_decode(L[wn][e]).astype(np.float32)
+            T[f"layers.0.mlp.experts.{e}.{proj}.weight_scale_inv"] = L[sn][e]
+    m.T = T
+    outs, idxs = [], []
+    for t in range(x.shape[0]):
+        y, idx = m.moe(0, x[t])
+        outs.append(np.asarray(y, np.float32))
+        idxs.append(np.asarray(idx, np.uint32))
+    np.savez_compressed(os.path.join(HERE, "moe_shared_bf16_tiny.npz"), x=x, out=np.stack(outs),
+                        idx=np.stack(idxs), H=H, E=E, I=I, K=K, SI=SI, **L, **sh)
+
+
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
+    # make_golden.py <reference root> [shared_bf16]: every fixture, or only the named one
+    if len(sys.argv) not in (2, 3):
         sys.exit(__doc__)
-    main(sys.argv[1])
+    if len(sys.argv) == 3:
+        sys.path.insert(0, os.path.join(sys.argv[1], "tools", "reference"))
+        import qwen38_ref  # noqa: E402
+
+        {"shared_bf16": shared_bf16}[sys.argv[2]](qwen38_ref)
+    else:
+        main(sys.argv[1])

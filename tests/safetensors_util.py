@@ -60,4 +60,8 @@ def layer_tensors(w, l, prefix="model", router_bf16=False, scales_bf16=False):
             t[f"{pre}shared_expert.{proj}.weight"] = ("F8_E4M3", w[wk])
             t[f"{pre}shared_expert.{proj}.weight_scale_inv"] = sc(w[sk])
         t[pre + "shared_expert_gate.weight"] = ("F32", w["sh_gate"].astype(np.float32)[None, :])
+    elif "sh_gate_bf16" in w:  # the reference's BF16 shared expert: bf16 weights, no scales
+        for proj, wk in (("gate_proj", "sh_gate_bf16"), ("up_proj", "sh_up_bf16"), ("down_proj", "sh_down_bf16")):
+            t[f"{pre}shared_expert.{proj}.weight"] = ("BF16", np.ascontiguousarray(w[wk], np.uint16))
+        t[pre + "shared_expert_gate.weight"] = ("F32", w["sh_gate"].astype(np.float32)[None, :])
     return t

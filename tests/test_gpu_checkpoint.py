@@ -87,3 +87,20 @@ def test_loaded_shared_expert_layer_matches_golden(tmp_path):
         assert_close(out, z["out"])
     finally:
         A.unregister()
+
+
+def test_loaded_bf16_shared_expert_layer_matches_golden(tmp_path):
+    """A BF16 shared expert as real Qwen4-Exp checkpoints hold it (no scales),
+    from the fixture made by the reference's numpy model."""
+    z = golden("moe_shared_bf16_tiny.npz")
+    d = moe.Dims(int(z["H"]), int(z["E"]), int(z["K"]), int(z["I"]), int(z["SI"]), True)
+    w = {k: np.ascontiguousarray(z[k]) for k in z.files if not k.isupper() and k not in ("x", "out", "idx")}
+    p = tmp_path / "tiny_bf16.safetensors"
+    write_safetensors(p, layer_tensors(w, 0))
+    A = checkpoint.load_layer(9204, [p], 0, d, prefix="model")
+    try:
+        out, idx, _ = moe.forward(A, z["x"])
+        assert np.array_equal(idx, z["idx"])
+        assert_close(out, z["out"])
+    finally:
+        A.unregister()

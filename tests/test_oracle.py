@@ -186,6 +186,40 @@ def test_moe_shared_expert_matches_reference_numpy():
         assert_close(o1[0], z["out"][t], 1e-5)
 
 
+def _layer_bf16_shared(z):
+    kw = {k: z[k] for k in LAYER_KEYS}
+    kw.update({k: np.ascontiguousarray(z[k]) for k in ("sh_gate_bf16", "sh_up_bf16", "sh_down_bf16", "sh_gate")})
+    return oracle.LayerWeights(**kw)
+
+
+def test_moe_bf16_shared_expert_matches_reference_numpy():
+    """BF16 NativeMatrix shared expert (moe.zig:297-338, dotBf16 matmul.zig:84-106)
+    vs qwen38_ref.Model.moe on the same weights widened to f32."""
+    z = golden("moe_shared_bf16_tiny.npz")
+    assert z["sh_gate_bf16"].dtype == np.uint16
+    d = oracle.Dims(int(z["H"]), int(z["E"]), int(z["K"]), int(z["I"]), int(z["SI"]), True)
+    L = _layer_bf16_shared(z)
+    out, idx, _ = oracle.moe_forward(L, d, z["x"])
+    assert np.array_equal(idx, z["idx"])
+    assert_close(out, z["out"], 1e-5)
+    for t in range(z["x"].shape[0]):
+        o1, i1, _ = oracle.moe_forward(L, d, z["x"][t])
+        assert np.array_equal(i1[0], z["idx"][t])
+        assert_close(o1[0], z["out"][t], 1e-5)
+
+
+def test_dot_bf16_widens_exactly():
+    """dotBf16 equals dotF32 on the same weights widened to f32 (both 4 chains x 8 lanes)."""
+    rng = np.random.default_rng(3)
+    for n in (256, 200, 37):
+        a = rng.standard_normal(n).astype(np.float32)
+        b = (rng.standard_normal(n) * 0.1).astype(np.float32)
+        bits = (b.view(np.uint32) >> 16).astype(np.uint16)
+        wide = (bits.astype(np.uint32) << 16).view(np.float32)
+        y = oracle.matmul_bf16(a[None, :], bits[None, :])
+        assert y[0, 0] == np.float32(oracle.dot_f32(a, wide))
+
+
 def test_grouped_prefill_close_to_dense():  # moe.zig:720-728
     z = golden("moe_c1.npz")
     d = oracle.Dims(256, 16, 4, 128, 0, True)
