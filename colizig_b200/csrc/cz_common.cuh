@@ -242,9 +242,6 @@ CZ_DEV void prefetch_tensormap(const void* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// L2 prefetch of the 128-byte line holding `p`, through the load/store unit (not the
-// bulk-copy unit, whose queue of tensor copies it would wait behind).
-CZ_DEV void prefetch_line_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 // L2 prefetch of `bytes` (a multiple of 16) from a 16-byte aligned global address.
 CZ_DEV void prefetch_l2(const void* src, uint32_t bytes) {

@@ -1079,30 +1079,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
             __syncwarp();
             bar_arrive_all(BAR_ROUTED);
             bar_sync_all(BAR_SPLIT);
-            // The down rows of this CTA's output rows (phase D's packs) are prefetched
-            // into L2 now, line by line from the producer warp's other lanes: their HBM
-            // reads then overlap the gate/up stream instead of following it (bulk
-            // prefetches would queue behind the tensor copies of the ring fill).
-            if (ok && lane > 0 && !s.abort) {
-                const int o_lo = split_at(c, H, G), drows = s.geo_drows;
-                const int rb0 = o_lo >> 7, nkbH = cz_nblk(H);
-                for (int v = 0; v < s.U; ++v) {
-                    if (s.g_pack[v] < 0) continue;
-                    const int ev = s.g_expert[v];
-                    const bool sh = ev == E;
-                    const int iu = sh ? SI : Ir;
-                    const uint8_t* w = sh ? p.sh_down_w + (size_t)o_lo * SI
-                                          : p.down_w + ((size_t)(ev - p.e_lo) * H + o_lo) * Ir;
-                    const float* sc = sh ? p.sh_down_s + (size_t)rb0 * cz_nbp(SI)
-                                         : p.down_s + ((size_t)(ev - p.e_lo) * nkbH + rb0) * cz_nbp(Ir);
-                    const int nl = (drows * iu + 127) >> 7;
-                    for (int l = lane - 1; l < nl; l += 31) prefetch_line_l2(w + (size_t)l * 128);
-                    if (lane == 1) {  // the <= 2 row blocks of scales: first and last byte's lines
-                        prefetch_line_l2(sc);
-                        prefetch_line_l2(reinterpret_cast<const uint8_t*>(sc) + s.geo_nrb * cz_nbp(iu) * 4 - 1);
-                    }
-                }
-            }
             // The first ring fill goes out here, in the code right after routing (the
             // phase C loop below, cold in the instruction cache when it is first
             // reached, skips these stages).
