@@ -477,7 +477,8 @@ def stack_main(args, world, rank, local, torch, dist, cz, _abi, moe, synth):
             "dtype": "e4m3 x e4m3 -> f32", "data": "synthetic",
             "config": stack_config(args, d, NL, T, world),
             "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
-            "gpu_launches": args.steps * NL * (12 if prefill else -(-args.tokens * world // 4)),  # prefill: rms + 11
+            "gpu_launches": args.steps * NL * (12 if prefill else  # prefill: rms + 11
+                                               -(-T // L.colizig_cuda_moe_decode_batch(layers[0].id, 0))),
         }
         print(json.dumps(line), flush=True)
     for lay in layers:
@@ -869,7 +870,9 @@ def main():
     timing = {"replays": REPLAYS, "replay_ms": replay_ms, "statistic": "median over replays, max over ranks",
               "l2": "flushed (256 MB write) before each replay; steps cycle through "
                     f"{len(layers)} layers, so no step finds its weights in L2"}
-    launches_per_step = 11 if prefill else -(-T // 4)  # prefill: logits, topk, xterms, count, scan, place, tokpos, dispatch, 2 GEMMs, combine
+    # prefill: logits, topk, xterms, count, scan, place, tokpos, dispatch, 2 GEMMs, combine;
+    # decode: ceil(T / tokens per launch) launches of the decode kernel
+    launches_per_step = 11 if prefill else -(-T // L.colizig_cuda_moe_decode_batch(layers[0].id, _abi.COLIZIG_X_BF16))
     if prefill:
         # tensor-bound.  Dominant kernel: the gate/up grouped GEMM.  Its algorithmic FLOPs
         # (2 x pairs x H x 2I routed + 2 x T x H x 2SI shared, pairs on this rank's

@@ -43,6 +43,7 @@ MOE_SYMBOLS = (
     "colizig_cuda_ep_set_timeout",
     "colizig_cuda_ep_abort",
     "colizig_cuda_ep_combine_mode",
+    "colizig_cuda_moe_decode_batch",
     "colizig_cuda_ep_set_combine",
     "colizig_cuda_kernel_timer",
     "colizig_cuda_kernel_timer_read",
@@ -162,6 +163,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         L.colizig_cuda_ep_abort.argtypes = []
         L.colizig_cuda_ep_combine_mode.restype = i32
         L.colizig_cuda_ep_combine_mode.argtypes = []
+        L.colizig_cuda_moe_decode_batch.restype = i32
+        L.colizig_cuda_moe_decode_batch.argtypes = [u32, i32]
         L.colizig_cuda_ep_set_combine.restype = i32
         L.colizig_cuda_ep_set_combine.argtypes = [i32]
         L.colizig_cuda_kernel_timer.restype = i32

@@ -95,6 +95,14 @@ struct DevBuf {
         cap = need;
         return true;
     }
+    // Like ensure, but a growth takes at least 1.5x the old capacity: buffers sized
+    // by data-dependent counts (the sharded exchange) then reallocate, and so
+    // synchronise the device, only a few times.
+    bool ensure_grow(size_t need) {
+        if (cap >= need && p) return true;
+        const size_t want = need > cap + cap / 2 ? need : cap + cap / 2;
+        return ensure(want) || ensure(need);
+    }
     void release() {
         if (p) cudaFree(p);
         p = nullptr;
@@ -828,11 +836,12 @@ int moe_run_sharded(const MoeLayer& L, const void* x, int x_bf16, int T, float* 
                 std::max<size_t>(Sr, 1) > (size_t)mr[4];
     }
     const bool bufs_ok =
-        g.sh_send.ensure((S ? S : 1) * rs) && g.sh_recv.ensure((R ? R : 1) * rs) &&
-        g.sh_x.ensure((R ? R : 1) * xrow) && g.sh_ridx.ensure((R ? R : 1) * K * 4) &&
-        g.sh_rgates.ensure((R ? R : 1) * K * 4) && g.sh_part.ensure((R ? R : 1) * (size_t)H * 4) &&
-        g.sh_back.ensure((S ? S : 1) * (size_t)H * 4) &&
-        (R == 0 || g.pf_scratch.ensure(cz::prefill_scratch_bytes((int)R, H, E, K, (int)L.d.inter, 0, g.num_sms)));
+        g.sh_send.ensure_grow((S ? S : 1) * rs) && g.sh_recv.ensure_grow((R ? R : 1) * rs) &&
+        g.sh_x.ensure_grow((R ? R : 1) * xrow) && g.sh_ridx.ensure_grow((R ? R : 1) * K * 4) &&
+        g.sh_rgates.ensure_grow((R ? R : 1) * K * 4) && g.sh_part.ensure_grow((R ? R : 1) * (size_t)H * 4) &&
+        g.sh_back.ensure_grow((S ? S : 1) * (size_t)H * 4) &&
+        (R == 0 ||
+         g.pf_scratch.ensure_grow(cz::prefill_scratch_bytes((int)R, H, E, K, (int)L.d.inter, 0, g.num_sms)));
     if (grow) {
         const int v = bufs_ok ? 1 : 0;
         int all = 0;
@@ -1604,6 +1613,18 @@ CZ_EXPORT int colizig_cuda_ep_abort(void) {
     return CZ_OK;
 }
 
+// Tokens one decode launch of this layer takes (a decode-sized call of T tokens is
+// ceil(T / n) launches); 0 when the layer is unknown or the decode kernel cannot
+// take its dims.
+CZ_EXPORT int colizig_cuda_moe_decode_batch(uint32_t layer, int x_dtype) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g.layers.find(layer);
+    if (!g.inited || it == g.layers.end() || (x_dtype != COLIZIG_X_F32 && x_dtype != COLIZIG_X_BF16)) return 0;
+    const colizig_moe_dims& d = it->second.d;
+    return cz::decode_max_tokens((int)d.hidden, (int)d.experts, (int)d.topk, (int)d.inter, (int)d.shared_inter,
+                                 x_dtype == COLIZIG_X_BF16, g.num_sms);
+}
+
 // How expert-parallel decode calls sum the ranks: 1 = inside the decode kernel
 // (peer stores into every rank's receive buffer), 0 = one NCCL all-reduce per call.
 CZ_EXPORT int colizig_cuda_ep_combine_mode(void) {
@@ -1645,10 +1666,10 @@ constexpr int kNoAllocMaxTokens = 4;  // tokens per launch through the static sc
 constexpr size_t kNoAllocSyncBytes = 768;
 constexpr int kNoAllocMaxInter = 1024;  // moe_intermediate and shared_intermediate
 // tagged 8-byte exchange words (router logits, h rows), as the decode kernel reads them
-constexpr size_t kNoAllocLogitBytes = (size_t)cz::kDecodeMaxTokens * ((cz::kMaxExperts + 1 + 3) & ~3) * 8;
-constexpr size_t kNoAllocHBytes = (size_t)cz::kDecodeMaxTokens * (cz::kMaxTopk + 1) * kNoAllocMaxInter * 8;
+constexpr size_t kNoAllocLogitBytes = (size_t)kNoAllocMaxTokens * ((cz::kMaxExperts + 1 + 3) & ~3) * 8;
+constexpr size_t kNoAllocHBytes = (size_t)kNoAllocMaxTokens * (cz::kMaxTopk + 1) * kNoAllocMaxInter * 8;
 constexpr size_t kNoAllocBytes = kNoAllocSyncBytes + kNoAllocLogitBytes + kNoAllocHBytes;
-static_assert(kNoAllocMaxTokens == cz::kDecodeMaxTokens, "one launch's scratch");
+static_assert(kNoAllocMaxTokens <= cz::kDecodeMaxTokens, "one launch's scratch");
 static_assert(cz::kSyncWords * sizeof(uint32_t) <= kNoAllocSyncBytes, "sync words");
 static_assert(kNoAllocBytes == 574336, "the size stated in colizig_cuda.h");
 

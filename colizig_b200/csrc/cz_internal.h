@@ -9,7 +9,7 @@
 
 namespace cz {
 
-constexpr int kDecodeMaxTokens = 4;   // per decode launch (more tokens cost more slabs of the down pass than a second launch)
+constexpr int kDecodeMaxTokens = 8;   // per decode launch (one kernel instance per count; tokens sharing an expert read its rows once)
 constexpr int kMaxTopk = 16;
 constexpr int kMaxExperts = 512;
 constexpr int kMaxGrid = 160;         // decode CTAs (one per SM) the no-allocation scratch is sized for

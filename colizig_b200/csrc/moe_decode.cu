@@ -77,12 +77,17 @@ constexpr int SLOT_BYTES = 33 * 1024;     // >= GU_BYTES + SC_BYTES; also one pa
 constexpr int NSLOT = 4;                  // ring slots at least (more when shared memory allows)
 constexpr int MAXSLOT = 6;
 constexpr int RING_BYTES = NSLOT * SLOT_BYTES;  // the smallest ring (also stages phase R)
-constexpr int MAXT = kDecodeMaxTokens;    // 4
+constexpr int MAXT = kDecodeMaxTokens;    // 8
 constexpr int DHW = 1024;                 // phase D: words of a warp's f16 h terms (intermediate <= 1024)
 constexpr int DMR = 32;                   // phase D: output rows per CTA at most
 constexpr int MAXK = kMaxTopk;            // 16
 constexpr int MAXE = kMaxExperts;         // 512
-constexpr int MAXP = MAXT * (MAXK + 1);   // (token, slot) pairs incl. shared-expert pairs: 68
+// (token, slot) pairs of one launch incl. shared-expert pairs: at most 68 (four
+// tokens at the largest top-k; eight at top-8), decode_max_tokens keeps T * (K + 1)
+// below; the grouping warp sorts up to 96 (3 positions a lane)
+constexpr int MAXSORT = 4 * (MAXK + 1);
+constexpr int MAXP = MAXSORT;
+static_assert(MAXP <= 96, "the grouping warp's 3 positions a lane");
 constexpr int MAXG = MAXP;                // groups <= pairs
 constexpr int SMEM_LIMIT = 227 * 1024;
 
@@ -1956,8 +1961,9 @@ int decode_max_tokens(int H, int E, int K, int I, int SI, int x_bf16, int num_sm
     const int max_rows = (E + (SI ? 1 : 0) + num_sms - 1) / num_sms;  // router rows staged per CTA
     int t = MAXT;
     while (t > 0) {
-        // gate/up MMA columns: a group holds at most t pairs, each as JX E4M3 term columns (<= 16)
-        if (t * (x_bf16 ? 2 : 3) > 16) {
+        // gate/up MMA columns: a group holds at most t pairs, each as JX E4M3 term columns (<= 16);
+        // a launch holds at most MAXSORT (token, slot) pairs
+        if (t * (x_bf16 ? 2 : 3) > 16 || t * (K + (SI ? 1 : 0)) > MAXSORT) {
             --t;
             continue;
         }
@@ -2022,9 +2028,10 @@ int decode_launch(const DecodeParams& prm, int num_sms, cudaStream_t stream) {
     const int tmax = decode_max_tokens(prm.H, prm.E, prm.K, prm.I, prm.SI, prm.x_bf16, num_sms);
     if (prm.T < 1 || prm.T > tmax) return CZ_ESHAPE;
     if (prm.rms_w && prm.x_bf16) return CZ_EARGS;
-    static_assert(MAXT == 4, "one kernel instance per token count");
+    static_assert(MAXT == 8, "one kernel instance per token count");
     static void (*const kern[MAXT])(DecodeParams) = {moe_decode_kernel<1>, moe_decode_kernel<2>, moe_decode_kernel<3>,
-                                                      moe_decode_kernel<4>};
+                                                      moe_decode_kernel<4>, moe_decode_kernel<5>, moe_decode_kernel<6>,
+                                                      moe_decode_kernel<7>, moe_decode_kernel<8>};
     if (!g_attr_set) {
         for (int i = 0; i < MAXT; ++i)
             if (cudaFuncSetAttribute(kern[i], cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT) != cudaSuccess)

@@ -211,6 +211,12 @@ int colizig_cuda_ep_abort(void);
  * host waits for a collective (colizig_cuda_ep_set_timeout, 60 s by default);
  * rows that never arrive make the call (or colizig_cuda_moe_check) return -7. */
 int colizig_cuda_ep_combine_mode(void);
+
+/* No reference counterpart.  How many tokens one decode launch of registered
+ * layer `layer` takes for x_dtype (COLIZIG_X_F32 / COLIZIG_X_BF16): a call of T
+ * tokens below the prefill size (32) runs ceil(T / n) decode launches.  0 when
+ * the layer is unknown.  For hosts that budget launches (and the benchmark). */
+int colizig_cuda_moe_decode_batch(uint32_t layer, int x_dtype);
 int colizig_cuda_ep_set_combine(int in_kernel);
 
 /* Device-side error word of the last asynchronous call(s) on the library's

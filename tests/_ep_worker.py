@@ -54,9 +54,11 @@ def main() -> int:
             ep.set_combine(True)
             torch.cuda.synchronize()
             moe.check()
-            if not torch.equal(out, out_nccl):
-                print(f"rank {rank} {cfg} T={T}: in-kernel and NCCL combines differ by "
-                      f"{(out - out_nccl).abs().max().item():.3e}", flush=True)
+            # two ranks: a + b commutes, so the bits agree; more ranks: NCCL's summation
+            # order is its own, so within a few f32 roundings of the output
+            diff = (out - out_nccl).abs().max().item()
+            if (world == 2 and diff != 0.0) or diff > 1e-6 * out.abs().max().item():
+                print(f"rank {rank} {cfg} T={T}: in-kernel and NCCL combines differ by {diff:.3e}", flush=True)
                 ok = False
             if rank == 0:
                 ol = oracle.layer_from_dict(wn)
@@ -69,7 +71,7 @@ def main() -> int:
                 ok &= same and e_or <= OUT_TOL and e_one <= OUT_TOL and torch.equal(idx, ridx) and torch.equal(gates, rg)
         if cfg == "c2":
             # many calls back to back (receive slots reused every second call, the
-            # 4-token launches of a 9-token call each exchanging): each equals its first result
+            # decode launches of a 9-token call each exchanging): each equals its first result
             xs = [synth.make_tokens(T, d.hidden, 500 + T, device="cuda", dtype=torch.bfloat16) for T in (1, 9, 3)]
             firsts = [moe.forward(Lep, x)[0] for x in xs]
             same = True
@@ -89,7 +91,9 @@ def main() -> int:
     Lep = moe.Layer.from_weights(lid, d, w, ep=True)
     Lfull = moe.Layer.from_weights(lid + 1, d, w)
     wn = synth.to_numpy_layer(w) if rank == 0 else None
-    for Ts in ((40, 72), (48, 0), (3, 5)):
+    # per-rank batch sizes (two-rank cases extended to `world` ranks)
+    for Ts in [tuple((b[r] if r < 2 else (17 * r + 5) % 60) for r in range(world))
+               for b in ((40, 72), (48, 0), (3, 5))]:
         xs = [synth.make_tokens(t, d.hidden, 900 + 17 * i + t, device="cuda", dtype=torch.bfloat16)
               for i, t in enumerate(Ts)]
         xall = torch.cat(xs)
@@ -122,7 +126,7 @@ def main() -> int:
     full_l = [moe.Layer.from_weights(lid + 10 + l, d, ws[l]) for l in range(NL)]
     rng = np.random.default_rng(5)
     norm_w = (1.0 + 0.05 * rng.standard_normal((NL, d.hidden))).astype(np.float32)
-    Ts = (40, 24)
+    Ts = tuple((40, 24)[r] if r < 2 else 8 * r for r in range(world))
     h0 = [rng.standard_normal((t, d.hidden)).astype(np.float32) for t in Ts]
     od = oracle.Dims(d.hidden, d.experts, d.topk, d.inter, d.shared_inter, d.norm_topk)
     h = h0[rank].copy()
