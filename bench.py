@@ -48,7 +48,7 @@ EXPERT_BYTES = {}  # per config: bytes of one expert (3 projections + scales)
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
 # moe_decode_kernel launch, from an ncu capture of the same workload; other
 # (config, tokens) pairs report null until captured.
-NCU_TRAFFIC = {("c2", 1): 39.03e6, ("c3", 2048): 535.5e6}
+NCU_TRAFFIC = {("c2", 1): 39.02e6, ("c3", 2048): 535.5e6}
 
 
 def expert_bytes(d) -> int:
