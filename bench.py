@@ -234,6 +234,9 @@ def reference_arm(args):
     if args.config == "c4":
         reference_stack(args)
         return
+    if args.config == "attn":
+        attn_reference(args)
+        return
     d = synth.CONFIGS[args.config]
     T = args.tokens
     Ts = min(T, 64)  # each step: a bounded sample of the batch (prefill batches are thousands of tokens)
@@ -631,6 +634,185 @@ def sharded_main(args, world, rank, local, torch, dist, cz, _abi, moe, synth):
         lay.unregister()
 
 
+# ---- attention projections (config "attn") -----------------------------------
+# The FP8 projections of Qwen3-30B-A3B's attention (src/qwen3moe/attn.zig:46-78):
+# q [32*128, 2048], k and v [4*128, 2048], o [2048, 32*128], E4M3 with 128 x 128
+# block scales, keyed by attnKey and computed by the per-matrix call
+# colizig_cuda_matmul_fp8 (matmulFp8Keyed, src/ops/fp8.zig:165-188).  One step =
+# the four projections of one layer for the step's tokens (the attention core
+# between them is outside this path).
+ATTN_SHAPES = ((32 * 128, 2048), (4 * 128, 2048), (4 * 128, 2048), (2048, 32 * 128))  # q, k, v, o: (O, I)
+
+
+def attn_layer(l, synth, torch):
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(7000 + l)
+    return [(synth._e4m3((O, I), gen, "cpu").numpy(), synth._scales(((O + 127) // 128, (I + 127) // 128), gen,
+                                                                       "cpu").numpy()) for O, I in ATTN_SHAPES]
+
+
+def attn_inputs(T, i):
+    rng = np.random.default_rng(9100 + i)
+    return (rng.standard_normal((T, ATTN_SHAPES[0][1])).astype(np.float32),
+            rng.standard_normal((T, ATTN_SHAPES[3][1])).astype(np.float32))
+
+
+def attn_bytes(T):
+    nb = lambda x: (x + 127) // 128  # noqa: E731
+    return sum(O * I + nb(O) * nb(I) * 4 + T * (I + O) * 4 for O, I in ATTN_SHAPES)
+
+
+def attn_config(args):
+    return {"workload": f"Qwen3-30B-A3B attention projections q/k/v/o (FP8 E4M3, 128x128 block scales), "
+                        f"{args.tokens} token(s)/step, one layer's four keyed calls per step",
+            "hidden": 2048, "q_heads": 32, "kv_heads": 4, "head_dim": 128, "tokens_per_step": args.tokens,
+            "global_batch": args.tokens, "layers_cycled": args.layers,
+            "l2": "inputs larger than L2: steps cycle through the layers' weights",
+            "parallelism": "single GPU"}
+
+
+def attn_main(args, torch, cz, moe, synth):
+    """Our arm.  value: the four projections of every step as device-pointer
+    launches (colizig_cuda_matmul_fp8_device) in one captured CUDA graph, timed by
+    CUDA events (median of the replays, L2 flushed before each).  e2e: the keyed
+    host-pointer calls the reference makes (colizig_cuda_matmul_fp8 with attnKey
+    keys, synchronous, weights resident after the first call of each key)."""
+    from colizig_b200 import _abi
+
+    T, NL = args.tokens, args.layers
+    L = [attn_layer(l, synth, torch) for l in range(NL)]
+    xs = [attn_inputs(T, i) for i in range(16)]
+    dev = torch.device("cuda", 0)
+    lib = _abi.load()
+    Wd = [[(torch.from_numpy(w).to(dev), torch.from_numpy(sc).to(dev)) for w, sc in L[l]] for l in range(NL)]
+    xd = [(torch.from_numpy(x).to(dev), torch.from_numpy(a).to(dev)) for x, a in xs]
+    outs = [torch.empty((T, O), dtype=torch.float32, device=dev) for O, _ in ATTN_SHAPES]
+
+    def dstep(i, sh):
+        x, a = xd[i % len(xd)]
+        for r, (O, I) in enumerate(ATTN_SHAPES):
+            w, sc = Wd[i % NL][r]
+            rc = lib.colizig_cuda_matmul_fp8_device(outs[r].data_ptr(), (a if r == 3 else x).data_ptr(),
+                                                    w.data_ptr(), sc.data_ptr(), T, I, O, sh)
+            if rc:
+                raise cz.ColizigError("colizig_cuda_matmul_fp8_device", rc)
+
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        dstep(i, stream.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=dev)):
+        gs = torch.cuda.current_stream().cuda_stream
+        for k in range(args.steps):
+            dstep(args.warmup + k, gs)
+    graph.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(0)
+    sampler.start()
+    time.sleep(0.3)
+    replay_ms = timed_replays(torch, graph, stream, dev, REPLAYS)
+    clocks = sampler.stop()
+    del graph
+    step_ms = float(statistics.median(replay_ms)) / args.steps
+    hbm_peak, _, peak_kind = load_peaks()
+    gbs = attn_bytes(T) / (step_ms / 1e3) / 1e9
+
+    # end to end: the reference's calls, host buffers, keyed residency
+    cz.gpu.set_vram_budget(1 << 34)
+    key = cz.fp8.attn_key
+
+    def hstep(i):
+        l = i % NL
+        x, a = xs[i % len(xs)]
+        for r in range(4):
+            cz.fp8.matmul_fp8_keyed(a if r == 3 else x, *L[l][r], key=key(l, r))
+
+    for i in range(max(args.warmup, NL)):  # every key uploaded once (misses), then hits
+        hstep(i)
+    h0, m0, _, _ = cz.gpu.stats()
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        hstep(args.warmup + k)
+    e2e_s = time.perf_counter() - t0
+    h1, m1, _, _ = cz.gpu.stats()
+    if (h1 - h0, m1 - m0) != (4 * args.steps, 0):
+        raise RuntimeError(f"keyed store: {h1 - h0} hits, {m1 - m0} misses in the timed calls")
+    cz.gpu.set_vram_budget(0)
+    cpu = None
+    if not args.no_cpu:
+        import oracle
+
+        cores = os.cpu_count() or 1
+        oracle.set_threads(cores)
+        n, c0 = 0, time.perf_counter()
+        while time.perf_counter() - c0 < args.cpu_seconds / 3 and n < 10000:
+            x, a = xs[n % len(xs)]
+            for r in range(4):
+                oracle.matmul_fp8(a if r == 3 else x, *L[n % NL][r])
+            n += 1
+        dt = time.perf_counter() - c0
+        oracle.set_threads(1)
+        cpu = {"value": n * T / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{n} steps (4 projections of T={T}) in {dt:.1f} s over {NL} layers (C restatement of "
+                         f"matmulFp8Cpu, {cores} threads)"}
+    line = {
+        "metric": f"attention-projection tokens/s (Qwen3-30B-A3B q/k/v/o, T={T})",
+        "value": T / (step_ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 weights (f16 decode) x f32 tokens -> f32",
+        "data": "synthetic", "config": attn_config(args),
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                     "traffic": None, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "kernel": "fp8_matmul_kernel (four launches a step)", "bytes_per_step": attn_bytes(T)},
+        "e2e": {"value": args.steps * T / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * (3 * 2048 + 4096) * 4,
+                "d2h_bytes_per_step": T * (4096 + 512 + 512 + 2048) * 4, "ms_per_step": e2e_s / args.steps * 1e3,
+                "caller": "python ctypes, four synchronous host-pointer colizig_cuda_matmul_fp8 calls a step "
+                          "(attnKey keys, resident)"},
+        "cpu_baseline": cpu, "clocks": clocks,
+        "timing": {"replays": REPLAYS, "replay_ms": replay_ms, "statistic": "median over replays",
+                   "l2": f"flushed before each replay; steps cycle through {NL} layers ({NL * attn_bytes(0) >> 20} MiB)"},
+        "gpu_launches": 4 * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def attn_reference(args):
+    """Reference arm: the oracle's restatement of matmulFp8Cpu on the same calls."""
+    import torch
+
+    import oracle
+    from colizig_b200 import synth
+
+    T, NL = args.tokens, min(args.layers, 4)
+    L = [attn_layer(l, synth, torch) for l in range(NL)]
+    xs = [attn_inputs(T, i) for i in range(16)]
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+
+    def step(i):
+        x, a = xs[i % len(xs)]
+        for r in range(4):
+            oracle.matmul_fp8(a if r == 3 else x, *L[i % NL][r])
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        step(args.warmup + k)
+    dt = time.perf_counter() - t0
+    value = args.steps * T / dt
+    print(json.dumps({
+        "impl": "reference", "metric": f"attention-projection tokens/s (Qwen3-30B-A3B q/k/v/o, T={T})",
+        "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "config": attn_config(args),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} steps of the four projections over {NL} layers (C restatement "
+                                   f"of matmulFp8Cpu, {cores} threads)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
+
+
 def metric_name(args, T):
     mode = "prefill" if T >= PREFILL_MIN_TOKENS else "decode"
     return f"MoE-layer {mode} tokens/s ({args.config}, T={T})"
@@ -710,6 +892,11 @@ def main():
         from colizig_b200 import ep
 
         ep.init()
+    if args.config == "attn":
+        if world > 1:
+            raise SystemExit("--config attn runs on one GPU")
+        attn_main(args, torch, cz, moe, synth)
+        return
     if args.config == "c4":
         stack_main(args, world, rank, local, torch, dist, cz, _abi, moe, synth)
         if world > 1:

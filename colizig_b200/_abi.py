@@ -21,6 +21,7 @@ REFERENCE_SYMBOLS = (
     "colizig_cuda_device_name",
     "colizig_cuda_shutdown",
     "colizig_cuda_matmul_fp8",
+    "colizig_cuda_matmul_fp8_device",
     "colizig_cuda_set_vram_budget",
     "colizig_cuda_stats",
 )
@@ -135,6 +136,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         L.colizig_cuda_stats.argtypes = [P64, P64, P64, P64]
         L.colizig_cuda_matmul_fp8.restype = i32
         L.colizig_cuda_matmul_fp8.argtypes = [vp, vp, vp, vp, i32, i32, i32, u64]
+        L.colizig_cuda_matmul_fp8_device.restype = i32
+        L.colizig_cuda_matmul_fp8_device.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp]
         L.colizig_cuda_moe_register_layer.restype = i32
         L.colizig_cuda_moe_register_layer.argtypes = [u32, ctypes.POINTER(MoeDims), vp, ctypes.POINTER(MoeExpert),
                                                       ctypes.POINTER(MoeExpert), vp, u32]

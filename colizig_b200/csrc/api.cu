@@ -181,6 +181,7 @@ struct Ctx {
     DevBuf logits, hrows, io_x, io_out, io_res, ones, pf_scratch;
     DevBuf shb_scratch;  // BF16 shared expert: gate/up rows and sigmoid gates of the call's tokens
     HostBuf io_host;  // pinned staging of io_res (host-pointer forward, up to kHostStageCap bytes)
+    HostBuf mm_xh, mm_yh;  // pinned staging of colizig_cuda_matmul_fp8's x and y (up to kHostStageCap bytes)
     HostBuf io_xh;    // pinned staging of the tokens (host-pointer forward, up to kHostStageCap bytes)
     uint32_t* sync = nullptr;
     // expert parallelism (one process per GPU)
@@ -476,6 +477,8 @@ void shutdown_locked() {
     drop_host_graphs(true, 0);
     g.io_host.release();
     g.io_xh.release();
+    g.mm_xh.release();
+    g.mm_yh.release();
     for (DevBuf* b : {&g.d_x, &g.d_y, &g.d_w, &g.d_s, &g.logits, &g.hrows, &g.pf_scratch, &g.shb_scratch, &g.io_x, &g.io_out, &g.io_res,
                       &g.ones, &g.sh_idx, &g.sh_gates, &g.sh_xn, &g.sh_slot, &g.sh_counts, &g.sh_allc,
                       &g.sh_tmp, &g.sh_send, &g.sh_recv, &g.sh_x, &g.sh_ridx, &g.sh_rgates, &g.sh_part, &g.sh_back})
@@ -610,7 +613,7 @@ void take_debug_hold(cz::DecodeParams& p) {
 }
 
 // Kernel timer.  Kinds of the recorded launch pairs.
-constexpr int kTimerDecode = 1, kTimerPrefillGateUp = 2, kTimerPrefillDown = 3;
+constexpr int kTimerDecode = 1, kTimerPrefillGateUp = 2, kTimerPrefillDown = 3, kTimerMatmul = 4;
 
 // Reserves `pairs` consecutive begin/end event pairs of the timer (all of kind
 // `kind`); nullptr when the timer is off or full.  The events are recorded with
@@ -937,6 +940,18 @@ CZ_EXPORT int colizig_cuda_init_device(int device) {
 
 CZ_EXPORT const char* colizig_cuda_device_name(void) { return g.inited ? g.name : ""; }
 
+// colizig_cuda_matmul_fp8's computation on device pointers, asynchronous on
+// `stream` (NULL = the default stream): for hosts that keep activations and
+// weights on the GPU (no keyed store, no staging).
+CZ_EXPORT int colizig_cuda_matmul_fp8_device(float* y, const float* x, const unsigned char* w, const float* scales,
+                                             int S, int I, int O, void* stream) {
+    CsrGuard _csr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited || S < 1 || I < 1 || O < 1 || !y || !x || !w || !scales) return CZ_EARGS;
+    cudaSetDevice(g.dev);
+    return cz::fp8_matmul_launch(y, x, w, scales, S, I, O, reinterpret_cast<cudaStream_t>(stream));
+}
+
 CZ_EXPORT void colizig_cuda_set_vram_budget(uint64_t bytes) {
     CsrGuard _csr;
     std::lock_guard<std::mutex> lk(g_mu);
@@ -976,7 +991,13 @@ CZ_EXPORT int colizig_cuda_matmul_fp8(float* y, const float* x, const unsigned c
     const size_t sb = nb(O) * nb(I) * sizeof(float);
     const size_t yb = (size_t)S * O * sizeof(float);
     if (!g.d_x.ensure(xb) || !g.d_y.ensure(yb)) return CZ_EALLOC;
-    if (cudaMemcpyAsync(g.d_x.p, x, xb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess) return CZ_EH2D;
+    // decode-sized calls (the attention projections of one token, attn.zig:46-50) go through
+    // the library's page-locked staging: x is copied from it, and the kernel writes y into
+    // its mapped device view, so the call makes one host copy each way and no D2H copy
+    const bool staged = xb <= kHostStageCap && yb <= kHostStageCap && g.mm_xh.ensure(xb) && g.mm_yh.ensure(yb);
+    if (staged) memcpy(g.mm_xh.p, x, xb);
+    if (cudaMemcpyAsync(g.d_x.p, staged ? g.mm_xh.p : x, xb, cudaMemcpyHostToDevice, g.stream) != cudaSuccess)
+        return CZ_EH2D;
 
     const void* wdev = nullptr;
     const void* sdev = nullptr;
@@ -1033,11 +1054,16 @@ CZ_EXPORT int colizig_cuda_matmul_fp8(float* y, const float* x, const unsigned c
         wdev = g.d_w.p;
         sdev = g.d_s.p;
     }
-    if (cz::fp8_matmul_launch(g.d_y.as<float>(), g.d_x.as<float>(), (const uint8_t*)wdev, (const float*)sdev, S, I,
-                              O, g.stream) != CZ_OK)
+    float* const ydev = staged ? static_cast<float*>(g.mm_yh.dev) : g.d_y.as<float>();
+    cudaEvent_t* ev = timer_take(kTimerMatmul, 1);
+    if (ev && cudaEventRecord(ev[0], g.stream) != cudaSuccess) return CZ_ELAUNCH;
+    if (cz::fp8_matmul_launch(ydev, g.d_x.as<float>(), (const uint8_t*)wdev, (const float*)sdev, S, I, O, g.stream) !=
+        CZ_OK)
         return CZ_ELAUNCH;
-    if (cudaMemcpyAsync(y, g.d_y.p, yb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess) return CZ_ED2H;
+    if (ev && cudaEventRecord(ev[1], g.stream) != cudaSuccess) return CZ_ELAUNCH;
+    if (!staged && cudaMemcpyAsync(y, g.d_y.p, yb, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess) return CZ_ED2H;
     if (cudaStreamSynchronize(g.stream) != cudaSuccess) return CZ_ED2H;
+    if (staged) memcpy(y, g.mm_yh.p, yb);
     return CZ_OK;
 }
 

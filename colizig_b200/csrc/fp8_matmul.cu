@@ -14,6 +14,7 @@
 namespace cz {
 
 constexpr int kMmWarps = 8;
+constexpr int kMmChunks = 4;
 
 __global__ void __launch_bounds__(kMmWarps * 32) fp8_matmul_kernel(float* __restrict__ y, const float* __restrict__ x,
                                                                   const uint8_t* __restrict__ w,
@@ -30,24 +31,37 @@ __global__ void __launch_bounds__(kMmWarps * 32) fp8_matmul_kernel(float* __rest
         const int ns = min(4, S - s0);
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         if (vec) {
-            for (int ch = lane; ch < (I >> 4); ch += 32) {
-                float f[16];
-                decode16(__ldg(reinterpret_cast<const uint4*>(wr) + ch), f);
-                const float sc = __ldg(sr + (ch >> 3));
+            // kMmChunks 16-byte chunks of the row in flight per lane before any is used
+            // (a decode-sized call is one pass: the loads, not the arithmetic, set its time)
+            const int nch = I >> 4;
+            for (int c0 = lane; c0 < nch; c0 += 32 * kMmChunks) {
+                uint4 wv[kMmChunks];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    if (q < ns) {
-                        const float4* xp = reinterpret_cast<const float4*>(x + (size_t)(s0 + q) * I) + ch * 4;
-                        float d0 = 0.f, d1 = 0.f;
+                for (int u = 0; u < kMmChunks; ++u)
+                    wv[u] = c0 + 32 * u < nch ? __ldg(reinterpret_cast<const uint4*>(wr) + c0 + 32 * u)
+                                              : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-                        for (int v = 0; v < 4; ++v) {
-                            const float4 xv = __ldg(xp + v);
-                            d0 = __fmaf_rn(xv.x, f[4 * v + 0], d0);
-                            d1 = __fmaf_rn(xv.y, f[4 * v + 1], d1);
-                            d0 = __fmaf_rn(xv.z, f[4 * v + 2], d0);
-                            d1 = __fmaf_rn(xv.w, f[4 * v + 3], d1);
+                for (int u = 0; u < kMmChunks; ++u) {
+                    const int ch = c0 + 32 * u;
+                    if (ch >= nch) break;
+                    float f[16];
+                    decode16(wv[u], f);
+                    const float sc = __ldg(sr + (ch >> 3));
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        if (q < ns) {
+                            const float4* xp = reinterpret_cast<const float4*>(x + (size_t)(s0 + q) * I) + ch * 4;
+                            float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+                            for (int v = 0; v < 4; ++v) {
+                                const float4 xv = __ldg(xp + v);
+                                d0 = __fmaf_rn(xv.x, f[4 * v + 0], d0);
+                                d1 = __fmaf_rn(xv.y, f[4 * v + 1], d1);
+                                d0 = __fmaf_rn(xv.z, f[4 * v + 2], d0);
+                                d1 = __fmaf_rn(xv.w, f[4 * v + 3], d1);
+                            }
+                            acc[q] = __fmaf_rn(sc, d0 + d1, acc[q]);
                         }
-                        acc[q] = __fmaf_rn(sc, d0 + d1, acc[q]);
                     }
                 }
             }

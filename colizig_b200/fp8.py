@@ -43,3 +43,12 @@ def matmul_fp8(x: np.ndarray, w: np.ndarray, scales: np.ndarray) -> np.ndarray:
 def expert_key(layer: int, expert: int, role: int) -> int:
     """moe.zig:97-99: 1 + ((layer*512 + expert)*4 + role), role 0/1/2 = gate/up/down."""
     return 1 + (layer * 512 + expert) * 4 + role
+
+
+def attn_key(layer: int, role: int) -> int:
+    """src/qwen3moe/attn.zig:46-50 attnKey: the expert slot 1020 + role (0..3 = q/k/v/o)
+    of the expert key scheme, so attention projections share the keyed store."""
+    if not 0 <= role <= 3:
+        raise ValueError("role is 0..3 (q, k, v, o)")
+    return expert_key(layer, 1020 + role, 0)
+

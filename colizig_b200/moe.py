@@ -315,7 +315,7 @@ def check(stream=None) -> None:
     _abi.check("colizig_cuda_moe_check", _abi.load().colizig_cuda_moe_check(h))
 
 
-TIMER_DECODE, TIMER_PREFILL_GATE_UP, TIMER_PREFILL_DOWN = 1, 2, 3
+TIMER_DECODE, TIMER_PREFILL_GATE_UP, TIMER_PREFILL_DOWN, TIMER_MATMUL = 1, 2, 3, 4
 
 
 def kernel_timer(capacity: int) -> None:
@@ -327,7 +327,8 @@ def kernel_timer(capacity: int) -> None:
 
 def kernel_timer_read(max_n: int = 1 << 16) -> list:
     """[(kind, ms)] of the launch pairs recorded since the timer was armed (waits
-    for them).  kind is TIMER_DECODE, TIMER_PREFILL_GATE_UP or TIMER_PREFILL_DOWN."""
+    for them).  kind is TIMER_DECODE, TIMER_PREFILL_GATE_UP, TIMER_PREFILL_DOWN or
+    TIMER_MATMUL (a colizig_cuda_matmul_fp8 kernel)."""
     kinds = (ctypes.c_int * max_n)()
     ms = (ctypes.c_float * max_n)()
     n = _abi.load().colizig_cuda_kernel_timer_read(ctypes.addressof(kinds), ctypes.addressof(ms), max_n)

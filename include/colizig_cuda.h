@@ -73,6 +73,14 @@ void colizig_cuda_shutdown(void);
 int colizig_cuda_matmul_fp8(float* y, const float* x, const unsigned char* w, const float* scales, int S,
                             int I, int O, uint64_t key);
 
+/* No reference counterpart: colizig_cuda_matmul_fp8 on device pointers, queued
+ * on `stream` (NULL = the default stream) and returning at once; weights and
+ * scales are the caller's device arrays (no keyed store).  For hosts that keep
+ * activations on the GPU, e.g. the attention projections of a decoder loop
+ * captured into a CUDA graph.  0, -1 (arguments), -4 (launch). */
+int colizig_cuda_matmul_fp8_device(float* y, const float* x, const unsigned char* w, const float* scales, int S,
+                                   int I, int O, void* stream);
+
 /* ---- Part 2: MoE layer entry points (no reference counterpart) ---------- */
 
 /* Mirrors moe.zig:23-30 Dims.  shared_inter == 0 -> no shared expert. */
@@ -257,9 +265,11 @@ int colizig_cuda_moe_forward_noalloc(uint32_t layer, const void* x, int x_dtype,
  * MoE forward records a CUDA event pair around each decode kernel launch and
  * around each of the two grouped GEMM launches of a prefill forward; the
  * records are external event nodes when the forward is captured into a CUDA
- * graph, so graph replays are timed too.  colizig_cuda_kernel_timer_read waits
- * for the events and writes, per recorded pair, its kind (1 decode kernel,
- * 2 prefill gate/up GEMM, 3 prefill down GEMM) and device time in ms; it
+ * graph, so graph replays are timed too; so does every colizig_cuda_matmul_fp8
+ * call around its kernel.  colizig_cuda_kernel_timer_read waits for the events
+ * and writes, per recorded pair, its kind (1 decode kernel, 2 prefill gate/up
+ * GEMM, 3 prefill down GEMM, 4 per-matrix block-FP8 matmul) and device time in
+ * ms; it
  * returns the number of pairs written, or -2 when pairs were dropped because
  * the timer was full. */
 int colizig_cuda_kernel_timer(int capacity);
