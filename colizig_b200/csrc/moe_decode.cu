@@ -1159,10 +1159,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
         }
         __syncthreads();
         // The first nd warps form the router logits (one (row, token) item each, in
-        // turn); each logit goes out as one tagged word the moment it is formed.  The
-        // other warps split the tokens into E4M3 terms meanwhile:
+        // turn); each logit goes out as one tagged word the moment it is formed.  Then
+        // every warp (the others at once) splits the tokens into E4M3 terms:
         //   x_t * 2^s_t = term 0 + term 1 (+ term 2), column (t, j) holding term j of
         //   token t, H bytes at xterm + (t*JX + j)*CS.
+        // The CTA polls the grid's logits only after the split, so the split is shared
+        // by all warps rather than left to the few without a router item.
         const int nd = nitems < NWARPS ? nitems : NWARPS;
         if (!s.abort) {
             if (warp < nd) {
@@ -1175,9 +1177,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_decode_kernel(const __grid_co
                         st_relaxed_u64(p.logits + (size_t)t * LS + row_lo + r, tag_word(tag, v));
                 }
             }
-            if (warp >= nd || nd == NWARPS) {
-                const int nsw = nd == NWARPS ? NWARPS : NWARPS - nd;  // warps on the split
-                const int st0 = (nd == NWARPS ? warp : warp - nd) * 32 + lane;
+            {
+                const int nsw = NWARPS;  // warps on the split
+                const int st0 = warp * 32 + lane;
                 for (int t = 0; t < T; ++t) {
                     const int sx = prescale_exp(__uint_as_float(s.xmax[t]));
                     uint8_t* col = xterm + (size_t)(t * cv.JX) * cv.CS;
