@@ -80,7 +80,7 @@ class Layer:
     def __init__(self, layer_id: int, dims: Dims, router, gate_w, gate_s, up_w, up_s, down_w, down_s,
                  shared: Optional[dict] = None, shared_gate=None, ep: bool = False):
         """ep=True: hold only this rank's experts (after ep.init); every forward then
-        sums the ranks' outputs (one NCCL all-reduce)."""
+        sums the ranks' outputs (inside the decode kernel, or one NCCL all-reduce)."""
         if not gpu.available():
             gpu.init()
         self.id = int(layer_id)

@@ -112,7 +112,9 @@ typedef struct colizig_moe_expert {
 
 #define COLIZIG_EP 2u /* register_layer: hold only this rank's experts (expert parallelism,
                          after colizig_cuda_ep_init); every forward of the layer then sums
-                         the ranks' outputs with one NCCL all-reduce on `stream` */
+                         the ranks' outputs on `stream`: inside the decode kernel for
+                         decode batches (see colizig_cuda_ep_combine_mode), else with one
+                         NCCL all-reduce */
 
 #define COLIZIG_EP_SHARDED 4u /* moe_forward / moe_stack_forward on COLIZIG_EP layers: x (h)
     holds this rank's own tokens (T may differ between ranks, 0 included) and
